@@ -1,0 +1,181 @@
+/*
+ * kvcache.h — C ABI of libkvcache.so, the B200 (sm_100a) paged-KV hot path.
+ *
+ * This library replaces the MLX/nanobind extension `_ext` of sglang-mlx
+ * (bindings.cpp, paged_attention/mlx_paged_attention.cpp,
+ * paged_attention/mlx_cache.cpp, paged_attention/mlx_device.cpp).  Every
+ * compute entry point takes tensors as DLPack `DLTensor` structs (restated
+ * below from the public DLPack specification, layout-identical), plain scalars
+ * and a CUDA stream handle.  Nothing here depends on PyTorch, MLX or Triton.
+ *
+ * Conventions
+ *  - Return value: KVC_OK (0) or a KVC_E* code.  The message of the last
+ *    failure on the calling thread is returned by kvc_last_error().  Messages of
+ *    argument errors reuse the reference's `std::invalid_argument` texts so a
+ *    Python shim can raise ValueError with the same wording.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream).  All launches
+ *    are asynchronous; no entry point allocates device memory on the compute
+ *    path (the caller owns `out` and any split-K workspace).
+ *  - Tensors must live on a CUDA device (kDLCUDA or kDLCUDAManaged).  The
+ *    launch runs on that device; the calling thread's current device is
+ *    restored afterwards.
+ *  - Kernels bounds-check slot ids and block ids against the cache extents and
+ *    skip out-of-range entries instead of faulting; the skip is recorded in a
+ *    sticky per-device status word read by kvc_get_status().
+ */
+#ifndef KVCACHE_H_
+#define KVCACHE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- DLPack structs (DLPack v0.8+ ABI, public spec) ---------------------- */
+typedef struct {
+  int32_t device_type; /* 1 = CPU, 2 = CUDA, 3 = CUDA host, 13 = CUDA managed */
+  int32_t device_id;
+} kvc_dldevice;
+
+typedef struct {
+  uint8_t code;   /* 0 int, 1 uint, 2 float, 4 bfloat */
+  uint8_t bits;
+  uint16_t lanes; /* must be 1 */
+} kvc_dldtype;
+
+typedef struct {
+  void* data;
+  kvc_dldevice device;
+  int32_t ndim;
+  kvc_dldtype dtype;
+  int64_t* shape;
+  int64_t* strides; /* in elements; NULL = compact row-major */
+  uint64_t byte_offset;
+} kvc_dltensor;
+
+/* ---- status codes --------------------------------------------------------- */
+#define KVC_OK 0
+#define KVC_EINVAL 1      /* bad shape / dtype / argument (reference: ValueError) */
+#define KVC_ECUDA 2       /* CUDA runtime error */
+#define KVC_ENOMEM 3      /* allocation failed (runtime helpers only) */
+#define KVC_EUNSUPPORTED 4
+
+/* Bits of the per-device status word (kvc_get_status). */
+#define KVC_STATUS_SLOT_OOB 0x1u    /* a slot id beyond the cache was skipped */
+#define KVC_STATUS_BLOCK_OOB 0x2u   /* a block-table entry beyond the cache was skipped */
+#define KVC_STATUS_WAIT_TIMEOUT 0x4u /* a bounded pipeline wait gave up */
+#define KVC_STATUS_INDEX_OOB 0x8u   /* a gather/copy index beyond its buffer was skipped */
+
+/* ---- errors / info --------------------------------------------------------- */
+/* Thread-local message of the last failing call ("" if none). */
+const char* kvc_last_error(void);
+/* Library version string. */
+const char* kvc_version(void);
+/* Reads (and optionally clears) the sticky status word of `device`.  This
+ * synchronises the device. */
+int kvc_get_status(int device, uint32_t* flags, int clear);
+
+/* ---- paged attention (decode) --------------------------------------------
+ * Replaces `_ext.paged_attention_v1` (bindings.cpp:44-65) and the C++ op
+ * `paged_attention_v1` (paged_attention/mlx_paged_attention.cpp:150-213) with
+ * its dispatch `PagedAttentionV1::eval_gpu` (mlx_paged_attention.cpp:93-144).
+ *   out          [num_seqs, num_heads, head_size], dtype of query, written
+ *   query        [num_seqs, num_heads, head_size]  f32 / f16 / bf16
+ *   key_cache    [num_blocks, num_kv_heads, head_size/x, block_size, x], x = 16/sizeof(cache)
+ *   value_cache  [num_blocks, num_kv_heads, head_size, block_size]
+ *   block_tables [num_seqs, max_num_blocks_per_seq] int32 or uint32 (read as uint32)
+ *   context_lens [num_seqs] int32 or uint32 (read as uint32)
+ *   alibi_slopes [num_heads] f32, or NULL
+ * Sequences with context_len == 0 or context_len > max_seq_len produce zeros
+ * (paged_attention_kernels.metal:45-50).  Softmax denominator is
+ * sum + 1e-6 (paged_attention_kernels.metal:144). */
+int kvc_paged_attention_v1(kvc_dltensor* out, const kvc_dltensor* query,
+                           const kvc_dltensor* key_cache, const kvc_dltensor* value_cache,
+                           const kvc_dltensor* block_tables, const kvc_dltensor* context_lens,
+                           int num_kv_heads, float scale, int block_size, int max_seq_len,
+                           const kvc_dltensor* alibi_slopes, void* stream);
+
+/* Split-K (partitioned) decode with a cross-partition log-sum-exp reduce.  No
+ * reference counterpart: sglang-mlx defers it (README.md:11-20); the argument
+ * list extends kvc_paged_attention_v1 with the caller-owned workspace
+ *   max_logits [num_seqs, num_heads, max_num_partitions] f32
+ *   exp_sums   [num_seqs, num_heads, max_num_partitions] f32
+ *   tmp_out    [num_seqs, num_heads, max_num_partitions, head_size] f32
+ * where max_num_partitions = ceil(max_seq_len / partition_size).  Results agree
+ * with kvc_paged_attention_v1 within floating-point reassociation. */
+int kvc_paged_attention_v2(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltensor* max_logits,
+                           kvc_dltensor* tmp_out, const kvc_dltensor* query,
+                           const kvc_dltensor* key_cache, const kvc_dltensor* value_cache,
+                           const kvc_dltensor* block_tables, const kvc_dltensor* context_lens,
+                           int num_kv_heads, float scale, int block_size, int max_seq_len,
+                           const kvc_dltensor* alibi_slopes, int partition_size, void* stream);
+
+/* ---- cache ops -------------------------------------------------------------
+ * Replaces `_ext.reshape_and_cache` (bindings.cpp:67-80), the C++ op
+ * `reshape_and_cache` (paged_attention/mlx_cache.cpp:256-278) and
+ * `ReshapeAndCache::eval_gpu` (mlx_cache.cpp:60-96).  key_cache/value_cache are
+ * updated in place (the reference aliases them, mlx_cache.cpp:65-66).
+ *   key, value   [num_tokens, num_kv_heads, head_size] f32 / f16 / bf16 (token stride free)
+ *   slot_mapping [num_tokens] int32 or int64; slot < 0 skips the token. */
+int kvc_reshape_and_cache(const kvc_dltensor* key, const kvc_dltensor* value,
+                          kvc_dltensor* key_cache, kvc_dltensor* value_cache,
+                          const kvc_dltensor* slot_mapping, void* stream);
+
+/* Replaces `_ext.reshape_and_cache_flash` (bindings.cpp:82-95,
+ * mlx_cache.cpp:280-300, eval mlx_cache.cpp:118-152).  Caches are
+ * [num_blocks, block_size, num_kv_heads, head_size] (the MHATokenPool layout
+ * (pool_size + 1, H, D) is the block_size = 1 case when passed as 3-D).  The
+ * source may have any token and head strides, so MHATokenPool.store's
+ * (1, H, S, D) -> (S, H, D) transpose (memory_pool.py:117-137) needs no copy. */
+int kvc_reshape_and_cache_flash(const kvc_dltensor* key, const kvc_dltensor* value,
+                                kvc_dltensor* key_cache, kvc_dltensor* value_cache,
+                                const kvc_dltensor* slot_mapping, void* stream);
+
+/* Slot gather behind MHATokenPool.fetch (memory_pool.py:139-159): for both K
+ * and V, out[0, h, t, :] = buffer[indices[t], h, :].
+ *   k_out, v_out         [1, H, T, D]  (any strides)
+ *   k_buffer, v_buffer   [pool_size + 1, H, D] (or [nb, bs, H, D], slots flattened)
+ *   indices              [T] int32 or int64 */
+int kvc_gather_kv(kvc_dltensor* k_out, kvc_dltensor* v_out, const kvc_dltensor* k_buffer,
+                  const kvc_dltensor* v_buffer, const kvc_dltensor* indices, void* stream);
+
+/* ---- device attributes (paged_attention/mlx_device.cpp) -------------------- */
+/* mlx_device.cpp:16-20: max shared memory per block (opt-in) of `device`. */
+int kvc_get_max_shared_memory_per_block_device_attribute(int device, int64_t* out);
+/* mlx_device.cpp:12-14 throws on Metal; here it returns cudaDeviceGetAttribute. */
+int kvc_get_device_attribute(int attribute, int device, int64_t* out);
+
+/* ---- runtime helpers (the MLX allocator/stream roles, e.g.
+ * mlx_paged_attention.cpp:99 `mx::allocator::malloc`; used by the Python
+ * DeviceArray and the benches, never inside a compute entry point) ---------- */
+int kvc_device_count(int* count);
+int kvc_set_device(int device);
+int kvc_get_device(int* device);
+int kvc_malloc(void** ptr, size_t bytes);
+int kvc_free(void* ptr);
+int kvc_malloc_host(void** ptr, size_t bytes); /* pinned host memory */
+int kvc_free_host(void* ptr);
+/* kind: 0 host->host, 1 host->device, 2 device->host, 3 device->device, 4 default */
+int kvc_memcpy_async(void* dst, const void* src, size_t bytes, int kind, void* stream);
+int kvc_memset_async(void* dst, int value, size_t bytes, void* stream);
+int kvc_stream_create(void** stream);
+int kvc_stream_destroy(void* stream);
+int kvc_stream_synchronize(void* stream);
+int kvc_device_synchronize(void);
+int kvc_event_create(void** event);
+int kvc_event_destroy(void* event);
+int kvc_event_record(void* event, void* stream);
+int kvc_event_synchronize(void* event);
+int kvc_event_elapsed_ms(void* start, void* end, float* ms);
+/* Writes `bytes` of garbage over a device buffer to evict it from L2. */
+int kvc_l2_flush(void* scratch, size_t bytes, void* stream);
+/* Number of kernels this library has launched in this process. */
+uint64_t kvc_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVCACHE_H_ */

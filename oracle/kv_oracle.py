@@ -1,0 +1,252 @@
+"""CPU oracle of the paged-KV hot path (TEST INFRASTRUCTURE ONLY).
+
+A NumPy restatement of sglang-mlx's reference algorithms, used by tests/,
+__graft_entry__.smoke() and bench.py's CPU baseline as the checker.  The
+product (libkvcache.so and its Python shim) never imports this package.
+
+Pinned against the reference's own NumPy oracles
+(tests/test_paged_attention_kernel.py:33-120, run on the reference's test
+shapes and on config 1 by tests/golden/make_golden.py) and against the
+reference MHATokenPool store/fetch run on a NumPy-backed mlx.core stand-in
+(same script).  The fixtures live in tests/golden/.
+
+Data formats (all NumPy; bf16 is carried as float32 values that are exactly
+representable in bf16, or as uint16 bit patterns where marked):
+  key_cache   [num_blocks, H, D/x, block_size, x]
+  value_cache [num_blocks, H, D, block_size]
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+
+# ---------------------------------------------------------------------------
+# element conversion (reshape_and_cache.metal:9-12: static_cast, i.e. round to
+# nearest even when narrowing)
+# ---------------------------------------------------------------------------
+def f32_to_bf16_bits(a: np.ndarray) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    u = a.view(np.uint32).astype(np.uint64)
+    out = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    nan = np.isnan(a)
+    if nan.any():
+        out = out.copy()
+        out[nan] = 0x7FC0  # utils.metal:23-26
+    return out
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def round_to(a: np.ndarray, dtype: str) -> np.ndarray:
+    """Values of `a` rounded to `dtype` ('float32'|'float16'|'bfloat16'), returned as float32."""
+    if dtype == "float32":
+        return np.asarray(a, dtype=np.float32)
+    if dtype == "float16":
+        return np.asarray(a, dtype=np.float32).astype(np.float16).astype(np.float32)
+    if dtype == "bfloat16":
+        return bf16_bits_to_f32(f32_to_bf16_bits(a))
+    raise ValueError(dtype)
+
+
+# ---------------------------------------------------------------------------
+# reshape_and_cache — reshape_and_cache.metal:35-69
+# ---------------------------------------------------------------------------
+def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping):
+    """In-place scatter of key/value [T, H, D] into the vLLM-layout caches.
+
+    slot < 0 skips the token (:36-39); block = slot // bs, offset = slot % bs
+    (:41-42); K[block, h, d // x, offset, d % x] = key[t, h, d] (:54-59);
+    V[block, h, d, offset] = value[t, h, d] (:61-65).  Element conversion is the
+    caller's job (pass key/value already in the cache dtype).
+    """
+    slots = np.asarray(slot_mapping).astype(np.int64)
+    keep = slots >= 0
+    if not keep.any():
+        return key_cache, value_cache
+    s = slots[keep]
+    k = np.asarray(key)[keep]
+    v = np.asarray(value)[keep]
+    T, H, D = k.shape
+    bs = value_cache.shape[3]
+    x = key_cache.shape[4]
+    blk, off = s // bs, s % bs
+    # K: [T, H, D] -> [T, H, D/x, x]
+    kc = k.reshape(T, H, D // x, x)
+    key_cache[blk[:, None, None], np.arange(H)[None, :, None], np.arange(D // x)[None, None, :], off[:, None, None], :] = kc
+    value_cache[blk[:, None, None], np.arange(H)[None, :, None], np.arange(D)[None, None, :], off[:, None, None]] = v
+    return key_cache, value_cache
+
+
+# ---------------------------------------------------------------------------
+# reshape_and_cache_flash — reshape_and_cache.metal:115-136
+# ---------------------------------------------------------------------------
+def reshape_and_cache_flash(key, value, key_cache, value_cache, slot_mapping):
+    """Caches [nb, bs, H, D] (or the pool's [slots, H, D]); row copy at slot."""
+    slots = np.asarray(slot_mapping).astype(np.int64)
+    keep = slots >= 0
+    kflat = key_cache.reshape(-1, *key_cache.shape[-2:])
+    vflat = value_cache.reshape(-1, *value_cache.shape[-2:])
+    kflat[slots[keep]] = np.asarray(key)[keep]
+    vflat[slots[keep]] = np.asarray(value)[keep]
+    return key_cache, value_cache
+
+
+# ---------------------------------------------------------------------------
+# MHATokenPool.store / fetch — memory_pool.py:117-159
+# ---------------------------------------------------------------------------
+def pool_store(k_buffer, v_buffer, indices, keys, values):
+    """keys/values (1, H, S, D) -> transpose to (S, H, D) -> scatter at indices."""
+    idx = np.asarray(indices, dtype=np.int64)
+    k_buffer[idx] = np.transpose(np.asarray(keys)[0], (1, 0, 2))
+    v_buffer[idx] = np.transpose(np.asarray(values)[0], (1, 0, 2))
+
+
+def pool_fetch(k_buffer, v_buffer, indices):
+    """Gather (T, H, D) at indices -> transpose -> (1, H, T, D)."""
+    idx = np.asarray(indices, dtype=np.int64)
+    k = np.transpose(k_buffer[idx], (1, 0, 2))[None]
+    v = np.transpose(v_buffer[idx], (1, 0, 2))[None]
+    return k, v
+
+
+# ---------------------------------------------------------------------------
+# paged attention decode — paged_attention_kernels.metal:37-168
+# ---------------------------------------------------------------------------
+def gather_seq(key_cache, value_cache, block_table, n_tokens, kv_head):
+    """(n_tokens, D) K and V of one sequence and KV head, through its block table."""
+    bs = value_cache.shape[3]
+    x = key_cache.shape[4]
+    nb = -(-n_tokens // bs)
+    blocks = np.asarray(block_table[:nb]).astype(np.uint32).astype(np.int64)
+    # K page [D/x, bs, x] -> [bs, D]
+    kp = key_cache[blocks, kv_head]                     # [nb, D/x, bs, x]
+    k = np.transpose(kp, (0, 2, 1, 3)).reshape(nb * bs, -1)[:n_tokens]
+    vp = value_cache[blocks, kv_head]                   # [nb, D, bs]
+    v = np.transpose(vp, (0, 2, 1)).reshape(nb * bs, -1)[:n_tokens]
+    return k, v
+
+
+def attend(q, k, v, scale, alibi_slope=0.0, context_len=None):
+    """softmax(scale * k @ q (+ alibi)) @ v in float64, denominator sum + 1e-6.
+
+    q [G, D], k/v [T, D].  Mirrors paged_attention_kernels.metal:88-97 (logits),
+    :104-144 (max-subtracted softmax, inv_sum = 1 / (sum + 1e-6)) and :146-168.
+    """
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    v = np.asarray(v, dtype=np.float64)
+    T = k.shape[0]
+    logits = (q @ k.T) * float(scale)                  # [G, T]
+    if context_len is None:
+        context_len = T
+    slope = np.broadcast_to(np.asarray(alibi_slope, dtype=np.float64), (q.shape[0],))
+    if np.any(slope != 0):
+        pos = np.arange(T, dtype=np.float64) - context_len + 1
+        logits = logits + slope[:, None] * pos[None, :]
+    m = logits.max(axis=1, keepdims=True)
+    p = np.exp(logits - m)
+    return (p @ v) / (p.sum(axis=1, keepdims=True) + 1e-6)
+
+
+def paged_attention_v1(query, key_cache, value_cache, block_tables, context_lens, num_kv_heads, scale,
+                       block_size, max_seq_len, alibi_slopes=None):
+    """Float64 result [B, Hq, D] of paged_attention_v1 (not rounded).
+
+    context_len == 0 or > max_seq_len -> zeros (:45-50); kv_head = h // G (:57-58);
+    block tables / context lens read as uint32 (:22-23).
+    """
+    q = np.asarray(query, dtype=np.float64)
+    B, Hq, D = q.shape
+    G = Hq // num_kv_heads
+    out = np.zeros((B, Hq, D), dtype=np.float64)
+    lens = np.asarray(context_lens).astype(np.uint32)
+    for b in range(B):
+        C = int(lens[b])
+        if C == 0 or C > max_seq_len:
+            continue
+        for kvh in range(num_kv_heads):
+            k, v = gather_seq(key_cache, value_cache, block_tables[b], C, kvh)
+            hs = slice(kvh * G, (kvh + 1) * G)
+            slope = 0.0 if alibi_slopes is None else np.asarray(alibi_slopes, dtype=np.float64)[hs]
+            out[b, hs] = attend(q[b, hs], k, v, scale, slope, C)
+    return out
+
+
+def paged_attention_splitk(query, key_cache, value_cache, block_tables, context_lens, num_kv_heads, scale,
+                           block_size, max_seq_len, partition_size, alibi_slopes=None):
+    """Split-K restatement: per partition (m_p, l_p, o_p), merged with LSE weights.
+
+    Returns (out [B, Hq, D], partial maxima, partial sums) in float64.  The
+    merge is out = sum_p e^{m_p - M} o_p / (sum_p e^{m_p - M} l_p + 1e-6).
+    """
+    q = np.asarray(query, dtype=np.float64)
+    B, Hq, D = q.shape
+    G = Hq // num_kv_heads
+    P = -(-max_seq_len // partition_size)
+    out = np.zeros((B, Hq, D))
+    pm = np.full((B, Hq, P), -np.inf)
+    pl = np.zeros((B, Hq, P))
+    lens = np.asarray(context_lens).astype(np.uint32)
+    for b in range(B):
+        C = int(lens[b])
+        if C == 0 or C > max_seq_len:
+            continue
+        for kvh in range(num_kv_heads):
+            k, v = gather_seq(key_cache, value_cache, block_tables[b], C, kvh)
+            hs = slice(kvh * G, (kvh + 1) * G)
+            qq = q[b, hs]
+            logits = (qq @ np.asarray(k, np.float64).T) * float(scale)
+            if alibi_slopes is not None:
+                sl = np.asarray(alibi_slopes, dtype=np.float64)[hs]
+                logits = logits + sl[:, None] * (np.arange(C) - C + 1)[None, :]
+            acc = np.zeros((G, D))
+            nparts = -(-C // partition_size)
+            ms = np.empty((G, nparts))
+            ls = np.empty((G, nparts))
+            os_ = np.empty((nparts, G, D))
+            for p in range(nparts):
+                seg = slice(p * partition_size, min(C, (p + 1) * partition_size))
+                lg = logits[:, seg]
+                m = lg.max(axis=1)
+                e = np.exp(lg - m[:, None])
+                ms[:, p], ls[:, p] = m, e.sum(axis=1)
+                os_[p] = e @ np.asarray(v[seg], np.float64)
+            M = ms.max(axis=1)
+            w = np.exp(ms - M[:, None])
+            L = (w * ls).sum(axis=1)
+            acc = np.einsum("gp,pgd->gd", w, os_)
+            out[b, hs] = acc / (L[:, None] + 1e-6)
+            pm[b, hs, :nparts] = ms
+            pl[b, hs, :nparts] = ls
+    return out, pm, pl
+
+
+# ---------------------------------------------------------------------------
+# gather + SDPA dataflow of the reference's serving path (memory_pool.py:139-159
+# then mx.fast.scaled_dot_product_attention; bench_paged_vs_gather.py:83-103)
+# ---------------------------------------------------------------------------
+def gather_sdpa(query, k_contig, v_contig, scale):
+    """query [B, Hq, D]; k/v (1, Hkv, T, D) gathered; GQA broadcast.  Float64."""
+    q = np.asarray(query, dtype=np.float64)
+    B, Hq, D = q.shape
+    Hkv = k_contig.shape[1]
+    G = Hq // Hkv
+    out = np.zeros((B, Hq, D))
+    for h in range(Hkv):
+        k = np.asarray(k_contig[0, h], np.float64)
+        v = np.asarray(v_contig[0, h], np.float64)
+        out[:, h * G:(h + 1) * G] = attend(q[:, h * G:(h + 1) * G].reshape(-1, D), k, v, scale).reshape(B, G, D)
+    return out
+
+
+def allclose_report(got, ref, atol, rtol):
+    """(ok, max_abs_err, worst_excess) for |got - ref| <= atol + rtol * |ref|."""
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    err = np.abs(got - ref)
+    bound = atol + rtol * np.abs(ref)
+    excess = float(np.max(err - bound)) if err.size else 0.0
+    return bool(np.all(err <= bound)), float(err.max() if err.size else 0.0), excess

@@ -1,0 +1,459 @@
+// decode.cu — paged-attention decode for sm_100a: the single-pass form
+// (paged_attention_v1), the split-K form with its log-sum-exp reduce, and the
+// dispatch between the tensor-core kernel (decode_mma.cuh) and the generic
+// CUDA-core kernel below.
+//
+// Semantics follow paged_attention_kernels.metal:
+//   * context_len == 0 or context_len > max_seq_len -> zeros (:45-50)
+//   * kv_head = head / (num_heads / num_kv_heads) (:57-58)
+//   * logit = scale * q.k (+ alibi_slope * (token - context_len + 1)) (:88-97)
+//   * out = sum_t exp(logit_t - max) v_t / (sum_t exp(logit_t - max) + 1e-6) (:122-168)
+//   * block tables and context lengths are read as uint32 (:22-23)
+// The reference keeps every logit of a sequence in threadgroup memory; here the
+// softmax is online (running max / sum per warp, merged across warps), so
+// max_seq_len has no shared-memory bound.
+#include <cuda_runtime.h>
+#include <float.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "kvc_common.cuh"
+
+namespace kvc {
+
+__device__ unsigned int g_decode_status = 0;
+
+struct DecodeParams {
+  void* out;
+  const void* q;
+  const void* k_cache;
+  const void* v_cache;
+  const uint32_t* block_tables;
+  const uint32_t* context_lens;
+  const float* alibi;
+  float* part_max;
+  float* part_sum;
+  float* part_out;
+  int num_seqs, num_heads, num_kv_heads, block_size;
+  int max_seq_len, partition_size, num_partitions;
+  int heads_per_cta;  // q heads of one KV group handled by one CTA
+  int64_t num_blocks;
+  int64_t q_seq_stride, q_head_stride, out_seq_stride, out_head_stride;
+  int64_t k_block_stride, k_head_stride, v_block_stride, v_head_stride;
+  int64_t table_stride;
+  int64_t part_seq_stride, part_head_stride;
+  int64_t part_out_seq_stride, part_out_head_stride, part_out_part_stride;
+  float scale;
+};
+
+// Token range [begin, end) of this CTA's partition; returns false when the
+// CTA has nothing to do.  `zero_out` is set when the sequence must produce
+// zeros (reference edge rule) and this CTA owns writing them.
+__device__ __forceinline__ bool partition_range(const DecodeParams& p, int seq, int part, uint32_t ctx, int* begin,
+                                                int* end, bool* zero_out) {
+  *zero_out = false;
+  if (ctx == 0 || ctx > (uint32_t)p.max_seq_len) {
+    // Single pass: this CTA writes the zeros.  Split: the reduce does.
+    *zero_out = (p.num_partitions == 1);
+    return false;
+  }
+  if (p.num_partitions == 1) {
+    *begin = 0;
+    *end = (int)ctx;
+    return true;
+  }
+  const int64_t b = (int64_t)part * p.partition_size;
+  if (b >= (int64_t)ctx) return false;  // the reduce never reads this partition
+  *begin = (int)b;
+  const int64_t e = b + p.partition_size;
+  *end = (int)((int64_t)ctx < e ? (int64_t)ctx : e);
+  return true;
+}
+
+template <typename T>
+__device__ __forceinline__ void write_zero_heads(const DecodeParams& p, int seq, int h0, int nh, int D) {
+  T* out = reinterpret_cast<T*>(p.out);
+  for (int i = threadIdx.x; i < nh * D; i += blockDim.x) {
+    const int g = i / D, d = i - g * D;
+    out[(int64_t)seq * p.out_seq_stride + (int64_t)(h0 + g) * p.out_head_stride + d] = from_float<T>(0.f);
+  }
+}
+
+// Writes one merged (max, sum, acc) triple: the final output in single-pass
+// mode, the partition's partials in split mode.
+template <typename T>
+__device__ __forceinline__ void emit(const DecodeParams& p, int seq, int head, int part, int d, float m, float l,
+                                     float acc, bool first_d) {
+  if (p.num_partitions == 1) {
+    T* out = reinterpret_cast<T*>(p.out);
+    // paged_attention_kernels.metal:144 — inv_sum = 1 / (sum + 1e-6)
+    const float inv = 1.f / (l + 1e-6f);
+    out[(int64_t)seq * p.out_seq_stride + (int64_t)head * p.out_head_stride + d] = from_float<T>(acc * inv);
+  } else {
+    p.part_out[(int64_t)seq * p.part_out_seq_stride + (int64_t)head * p.part_out_head_stride +
+               (int64_t)part * p.part_out_part_stride + d] = acc;
+    if (first_d) {
+      const int64_t o = (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride + part;
+      p.part_max[o] = m;
+      p.part_sum[o] = l;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Generic CUDA-core kernel: every (query, cache) dtype pair, every head size
+// and block size of the validated set, any group size.  fp32 math throughout.
+// CTA = (kv head x chunk of up to GC q heads, sequence, partition); each of
+// the 4 warps walks every 4th page of the range with its own online softmax.
+// ---------------------------------------------------------------------------
+constexpr int kGenericWarps = 4;
+constexpr int kGenericGC = 8;
+
+template <typename Q_T, typename CACHE_T, int D>
+__global__ void __launch_bounds__(kGenericWarps * 32) paged_decode_generic_kernel(DecodeParams p) {
+  constexpr int X = 16 / sizeof(CACHE_T);
+  constexpr int NCHUNK = D / X;
+  constexpr int DPL = (D + 31) / 32;  // output dims per lane
+  constexpr int GC = kGenericGC;
+  __shared__ float qs[GC][D];
+  __shared__ float ps[kGenericWarps][GC][32];
+  __shared__ float red_m[kGenericWarps][GC];
+  __shared__ float red_l[kGenericWarps][GC];
+  __shared__ float red_o[kGenericWarps][GC][D];
+
+  const int G = p.num_heads / p.num_kv_heads;
+  const int chunks_per_kv = (G + GC - 1) / GC;
+  const int kvh = blockIdx.x / chunks_per_kv;
+  const int hc = blockIdx.x - kvh * chunks_per_kv;
+  const int h0 = kvh * G + hc * GC;
+  const int nh = min(GC, G - hc * GC);
+  const int seq = blockIdx.y;
+  const int part = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bs = p.block_size;
+
+  const uint32_t ctx = p.context_lens[seq];
+  int begin = 0, end = 0;
+  bool zero_out = false;
+  if (!partition_range(p, seq, part, ctx, &begin, &end, &zero_out)) {
+    if (zero_out) write_zero_heads<Q_T>(p, seq, h0, nh, D);
+    return;
+  }
+
+  const Q_T* q = reinterpret_cast<const Q_T*>(p.q);
+  for (int i = threadIdx.x; i < GC * D; i += blockDim.x) {
+    const int g = i / D, d = i - g * D;
+    qs[g][d] = g < nh ? to_float(q[(int64_t)seq * p.q_seq_stride + (int64_t)(h0 + g) * p.q_head_stride + d]) : 0.f;
+  }
+  float slope[GC];
+#pragma unroll
+  for (int g = 0; g < GC; ++g) slope[g] = (p.alibi && g < nh) ? p.alibi[h0 + g] : 0.f;
+  __syncthreads();
+
+  float m[GC], l[GC], o[GC][DPL];
+#pragma unroll
+  for (int g = 0; g < GC; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) o[g][i] = 0.f;
+  }
+
+  const CACHE_T* kcache = reinterpret_cast<const CACHE_T*>(p.k_cache);
+  const CACHE_T* vcache = reinterpret_cast<const CACHE_T*>(p.v_cache);
+  const uint32_t* table = p.block_tables + (int64_t)seq * p.table_stride;
+  const int tpl = 32 / bs;  // lanes per token in the QK phase
+  const int t = lane % bs, sub = lane / bs;
+  const int first_page = begin / bs, last_page = (end - 1) / bs;
+
+  for (int pg = first_page + warp; pg <= last_page; pg += kGenericWarps) {
+    const int64_t blk = (int64_t)table[pg];
+    const bool blk_ok = blk < p.num_blocks;
+    if (!blk_ok) {
+      if (lane == 0) set_status(&g_decode_status, KVC_STATUS_BLOCK_OOB);
+      continue;
+    }
+    // ---- QK: lanes (t, sub) take chunks sub, sub + tpl, ... of token t.
+    const CACHE_T* kp = kcache + blk * p.k_block_stride + (int64_t)kvh * p.k_head_stride;
+    float acc[GC];
+#pragma unroll
+    for (int g = 0; g < GC; ++g) acc[g] = 0.f;
+    for (int c = sub; c < NCHUNK; c += tpl) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(kp + ((int64_t)c * bs + t) * X);
+      const CACHE_T* kv = reinterpret_cast<const CACHE_T*>(&raw);
+#pragma unroll
+      for (int e = 0; e < X; ++e) {
+        const float kf = to_float(kv[e]);
+#pragma unroll
+        for (int g = 0; g < GC; ++g) acc[g] += qs[g][c * X + e] * kf;
+      }
+    }
+    for (int off = bs; off < 32; off <<= 1) {
+#pragma unroll
+      for (int g = 0; g < GC; ++g) acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], off);
+    }
+    const int token = pg * bs + t;
+    const bool valid = token >= begin && token < end;
+    float pexp[GC];
+#pragma unroll
+    for (int g = 0; g < GC; ++g) {
+      float s = acc[g] * p.scale;
+      if (p.alibi) s += slope[g] * (float)(token - (int)ctx + 1);
+      s = valid ? s : -INFINITY;
+      float pm = s;
+      for (int off = 1; off < bs; off <<= 1) pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, off));
+      const float mn = fmaxf(m[g], pm);
+      const float alpha = (m[g] == -INFINITY) ? 0.f : expf(m[g] - mn);
+      const float e = valid ? expf(s - mn) : 0.f;
+      float es = e;
+      for (int off = 1; off < bs; off <<= 1) es += __shfl_xor_sync(0xffffffffu, es, off);
+      l[g] = l[g] * alpha + es;
+      m[g] = mn;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) o[g][i] *= alpha;
+      pexp[g] = e;
+    }
+    if (sub == 0) {
+#pragma unroll
+      for (int g = 0; g < GC; ++g) ps[warp][g][t] = pexp[g];
+    }
+    __syncwarp();
+    // ---- PV: lane owns dims lane, lane + 32, ...  Tokens past the context
+    // are skipped (paged_attention_kernels.metal:154): their slots may hold
+    // anything, and 0 * NaN would poison the sum.
+    const CACHE_T* vp = vcache + blk * p.v_block_stride + (int64_t)kvh * p.v_head_stride;
+    const int nvalid = min(bs, end - pg * bs);
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+      const int d = lane + 32 * i;
+      if (d < D) {
+        const CACHE_T* row = vp + (int64_t)d * bs;
+        for (int t0 = 0; t0 < bs; t0 += X) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(row + t0);
+          const CACHE_T* vv = reinterpret_cast<const CACHE_T*>(&raw);
+#pragma unroll
+          for (int e = 0; e < X; ++e) {
+            const float vf = (t0 + e < nvalid) ? to_float(vv[e]) : 0.f;
+#pragma unroll
+            for (int g = 0; g < GC; ++g) o[g][i] += ps[warp][g][t0 + e] * vf;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  }
+
+  // ---- merge the warps' partial softmax states.
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < GC; ++g) {
+      red_m[warp][g] = m[g];
+      red_l[warp][g] = l[g];
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < GC; ++g)
+#pragma unroll
+    for (int i = 0; i < DPL; ++i)
+      if (lane + 32 * i < D) red_o[warp][g][lane + 32 * i] = o[g][i];
+  __syncthreads();
+  for (int i = threadIdx.x; i < nh * D; i += blockDim.x) {
+    const int g = i / D, d = i - g * D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kGenericWarps; ++w) M = fmaxf(M, red_m[w][g]);
+    float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kGenericWarps; ++w) {
+        const float wt = red_m[w][g] == -INFINITY ? 0.f : expf(red_m[w][g] - M);
+        L += wt * red_l[w][g];
+        A += wt * red_o[w][g][d];
+      }
+    }
+    emit<Q_T>(p, seq, h0 + g, part, d, M, L, A, d == 0);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Split-K reduce: out = sum_p e^{m_p - M} o_p / (sum_p e^{m_p - M} l_p + 1e-6)
+// over the partitions that hold tokens of the sequence.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(128) splitk_reduce_kernel(DecodeParams p, int head_size) {
+  extern __shared__ float w[];  // [num_partitions]
+  __shared__ float s_inv;
+  const int head = blockIdx.x, seq = blockIdx.y;
+  const uint32_t ctx = p.context_lens[seq];
+  T* out = reinterpret_cast<T*>(p.out) + (int64_t)seq * p.out_seq_stride + (int64_t)head * p.out_head_stride;
+  if (ctx == 0 || ctx > (uint32_t)p.max_seq_len) {
+    for (int d = threadIdx.x; d < head_size; d += blockDim.x) out[d] = from_float<T>(0.f);
+    return;
+  }
+  const int nparts = (int)((ctx + p.partition_size - 1) / p.partition_size);
+  const float* pm = p.part_max + (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride;
+  const float* pl = p.part_sum + (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride;
+  // max over partitions (block reduce)
+  float M = -INFINITY;
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) M = fmaxf(M, pm[i]);
+  __shared__ float red[32];
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = M;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : -INFINITY;
+    for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  M = red[0];
+  __syncthreads();
+  float L = 0.f;
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
+    const float wt = (M == -INFINITY || pm[i] == -INFINITY) ? 0.f : expf(pm[i] - M);
+    w[i] = wt;
+    L += wt * pl[i];
+  }
+  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = L;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float v = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) v += red[i];
+    s_inv = 1.f / (v + 1e-6f);
+  }
+  __syncthreads();
+  const float* po = p.part_out + (int64_t)seq * p.part_out_seq_stride + (int64_t)head * p.part_out_head_stride;
+  for (int d = threadIdx.x; d < head_size; d += blockDim.x) {
+    float a = 0.f;
+    for (int i = 0; i < nparts; ++i) a += w[i] * po[(int64_t)i * p.part_out_part_stride + d];
+    out[d] = from_float<T>(a * s_inv);
+  }
+}
+
+}  // namespace kvc
+
+#include "decode_mma.cuh"
+
+namespace kvc {
+
+template <typename Q_T, typename CACHE_T, int D>
+static cudaError_t launch_generic(const DecodeParams& p, cudaStream_t stream) {
+  const int G = p.num_heads / p.num_kv_heads;
+  const int chunks = (G + kGenericGC - 1) / kGenericGC;
+  dim3 grid((unsigned)(p.num_kv_heads * chunks), (unsigned)p.num_seqs, (unsigned)p.num_partitions);
+  paged_decode_generic_kernel<Q_T, CACHE_T, D><<<grid, kGenericWarps * 32, 0, stream>>>(p);
+  count_launch();
+  return cudaGetLastError();
+}
+
+template <typename Q_T, typename CACHE_T>
+static cudaError_t launch_generic_d(const DecodeParams& p, int D, cudaStream_t stream) {
+  switch (D) {
+    case 32: return launch_generic<Q_T, CACHE_T, 32>(p, stream);
+    case 64: return launch_generic<Q_T, CACHE_T, 64>(p, stream);
+    case 80: return launch_generic<Q_T, CACHE_T, 80>(p, stream);
+    case 96: return launch_generic<Q_T, CACHE_T, 96>(p, stream);
+    case 112: return launch_generic<Q_T, CACHE_T, 112>(p, stream);
+    case 120: return launch_generic<Q_T, CACHE_T, 120>(p, stream);
+    case 128: return launch_generic<Q_T, CACHE_T, 128>(p, stream);
+    case 192: return launch_generic<Q_T, CACHE_T, 192>(p, stream);
+    case 256: return launch_generic<Q_T, CACHE_T, 256>(p, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename Q_T>
+static cudaError_t launch_reduce(const DecodeParams& p, int D, cudaStream_t stream) {
+  dim3 grid((unsigned)p.num_heads, (unsigned)p.num_seqs);
+  const size_t smem = (size_t)p.num_partitions * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(splitk_reduce_kernel<Q_T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  splitk_reduce_kernel<Q_T><<<grid, 128, smem, stream>>>(p, D);
+  count_launch();
+  return cudaGetLastError();
+}
+
+static DecodeParams to_params(const DecodeArgs& a) {
+  DecodeParams p;
+  p.out = a.out;
+  p.q = a.q;
+  p.k_cache = a.k_cache;
+  p.v_cache = a.v_cache;
+  p.block_tables = a.block_tables;
+  p.context_lens = a.context_lens;
+  p.alibi = a.alibi;
+  p.part_max = a.part_max;
+  p.part_sum = a.part_sum;
+  p.part_out = a.part_out;
+  p.num_seqs = a.num_seqs;
+  p.num_heads = a.num_heads;
+  p.num_kv_heads = a.num_kv_heads;
+  p.block_size = a.block_size;
+  p.max_seq_len = a.max_seq_len;
+  p.partition_size = a.partition_size;
+  p.num_partitions = a.num_partitions;
+  p.heads_per_cta = 0;
+  p.num_blocks = a.num_blocks;
+  p.q_seq_stride = a.q_seq_stride;
+  p.q_head_stride = a.q_head_stride;
+  p.out_seq_stride = a.out_seq_stride;
+  p.out_head_stride = a.out_head_stride;
+  p.k_block_stride = a.k_block_stride;
+  p.k_head_stride = a.k_head_stride;
+  p.v_block_stride = a.v_block_stride;
+  p.v_head_stride = a.v_head_stride;
+  p.table_stride = a.table_stride;
+  p.part_seq_stride = a.part_seq_stride;
+  p.part_head_stride = a.part_head_stride;
+  p.part_out_seq_stride = a.part_out_seq_stride;
+  p.part_out_head_stride = a.part_out_head_stride;
+  p.part_out_part_stride = a.part_out_part_stride;
+  p.scale = a.scale;
+  return p;
+}
+
+static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
+  if (a.num_seqs > 65535) return cudaErrorInvalidValue;
+  DecodeParams p = to_params(a);
+  const int D = a.head_size;
+  cudaError_t e = cudaErrorInvalidValue;
+  // Loads are 16-byte vectors: page bases must be 16-byte aligned.
+  const int cs = elem_size(a.cache_type);
+  const bool pages_aligned = aligned16(a.k_cache) && aligned16(a.v_cache) && (a.k_block_stride * cs) % 16 == 0 &&
+                             (a.k_head_stride * cs) % 16 == 0 && (a.v_block_stride * cs) % 16 == 0 &&
+                             (a.v_head_stride * cs) % 16 == 0;
+  if (!pages_aligned) return cudaErrorMisalignedAddress;
+  if (mma_supported(a)) {
+    e = launch_mma(p, a, stream);
+  } else if (a.q_type == ElemType::F32) {
+    if (a.cache_type == ElemType::F32) e = launch_generic_d<float, float>(p, D, stream);
+    else if (a.cache_type == ElemType::F16) e = launch_generic_d<float, __half>(p, D, stream);
+    else if (a.cache_type == ElemType::BF16) e = launch_generic_d<float, __nv_bfloat16>(p, D, stream);
+  } else if (a.q_type == ElemType::F16 && a.cache_type == ElemType::F16) {
+    e = launch_generic_d<__half, __half>(p, D, stream);
+  } else if (a.q_type == ElemType::BF16 && a.cache_type == ElemType::BF16) {
+    e = launch_generic_d<__nv_bfloat16, __nv_bfloat16>(p, D, stream);
+  }
+  if (e != cudaSuccess || a.num_partitions == 1) return e;
+  if (a.q_type == ElemType::F32) return launch_reduce<float>(p, D, stream);
+  if (a.q_type == ElemType::F16) return launch_reduce<__half>(p, D, stream);
+  return launch_reduce<__nv_bfloat16>(p, D, stream);
+}
+
+}  // namespace kvc
+
+unsigned int kvc_decode_status(int clear, cudaError_t* err) {
+  unsigned int v = 0;
+  *err = cudaMemcpyFromSymbol(&v, kvc::g_decode_status, sizeof(v));
+  if (*err == cudaSuccess && clear) {
+    const unsigned int zero = 0;
+    *err = cudaMemcpyToSymbol(kvc::g_decode_status, &zero, sizeof(zero));
+  }
+  return v;
+}

@@ -1,0 +1,637 @@
+// kvc_abi.cpp — the extern "C" surface of libkvcache.so: argument validation
+// (mirroring the reference's std::invalid_argument checks), device guards,
+// dispatch to the kernel launchers, and the small runtime the Python shim uses
+// in place of MLX's allocator and streams.
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <atomic>
+#include <string>
+
+#include "kvc_tensor.h"
+#include "kvcache.h"
+
+namespace kvc {
+
+static thread_local std::string g_last_error;
+static std::atomic<uint64_t> g_launches{0};
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+static int fail(int code, const std::string& msg) {
+  set_error(msg);
+  return code;
+}
+
+static int cuda_fail(cudaError_t e, const char* what) {
+  std::string m = std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+  return fail(KVC_ECUDA, m);
+}
+
+static ElemType decode_dtype(const kvc_dldtype& d) {
+  if (d.lanes != 1) return ElemType::INVALID;
+  if (d.code == 2 && d.bits == 32) return ElemType::F32;
+  if (d.code == 2 && d.bits == 16) return ElemType::F16;
+  if (d.code == 4 && d.bits == 16) return ElemType::BF16;
+  if (d.code == 0 && d.bits == 32) return ElemType::I32;
+  if (d.code == 1 && d.bits == 32) return ElemType::U32;
+  if (d.code == 0 && d.bits == 64) return ElemType::I64;
+  return ElemType::INVALID;
+}
+
+bool parse(const kvc_dltensor* t, const char* name, View* v) {
+  if (t == nullptr) {
+    set_error(std::string(name) + " is null");
+    return false;
+  }
+  if (t->ndim < 0 || t->ndim > 8) {
+    set_error(std::string(name) + ": unsupported rank " + std::to_string(t->ndim));
+    return false;
+  }
+  v->dtype = decode_dtype(t->dtype);
+  if (v->dtype == ElemType::INVALID) {
+    set_error(std::string(name) + ": unsupported dtype (code " + std::to_string(t->dtype.code) +
+              ", bits " + std::to_string(t->dtype.bits) + ", lanes " + std::to_string(t->dtype.lanes) + ")");
+    return false;
+  }
+  v->ndim = t->ndim;
+  int64_t expect = 1;
+  for (int i = t->ndim - 1; i >= 0; --i) {
+    v->shape[i] = t->shape[i];
+    if (v->shape[i] < 0) {
+      set_error(std::string(name) + ": negative extent");
+      return false;
+    }
+    v->strides[i] = t->strides ? t->strides[i] : expect;
+    expect *= v->shape[i];
+  }
+  v->data = static_cast<char*>(t->data) + t->byte_offset;
+  v->on_cuda = (t->device.device_type == 2 || t->device.device_type == 13);
+  v->device = t->device.device_id;
+  return true;
+}
+
+// Sets the launch device from the tensors and restores the caller's device.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int device) {
+    cudaGetDevice(&prev_);
+    if (device >= 0 && device != prev_) {
+      ok_ = cudaSetDevice(device) == cudaSuccess;
+      changed_ = true;
+    }
+  }
+  ~DeviceGuard() {
+    if (changed_) cudaSetDevice(prev_);
+  }
+  bool ok() const { return ok_; }
+
+ private:
+  int prev_ = 0;
+  bool changed_ = false;
+  bool ok_ = true;
+};
+
+static bool is_valid_attention_config(int head_size, int block_size) {
+  // mlx_paged_attention.cpp:52-59 (the Metal instantiation matrix).
+  static const int hs[] = {32, 64, 80, 96, 112, 120, 128, 192, 256};
+  static const int bs[] = {8, 16, 32};
+  bool ok_hs = false, ok_bs = false;
+  for (int v : hs) ok_hs |= (v == head_size);
+  for (int v : bs) ok_bs |= (v == block_size);
+  return ok_hs && ok_bs;
+}
+
+static bool is_float(ElemType t) { return t == ElemType::F32 || t == ElemType::F16 || t == ElemType::BF16; }
+
+// (query dtype, cache dtype) pairs of paged_attention_inst.metal:64-73 and
+// (kv dtype, cache dtype) pairs of reshape_and_cache.metal:91-95.
+static bool is_supported_pair(ElemType a, ElemType c) {
+  if (a == c && is_float(a)) return true;
+  return a == ElemType::F32 && (c == ElemType::F16 || c == ElemType::BF16);
+}
+
+static int check_all_cuda(std::initializer_list<const View*> views, int* device) {
+  int dev = -1;
+  for (const View* v : views) {
+    if (v == nullptr) continue;
+    if (!v->on_cuda) return fail(KVC_EINVAL, "all tensors must live on a CUDA device");
+    if (dev < 0) dev = v->device;
+    if (v->device != dev) return fail(KVC_EINVAL, "all tensors must live on the same CUDA device");
+  }
+  *device = dev;
+  return KVC_OK;
+}
+
+static int check_index_type(const View& v, const char* name, bool allow_i64) {
+  if (v.dtype == ElemType::I32 || v.dtype == ElemType::U32) return KVC_OK;
+  if (allow_i64 && v.dtype == ElemType::I64) return KVC_OK;
+  return fail(KVC_EINVAL, std::string(name) + " must be int32 or uint32" + (allow_i64 ? " or int64" : ""));
+}
+
+// Shared validation + argument packing of the v1 and v2 decode entry points.
+static int prepare_decode(kvc_dltensor* out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                          const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                          const kvc_dltensor* context_lens, int num_kv_heads, float scale, int block_size,
+                          int max_seq_len, const kvc_dltensor* alibi_slopes, DecodeArgs* a, int* device) {
+  View q, kc, vc, bt, cl, o, al;
+  if (!parse(query, "query", &q) || !parse(key_cache, "key_cache", &kc) ||
+      !parse(value_cache, "value_cache", &vc) || !parse(block_tables, "block_tables", &bt) ||
+      !parse(context_lens, "context_lens", &cl) || !parse(out, "out", &o))
+    return KVC_EINVAL;
+  if (alibi_slopes && !parse(alibi_slopes, "alibi_slopes", &al)) return KVC_EINVAL;
+
+  // mlx_paged_attention.cpp:156-188, same order and messages.
+  if (q.ndim != 3) return fail(KVC_EINVAL, "query must have shape [num_seqs, num_heads, head_size]");
+  if (kc.ndim != 5 || vc.ndim != 4)
+    return fail(KVC_EINVAL, "key_cache/value_cache must use paged attention layouts");
+  if (bt.ndim != 2 || cl.ndim != 1)
+    return fail(KVC_EINVAL, "block_tables must be 2D and context_lens must be 1D");
+  if (q.shape[0] != bt.shape[0] || q.shape[0] != cl.shape[0])
+    return fail(KVC_EINVAL, "query, block_tables, and context_lens sequence counts differ");
+  if (num_kv_heads <= 0 || q.shape[1] % num_kv_heads != 0)
+    return fail(KVC_EINVAL, "num_heads must be divisible by num_kv_heads");
+  if (kc.shape[1] != num_kv_heads || vc.shape[1] != num_kv_heads)
+    return fail(KVC_EINVAL, "cache KV-head count does not match num_kv_heads");
+  if (kc.shape[2] * kc.shape[4] != q.shape[2] || vc.shape[2] != q.shape[2])
+    return fail(KVC_EINVAL, "cache head size does not match query head size");
+  if (kc.shape[0] != vc.shape[0] || kc.shape[3] != block_size || vc.shape[3] != block_size)
+    return fail(KVC_EINVAL, "cache block dimensions do not match block_size");
+  if (alibi_slopes && (al.ndim != 1 || al.shape[0] != q.shape[1]))
+    return fail(KVC_EINVAL, "alibi_slopes must have shape [num_heads]");
+  if (max_seq_len <= 0) return fail(KVC_EINVAL, "max_seq_len must be positive");
+  if ((int64_t)max_seq_len > bt.shape[1] * (int64_t)block_size)
+    return fail(KVC_EINVAL, "max_seq_len exceeds block table capacity");
+  const int head_size = (int)q.shape[2];
+  if (!is_valid_attention_config(head_size, block_size))
+    return fail(KVC_EINVAL, "Unsupported head_size/block_size for paged_attention");
+
+  // Checks the Metal path leaves to kernel lookup or to luck.
+  if (!is_float(q.dtype) || !is_float(kc.dtype) || kc.dtype != vc.dtype || !is_supported_pair(q.dtype, kc.dtype))
+    return fail(KVC_EINVAL, std::string("Unsupported dtype combination for paged_attention: query ") +
+                                elem_name(q.dtype) + ", cache " + elem_name(kc.dtype) + "/" + elem_name(vc.dtype));
+  const int x = 16 / elem_size(kc.dtype);
+  if (kc.shape[4] != x)
+    return fail(KVC_EINVAL, "key_cache last dimension must be x = 16 / sizeof(cache element) = " + std::to_string(x));
+  if (int rc = check_index_type(bt, "block_tables", false)) return rc;
+  if (int rc = check_index_type(cl, "context_lens", false)) return rc;
+  if (alibi_slopes && al.dtype != ElemType::F32) return fail(KVC_EINVAL, "alibi_slopes must be float32");
+  if (o.ndim != 3 || o.shape[0] != q.shape[0] || o.shape[1] != q.shape[1] || o.shape[2] != q.shape[2] ||
+      o.dtype != q.dtype)
+    return fail(KVC_EINVAL, "out must have the shape and dtype of query");
+  if (q.stride(2) != 1 || o.stride(2) != 1) return fail(KVC_EINVAL, "query/out head_size dimension must be contiguous");
+  if (!kc.dense_from(2) || !vc.dense_from(2))
+    return fail(KVC_EINVAL, "key_cache/value_cache pages must be dense ([D/x, bs, x] and [D, bs])");
+  if (bt.stride(1) != 1 || cl.stride(0) != 1 || (alibi_slopes && al.stride(0) != 1))
+    return fail(KVC_EINVAL, "block_tables rows, context_lens and alibi_slopes must be contiguous");
+  if (int rc = check_all_cuda({&q, &kc, &vc, &bt, &cl, &o, alibi_slopes ? &al : nullptr}, device)) return rc;
+
+  memset(a, 0, sizeof(*a));
+  a->out = o.data;
+  a->q = q.data;
+  a->k_cache = kc.data;
+  a->v_cache = vc.data;
+  a->block_tables = reinterpret_cast<const uint32_t*>(bt.data);
+  a->context_lens = reinterpret_cast<const uint32_t*>(cl.data);
+  a->alibi = alibi_slopes ? reinterpret_cast<const float*>(al.data) : nullptr;
+  a->q_type = q.dtype;
+  a->cache_type = kc.dtype;
+  a->num_seqs = (int)q.shape[0];
+  a->num_heads = (int)q.shape[1];
+  a->num_kv_heads = num_kv_heads;
+  a->head_size = head_size;
+  a->block_size = block_size;
+  a->max_blocks_per_seq = (int)bt.shape[1];
+  a->max_seq_len = max_seq_len;
+  a->num_blocks = kc.shape[0];
+  a->q_seq_stride = q.stride(0);
+  a->q_head_stride = q.stride(1);
+  a->out_seq_stride = o.stride(0);
+  a->out_head_stride = o.stride(1);
+  a->k_block_stride = kc.stride(0);
+  a->k_head_stride = kc.stride(1);
+  a->v_block_stride = vc.stride(0);
+  a->v_head_stride = vc.stride(1);
+  a->table_stride = bt.stride(0);
+  a->scale = scale;
+  a->num_partitions = 1;
+  a->partition_size = 0;
+  return KVC_OK;
+}
+
+}  // namespace kvc
+
+using namespace kvc;
+
+extern "C" {
+
+const char* kvc_last_error(void) { return g_last_error.c_str(); }
+
+const char* kvc_version(void) { return "libkvcache 0.1.0 (sm_100a)"; }
+
+uint64_t kvc_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int kvc_get_status(int device, uint32_t* flags, int clear) {
+  if (!flags) return fail(KVC_EINVAL, "flags is null");
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e1 = cudaSuccess, e2 = cudaSuccess;
+  unsigned int f = kvc_cache_ops_status(clear, &e1) | kvc_decode_status(clear, &e2);
+  if (e1 != cudaSuccess) return cuda_fail(e1, "kvc_get_status");
+  if (e2 != cudaSuccess) return cuda_fail(e2, "kvc_get_status");
+  *flags = f;
+  return KVC_OK;
+}
+
+int kvc_paged_attention_v1(kvc_dltensor* out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                           const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                           const kvc_dltensor* context_lens, int num_kv_heads, float scale, int block_size,
+                           int max_seq_len, const kvc_dltensor* alibi_slopes, void* stream) {
+  DecodeArgs a;
+  int device = -1;
+  if (int rc = prepare_decode(out, query, key_cache, value_cache, block_tables, context_lens, num_kv_heads, scale,
+                              block_size, max_seq_len, alibi_slopes, &a, &device))
+    return rc;
+  if (a.num_seqs == 0) return KVC_OK;
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_paged_decode(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "paged_attention_v1 launch");
+  return KVC_OK;
+}
+
+int kvc_paged_attention_v2(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltensor* max_logits, kvc_dltensor* tmp_out,
+                           const kvc_dltensor* query, const kvc_dltensor* key_cache, const kvc_dltensor* value_cache,
+                           const kvc_dltensor* block_tables, const kvc_dltensor* context_lens, int num_kv_heads,
+                           float scale, int block_size, int max_seq_len, const kvc_dltensor* alibi_slopes,
+                           int partition_size, void* stream) {
+  DecodeArgs a;
+  int device = -1;
+  if (int rc = prepare_decode(out, query, key_cache, value_cache, block_tables, context_lens, num_kv_heads, scale,
+                              block_size, max_seq_len, alibi_slopes, &a, &device))
+    return rc;
+  if (partition_size <= 0 || partition_size % 32 != 0 || partition_size % block_size != 0)
+    return fail(KVC_EINVAL, "partition_size must be a positive multiple of 32 and of block_size");
+  View es, ml, to;
+  if (!parse(exp_sums, "exp_sums", &es) || !parse(max_logits, "max_logits", &ml) || !parse(tmp_out, "tmp_out", &to))
+    return KVC_EINVAL;
+  const int parts = (max_seq_len + partition_size - 1) / partition_size;
+  if (es.dtype != ElemType::F32 || ml.dtype != ElemType::F32 || to.dtype != ElemType::F32)
+    return fail(KVC_EINVAL, "exp_sums, max_logits and tmp_out must be float32");
+  if (es.ndim != 3 || ml.ndim != 3 || to.ndim != 4 || es.shape[0] != a.num_seqs || es.shape[1] != a.num_heads ||
+      es.shape[2] < parts || ml.shape[0] != a.num_seqs || ml.shape[1] != a.num_heads || ml.shape[2] < parts ||
+      to.shape[0] != a.num_seqs || to.shape[1] != a.num_heads || to.shape[2] < parts || to.shape[3] != a.head_size)
+    return fail(KVC_EINVAL,
+                "split-K workspace must be exp_sums/max_logits [num_seqs, num_heads, P] and tmp_out "
+                "[num_seqs, num_heads, P, head_size] with P >= ceil(max_seq_len / partition_size) = " +
+                    std::to_string(parts));
+  if (es.stride(2) != 1 || ml.stride(2) != 1 || to.stride(3) != 1 || es.stride(0) != ml.stride(0) ||
+      es.stride(1) != ml.stride(1))
+    return fail(KVC_EINVAL, "exp_sums and max_logits must share strides with a contiguous last dimension");
+  int dev2 = -1;
+  if (int rc = check_all_cuda({&es, &ml, &to}, &dev2)) return rc;
+  if (dev2 != device) return fail(KVC_EINVAL, "all tensors must live on the same CUDA device");
+  if (a.num_seqs == 0) return KVC_OK;
+  a.part_sum = reinterpret_cast<float*>(es.data);
+  a.part_max = reinterpret_cast<float*>(ml.data);
+  a.part_out = reinterpret_cast<float*>(to.data);
+  a.part_seq_stride = es.stride(0);
+  a.part_head_stride = es.stride(1);
+  a.part_out_seq_stride = to.stride(0);
+  a.part_out_head_stride = to.stride(1);
+  a.part_out_part_stride = to.stride(2);
+  a.partition_size = partition_size;
+  a.num_partitions = parts;
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_paged_decode(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "paged_attention_v2 launch");
+  return KVC_OK;
+}
+
+// Shared validation of the two append layouts.
+static int prepare_reshape(const kvc_dltensor* key, const kvc_dltensor* value, kvc_dltensor* key_cache,
+                           kvc_dltensor* value_cache, const kvc_dltensor* slot_mapping, bool flash,
+                           ReshapeArgs* a, int* device) {
+  View k, v, kc, vc, sm;
+  if (!parse(key, "key", &k) || !parse(value, "value", &v) || !parse(key_cache, "key_cache", &kc) ||
+      !parse(value_cache, "value_cache", &vc) || !parse(slot_mapping, "slot_mapping", &sm))
+    return KVC_EINVAL;
+  if (k.ndim != 3 || v.ndim != 3 || k.shape[0] != v.shape[0] || k.shape[1] != v.shape[1] || k.shape[2] != v.shape[2])
+    return fail(KVC_EINVAL, "key and value must both have shape [num_tokens, num_heads, head_size]");
+  // The Metal kernel reads slot_mapping[token] for token < key.shape(0), so a
+  // longer mapping is accepted and its tail ignored (the reference test
+  // fixture relies on this, test_paged_attention_kernel.py:171-177).
+  if (sm.ndim != 1 || sm.shape[0] < k.shape[0])
+    return fail(KVC_EINVAL, "slot_mapping must have shape [num_tokens]");
+  if (int rc = check_index_type(sm, "slot_mapping", true)) return rc;
+  if (k.dtype != v.dtype || kc.dtype != vc.dtype || !is_supported_pair(k.dtype, kc.dtype))
+    return fail(KVC_EINVAL, std::string("Unsupported dtype combination for reshape_and_cache: kv ") +
+                                elem_name(k.dtype) + "/" + elem_name(v.dtype) + ", cache " + elem_name(kc.dtype) +
+                                "/" + elem_name(vc.dtype));
+  if (flash && kc.dtype != k.dtype)
+    return fail(KVC_EINVAL, "reshape_and_cache_flash requires key and cache dtypes to match");
+  const int64_t H = k.shape[1], D = k.shape[2];
+  if (k.stride(2) != 1 || v.stride(2) != 1 || sm.stride(0) != 1)
+    return fail(KVC_EINVAL, "key/value head_size dimension and slot_mapping must be contiguous");
+  memset(a, 0, sizeof(*a));
+  if (flash) {
+    // [nb, bs, H, D] or the pool's [slots, H, D] (block_size 1).
+    if (!((kc.ndim == 4 && vc.ndim == 4) || (kc.ndim == 3 && vc.ndim == 3)))
+      return fail(KVC_EINVAL, "flash caches must have shape [num_blocks, block_size, num_heads, head_size]");
+    for (int i = 0; i < kc.ndim; ++i)
+      if (kc.shape[i] != vc.shape[i]) return fail(KVC_EINVAL, "key_cache and value_cache shapes differ");
+    if (kc.size(-2) != H || kc.size(-1) != D)
+      return fail(KVC_EINVAL, "cache num_heads/head_size do not match key");
+    if (kc.stride(-1) != 1 || vc.stride(-1) != 1)
+      return fail(KVC_EINVAL, "cache head_size dimension must be contiguous");
+    a->block_size = kc.ndim == 4 ? (int)kc.shape[1] : 1;
+    a->num_blocks = kc.shape[0];
+    a->kc_block_stride = kc.stride(0);
+    a->vc_block_stride = vc.stride(0);
+    a->kc_tok_stride = kc.ndim == 4 ? kc.stride(1) : kc.stride(0);
+    a->vc_tok_stride = vc.ndim == 4 ? vc.stride(1) : vc.stride(0);
+    a->kc_head_stride = kc.stride(-2);
+    a->vc_head_stride = vc.stride(-2);
+  } else {
+    const int x = 16 / elem_size(kc.dtype);
+    if (kc.ndim != 5 || vc.ndim != 4)
+      return fail(KVC_EINVAL, "key_cache/value_cache must use paged attention layouts");
+    if (kc.shape[1] != H || vc.shape[1] != H)
+      return fail(KVC_EINVAL, "cache KV-head count does not match key");
+    if (kc.shape[2] * kc.shape[4] != D || vc.shape[2] != D)
+      return fail(KVC_EINVAL, "cache head size does not match key head size");
+    if (kc.shape[4] != x)
+      return fail(KVC_EINVAL, "key_cache last dimension must be x = 16 / sizeof(cache element) = " + std::to_string(x));
+    if (kc.shape[0] != vc.shape[0] || kc.shape[3] != vc.shape[3])
+      return fail(KVC_EINVAL, "cache block dimensions of key_cache and value_cache differ");
+    if (!kc.dense_from(2) || !vc.dense_from(2))
+      return fail(KVC_EINVAL, "key_cache/value_cache pages must be dense ([D/x, bs, x] and [D, bs])");
+    a->block_size = (int)kc.shape[3];
+    a->num_blocks = kc.shape[0];
+    a->kc_block_stride = kc.stride(0);
+    a->kc_head_stride = kc.stride(1);
+    a->vc_block_stride = vc.stride(0);
+    a->vc_head_stride = vc.stride(1);
+  }
+  if (H <= 0 || D <= 0 || H * D > (int64_t)1 << 24) return fail(KVC_EINVAL, "unsupported num_heads * head_size");
+  if (int rc = check_all_cuda({&k, &v, &kc, &vc, &sm}, device)) return rc;
+  a->key = k.data;
+  a->value = v.data;
+  a->key_cache = kc.data;
+  a->value_cache = vc.data;
+  a->slots = sm.data;
+  a->kv_type = k.dtype;
+  a->cache_type = kc.dtype;
+  a->slot_type = sm.dtype;
+  a->num_tokens = k.shape[0];
+  a->num_heads = (int)H;
+  a->head_size = (int)D;
+  a->key_tok_stride = k.stride(0);
+  a->key_head_stride = k.stride(1);
+  a->value_tok_stride = v.stride(0);
+  a->value_head_stride = v.stride(1);
+  return KVC_OK;
+}
+
+int kvc_reshape_and_cache(const kvc_dltensor* key, const kvc_dltensor* value, kvc_dltensor* key_cache,
+                          kvc_dltensor* value_cache, const kvc_dltensor* slot_mapping, void* stream) {
+  ReshapeArgs a;
+  int device = -1;
+  if (int rc = prepare_reshape(key, value, key_cache, value_cache, slot_mapping, false, &a, &device)) return rc;
+  if (a.num_tokens == 0) return KVC_OK;
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_reshape_and_cache(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "reshape_and_cache launch");
+  return KVC_OK;
+}
+
+int kvc_reshape_and_cache_flash(const kvc_dltensor* key, const kvc_dltensor* value, kvc_dltensor* key_cache,
+                                kvc_dltensor* value_cache, const kvc_dltensor* slot_mapping, void* stream) {
+  ReshapeArgs a;
+  int device = -1;
+  if (int rc = prepare_reshape(key, value, key_cache, value_cache, slot_mapping, true, &a, &device)) return rc;
+  if (a.num_tokens == 0) return KVC_OK;
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_reshape_and_cache_flash(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "reshape_and_cache_flash launch");
+  return KVC_OK;
+}
+
+int kvc_gather_kv(kvc_dltensor* k_out, kvc_dltensor* v_out, const kvc_dltensor* k_buffer,
+                  const kvc_dltensor* v_buffer, const kvc_dltensor* indices, void* stream) {
+  View ko, vo, kb, vb, ix;
+  if (!parse(k_out, "k_out", &ko) || !parse(v_out, "v_out", &vo) || !parse(k_buffer, "k_buffer", &kb) ||
+      !parse(v_buffer, "v_buffer", &vb) || !parse(indices, "indices", &ix))
+    return KVC_EINVAL;
+  if (ix.ndim != 1) return fail(KVC_EINVAL, "indices must be 1-D");
+  if (int rc = check_index_type(ix, "indices", true)) return rc;
+  if (!((kb.ndim == 3 && vb.ndim == 3) || (kb.ndim == 4 && vb.ndim == 4)))
+    return fail(KVC_EINVAL, "k_buffer/v_buffer must have shape [slots, H, D] or [num_blocks, block_size, H, D]");
+  for (int i = 0; i < kb.ndim; ++i)
+    if (kb.shape[i] != vb.shape[i]) return fail(KVC_EINVAL, "k_buffer and v_buffer shapes differ");
+  if (kb.dtype != vb.dtype || ko.dtype != kb.dtype || vo.dtype != kb.dtype || !is_float(kb.dtype))
+    return fail(KVC_EINVAL, "gather buffers and outputs must share one float dtype");
+  const int64_t H = kb.size(-2), D = kb.size(-1), T = ix.shape[0];
+  if (ko.ndim != 4 || vo.ndim != 4 || ko.shape[0] != 1 || ko.shape[1] != H || ko.shape[2] != T || ko.shape[3] != D ||
+      vo.shape[0] != 1 || vo.shape[1] != H || vo.shape[2] != T || vo.shape[3] != D)
+    return fail(KVC_EINVAL, "k_out/v_out must have shape [1, H, T, D]");
+  if (kb.stride(-1) != 1 || vb.stride(-1) != 1 || ko.stride(3) != 1 || vo.stride(3) != 1 || ix.stride(0) != 1)
+    return fail(KVC_EINVAL, "head_size dimensions and indices must be contiguous");
+  int64_t slots = kb.shape[0];
+  int64_t kslot = kb.stride(0), vslot = vb.stride(0);
+  if (kb.ndim == 4) {
+    // [nb, bs, H, D] flattened to slots: requires the block dim to be a whole
+    // multiple of the token stride.
+    if (kb.stride(0) != kb.shape[1] * kb.stride(1) || vb.stride(0) != vb.shape[1] * vb.stride(1))
+      return fail(KVC_EINVAL, "block-layout buffers must have dense [num_blocks, block_size] dims");
+    slots = kb.shape[0] * kb.shape[1];
+    kslot = kb.stride(1);
+    vslot = vb.stride(1);
+  }
+  int device = -1;
+  if (int rc = check_all_cuda({&ko, &vo, &kb, &vb, &ix}, &device)) return rc;
+  if (T == 0 || H == 0 || D == 0) return KVC_OK;
+  GatherArgs a;
+  memset(&a, 0, sizeof(a));
+  a.k_out = ko.data;
+  a.v_out = vo.data;
+  a.k_buf = kb.data;
+  a.v_buf = vb.data;
+  a.indices = ix.data;
+  a.type = kb.dtype;
+  a.index_type = ix.dtype;
+  a.num_indices = T;
+  a.num_slots = slots;
+  a.num_heads = (int)H;
+  a.head_size = (int)D;
+  a.kb_slot_stride = kslot;
+  a.kb_head_stride = kb.stride(-2);
+  a.vb_slot_stride = vslot;
+  a.vb_head_stride = vb.stride(-2);
+  a.ko_tok_stride = ko.stride(2);
+  a.ko_head_stride = ko.stride(1);
+  a.vo_tok_stride = vo.stride(2);
+  a.vo_head_stride = vo.stride(1);
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_gather_kv(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gather_kv launch");
+  return KVC_OK;
+}
+
+int kvc_get_max_shared_memory_per_block_device_attribute(int device, int64_t* out) {
+  if (!out) return fail(KVC_EINVAL, "out is null");
+  int v = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  *out = v;
+  return KVC_OK;
+}
+
+int kvc_get_device_attribute(int attribute, int device, int64_t* out) {
+  if (!out) return fail(KVC_EINVAL, "out is null");
+  int v = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&v, static_cast<cudaDeviceAttr>(attribute), device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  *out = v;
+  return KVC_OK;
+}
+
+// ---- runtime helpers ---------------------------------------------------------
+
+int kvc_device_count(int* count) {
+  if (!count) return fail(KVC_EINVAL, "count is null");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    *count = 0;
+    return cuda_fail(e, "cudaGetDeviceCount");
+  }
+  *count = n;
+  return KVC_OK;
+}
+
+int kvc_set_device(int device) {
+  cudaError_t e = cudaSetDevice(device);
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaSetDevice");
+}
+
+int kvc_get_device(int* device) {
+  if (!device) return fail(KVC_EINVAL, "device is null");
+  cudaError_t e = cudaGetDevice(device);
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaGetDevice");
+}
+
+int kvc_malloc(void** ptr, size_t bytes) {
+  if (!ptr) return fail(KVC_EINVAL, "ptr is null");
+  *ptr = nullptr;
+  if (bytes == 0) bytes = 16;
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e == cudaErrorMemoryAllocation) {
+    cudaGetLastError();
+    return fail(KVC_ENOMEM, "cudaMalloc of " + std::to_string(bytes) + " bytes failed: out of device memory");
+  }
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaMalloc");
+}
+
+int kvc_free(void* ptr) {
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaFree");
+}
+
+int kvc_malloc_host(void** ptr, size_t bytes) {
+  if (!ptr) return fail(KVC_EINVAL, "ptr is null");
+  *ptr = nullptr;
+  if (bytes == 0) bytes = 16;
+  cudaError_t e = cudaMallocHost(ptr, bytes);
+  if (e == cudaErrorMemoryAllocation) {
+    cudaGetLastError();
+    return fail(KVC_ENOMEM, "cudaMallocHost failed: out of pinned memory");
+  }
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaMallocHost");
+}
+
+int kvc_free_host(void* ptr) {
+  cudaError_t e = cudaFreeHost(ptr);
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaFreeHost");
+}
+
+int kvc_memcpy_async(void* dst, const void* src, size_t bytes, int kind, void* stream) {
+  if (kind < 0 || kind > 4) return fail(KVC_EINVAL, "invalid memcpy kind");
+  if (bytes == 0) return KVC_OK;
+  cudaError_t e = cudaMemcpyAsync(dst, src, bytes, static_cast<cudaMemcpyKind>(kind), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaMemcpyAsync");
+}
+
+int kvc_memset_async(void* dst, int value, size_t bytes, void* stream) {
+  if (bytes == 0) return KVC_OK;
+  cudaError_t e = cudaMemsetAsync(dst, value, bytes, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaMemsetAsync");
+}
+
+int kvc_stream_create(void** stream) {
+  if (!stream) return fail(KVC_EINVAL, "stream is null");
+  cudaStream_t s;
+  cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamCreate");
+  *stream = s;
+  return KVC_OK;
+}
+
+int kvc_stream_destroy(void* stream) {
+  cudaError_t e = cudaStreamDestroy(static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaStreamDestroy");
+}
+
+int kvc_stream_synchronize(void* stream) {
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaStreamSynchronize");
+}
+
+int kvc_device_synchronize(void) {
+  cudaError_t e = cudaDeviceSynchronize();
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaDeviceSynchronize");
+}
+
+int kvc_event_create(void** event) {
+  if (!event) return fail(KVC_EINVAL, "event is null");
+  cudaEvent_t ev;
+  cudaError_t e = cudaEventCreate(&ev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+  *event = ev;
+  return KVC_OK;
+}
+
+int kvc_event_destroy(void* event) {
+  cudaError_t e = cudaEventDestroy(static_cast<cudaEvent_t>(event));
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaEventDestroy");
+}
+
+int kvc_event_record(void* event, void* stream) {
+  cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(event), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaEventRecord");
+}
+
+int kvc_event_synchronize(void* event) {
+  cudaError_t e = cudaEventSynchronize(static_cast<cudaEvent_t>(event));
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaEventSynchronize");
+}
+
+int kvc_event_elapsed_ms(void* start, void* end, float* ms) {
+  if (!ms) return fail(KVC_EINVAL, "ms is null");
+  cudaError_t e = cudaEventElapsedTime(ms, static_cast<cudaEvent_t>(start), static_cast<cudaEvent_t>(end));
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaEventElapsedTime");
+}
+
+int kvc_l2_flush(void* scratch, size_t bytes, void* stream) {
+  if (bytes == 0) return KVC_OK;
+  cudaError_t e = cudaMemsetAsync(scratch, 0x5a, bytes, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "kvc_l2_flush");
+}
+
+}  // extern "C"

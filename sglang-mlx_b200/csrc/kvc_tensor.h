@@ -1,0 +1,138 @@
+// kvc_tensor.h — host-side view of a kvc_dltensor plus the parameter blocks the
+// ABI layer hands to the kernel launchers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "kvcache.h"
+
+namespace kvc {
+
+enum class ElemType : int { F32 = 0, F16 = 1, BF16 = 2, I32 = 3, U32 = 4, I64 = 5, INVALID = -1 };
+
+inline int elem_size(ElemType t) {
+  switch (t) {
+    case ElemType::F32: case ElemType::I32: case ElemType::U32: return 4;
+    case ElemType::F16: case ElemType::BF16: return 2;
+    case ElemType::I64: return 8;
+    default: return 0;
+  }
+}
+
+inline const char* elem_name(ElemType t) {
+  switch (t) {
+    case ElemType::F32: return "float32";
+    case ElemType::F16: return "float16";
+    case ElemType::BF16: return "bfloat16";
+    case ElemType::I32: return "int32";
+    case ElemType::U32: return "uint32";
+    case ElemType::I64: return "int64";
+    default: return "invalid";
+  }
+}
+
+struct View {
+  char* data = nullptr;  // data + byte_offset
+  ElemType dtype = ElemType::INVALID;
+  int ndim = 0;
+  int64_t shape[8] = {0};
+  int64_t strides[8] = {0};  // elements
+  int device = -1;
+  bool on_cuda = false;
+
+  int64_t size(int i) const { return shape[i < 0 ? i + ndim : i]; }
+  int64_t stride(int i) const { return strides[i < 0 ? i + ndim : i]; }
+  int64_t numel() const {
+    int64_t n = 1;
+    for (int i = 0; i < ndim; ++i) n *= shape[i];
+    return n;
+  }
+  // True when dims [first, ndim) are dense row-major.
+  bool dense_from(int first) const {
+    int64_t expect = 1;
+    for (int i = ndim - 1; i >= first; --i) {
+      if (shape[i] != 1 && strides[i] != expect) return false;
+      expect *= shape[i];
+    }
+    return true;
+  }
+};
+
+// Parses `t` into `v`.  Returns false (and sets the error message) on a
+// malformed descriptor.  `name` is used in messages.
+bool parse(const kvc_dltensor* t, const char* name, View* v);
+
+// Parameters of one decode launch (both the single-pass and split-K forms).
+struct DecodeArgs {
+  void* out;
+  const void* q;
+  const void* k_cache;
+  const void* v_cache;
+  const uint32_t* block_tables;
+  const uint32_t* context_lens;
+  const float* alibi;  // nullptr = off
+  float* part_max;     // split-K workspace (nullptr = single pass)
+  float* part_sum;
+  float* part_out;
+  ElemType q_type, cache_type;
+  int num_seqs, num_heads, num_kv_heads, head_size, block_size;
+  int max_blocks_per_seq, max_seq_len;
+  int64_t num_blocks;
+  int64_t q_seq_stride, q_head_stride;        // elements
+  int64_t out_seq_stride, out_head_stride;    // elements
+  int64_t k_block_stride, k_head_stride;      // elements
+  int64_t v_block_stride, v_head_stride;      // elements
+  int64_t table_stride;                       // elements
+  int partition_size;                         // tokens per partition (split-K)
+  int num_partitions;                         // 1 = single pass
+  int64_t part_seq_stride, part_head_stride;  // elements of part_max / part_sum
+  int64_t part_out_seq_stride, part_out_head_stride, part_out_part_stride;
+  float scale;
+};
+
+struct ReshapeArgs {
+  const void* key;
+  const void* value;
+  void* key_cache;
+  void* value_cache;
+  const void* slots;
+  ElemType kv_type, cache_type, slot_type;
+  int64_t num_tokens;
+  int num_heads, head_size, block_size;
+  int64_t num_blocks;
+  int64_t key_tok_stride, key_head_stride;      // elements
+  int64_t value_tok_stride, value_head_stride;  // elements
+  int64_t kc_block_stride, kc_head_stride;      // vLLM: [nb, H, D/x, bs, x]; flash: [nb, bs, H, D]
+  int64_t vc_block_stride, vc_head_stride;
+  int64_t kc_tok_stride, vc_tok_stride;         // flash layout only
+};
+
+struct GatherArgs {
+  void* k_out;
+  void* v_out;
+  const void* k_buf;
+  const void* v_buf;
+  const void* indices;
+  ElemType type, index_type;
+  int64_t num_indices;
+  int64_t num_slots;
+  int num_heads, head_size;
+  int64_t kb_slot_stride, kb_head_stride;
+  int64_t vb_slot_stride, vb_head_stride;
+  int64_t ko_tok_stride, ko_head_stride;
+  int64_t vo_tok_stride, vo_head_stride;
+};
+
+cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream);
+cudaError_t launch_reshape_and_cache(const ReshapeArgs& a, cudaStream_t stream);
+cudaError_t launch_reshape_and_cache_flash(const ReshapeArgs& a, cudaStream_t stream);
+cudaError_t launch_gather_kv(const GatherArgs& a, cudaStream_t stream);
+
+}  // namespace kvc
+
+// Host accessors of each translation unit's sticky status word.
+unsigned int kvc_cache_ops_status(int clear, cudaError_t* err);
+unsigned int kvc_decode_status(int clear, cudaError_t* err);

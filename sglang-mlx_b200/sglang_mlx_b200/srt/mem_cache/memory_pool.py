@@ -1,0 +1,209 @@
+"""KV memory pool on B200, API-compatible with
+sglang_mlx/srt/mem_cache/memory_pool.py.
+
+- TokenPoolAllocator: the same LIFO free list (memory_pool.py:27-68); a fresh
+  pool hands out slots in descending order and slot 0 is never allocated.
+- MHATokenPool: per-layer K/V device buffers of shape (pool_size + 1, H, D)
+  (memory_pool.py:76-108).  `store` is one libkvcache append launch that reads
+  the (1, H, S, D) input through its strides (no transpose copy); `fetch` is one
+  gather launch writing (1, H, T, D) (memory_pool.py:117-159).
+- PooledKVCache: the per-request adapter (memory_pool.py:167-269), unchanged
+  in behaviour.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from ... import _lib, dtypes
+from ...device_array import DeviceArray, _stream
+from ...dlpack import as_dltensor, describe, make_dltensor
+
+_L = _lib.lib
+
+
+class TokenPoolAllocator:
+    """Manages allocation of token slots in the KV pool.
+
+    Slot 0 is reserved as padding and never allocated.
+    """
+
+    def __init__(self, pool_size: int):
+        if pool_size <= 0:
+            raise ValueError(f"pool_size must be positive, got {pool_size}")
+        self._pool_size = pool_size
+        # Slots 1..pool_size are allocatable; kept as a stack (memory_pool.py:38).
+        self._free_slots: list[int] = list(range(pool_size, 0, -1))
+
+    def alloc(self, n: int) -> list[int]:
+        """Pops the last *n* free slots; MemoryError if fewer are free."""
+        if n <= 0:
+            return []
+        if n > len(self._free_slots):
+            raise MemoryError(f"Cannot allocate {n} slots: only {len(self._free_slots)} available")
+        allocated = self._free_slots[-n:]
+        del self._free_slots[-n:]
+        return allocated
+
+    def free(self, indices: list[int]) -> None:
+        """Returns *indices* to the free list."""
+        self._free_slots.extend(indices)
+
+    @property
+    def available_size(self) -> int:
+        return len(self._free_slots)
+
+    def clear(self) -> None:
+        """Resets all slots to free."""
+        self._free_slots = list(range(self._pool_size, 0, -1))
+
+
+def _index_array(indices, device: int) -> DeviceArray:
+    if isinstance(indices, DeviceArray):
+        return indices
+    if hasattr(indices, "__dlpack_device__") and not isinstance(indices, np.ndarray):
+        return indices
+    arr = np.asarray(indices, dtype=np.int64)
+    if arr.size and (arr.min() < np.iinfo(np.int32).min or arr.max() > np.iinfo(np.int32).max):
+        return DeviceArray.from_numpy(arr, device=device)
+    return DeviceArray.from_numpy(arr.astype(np.int32), device=device)
+
+
+class MHATokenPool:
+    """Pre-allocated KV cache buffers for all layers.
+
+    Buffer layout per layer: ``(pool_size + 1, n_kv_heads, head_dim)``; slot 0
+    is padding.  Token-first layout; store/fetch convert to/from the
+    ``(1, n_kv_heads, S, head_dim)`` attention format.
+    """
+
+    def __init__(self, pool_size: int, num_layers: int, n_kv_heads: int, head_dim: int,
+                 dtype=dtypes.float16, device: int | None = None):
+        self.pool_size = pool_size
+        self.num_layers = num_layers
+        self.n_kv_heads = n_kv_heads
+        self.head_dim = head_dim
+        self.dtype = dtypes.canonical(dtype)
+        self.device = _lib.current_device() if device is None else int(device)
+        shape = (pool_size + 1, n_kv_heads, head_dim)  # +1 for slot 0 padding
+        self.k_buffer: list[DeviceArray] = [DeviceArray.zeros(shape, self.dtype, self.device)
+                                            for _ in range(num_layers)]
+        self.v_buffer: list[DeviceArray] = [DeviceArray.zeros(shape, self.dtype, self.device)
+                                            for _ in range(num_layers)]
+
+    def store(self, layer_idx: int, indices, keys, values, *, stream=None) -> None:
+        """Writes KV data into the pool at the given slot indices.
+
+        Args:
+            layer_idx: Which transformer layer.
+            indices: Pool slot indices, length S (list, NumPy or device array).
+            keys: ``(1, n_kv_heads, S, head_dim)``; values: same shape.
+        """
+        kshape, kstr, kdt, _, kdev = describe(keys)
+        vshape, vstr, vdt, _, _ = describe(values)
+        if len(kshape) != 4 or kshape[0] != 1 or tuple(vshape) != tuple(kshape):
+            raise ValueError("keys and values must have shape (1, n_kv_heads, S, head_dim)")
+        S = kshape[2]
+        if S == 0:
+            return
+        idx = _index_array(indices, kdev)
+        if describe(idx)[0][0] != S:
+            raise ValueError(f"store: {describe(idx)[0][0]} indices for {S} tokens")
+        kptr, kkeep = as_dltensor(keys, "keys")
+        vptr, vkeep = as_dltensor(values, "values")
+        # (1, H, S, D) read as (S, H, D) through strides: the transpose of
+        # memory_pool.py:131-133 without a copy.
+        kt, kk = make_dltensor(kptr.contents.data + kptr.contents.byte_offset, (S, kshape[1], kshape[3]),
+                               (kstr[2], kstr[1], kstr[3]), kdt, kptr.contents.device.device_id)
+        vt, vk = make_dltensor(vptr.contents.data + vptr.contents.byte_offset, (S, vshape[1], vshape[3]),
+                               (vstr[2], vstr[1], vstr[3]), vdt, vptr.contents.device.device_id)
+        ip, ikeep = as_dltensor(idx, "indices")
+        kb = self.k_buffer[layer_idx]._dltensor()
+        vb = self.v_buffer[layer_idx]._dltensor()
+        _lib.check(_L.kvc_reshape_and_cache_flash(ctypes.pointer(kt), ctypes.pointer(vt), ctypes.pointer(kb),
+                                                  ctypes.pointer(vb), ip, _stream(stream)))
+        del kkeep, vkeep, kk, vk, ikeep
+
+    def fetch(self, layer_idx: int, indices, *, stream=None, k_out=None, v_out=None):
+        """Gathers KV data from the pool in ``(1, n_kv_heads, T, head_dim)`` format."""
+        idx = _index_array(indices, self.device)
+        T = describe(idx)[0][0]
+        shape = (1, self.n_kv_heads, T, self.head_dim)
+        if k_out is None:
+            k_out = DeviceArray.empty(shape, self.dtype, self.device)
+        if v_out is None:
+            v_out = DeviceArray.empty(shape, self.dtype, self.device)
+        if T == 0:
+            return k_out, v_out
+        ptrs = [as_dltensor(a, n) for a, n in ((k_out, "k_out"), (v_out, "v_out"), (self.k_buffer[layer_idx], "k"),
+                                               (self.v_buffer[layer_idx], "v"), (idx, "indices"))]
+        _lib.check(_L.kvc_gather_kv(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ptrs[4][0], _stream(stream)))
+        return k_out, v_out
+
+
+class PooledKVCache:
+    """Adapter that makes the shared KV pool look like a per-request KV cache.
+
+    Models call ``cache.update_and_fetch(keys, values)`` in each attention
+    layer: the new tokens are stored into the pool and all (prefix + new)
+    tokens are gathered back contiguously.
+    """
+
+    def __init__(self, pool: MHATokenPool, layer_idx: int):
+        self._pool = pool
+        self._layer_idx = layer_idx
+        self._prefix_indices: list[int] = []
+        self._new_indices: list[int] = []
+        self._store_offset: int = 0
+
+    def set_indices(self, prefix_indices: list[int], new_indices: list[int]) -> None:
+        """Configures this layer's slots before a forward pass (memory_pool.py:186-195)."""
+        self._prefix_indices = list(prefix_indices)
+        self._new_indices = list(new_indices)
+        self._store_offset = 0
+
+    @property
+    def offset(self) -> int:
+        """RoPE position offset of the new tokens (memory_pool.py:197-204)."""
+        return len(self._prefix_indices)
+
+    def _all_indices(self) -> list[int]:
+        return self._prefix_indices + self._new_indices[: self._store_offset]
+
+    def _store_new(self, keys, values) -> None:
+        n_new = describe(keys)[0][2]
+        store_indices = self._new_indices[self._store_offset: self._store_offset + n_new]
+        self._store_offset += n_new
+        self._pool.store(self._layer_idx, store_indices, keys, values)
+
+    def update_and_fetch(self, keys, values):
+        """Stores new KV and gathers all (prefix + new) KV (memory_pool.py:206-234)."""
+        self._store_new(keys, values)
+        return self._pool.fetch(self._layer_idx, self._all_indices())
+
+    @property
+    def state(self):
+        """Current cached KV, or (None, None) when empty (memory_pool.py:236-242)."""
+        all_indices = self._all_indices()
+        if not all_indices:
+            return None, None
+        return self._pool.fetch(self._layer_idx, all_indices)
+
+    def make_mask(self, N: int, return_array: bool = False, window_size: int | None = None):
+        """Attention mask of the mlx-lm convention the reference delegates to
+        (memory_pool.py:244-269; behaviour pinned by test_memory_pool.py:253-330):
+        None for single-token decode, "causal" for plain prefill, else a boolean
+        (N, offset + N) array."""
+        if N == 1:
+            return None
+        if not return_array and window_size is None:
+            return "causal"
+        offset = self.offset
+        rows = np.arange(offset, offset + N)[:, None]
+        cols = np.arange(offset + N)[None, :]
+        mask = cols <= rows
+        if window_size is not None:
+            mask &= cols > rows - window_size
+        return mask

@@ -1,0 +1,135 @@
+"""CPU oracle pinned against the reference's own outputs (tests/golden/golden.npz,
+made by tests/golden/make_golden.py from the reference's NumPy oracles and its
+MHATokenPool).  No GPU."""
+
+import numpy as np
+import pytest
+
+import cases
+from oracle import c_oracle, kv_oracle
+
+REF_CASES = {
+    "ref_setup": cases.ref_setup_data,
+    "ref_various_32_8": lambda: cases.ref_various(32, 8),
+    "ref_various_32_16": lambda: cases.ref_various(32, 16),
+    "ref_various_128_8": lambda: cases.ref_various(128, 8),
+    "ref_various_128_16": lambda: cases.ref_various(128, 16),
+    "ref_legacy_2048": cases.ref_legacy_2048,
+    "config1_fp16": lambda: cases.config1(dtype="float16"),
+    "config1_bf16": lambda: cases.config1(seed=12, dtype="bfloat16"),
+}
+
+
+def _fill(c):
+    kc, vc = c["k_cache"].copy(), c["v_cache"].copy()
+    T = c["k"].shape[0]
+    k = c["k"].astype(kc.dtype)
+    v = c["v"].astype(vc.dtype)
+    return kv_oracle.reshape_and_cache(k, v, kc, vc, c["slot_mapping"][:T])
+
+
+@pytest.mark.parametrize("name", list(REF_CASES))
+def test_inputs_match_fixture(name, golden):
+    c = REF_CASES[name]()
+    assert cases.digest(c["q"], c["k"], c["v"], c["block_tables"], c["context_lens"], c["slot_mapping"]) == str(
+        golden[f"{name}/inputs_sha"]), "seeded inputs drifted from the fixture"
+
+
+@pytest.mark.parametrize("name", list(REF_CASES))
+def test_reshape_and_cache_bit_exact(name, golden):
+    c = REF_CASES[name]()
+    kc, vc = _fill(c)
+    assert cases.digest(kc) == str(golden[f"{name}/k_cache_sha"])
+    assert cases.digest(vc) == str(golden[f"{name}/v_cache_sha"])
+    if f"{name}/k_cache" in golden:
+        np.testing.assert_array_equal(kc, golden[f"{name}/k_cache"])
+        np.testing.assert_array_equal(vc, golden[f"{name}/v_cache"])
+
+
+@pytest.mark.parametrize("name", list(REF_CASES))
+def test_paged_attention_matches_reference_oracle(name, golden):
+    c = REF_CASES[name]()
+    kc, vc = _fill(c)
+    out = kv_oracle.paged_attention_v1(c["q"], kc, vc, c["block_tables"], c["context_lens"], c["num_kv_heads"],
+                                       c["scale"], c["block_size"], c["max_seq_len"])
+    ref = golden[f"{name}/attn"]
+    # The reference oracle rounds its float64 result to the query dtype and has
+    # no +1e-6 in the denominator: agree to the output dtype's rounding.
+    got = out.astype(ref.dtype)
+    tol = 1e-3 if ref.dtype == np.float16 else 1e-5
+    np.testing.assert_allclose(got.astype(np.float64), ref.astype(np.float64), rtol=tol, atol=tol)
+
+
+def test_c_oracle_matches_numpy_oracle():
+    c = cases.config1(dtype="float16")
+    kc, vc = _fill(c)
+    ref = kv_oracle.paged_attention_v1(c["q"], kc, vc, c["block_tables"], c["context_lens"], c["num_kv_heads"],
+                                       c["scale"], c["block_size"], c["max_seq_len"])
+    got = c_oracle.paged_attention(c["q"], "float16", kc, vc, "float16", c["block_tables"], c["context_lens"],
+                                   c["num_kv_heads"], c["scale"], c["max_seq_len"])
+    np.testing.assert_allclose(got, ref, rtol=1e-10, atol=1e-12)
+
+
+def test_c_oracle_bf16_bits_and_alibi():
+    c = cases.config1(seed=12, dtype="bfloat16")
+    kc, vc = _fill(c)
+    slopes = np.linspace(-0.05, 0.05, c["q"].shape[1]).astype(np.float32)
+    ref = kv_oracle.paged_attention_v1(c["q"], kc, vc, c["block_tables"], c["context_lens"], c["num_kv_heads"],
+                                       c["scale"], c["block_size"], c["max_seq_len"], slopes)
+    bits = lambda a: kv_oracle.f32_to_bf16_bits(a)  # noqa: E731
+    got = c_oracle.paged_attention(bits(c["q"]), "bfloat16", bits(kc), bits(vc), "bfloat16", c["block_tables"],
+                                   c["context_lens"], c["num_kv_heads"], c["scale"], c["max_seq_len"], slopes)
+    np.testing.assert_allclose(got, ref, rtol=1e-10, atol=1e-12)
+
+
+def test_c_oracle_reshape_matches_numpy_oracle():
+    c = cases.config1(dtype="float16")
+    kc1, vc1 = _fill(c)
+    kc2, vc2 = c["k_cache"].copy(), c["v_cache"].copy()
+    c_oracle.reshape_and_cache(c["k"].astype(np.float16), c["v"].astype(np.float16), kc2, vc2, c["slot_mapping"])
+    np.testing.assert_array_equal(kc1, kc2)
+    np.testing.assert_array_equal(vc1, vc2)
+
+
+@pytest.mark.parametrize("psize", [16, 64, 512])
+def test_splitk_restatement_equals_single_pass(psize):
+    c = cases.config1(dtype="float16")
+    kc, vc = _fill(c)
+    one = kv_oracle.paged_attention_v1(c["q"], kc, vc, c["block_tables"], c["context_lens"], c["num_kv_heads"],
+                                       c["scale"], c["block_size"], c["max_seq_len"])
+    split, _, _ = kv_oracle.paged_attention_splitk(c["q"], kc, vc, c["block_tables"], c["context_lens"],
+                                                   c["num_kv_heads"], c["scale"], c["block_size"], c["max_seq_len"],
+                                                   psize)
+    np.testing.assert_allclose(split, one, rtol=1e-9, atol=1e-12)
+
+
+def test_zero_output_rules():
+    c = cases.ref_various(32, 16)
+    kc, vc = _fill(c)
+    for lens, msl in (([0], 16), ([16], 8)):
+        out = kv_oracle.paged_attention_v1(c["q"], kc, vc, c["block_tables"], np.array(lens), 2, c["scale"], 16, msl)
+        assert not out.any()
+
+
+def test_pool_store_fetch_matches_reference_pool(golden):
+    k_buf = [np.zeros((41, 4, 8), np.float32) for _ in range(2)]
+    v_buf = [np.zeros((41, 4, 8), np.float32) for _ in range(2)]
+    i = 0
+    while f"pool/write{i}/layer" in golden:
+        layer = int(golden[f"pool/write{i}/layer"])
+        kv_oracle.pool_store(k_buf[layer], v_buf[layer], golden[f"pool/write{i}/idx"], golden[f"pool/write{i}/k"],
+                             golden[f"pool/write{i}/v"])
+        i += 1
+    for layer in (0, 1):
+        k, v = kv_oracle.pool_fetch(k_buf[layer], v_buf[layer], golden["pool/fetch_idx"])
+        np.testing.assert_array_equal(k, golden[f"pool/fetch{layer}/k"])
+        np.testing.assert_array_equal(v, golden[f"pool/fetch{layer}/v"])
+
+
+def test_bf16_rounding_is_nearest_even():
+    vals = np.array([1.0, 1.00390625, 1.0078125, 1.01171875, -3.0e38, 3.4e38, 1e-40], np.float32)
+    bits = kv_oracle.f32_to_bf16_bits(vals)
+    back = kv_oracle.bf16_bits_to_f32(bits)
+    # 1 + 2^-8 is a tie between 1 and 1 + 2^-7: rounds to even (1.0)
+    assert back[1] == 1.0 and back[3] == np.float32(1.015625)
+    assert np.isinf(back[5])
