@@ -1,12 +1,540 @@
-// decode_mma.cuh — tensor-core paged decode (placeholder: dispatch only).
+// decode_mma.cuh — tensor-core paged decode for sm_100a (f16/f16 and bf16/bf16).
+//
+// Included by decode.cu (shares DecodeParams, partition_range, the status word).
+//
+// CTA = (kv head, sequence, partition).  All G = num_heads / num_kv_heads query
+// heads of the KV group are the M rows of one m16n8k16 tile (G <= 16), so each
+// K/V page is fetched from HBM once for the whole group (the reference's grid
+// is per query head and re-reads every page G times,
+// paged_attention_kernels.metal:81-83).
+//
+// Data movement: each warp owns a ring of STAGES shared-memory stages.  A stage
+// holds one 32-token group: 32/BS pages of K ([D/8][BS][8] elements, 16-byte
+// rows per token) and of V ([D][BS]).  Pages are contiguous in HBM, so one lane
+// moves each with a single 1-D bulk copy (cp.async.bulk, no multicast) that
+// completes on the stage's mbarrier; STAGES-1 groups stay in flight while the
+// warp computes on the current one.
+//
+// Math per group (natural token order):
+//   S[head][tok] = sum_d Q[head][d] K[tok][d]   A = Q (registers, loaded once),
+//       B = K^T via ldmatrix on the [D/8][BS][8] page: 8 tokens x 16 B rows.
+//   online softmax in the log2 domain (row max across the quad of lanes that
+//       share a head), masked tokens -> -inf.
+//   O[head][d] += P[head][tok] V[tok][d]        A = P taken straight from the S
+//       accumulators (two 8-token tiles form one 16-token k-step), B = V via
+//       ldmatrix on the [D][BS] page: 8 dims x 16 B (8 tokens) rows.
+// fp32 accumulation everywhere; P is rounded to the cache type for the second
+// product (the only rounding the reference's fp32 path does not have).
 #pragma once
 
 namespace kvc {
+namespace mma_detail {
 
-static bool mma_supported(const DecodeArgs&) { return false; }
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
 
-static cudaError_t launch_mma(const DecodeParams&, const DecodeArgs&, cudaStream_t) {
-  return cudaErrorNotSupported;
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits for the phase with `parity` to complete; gives up after ~1 s of wall
+// time (returns false) so a lost transfer can never hang the GPU.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0 && global_timer_ns() - t0 > 1000000000ull) return false;
+  }
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` (bytes).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+template <typename T> struct MmaOp;
+template <> struct MmaOp<__nv_bfloat16> {
+  __device__ __forceinline__ static void run(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+};
+template <> struct MmaOp<__half> {
+  __device__ __forceinline__ static void run(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+};
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+}  // namespace mma_detail
+
+template <int D, int BS, int NW, int STAGES>
+struct MmaGeom {
+  static constexpr int GT = 32;                    // tokens per group
+  static constexpr int PPG = GT / BS;              // pages per group
+  static constexpr int PAGE = D * BS * 2;          // bytes of one K (or V) page
+  static constexpr int STAGE = PPG * 2 * PAGE;     // K pages then V pages
+  static constexpr int RING = NW * STAGES * STAGE;
+  static constexpr int BAR_OFF = RING;             // NW*STAGES mbarriers
+  static constexpr int MASK_OFF = BAR_OFF + NW * STAGES * 8;
+  static constexpr int COMBINE = NW * 16 * D * 4 + NW * 16 * 2 * 4;  // reuses the ring
+  static constexpr int SMEM = MASK_OFF + NW * STAGES * 4;
+  static_assert(COMBINE <= RING, "combine buffer must fit in the ring");
+};
+
+template <typename T, int D, int BS, int NW, int STAGES>
+__global__ void __launch_bounds__(NW * 32) paged_decode_mma_kernel(DecodeParams p) {
+  using namespace mma_detail;
+  using Geo = MmaGeom<D, BS, NW, STAGES>;
+  constexpr int GT = Geo::GT, PPG = Geo::PPG, PAGE = Geo::PAGE;
+  constexpr int KS = D / 16;  // k-steps of Q.K^T
+  constexpr int NT = D / 8;   // n-tiles of P.V
+  extern __shared__ __align__(128) uint8_t smem[];
+
+  const int kvh = blockIdx.x, seq = blockIdx.y, part = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = lane >> 2, q4 = lane & 3;
+  const int G = p.num_heads / p.num_kv_heads;
+  const int h0 = kvh * G;
+
+  const uint32_t ctx = p.context_lens[seq];
+  int begin = 0, end = 0;
+  bool zero_out = false;
+  if (!partition_range(p, seq, part, ctx, &begin, &end, &zero_out)) {
+    if (zero_out) write_zero_heads<T>(p, seq, h0, G, D);
+    return;
+  }
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Geo::BAR_OFF) + warp * STAGES;
+  uint32_t* masks = reinterpret_cast<uint32_t*>(smem + Geo::MASK_OFF) + warp * STAGES;
+  uint8_t* ring = smem + (size_t)warp * STAGES * Geo::STAGE;
+  if (lane == 0) {
+    for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
+    mbar_fence_init();
+  }
+  __syncwarp();
+
+  // ---- Q as A fragments (natural dim order), rows = heads of the group.
+  uint32_t qa[KS][4];
+  {
+    const T* qp = reinterpret_cast<const T*>(p.q) + (int64_t)seq * p.q_seq_stride;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      const int d0 = ks * 16 + 2 * q4;
+      uint32_t v[4] = {0u, 0u, 0u, 0u};
+      if (r < G) {
+        const T* row = qp + (int64_t)(h0 + r) * p.q_head_stride;
+        v[0] = *reinterpret_cast<const uint32_t*>(row + d0);
+        v[2] = *reinterpret_cast<const uint32_t*>(row + d0 + 8);
+      }
+      if (r + 8 < G) {
+        const T* row = qp + (int64_t)(h0 + r + 8) * p.q_head_stride;
+        v[1] = *reinterpret_cast<const uint32_t*>(row + d0);
+        v[3] = *reinterpret_cast<const uint32_t*>(row + d0 + 8);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) qa[ks][i] = v[i];
+    }
+  }
+  const float qk_scale = p.scale * kLog2e;
+  float slope_lo = 0.f, slope_hi = 0.f;  // ALiBi slopes of rows r and r + 8 (log2 units)
+  if (p.alibi) {
+    if (r < G) slope_lo = p.alibi[h0 + r] * kLog2e;
+    if (r + 8 < G) slope_hi = p.alibi[h0 + r + 8] * kLog2e;
+  }
+
+  const T* kbase = reinterpret_cast<const T*>(p.k_cache) + (int64_t)kvh * p.k_head_stride;
+  const T* vbase = reinterpret_cast<const T*>(p.v_cache) + (int64_t)kvh * p.v_head_stride;
+  const uint32_t* table = p.block_tables + (int64_t)seq * p.table_stride;
+  const int ngroups = (end - begin + GT - 1) / GT;
+  const int n_mine = warp < ngroups ? (ngroups - warp + NW - 1) / NW : 0;
+  const int page_end = (end + BS - 1) / BS;  // first page past the context
+
+  // Lane i < PPG fetches the block id of page i of group `k` of this warp.
+  auto load_block = [&](int k) -> uint32_t {
+    uint32_t b = 0xffffffffu;
+    if (lane < PPG && k < n_mine) {
+      const int pg = (begin + (warp + k * NW) * GT) / BS + lane;
+      if (pg < page_end) b = __ldg(table + pg);
+    }
+    return b;
+  };
+  // Lane 0 issues the copies of group `k` into stage `s`; `blk` holds lane
+  // i's block id (from load_block).  Records which pages were loaded.
+  auto issue = [&](int k, int s, uint32_t blk) {
+    uint32_t ids[PPG];
+#pragma unroll
+    for (int i = 0; i < PPG; ++i) ids[i] = __shfl_sync(0xffffffffu, blk, i);
+    if (lane == 0) {
+      const int pg0 = (begin + (warp + k * NW) * GT) / BS;
+      uint32_t mask = 0, bytes = 0;
+#pragma unroll
+      for (int i = 0; i < PPG; ++i) {
+        if (pg0 + i < page_end) {
+          if ((int64_t)ids[i] < p.num_blocks) {
+            mask |= 1u << i;
+            bytes += 2 * PAGE;
+          } else {
+            set_status(&g_decode_status, KVC_STATUS_BLOCK_OOB);
+          }
+        }
+      }
+      masks[s] = mask;
+      uint8_t* st = ring + (size_t)s * Geo::STAGE;
+      if (bytes) {
+        mbar_arrive_expect_tx(&bars[s], bytes);
+#pragma unroll
+        for (int i = 0; i < PPG; ++i) {
+          if (mask & (1u << i)) {
+            const int64_t b = (int64_t)ids[i];
+            bulk_g2s(st + i * PAGE, kbase + b * p.k_block_stride, PAGE, &bars[s]);
+            bulk_g2s(st + (PPG + i) * PAGE, vbase + b * p.v_block_stride, PAGE, &bars[s]);
+          }
+        }
+      } else {
+        mbar_arrive(&bars[s]);
+      }
+    }
+  };
+
+  // ---- prologue: fill the ring
+#pragma unroll
+  for (int s = 0; s < STAGES; ++s) {
+    if (s < n_mine) issue(s, s, load_block(s));
+  }
+
+  float m_lo = -INFINITY, m_hi = -INFINITY;  // running max (log2 units), rows r / r+8
+  float l_lo = 0.f, l_hi = 0.f;              // this lane's share of the row sums
+  float o[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+  int k_fail = -1;  // group whose wait gave up
+
+  for (int k = 0; k < n_mine; ++k) {
+    const int s = k % STAGES;
+    const uint32_t next_blk = load_block(k + STAGES);  // latency hidden by this group's math
+    if (!mbar_wait_bounded(&bars[s], (uint32_t)((k / STAGES) & 1))) {
+      k_fail = k;
+      break;
+    }
+    const uint8_t* st = ring + (size_t)s * Geo::STAGE;
+    const uint32_t kst = smem_u32(st);
+    const uint32_t vst = smem_u32(st + PPG * PAGE);
+    const int tok0 = begin + (warp + k * NW) * GT;  // first token of the group
+    const uint32_t pmask = masks[s];
+    const bool tail = (tok0 + GT > end) || (pmask != (1u << PPG) - 1u);
+
+    // ---- S = Q K^T : 4 tiles of 8 tokens
+    float sacc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      // lane -> matrix (lane >> 3): chunk 2*ks + (lane>>3); row (lane & 7): token 8j + (lane & 7)
+      const int tok = 8 * j + (lane & 7);
+      const int pg = tok / BS, off = tok % BS;
+#pragma unroll
+      for (int ks = 0; ks < KS; ks += 2) {
+        const int chunk = 2 * ks + (lane >> 3);
+        const uint32_t addr = kst + pg * PAGE + (chunk * BS + off) * 16;
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4(addr, b0, b1, b2, b3);
+        MmaOp<T>::run(sacc[j], qa[ks], b0, b1);
+        MmaOp<T>::run(sacc[j], qa[ks + 1], b2, b3);
+      }
+    }
+
+    // ---- online softmax (log2 domain).  Lane holds tokens 8j + 2*q4 + e.
+    float mx_lo = -INFINITY, mx_hi = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = 8 * j + 2 * q4 + e;
+        float x_lo = sacc[j][e] * qk_scale;
+        float x_hi = sacc[j][2 + e] * qk_scale;
+        if (p.alibi) {
+          const float pos = (float)(tok0 + t - (int)ctx + 1);
+          x_lo += slope_lo * pos;
+          x_hi += slope_hi * pos;
+        }
+        if (tail) {
+          const bool ok = (tok0 + t < end) && ((pmask >> (t / BS)) & 1u);
+          x_lo = ok ? x_lo : -INFINITY;
+          x_hi = ok ? x_hi : -INFINITY;
+        }
+        sacc[j][e] = x_lo;
+        sacc[j][2 + e] = x_hi;
+        mx_lo = fmaxf(mx_lo, x_lo);
+        mx_hi = fmaxf(mx_hi, x_hi);
+      }
+    }
+    mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
+    mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
+    mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
+    mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
+    const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
+    // A row whose every token so far is masked keeps max -inf: use 0 as the
+    // reference so exp2 sees -inf - 0 = -inf (never -inf - -inf = NaN).
+    const float ref_lo = mn_lo == -INFINITY ? 0.f : mn_lo;
+    const float ref_hi = mn_hi == -INFINITY ? 0.f : mn_hi;
+    const float a_lo = fast_exp2(m_lo - ref_lo), a_hi = fast_exp2(m_hi - ref_hi);
+    m_lo = mn_lo;
+    m_hi = mn_hi;
+    float ps_lo = 0.f, ps_hi = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        sacc[j][e] = fast_exp2(sacc[j][e] - ref_lo);
+        sacc[j][2 + e] = fast_exp2(sacc[j][2 + e] - ref_hi);
+        ps_lo += sacc[j][e];
+        ps_hi += sacc[j][2 + e];
+      }
+    }
+    l_lo = l_lo * a_lo + ps_lo;
+    l_hi = l_hi * a_hi + ps_hi;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      o[nt][0] *= a_lo;
+      o[nt][1] *= a_lo;
+      o[nt][2] *= a_hi;
+      o[nt][3] *= a_hi;
+    }
+
+    // ---- O += P V : 2 k-steps of 16 tokens x NT tiles of 8 dims
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      uint32_t pa[4];
+      pa[0] = MmaOp<T>::pack(sacc[2 * kk][0], sacc[2 * kk][1]);
+      pa[1] = MmaOp<T>::pack(sacc[2 * kk][2], sacc[2 * kk][3]);
+      pa[2] = MmaOp<T>::pack(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1]);
+      pa[3] = MmaOp<T>::pack(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]);
+      // lane -> matrix mi = lane >> 3: dims 8*(nt + mi/2) + (lane & 7), tokens 16kk + 8*(mi & 1) ..+7
+      const int mi = lane >> 3;
+      const int vtok = 16 * kk + 8 * (mi & 1);
+      const int vpg = vtok / BS, voff = vtok % BS;
+      // tokens this lane holds in the B fragments: 16kk + 2*q4 + e (b0/b2) and +8 (b1/b3)
+      const int t_lo = tok0 + 16 * kk + 2 * q4;
+      bool ok_lo0 = true, ok_lo1 = true, ok_hi0 = true, ok_hi1 = true;
+      if (tail) {
+        const int tl = 16 * kk + 2 * q4;
+        ok_lo0 = (t_lo < end) && ((pmask >> (tl / BS)) & 1u);
+        ok_lo1 = (t_lo + 1 < end) && ((pmask >> ((tl + 1) / BS)) & 1u);
+        ok_hi0 = (t_lo + 8 < end) && ((pmask >> ((tl + 8) / BS)) & 1u);
+        ok_hi1 = (t_lo + 9 < end) && ((pmask >> ((tl + 9) / BS)) & 1u);
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; nt += 2) {
+        const int dim = 8 * (nt + (mi >> 1)) + (lane & 7);
+        const uint32_t addr = vst + vpg * PAGE + (dim * BS + voff) * 2;
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4(addr, b0, b1, b2, b3);
+        if (tail) {
+          // zero V of masked tokens: their slots may hold anything (NaN * 0 = NaN)
+          const uint32_t m_lo_bits = (ok_lo0 ? 0x0000ffffu : 0u) | (ok_lo1 ? 0xffff0000u : 0u);
+          const uint32_t m_hi_bits = (ok_hi0 ? 0x0000ffffu : 0u) | (ok_hi1 ? 0xffff0000u : 0u);
+          b0 &= m_lo_bits;
+          b2 &= m_lo_bits;
+          b1 &= m_hi_bits;
+          b3 &= m_hi_bits;
+        }
+        MmaOp<T>::run(o[nt], pa, b0, b1);
+        MmaOp<T>::run(o[nt + 1], pa, b2, b3);
+      }
+    }
+
+    // ---- recycle the stage
+    __syncwarp();
+    if (k + STAGES < n_mine) {
+      fence_proxy_async();
+      issue(k + STAGES, s, next_blk);
+    }
+  }
+
+  if (k_fail >= 0) {
+    // Groups k_fail .. k_fail + STAGES - 1 were issued and not consumed: give
+    // each in-flight copy another bounded wait before the ring is reused.
+    if (lane == 0) set_status(&g_decode_status, KVC_STATUS_WAIT_TIMEOUT);
+    for (int kk = k_fail; kk < n_mine && kk < k_fail + STAGES; ++kk)
+      mbar_wait_bounded(&bars[kk % STAGES], (uint32_t)((kk / STAGES) & 1));
+  }
+
+  // ---- merge: quad sums of l, then across warps through shared memory.
+  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
+  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
+  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
+  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
+  __syncthreads();  // every warp is done with its ring
+  float* red_o = reinterpret_cast<float*>(smem);          // [NW][16][D]
+  float* red_ml = red_o + NW * 16 * D;                     // [NW][16][2] (max, sum)
+  {
+    float* ow = red_o + (size_t)warp * 16 * D;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int d = 8 * nt + 2 * q4;
+      ow[r * D + d] = o[nt][0];
+      ow[r * D + d + 1] = o[nt][1];
+      ow[(r + 8) * D + d] = o[nt][2];
+      ow[(r + 8) * D + d + 1] = o[nt][3];
+    }
+    if (q4 == 0) {
+      red_ml[(warp * 16 + r) * 2 + 0] = m_lo;
+      red_ml[(warp * 16 + r) * 2 + 1] = l_lo;
+      red_ml[(warp * 16 + r + 8) * 2 + 0] = m_hi;
+      red_ml[(warp * 16 + r + 8) * 2 + 1] = l_hi;
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * D; i += NW * 32) {
+    const int g = i / D, d = i - g * D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, red_ml[(w * 16 + g) * 2]);
+    float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        const float mw = red_ml[(w * 16 + g) * 2];
+        const float wt = mw == -INFINITY ? 0.f : fast_exp2(mw - M);
+        L += wt * red_ml[(w * 16 + g) * 2 + 1];
+        A += wt * red_o[((size_t)w * 16 + g) * D + d];
+      }
+    }
+    // partial maxima are exchanged in natural-log units (as the generic kernel)
+    emit<T>(p, seq, h0 + g, part, d, M * kLn2, L, A, d == 0);
+  }
+}
+
+// ---- dispatch -------------------------------------------------------------------
+
+constexpr int kMmaWarps = 4;
+constexpr int kMmaStages = 3;
+
+static bool mma_disabled_by_env() {
+  const char* v = getenv("KVC_DECODE_KERNEL");
+  return v && (v[0] == 'g' || v[0] == 'G');  // "generic"
+}
+
+static bool mma_supported(const DecodeArgs& a) {
+  if (mma_disabled_by_env()) return false;
+  if (a.q_type != a.cache_type) return false;
+  if (a.q_type != ElemType::F16 && a.q_type != ElemType::BF16) return false;
+  if (!(a.head_size == 64 || a.head_size == 128)) return false;
+  if (a.block_size != 8 && a.block_size != 16 && a.block_size != 32) return false;
+  const int G = a.num_heads / a.num_kv_heads;
+  if (G < 1 || G > 16) return false;
+  if (a.num_partitions > 1 && a.partition_size % 32 != 0) return false;
+  // q rows are read as 4-byte pairs
+  if ((reinterpret_cast<uintptr_t>(a.q) & 3u) || (a.q_seq_stride & 1) || (a.q_head_stride & 1)) return false;
+  return true;
+}
+
+template <typename T, int D, int BS>
+static cudaError_t launch_mma_typed(const DecodeParams& p, cudaStream_t stream) {
+  using Geo = MmaGeom<D, BS, kMmaWarps, kMmaStages>;
+  auto kern = paged_decode_mma_kernel<T, D, BS, kMmaWarps, kMmaStages>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo::SMEM);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  dim3 grid((unsigned)p.num_kv_heads, (unsigned)p.num_seqs, (unsigned)p.num_partitions);
+  kern<<<grid, kMmaWarps * 32, Geo::SMEM, stream>>>(p);
+  count_launch();
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_mma_t(const DecodeParams& p, const DecodeArgs& a, cudaStream_t stream) {
+  if (a.head_size == 128) {
+    if (a.block_size == 8) return launch_mma_typed<T, 128, 8>(p, stream);
+    if (a.block_size == 16) return launch_mma_typed<T, 128, 16>(p, stream);
+    return launch_mma_typed<T, 128, 32>(p, stream);
+  }
+  if (a.block_size == 8) return launch_mma_typed<T, 64, 8>(p, stream);
+  if (a.block_size == 16) return launch_mma_typed<T, 64, 16>(p, stream);
+  return launch_mma_typed<T, 64, 32>(p, stream);
+}
+
+static cudaError_t launch_mma(const DecodeParams& p, const DecodeArgs& a, cudaStream_t stream) {
+  if (a.q_type == ElemType::BF16) return launch_mma_t<__nv_bfloat16>(p, a, stream);
+  return launch_mma_t<__half>(p, a, stream);
 }
 
 }  // namespace kvc

@@ -332,3 +332,25 @@ def test_torch_tensors_via_dlpack(gpu):
     assert_close(out.to_numpy(), golden["config1_fp16/attn"].astype(np.float64), ATOL_NS, RTOL_NS, "torch")
     back = torch.from_dlpack(out)
     assert back.shape == (8, 32, 128) and back.dtype == torch.float16
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+@pytest.mark.parametrize("bs", [8, 16, 32])
+def test_tensor_core_and_generic_kernels_agree(gpu, monkeypatch, dtype, bs):
+    """The same inputs through both decode kernels (KVC_DECODE_KERNEL=generic
+    forces the CUDA-core one) agree with each other and with the oracle."""
+    c = cases.paged_batch(500 + bs, dtype, 5, 28, 4, 128, bs, [3, 64, 65, 700, 2049])
+    d = upload_case(c)
+    fill_cache(d)
+    kc, vc = oracle_fill(c, dtype)
+    ref = kv_oracle.paged_attention_v1(kv_oracle.round_to(c["q"], dtype), kc, vc, c["block_tables"],
+                                       c["context_lens"], 4, c["scale"], bs, c["max_seq_len"])
+    fast = run_v1(d, c).to_numpy()
+    fast2 = run_v2(d, c, partition_size=128).to_numpy()
+    monkeypatch.setenv("KVC_DECODE_KERNEL", "generic")
+    slow = run_v1(d, c).to_numpy()
+    slow2 = run_v2(d, c, partition_size=128).to_numpy()
+    monkeypatch.delenv("KVC_DECODE_KERNEL")
+    for name, out in (("mma v1", fast), ("mma v2", fast2), ("generic v1", slow), ("generic v2", slow2)):
+        assert_close(out, ref, ATOL_NS, RTOL_NS, name)
+    assert_close(fast, slow, ATOL_NS, RTOL_NS, "mma vs generic")
