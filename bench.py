@@ -366,17 +366,19 @@ def run_ours(args, cfg, rank, world, local_rank):
             decode(i)
             out[i].copy_to_host(h_o[i])
 
-    for _ in range(max(1, args.warmup)):
-        e2e_step()
-    _lib.synchronize()
-    barrier()
-    e0, e1 = Event(), Event()
-    e0.record()
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record()
-    e1.synchronize()
-    e2e_ms = e0.elapsed_ms(e1)
+    e2e_ms = float("nan")
+    if not args.no_e2e:
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        _lib.synchronize()
+        barrier()
+        e0, e1 = Event(), Event()
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        e1.synchronize()
+        e2e_ms = e0.elapsed_ms(e1)
     h2d = (B * 4 * 2) + L * (B * hq * D * 2 + 2 * B * hkv * D * 2)
     d2h = L * B * hq * D * 2
 
@@ -420,8 +422,8 @@ def run_ours(args, cfg, rank, world, local_rank):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": None, "peak_kind": peak_kind, "kernel": "paged decode (per layer launch)",
                      "algorithmic_bytes_per_launch": alg, "mean_launch_ms": mean_dec_ms},
-        "e2e": {"value": B / (e2e_step_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
+        "e2e": None if args.no_e2e else {"value": B / (e2e_step_ms * 1e-3), "unit": "tokens/s",
+                                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": int(launches),
         "clocks": clocks,
     }
@@ -455,9 +457,16 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (profiling cases only)")
+    ap.add_argument("--batch", type=int, default=0, help="override the batch (profiling cases only)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.layers or args.batch:
+        cfg["layers"] = args.layers or cfg["layers"]
+        cfg["batch"] = args.batch or cfg["batch"]
+        cfg["name"] += f" (reduced: {cfg['layers']} layers, batch {cfg['batch']})"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

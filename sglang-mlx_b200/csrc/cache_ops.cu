@@ -24,7 +24,9 @@ __device__ unsigned int g_cache_ops_status = 0;
 // arithmetic is 64-bit throughout (the Metal kernel's `int` source offsets
 // overflow past 2^31 elements).
 // ---------------------------------------------------------------------------
-constexpr int kTokTile = 32;   // tokens per CTA (one per lane in the store phases)
+// Tokens per CTA: 32 for prefill-sized appends (long contiguous runs per
+// block), 8 for decode-sized ones so that a 256-token append still spreads
+// over hundreds of CTAs.
 constexpr int kAppendThreads = 256;
 
 struct ReshapeParams {
@@ -42,7 +44,7 @@ struct ReshapeParams {
   bool k_vec_store;  // key_cache rows are 16-byte aligned
 };
 
-template <typename KV_T, typename CACHE_T>
+template <typename KV_T, typename CACHE_T, int kTokTile, bool VEC>
 __global__ void __launch_bounds__(kAppendThreads) reshape_and_cache_kernel(ReshapeParams p) {
   constexpr int X = 16 / sizeof(CACHE_T);
   constexpr int VPAD = sizeof(CACHE_T) == 2 ? 2 : 1;  // odd word stride for the V tile
@@ -83,12 +85,33 @@ __global__ void __launch_bounds__(kAppendThreads) reshape_and_cache_kernel(Resha
   // Stage the tile's K and V rows (converted to the cache type) in shared memory.
   const KV_T* key = reinterpret_cast<const KV_T*>(p.key);
   const KV_T* value = reinterpret_cast<const KV_T*>(p.value);
-  for (int i = tid; i < ntok * D; i += kAppendThreads) {
-    const int t = i / D, d = i - t * D;
-    const int64_t tok = t0 + t;
-    ktile[t * kstride + d] = Convert<KV_T, CACHE_T>::apply(key[tok * p.key_tok_stride + h * p.key_head_stride + d]);
-    vtile[t * vstride + d] =
-        Convert<KV_T, CACHE_T>::apply(value[tok * p.value_tok_stride + h * p.value_head_stride + d]);
+  if (VEC) {
+    // 16-byte source loads (host checked alignment of rows and strides)
+    constexpr int VIN = 16 / sizeof(KV_T);
+    const int nvec = D / VIN;
+    for (int i = tid; i < ntok * nvec; i += kAppendThreads) {
+      const int t = i / nvec, d = (i - t * nvec) * VIN;
+      const int64_t tok = t0 + t;
+      const uint4 kr = *reinterpret_cast<const uint4*>(key + tok * p.key_tok_stride + h * p.key_head_stride + d);
+      const uint4 vr =
+          *reinterpret_cast<const uint4*>(value + tok * p.value_tok_stride + h * p.value_head_stride + d);
+      const KV_T* ke = reinterpret_cast<const KV_T*>(&kr);
+      const KV_T* ve = reinterpret_cast<const KV_T*>(&vr);
+#pragma unroll
+      for (int e = 0; e < VIN; ++e) {
+        ktile[t * kstride + d + e] = Convert<KV_T, CACHE_T>::apply(ke[e]);
+        vtile[t * vstride + d + e] = Convert<KV_T, CACHE_T>::apply(ve[e]);
+      }
+    }
+  } else {
+    for (int i = tid; i < ntok * D; i += kAppendThreads) {
+      const int t = i / D, d = i - t * D;
+      const int64_t tok = t0 + t;
+      ktile[t * kstride + d] =
+          Convert<KV_T, CACHE_T>::apply(key[tok * p.key_tok_stride + h * p.key_head_stride + d]);
+      vtile[t * vstride + d] =
+          Convert<KV_T, CACHE_T>::apply(value[tok * p.value_tok_stride + h * p.value_head_stride + d]);
+    }
   }
   __syncthreads();
 
@@ -227,6 +250,22 @@ static cudaError_t launch_row_copy(RowCopyParams& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+template <typename KV_T, typename CACHE_T, int TILE, bool VEC>
+static cudaError_t launch_reshape_tile(const ReshapeParams& p, const ReshapeArgs& a, cudaStream_t stream) {
+  constexpr int X = 16 / sizeof(CACHE_T);
+  constexpr int VPAD = sizeof(CACHE_T) == 2 ? 2 : 1;
+  auto kern = reshape_and_cache_kernel<KV_T, CACHE_T, TILE, VEC>;
+  const size_t smem = (size_t)TILE * ((a.head_size + X) + (a.head_size + VPAD)) * sizeof(CACHE_T);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  dim3 grid((unsigned)((a.num_tokens + TILE - 1) / TILE), (unsigned)a.num_heads);
+  kern<<<grid, kAppendThreads, smem, stream>>>(p);
+  count_launch();
+  return cudaGetLastError();
+}
+
 template <typename KV_T, typename CACHE_T>
 static cudaError_t launch_reshape_typed(const ReshapeArgs& a, cudaStream_t stream) {
   ReshapeParams p;
@@ -253,21 +292,20 @@ static cudaError_t launch_reshape_typed(const ReshapeArgs& a, cudaStream_t strea
   p.slots_i64 = a.slot_type == ElemType::I64;
   constexpr int X = 16 / sizeof(CACHE_T);
   p.k_vec_store = aligned16(a.key_cache) && (a.kc_block_stride % X == 0) && (a.kc_head_stride % X == 0);
-  constexpr int VPAD = sizeof(CACHE_T) == 2 ? 2 : 1;
-  const size_t smem = (size_t)kTokTile * ((a.head_size + X) + (a.head_size + VPAD)) * sizeof(CACHE_T);
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(reshape_and_cache_kernel<KV_T, CACHE_T>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+  constexpr int VIN = 16 / sizeof(KV_T);
+  const bool vec_in = aligned16(a.key) && aligned16(a.value) && a.head_size % VIN == 0 &&
+                      a.key_tok_stride % VIN == 0 && a.key_head_stride % VIN == 0 &&
+                      a.value_tok_stride % VIN == 0 && a.value_head_stride % VIN == 0;
+  if (a.num_tokens <= 4096) {
+    return vec_in ? launch_reshape_tile<KV_T, CACHE_T, 8, true>(p, a, stream)
+                  : launch_reshape_tile<KV_T, CACHE_T, 8, false>(p, a, stream);
   }
-  dim3 grid((unsigned)((a.num_tokens + kTokTile - 1) / kTokTile), (unsigned)a.num_heads);
-  reshape_and_cache_kernel<KV_T, CACHE_T><<<grid, kAppendThreads, smem, stream>>>(p);
-  count_launch();
-  return cudaGetLastError();
+  return vec_in ? launch_reshape_tile<KV_T, CACHE_T, 32, true>(p, a, stream)
+                : launch_reshape_tile<KV_T, CACHE_T, 32, false>(p, a, stream);
 }
 
 cudaError_t launch_reshape_and_cache(const ReshapeArgs& a, cudaStream_t stream) {
-  if (a.num_tokens > (int64_t)INT32_MAX * kTokTile) return cudaErrorInvalidValue;
+  if (a.num_tokens > (int64_t)INT32_MAX * 8) return cudaErrorInvalidValue;
   switch (a.kv_type) {
     case ElemType::F32:
       if (a.cache_type == ElemType::F32) return launch_reshape_typed<float, float>(a, stream);

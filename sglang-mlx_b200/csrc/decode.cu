@@ -16,6 +16,9 @@
 #include <float.h>
 #include <math.h>
 #include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "kvc_common.cuh"
 
@@ -45,6 +48,13 @@ struct DecodeParams {
   int64_t part_out_seq_stride, part_out_head_stride, part_out_part_stride;
   float scale;
 };
+
+// Programmatic dependent launch: the partition kernels let the split-K reduce be
+// scheduled early; the reduce waits for their completion before reading.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 // Token range [begin, end) of this CTA's partition; returns false when the
 // CTA has nothing to do.  `zero_out` is set when the sequence must produce
@@ -131,6 +141,7 @@ __global__ void __launch_bounds__(kGenericWarps * 32) paged_decode_generic_kerne
   const int part = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bs = p.block_size;
+  grid_dependents_launch();  // lets the split-K reduce get scheduled during our tail
 
   const uint32_t ctx = p.context_lens[seq];
   int begin = 0, end = 0;
@@ -277,13 +288,23 @@ __global__ void __launch_bounds__(kGenericWarps * 32) paged_decode_generic_kerne
 
 // ---------------------------------------------------------------------------
 // Split-K reduce: out = sum_p e^{m_p - M} o_p / (sum_p e^{m_p - M} l_p + 1e-6)
-// over the partitions that hold tokens of the sequence.
+// over the partitions that hold tokens of the sequence.  CTA = (head, seq);
+// warp w accumulates partitions w, w + 8, ... with 16-byte loads (lane = 4
+// dims), then the 8 partial rows are summed through shared memory.  Launched
+// as a programmatic dependent of the partition kernel: it may start during
+// that kernel's tail and waits (griddepcontrol.wait) before reading partials.
 // ---------------------------------------------------------------------------
-template <typename T>
-__global__ void __launch_bounds__(128) splitk_reduce_kernel(DecodeParams p, int head_size) {
-  extern __shared__ float w[];  // [num_partitions]
-  __shared__ float s_inv;
+constexpr int kReduceWarps = 8;
+
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(kReduceWarps * 32) splitk_reduce_kernel(DecodeParams p, int head_size) {
+  extern __shared__ float smem_f[];  // w[num_partitions] then acc[kReduceWarps][head_size]
+  __shared__ float red[kReduceWarps];
+  __shared__ float s_M, s_inv;
+  grid_dependency_wait();
   const int head = blockIdx.x, seq = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t ctx = p.context_lens[seq];
   T* out = reinterpret_cast<T*>(p.out) + (int64_t)seq * p.out_seq_stride + (int64_t)head * p.out_head_stride;
   if (ctx == 0 || ctx > (uint32_t)p.max_seq_len) {
@@ -293,21 +314,21 @@ __global__ void __launch_bounds__(128) splitk_reduce_kernel(DecodeParams p, int 
   const int nparts = (int)((ctx + p.partition_size - 1) / p.partition_size);
   const float* pm = p.part_max + (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride;
   const float* pl = p.part_sum + (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride;
-  // max over partitions (block reduce)
+  float* w = smem_f;
+  float* acc_s = smem_f + ((p.num_partitions + 3) & ~3);
+
   float M = -INFINITY;
   for (int i = threadIdx.x; i < nparts; i += blockDim.x) M = fmaxf(M, pm[i]);
-  __shared__ float red[32];
   for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = M;
+  if (lane == 0) red[warp] = M;
   __syncthreads();
-  if (threadIdx.x < 32) {
-    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : -INFINITY;
-    for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
-    if (threadIdx.x == 0) red[0] = v;
+  if (threadIdx.x == 0) {
+    float v = -INFINITY;
+    for (int i = 0; i < kReduceWarps; ++i) v = fmaxf(v, red[i]);
+    s_M = v;
   }
   __syncthreads();
-  M = red[0];
-  __syncthreads();
+  M = s_M;
   float L = 0.f;
   for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
     const float wt = (M == -INFINITY || pm[i] == -INFINITY) ? 0.f : expf(pm[i] - M);
@@ -315,19 +336,60 @@ __global__ void __launch_bounds__(128) splitk_reduce_kernel(DecodeParams p, int 
     L += wt * pl[i];
   }
   for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = L;
+  __syncthreads();  // red[] reuse
+  if (lane == 0) red[warp] = L;
   __syncthreads();
   if (threadIdx.x == 0) {
     float v = 0.f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) v += red[i];
+    for (int i = 0; i < kReduceWarps; ++i) v += red[i];
     s_inv = 1.f / (v + 1e-6f);
   }
-  __syncthreads();
   const float* po = p.part_out + (int64_t)seq * p.part_out_seq_stride + (int64_t)head * p.part_out_head_stride;
+  if (VEC) {
+    const int nv = head_size / 4;
+    for (int v4 = lane; v4 < nv; v4 += 32) {
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      int i = warp;
+      for (; i + 3 * kReduceWarps < nparts; i += 4 * kReduceWarps) {
+        float4 x[4];
+        float ww[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          x[u] = reinterpret_cast<const float4*>(po + (int64_t)(i + u * kReduceWarps) * p.part_out_part_stride)[v4];
+          ww[u] = w[i + u * kReduceWarps];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          a.x += ww[u] * x[u].x;
+          a.y += ww[u] * x[u].y;
+          a.z += ww[u] * x[u].z;
+          a.w += ww[u] * x[u].w;
+        }
+      }
+      for (; i < nparts; i += kReduceWarps) {
+        const float4 x = reinterpret_cast<const float4*>(po + (int64_t)i * p.part_out_part_stride)[v4];
+        const float ww = w[i];
+        a.x += ww * x.x;
+        a.y += ww * x.y;
+        a.z += ww * x.z;
+        a.w += ww * x.w;
+      }
+      reinterpret_cast<float4*>(acc_s + warp * head_size)[v4] = a;
+    }
+  } else {
+    for (int d = lane; d < head_size; d += 32) {
+      float a = 0.f;
+      for (int i = warp; i < nparts; i += kReduceWarps) a += w[i] * po[(int64_t)i * p.part_out_part_stride + d];
+      acc_s[warp * head_size + d] = a;
+    }
+  }
+  __syncthreads();
+  const float inv = s_inv;
   for (int d = threadIdx.x; d < head_size; d += blockDim.x) {
     float a = 0.f;
-    for (int i = 0; i < nparts; ++i) a += w[i] * po[(int64_t)i * p.part_out_part_stride + d];
-    out[d] = from_float<T>(a * s_inv);
+#pragma unroll
+    for (int k = 0; k < kReduceWarps; ++k) a += acc_s[k * head_size + d];
+    out[d] = from_float<T>(a * inv);
   }
 }
 
@@ -363,18 +425,35 @@ static cudaError_t launch_generic_d(const DecodeParams& p, int D, cudaStream_t s
   }
 }
 
-template <typename Q_T>
-static cudaError_t launch_reduce(const DecodeParams& p, int D, cudaStream_t stream) {
-  dim3 grid((unsigned)p.num_heads, (unsigned)p.num_seqs);
-  const size_t smem = (size_t)p.num_partitions * sizeof(float);
+template <typename Q_T, bool VEC>
+static cudaError_t launch_reduce_v(const DecodeParams& p, int D, cudaStream_t stream) {
+  auto kern = splitk_reduce_kernel<Q_T, VEC>;
+  const size_t smem = (size_t)(((p.num_partitions + 3) & ~3) + kReduceWarps * D) * sizeof(float);
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(splitk_reduce_kernel<Q_T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  splitk_reduce_kernel<Q_T><<<grid, 128, smem, stream>>>(p, D);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)p.num_heads, (unsigned)p.num_seqs);
+  cfg.blockDim = dim3(kReduceWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, D);
   count_launch();
-  return cudaGetLastError();
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+template <typename Q_T>
+static cudaError_t launch_reduce(const DecodeParams& p, int D, cudaStream_t stream) {
+  const bool vec = (D % 4 == 0) && (reinterpret_cast<uintptr_t>(p.part_out) % 16 == 0) &&
+                   (p.part_out_seq_stride % 4 == 0) && (p.part_out_head_stride % 4 == 0) &&
+                   (p.part_out_part_stride % 4 == 0);
+  return vec ? launch_reduce_v<Q_T, true>(p, D, stream) : launch_reduce_v<Q_T, false>(p, D, stream);
 }
 
 static DecodeParams to_params(const DecodeArgs& a) {

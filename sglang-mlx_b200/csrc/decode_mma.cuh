@@ -140,10 +140,11 @@ constexpr float kLn2 = 0.6931471805599453f;
 
 }  // namespace mma_detail
 
-template <int D, int BS, int NW, int STAGES>
+template <int D, int BS, int NW, int STAGES, int GT_ = 32>
 struct MmaGeom {
-  static constexpr int GT = 32;                    // tokens per group
+  static constexpr int GT = GT_;                   // tokens per group (16, 32 or 64)
   static constexpr int PPG = GT / BS;              // pages per group
+  static_assert(GT % 16 == 0 && GT >= BS, "a group is whole pages and whole 16-token k-steps");
   static constexpr int PAGE = D * BS * 2;          // bytes of one K (or V) page
   static constexpr int STAGE = PPG * 2 * PAGE;     // K pages then V pages
   static constexpr int RING = NW * STAGES * STAGE;
@@ -154,13 +155,15 @@ struct MmaGeom {
   static_assert(COMBINE <= RING, "combine buffer must fit in the ring");
 };
 
-template <typename T, int D, int BS, int NW, int STAGES>
+template <typename T, int D, int BS, int NW, int STAGES, int GTOK>
 __global__ void __launch_bounds__(NW * 32) paged_decode_mma_kernel(DecodeParams p) {
   using namespace mma_detail;
-  using Geo = MmaGeom<D, BS, NW, STAGES>;
+  using Geo = MmaGeom<D, BS, NW, STAGES, GTOK>;
   constexpr int GT = Geo::GT, PPG = Geo::PPG, PAGE = Geo::PAGE;
-  constexpr int KS = D / 16;  // k-steps of Q.K^T
-  constexpr int NT = D / 8;   // n-tiles of P.V
+  constexpr int KS = D / 16;    // k-steps of Q.K^T
+  constexpr int NT = D / 8;     // n-tiles of P.V
+  constexpr int ST = GT / 8;    // 8-token S tiles per group
+  constexpr int PK = GT / 16;   // 16-token k-steps of P.V per group
   extern __shared__ __align__(128) uint8_t smem[];
 
   const int kvh = blockIdx.x, seq = blockIdx.y, part = blockIdx.z;
@@ -169,6 +172,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_mma_kernel(DecodeParams 
   const int G = p.num_heads / p.num_kv_heads;
   const int h0 = kvh * G;
 
+  grid_dependents_launch();
   const uint32_t ctx = p.context_lens[seq];
   int begin = 0, end = 0;
   bool zero_out = false;
@@ -296,12 +300,12 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_mma_kernel(DecodeParams 
     const uint32_t pmask = masks[s];
     const bool tail = (tok0 + GT > end) || (pmask != (1u << PPG) - 1u);
 
-    // ---- S = Q K^T : 4 tiles of 8 tokens
-    float sacc[4][4];
+    // ---- S = Q K^T : ST tiles of 8 tokens
+    float sacc[ST][4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+    for (int j = 0; j < ST; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < ST; ++j) {
       // lane -> matrix (lane >> 3): chunk 2*ks + (lane>>3); row (lane & 7): token 8j + (lane & 7)
       const int tok = 8 * j + (lane & 7);
       const int pg = tok / BS, off = tok % BS;
@@ -319,7 +323,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_mma_kernel(DecodeParams 
     // ---- online softmax (log2 domain).  Lane holds tokens 8j + 2*q4 + e.
     float mx_lo = -INFINITY, mx_hi = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < ST; ++j) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int t = 8 * j + 2 * q4 + e;
@@ -355,7 +359,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_mma_kernel(DecodeParams 
     m_hi = mn_hi;
     float ps_lo = 0.f, ps_hi = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < ST; ++j) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         sacc[j][e] = fast_exp2(sacc[j][e] - ref_lo);
@@ -374,9 +378,9 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_mma_kernel(DecodeParams 
       o[nt][3] *= a_hi;
     }
 
-    // ---- O += P V : 2 k-steps of 16 tokens x NT tiles of 8 dims
+    // ---- O += P V : PK k-steps of 16 tokens x NT tiles of 8 dims
 #pragma unroll
-    for (int kk = 0; kk < 2; ++kk) {
+    for (int kk = 0; kk < PK; ++kk) {
       uint32_t pa[4];
       pa[0] = MmaOp<T>::pack(sacc[2 * kk][0], sacc[2 * kk][1]);
       pa[1] = MmaOp<T>::pack(sacc[2 * kk][2], sacc[2 * kk][3]);
@@ -479,9 +483,10 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_mma_kernel(DecodeParams 
 }
 
 // ---- dispatch -------------------------------------------------------------------
-
-constexpr int kMmaWarps = 4;
-constexpr int kMmaStages = 3;
+// (warps per CTA) x (ring stages per warp).  4x3 holds 192 KB of ring (one CTA
+// per SM); 2x3 / 2x2 / 1x4 fit two or three CTAs per SM so one CTA's pipeline
+// ramp overlaps another's streaming.  KVC_MMA_CONFIG="<warps>x<stages>"
+// overrides the default for tuning runs.
 
 static bool mma_disabled_by_env() {
   const char* v = getenv("KVC_DECODE_KERNEL");
@@ -502,10 +507,10 @@ static bool mma_supported(const DecodeArgs& a) {
   return true;
 }
 
-template <typename T, int D, int BS>
-static cudaError_t launch_mma_typed(const DecodeParams& p, cudaStream_t stream) {
-  using Geo = MmaGeom<D, BS, kMmaWarps, kMmaStages>;
-  auto kern = paged_decode_mma_kernel<T, D, BS, kMmaWarps, kMmaStages>;
+template <typename T, int D, int BS, int NW, int STAGES, int GT>
+static cudaError_t launch_mma_nw(const DecodeParams& p, cudaStream_t stream) {
+  using Geo = MmaGeom<D, BS, NW, STAGES, GT>;
+  auto kern = paged_decode_mma_kernel<T, D, BS, NW, STAGES, GT>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -515,9 +520,51 @@ static cudaError_t launch_mma_typed(const DecodeParams& p, cudaStream_t stream) 
     configured[dev] = true;
   }
   dim3 grid((unsigned)p.num_kv_heads, (unsigned)p.num_seqs, (unsigned)p.num_partitions);
-  kern<<<grid, kMmaWarps * 32, Geo::SMEM, stream>>>(p);
+  kern<<<grid, NW * 32, Geo::SMEM, stream>>>(p);
   count_launch();
   return cudaGetLastError();
+}
+
+// Variant id = warps * 1000 + stages * 100 + group tokens.
+static int mma_variant() {
+  const char* v = getenv("KVC_MMA_CONFIG");
+  if (!v) return 0;
+  int w = 0, s = 0, g = 32;
+  const int n = sscanf(v, "%dx%dx%d", &w, &s, &g);
+  if (n < 2) return 0;
+  return w * 1000 + s * 100 + g;
+}
+
+template <typename T, int D, int BS>
+static cudaError_t launch_mma_typed(const DecodeParams& p, cudaStream_t stream) {
+  const int v = mma_variant();
+  const int g = v % 100;
+  const bool part_ok = p.num_partitions == 1 || (g > 0 && p.partition_size % g == 0);
+  if (D == 128 && v && part_ok && g >= BS) {
+    switch (v) {
+      case 2332: return launch_mma_nw<T, D, BS, 2, 3, 32>(p, stream);
+      case 4332: return launch_mma_nw<T, D, BS, 4, 3, 32>(p, stream);
+      case 1232: return launch_mma_nw<T, D, BS, 1, 2, 32>(p, stream);
+      case 2232: return launch_mma_nw<T, D, BS, 2, 2, 32>(p, stream);
+      case 3232: return launch_mma_nw<T, D, BS, 3, 2, 32>(p, stream);
+      case 6232: return launch_mma_nw<T, D, BS, 6, 2, 32>(p, stream);
+      case 1332: return launch_mma_nw<T, D, BS, 1, 3, 32>(p, stream);
+      case 4316: if constexpr (BS <= 16) return launch_mma_nw<T, D, BS, 4, 3, 16>(p, stream); break;
+      case 8316: if constexpr (BS <= 16) return launch_mma_nw<T, D, BS, 8, 3, 16>(p, stream); break;
+      case 2416: if constexpr (BS <= 16) return launch_mma_nw<T, D, BS, 2, 4, 16>(p, stream); break;
+      case 4416: if constexpr (BS <= 16) return launch_mma_nw<T, D, BS, 4, 4, 16>(p, stream); break;
+      default: break;
+    }
+  }
+  // Defaults from sweeps on B200 (config 2 / config 3 shapes): 16-token
+  // groups, 4 warps x 3 stages (96 KB, two CTAs and 8 warps per SM) where the
+  // block size allows (98% of copy bandwidth on config 2, against 81% for
+  // 32-token groups); 32-token groups with 2 warps x 2 stages (64 KB, three
+  // CTAs per SM) for 32-token blocks.
+  if constexpr (BS <= 16) {
+    if (p.num_partitions == 1 || p.partition_size % 16 == 0) return launch_mma_nw<T, D, BS, 4, 3, 16>(p, stream);
+  }
+  return launch_mma_nw<T, D, BS, 2, 2, 32>(p, stream);
 }
 
 template <typename T>

@@ -354,3 +354,19 @@ def test_tensor_core_and_generic_kernels_agree(gpu, monkeypatch, dtype, bs):
     for name, out in (("mma v1", fast), ("mma v2", fast2), ("generic v1", slow), ("generic v2", slow2)):
         assert_close(out, ref, ATOL_NS, RTOL_NS, name)
     assert_close(fast, slow, ATOL_NS, RTOL_NS, "mma vs generic")
+
+
+@pytest.mark.parametrize("variant", ["2x3", "4x3", "1x2", "2x2", "3x2", "6x2", "1x3", "4x3x16", "8x3x16", "2x4x16",
+                                     "4x4x16"])
+@pytest.mark.parametrize("bs", [8, 16, 32])
+def test_ring_variants(gpu, monkeypatch, variant, bs):
+    """Every (warps x stages) ring configuration of the tensor-core kernel."""
+    monkeypatch.setenv("KVC_MMA_CONFIG", variant)
+    c = cases.paged_batch(900 + bs, "bfloat16", 6, 32, 8, 128, bs, [1, 31, 33, 128, 517, 1999])
+    d = upload_case(c)
+    fill_cache(d)
+    kc, vc = oracle_fill(c, "bfloat16")
+    ref = kv_oracle.paged_attention_v1(c["q"], kc, vc, c["block_tables"], c["context_lens"], 8, c["scale"], bs,
+                                       c["max_seq_len"])
+    assert_close(run_v1(d, c).to_numpy(), ref, ATOL_NS, RTOL_NS, f"{variant} v1")
+    assert_close(run_v2(d, c, partition_size=256).to_numpy(), ref, ATOL_NS, RTOL_NS, f"{variant} v2")
