@@ -41,6 +41,14 @@ sys.path.insert(0, ROOT)
 METRIC = "paged-decode KV GB/s (% of HBM peak) and decode tokens/s"
 
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one decode launch, from the ncu captures
+# summarised in profiles/ (config 2: captured at batch 64 and scaled by KV bytes to the full launch).
+TRAFFIC_PER_LAUNCH = {
+    2: (2.289e9 + 0.016e9, "profiles/paged_decode_mma_bs16_small.md (batch-64 capture scaled to batch 256)"),
+    3: (537.1e6 + 9.8e6, "profiles/paged_decode_mma_bs32_config3.md (partition kernel; reduce adds 8.6e6)"),
+}
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -397,6 +405,8 @@ def run_ours(args, cfg, rank, world, local_rank):
         return
     peak, peak_kind = load_peaks()
     alg = algorithmic_bytes(lens_after, hq, hkv, D, BS)
+    # the capture is of the default workload on one GPU; other shapes report null
+    traffic = TRAFFIC_PER_LAUNCH.get(args.config) if (world == 1 and not (args.layers or args.batch)) else None
     achieved = alg / (mean_dec_ms * 1e-3) / 1e9
     toks = B / (step_ms * 1e-3)
     kv_bytes_step = L * world * alg
@@ -420,7 +430,9 @@ def run_ours(args, cfg, rank, world, local_rank):
                    "kernel": "split-K v2" if split else "paged_attention_v1"},
         "kv_gbs": kv_bytes_step / (step_ms * 1e-3) / 1e9,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "peak_kind": peak_kind, "kernel": "paged decode (per layer launch)",
+                     "traffic": traffic[0] if traffic else None,
+                     "traffic_source": traffic[1] if traffic else None,
+                     "peak_kind": peak_kind, "kernel": "paged decode (per layer launch)",
                      "algorithmic_bytes_per_launch": alg, "mean_launch_ms": mean_dec_ms},
         "e2e": None if args.no_e2e else {"value": B / (e2e_step_ms * 1e-3), "unit": "tokens/s",
                                          "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
