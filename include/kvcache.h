@@ -112,6 +112,34 @@ int kvc_paged_attention_v2(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltens
                            int num_kv_heads, float scale, int block_size, int max_seq_len,
                            const kvc_dltensor* alibi_slopes, int partition_size, void* stream);
 
+/* Split-K decode for callers that cannot allocate device memory.  No
+ * counterpart in the reference: sglang-mlx has no split-K decode at all.
+ *
+ * Same arguments and result as kvc_paged_attention_v2, minus the three
+ * workspace tensors.  Some callers have no way to provide that workspace:
+ * code that runs inside a host framework whose own pool owns all device
+ * memory (a raw cudaMalloc beside it fragments or oversubscribes the pool),
+ * serving loops that cannot afford cudaMalloc/cudaFree stalling the device,
+ * and foreign-language bindings that carry no device allocator at all.  This
+ * entry point allocates nothing: the partials live in a static device array of
+ * KVC_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that loads the
+ * library holds until the process exits.
+ *   - Needs num_seqs * num_heads * ceil(max_seq_len / partition_size) *
+ *     (head_size + 2) * 4 bytes <= KVC_NOALLOC_SCRATCH_BYTES; larger calls
+ *     return KVC_EINVAL without launching anything.
+ *   - The first call on a device looks up the array's device address (with that
+ *     device current); make that first call before any stream capture.
+ *   - All calls on a device share the one array and it keeps the previous
+ *     call's contents (nothing in it needs to start at zero).  Calls that overlap
+ *     on the GPU — on different streams, or from different threads — race on it:
+ *     serialise them (one stream, or events). */
+#define KVC_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+int kvc_paged_attention_v2_noalloc(kvc_dltensor* out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                                   const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                                   const kvc_dltensor* context_lens, int num_kv_heads, float scale, int block_size,
+                                   int max_seq_len, const kvc_dltensor* alibi_slopes, int partition_size,
+                                   void* stream);
+
 /* ---- cache ops -------------------------------------------------------------
  * Replaces `_ext.reshape_and_cache` (bindings.cpp:67-80), the C++ op
  * `reshape_and_cache` (paged_attention/mlx_cache.cpp:256-278) and

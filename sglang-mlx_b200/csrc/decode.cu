@@ -20,6 +20,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "kvc_common.cuh"
 
 namespace kvc {
@@ -523,6 +525,59 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   if (a.q_type == ElemType::F32) return launch_reduce<float>(p, D, stream);
   if (a.q_type == ElemType::F16) return launch_reduce<__half>(p, D, stream);
   return launch_reduce<__nv_bfloat16>(p, D, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Scratch of kvc_paged_attention_v2_noalloc: the split-K partials
+// [tmp_out | max_logits | exp_sums] of one call, in a static array so callers
+// that cannot allocate device memory still get the split-K decode.  Every GPU
+// that loads this library holds the array until the process exits; all calls
+// on a device share it (overlapping calls race; nothing needs zeroing, every
+// partial the reduce reads is written first by the same call).
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) float g_noalloc_scratch[KVC_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+// Host code must not use g_noalloc_scratch as an address (it names the host
+// shadow).  The device address is looked up once per device, with that device
+// current, and cached.
+static float* noalloc_scratch_address(cudaError_t* err) {
+  static std::mutex mu;
+  static float* addr[64] = {nullptr};
+  int dev = 0;
+  *err = cudaGetDevice(&dev);
+  if (*err != cudaSuccess) return nullptr;
+  if (dev < 0 || dev >= 64) {
+    *err = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    *err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (*err != cudaSuccess) return nullptr;
+    addr[dev] = static_cast<float*>(p);
+  }
+  return addr[dev];
+}
+
+cudaError_t launch_paged_decode_noalloc(DecodeArgs a, cudaStream_t stream) {
+  const int64_t rows = (int64_t)a.num_seqs * a.num_heads * a.num_partitions;
+  const int64_t floats = rows * (a.head_size + 2);
+  if (floats * (int64_t)sizeof(float) > (int64_t)KVC_NOALLOC_SCRATCH_BYTES) return cudaErrorInvalidValue;
+  cudaError_t err = cudaSuccess;
+  float* base = noalloc_scratch_address(&err);
+  if (base == nullptr) return err;
+  // tmp_out first (16-byte rows for the reduce's vector loads), then the two
+  // [B, Hq, P] arrays.
+  a.part_out = base;
+  a.part_out_part_stride = a.head_size;
+  a.part_out_head_stride = (int64_t)a.num_partitions * a.head_size;
+  a.part_out_seq_stride = (int64_t)a.num_heads * a.part_out_head_stride;
+  a.part_max = base + rows * a.head_size;
+  a.part_sum = a.part_max + rows;
+  a.part_head_stride = a.num_partitions;
+  a.part_seq_stride = (int64_t)a.num_heads * a.num_partitions;
+  return launch_paged_decode(a, stream);
 }
 
 }  // namespace kvc

@@ -311,6 +311,37 @@ int kvc_paged_attention_v2(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltens
   return KVC_OK;
 }
 
+// Split-K decode whose partials live in the library's static scratch array, for
+// callers that cannot allocate device memory (see include/kvcache.h).
+int kvc_paged_attention_v2_noalloc(kvc_dltensor* out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                                   const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                                   const kvc_dltensor* context_lens, int num_kv_heads, float scale, int block_size,
+                                   int max_seq_len, const kvc_dltensor* alibi_slopes, int partition_size,
+                                   void* stream) {
+  DecodeArgs a;
+  int device = -1;
+  if (int rc = prepare_decode(out, query, key_cache, value_cache, block_tables, context_lens, num_kv_heads, scale,
+                              block_size, max_seq_len, alibi_slopes, &a, &device))
+    return rc;
+  if (partition_size <= 0 || partition_size % 32 != 0 || partition_size % block_size != 0)
+    return fail(KVC_EINVAL, "partition_size must be a positive multiple of 32 and of block_size");
+  const int parts = (max_seq_len + partition_size - 1) / partition_size;
+  const int64_t need = (int64_t)a.num_seqs * a.num_heads * parts * (a.head_size + 2) * (int64_t)sizeof(float);
+  if (need > (int64_t)KVC_NOALLOC_SCRATCH_BYTES)
+    return fail(KVC_EINVAL, "paged_attention_v2_noalloc needs " + std::to_string(need) +
+                                " bytes of split-K partials, more than its static scratch of " +
+                                std::to_string((size_t)KVC_NOALLOC_SCRATCH_BYTES) +
+                                " bytes; use kvc_paged_attention_v2 with caller-owned workspace");
+  if (a.num_seqs == 0) return KVC_OK;
+  a.partition_size = partition_size;
+  a.num_partitions = parts;
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_paged_decode_noalloc(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "paged_attention_v2_noalloc launch");
+  return KVC_OK;
+}
+
 // Shared validation of the two append layouts.
 static int prepare_reshape(const kvc_dltensor* key, const kvc_dltensor* value, kvc_dltensor* key_cache,
                            kvc_dltensor* value_cache, const kvc_dltensor* slot_mapping, bool flash,

@@ -127,6 +127,9 @@ struct GatherArgs {
 };
 
 cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream);
+// Split-K decode with its partials in the library's static scratch array
+// (kvc_paged_attention_v2_noalloc).  `a` carries no workspace pointers.
+cudaError_t launch_paged_decode_noalloc(DecodeArgs a, cudaStream_t stream);
 cudaError_t launch_reshape_and_cache(const ReshapeArgs& a, cudaStream_t stream);
 cudaError_t launch_reshape_and_cache_flash(const ReshapeArgs& a, cudaStream_t stream);
 cudaError_t launch_gather_kv(const GatherArgs& a, cudaStream_t stream);

@@ -47,6 +47,7 @@ SIGNATURES: dict[str, tuple] = {
         _i,
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _i, _p],
     ),
+    "kvc_paged_attention_v2_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _i, _p]),
     "kvc_reshape_and_cache": (_i, [_p, _p, _p, _p, _p, _p]),
     "kvc_reshape_and_cache_flash": (_i, [_p, _p, _p, _p, _p, _p]),
     "kvc_gather_kv": (_i, [_p, _p, _p, _p, _p, _p]),
