@@ -265,12 +265,14 @@ def run_ours(args, cfg, rank, world, local_rank):
     _lib.set_device(dev)
     torch.cuda.set_device(dev)
     tdev = torch.device("cuda", dev)
-    L, B, HQ, HKV, D, BS = cfg["layers"], cfg["batch"], cfg["hq"], cfg["hkv"], cfg["d"], cfg["bs"]
-    if HKV % world:
-        raise SystemExit(f"kv heads {HKV} do not shard over {world} GPUs")
-    hkv = HKV // world
-    hq = HQ // world
-    lens = context_lengths(cfg)
+    from sglang_mlx_b200 import sharding
+
+    L, B_all, HQ, HKV, D, BS = cfg["layers"], cfg["batch"], cfg["hq"], cfg["hkv"], cfg["d"], cfg["bs"]
+    lens_all = context_lengths(cfg)
+    plan = sharding.plan(HQ, HKV, world, rank, lens_all + 1)
+    hkv, hq = plan.num_kv_heads, plan.num_q_heads
+    lens = lens_all[plan.seqs]
+    B = len(lens)
     lens_after = lens + 1
     tables, total_blocks = build_tables(lens_after, BS)
     max_seq_len = int(tables.shape[1] * BS)
@@ -298,14 +300,23 @@ def run_ours(args, cfg, rank, world, local_rank):
     lens_d = DeviceArray.from_numpy(lens_after.astype(np.int32), device=dev)
     slots_d = DeviceArray.from_numpy(slots, device=dev)
     scale = 1.0 / math.sqrt(D)
-    split = cfg["partition"] > 0
-    ws = mk.splitk_workspace(B, hq, D, max_seq_len, cfg["partition"], dev) if split else None
+    # config 3 fixes 512-token partitions; otherwise the shim's heuristic decides
+    # (single pass at N = 1 for config 2, split-K once head sharding leaves too few CTAs)
+    psize = cfg["partition"] or mk.choose_decode(B, hkv, max_seq_len, BS)
+    if args.decode == "v1":
+        psize = 0
+    elif args.decode == "v2":
+        psize = args.partition or psize or 512
+    if args.partition and psize:
+        psize = args.partition
+    split = psize > 0
+    ws = mk.splitk_workspace(B, hq, D, max_seq_len, psize, dev) if split else None
     torch.cuda.synchronize()
 
     def decode(i, o=None):
         if split:
             return mk.paged_attention_v2(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, BS, max_seq_len,
-                                         partition_size=cfg["partition"], workspace=ws, out=o or out[i])
+                                         partition_size=psize, workspace=ws, out=o or out[i])
         return mk.paged_attention_v1(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, BS, max_seq_len,
                                      out=o or out[i])
 
@@ -390,26 +401,30 @@ def run_ours(args, cfg, rank, world, local_rank):
     h2d = (B * 4 * 2) + L * (B * hq * D * 2 + 2 * B * hkv * D * 2)
     d2h = L * B * hq * D * 2
 
-    # ---- reduce over ranks (max time) ----
+    # ---- reduce over ranks (max time; KV bytes summed) ----
     step_ms = total_ms / args.steps
     e2e_step_ms = e2e_ms / args.steps
     mean_dec_ms = float(np.mean(dec_ms))
+    alg = algorithmic_bytes(lens_after, hq, hkv, D, BS)
+    alg_all = float(alg)
     if dist is not None:
         t = torch.tensor([step_ms, e2e_step_ms, mean_dec_ms], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         step_ms, e2e_step_ms, mean_dec_ms_max = [float(x) for x in t]
+        s = torch.tensor([float(alg)], dtype=torch.float64)
+        dist.all_reduce(s, op=dist.ReduceOp.SUM)
+        alg_all = float(s[0])
     else:
         mean_dec_ms_max = mean_dec_ms
 
     if rank != 0:
         return
     peak, peak_kind = load_peaks()
-    alg = algorithmic_bytes(lens_after, hq, hkv, D, BS)
     # the capture is of the default workload on one GPU; other shapes report null
     traffic = TRAFFIC_PER_LAUNCH.get(args.config) if (world == 1 and not (args.layers or args.batch)) else None
     achieved = alg / (mean_dec_ms * 1e-3) / 1e9
-    toks = B / (step_ms * 1e-3)
-    kv_bytes_step = L * world * alg
+    toks = B_all / (step_ms * 1e-3)
+    kv_bytes_step = L * alg_all
     line = {
         "metric": METRIC,
         "value": toks,
@@ -423,18 +438,18 @@ def run_ours(args, cfg, rank, world, local_rank):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": cfg["name"], "global_batch": B, "layers": L, "heads": f"{HQ}q/{HKV}kv",
+        "config": {"workload": cfg["name"], "global_batch": B_all, "layers": L, "heads": f"{HQ}q/{HKV}kv",
                    "head_dim": D, "block_size": BS, "context": f"U[{cfg['lo']},{cfg['hi']}] (seeded)",
                    "parallelism": f"kv-head-shard{world}", "l2": "inputs larger than L2 (KV per layer "
                    f"{alg * world / 1e9:.2f} GB); no flush",
-                   "kernel": "split-K v2" if split else "paged_attention_v1"},
+                   "kernel": f"split-K v2, {psize}-token partitions" if split else "paged_attention_v1"},
         "kv_gbs": kv_bytes_step / (step_ms * 1e-3) / 1e9,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic[0] if traffic else None,
                      "traffic_source": traffic[1] if traffic else None,
                      "peak_kind": peak_kind, "kernel": "paged decode (per layer launch)",
                      "algorithmic_bytes_per_launch": alg, "mean_launch_ms": mean_dec_ms},
-        "e2e": None if args.no_e2e else {"value": B / (e2e_step_ms * 1e-3), "unit": "tokens/s",
+        "e2e": None if args.no_e2e else {"value": B_all / (e2e_step_ms * 1e-3), "unit": "tokens/s",
                                          "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": int(launches),
         "clocks": clocks,
@@ -470,6 +485,9 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
+    ap.add_argument("--decode", default="auto", choices=["auto", "v1", "v2"],
+                    help="decode form: the shim's choice (default), single pass, or split-K")
+    ap.add_argument("--partition", type=int, default=0, help="split-K partition size (tokens) when split")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (profiling cases only)")
     ap.add_argument("--batch", type=int, default=0, help="override the batch (profiling cases only)")
     args = ap.parse_args()

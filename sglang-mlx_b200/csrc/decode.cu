@@ -427,17 +427,70 @@ static cudaError_t launch_generic_d(const DecodeParams& p, int D, cudaStream_t s
   }
 }
 
-template <typename Q_T, bool VEC>
-static cudaError_t launch_reduce_v(const DecodeParams& p, int D, cudaStream_t stream) {
-  auto kern = splitk_reduce_kernel<Q_T, VEC>;
-  const size_t smem = (size_t)(((p.num_partitions + 3) & ~3) + kReduceWarps * D) * sizeof(float);
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+// Split-K reduce for few partitions (<= 32): one warp per (sequence, head),
+// lanes over the head dimension, partitions walked in order.  Same result as
+// splitk_reduce_kernel; a batch of sequences gives thousands of warps, so the
+// whole reduce is a couple of memory latencies.
+constexpr int kReduceHeadsPerCta = 4;
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(kReduceHeadsPerCta * 32) splitk_reduce_few_kernel(DecodeParams p, int head_size) {
+  grid_dependency_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = blockIdx.x * kReduceHeadsPerCta + warp, seq = blockIdx.y;
+  if (head >= p.num_heads) return;
+  const uint32_t ctx = p.context_lens[seq];
+  T* out = reinterpret_cast<T*>(p.out) + (int64_t)seq * p.out_seq_stride + (int64_t)head * p.out_head_stride;
+  if (ctx == 0 || ctx > (uint32_t)p.max_seq_len) {
+    for (int d = lane; d < head_size; d += 32) out[d] = from_float<T>(0.f);
+    return;
   }
+  const int nparts = (int)((ctx + p.partition_size - 1) / p.partition_size);
+  const float* pm = p.part_max + (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride;
+  const float* pl = p.part_sum + (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride;
+  float M = -INFINITY;
+  for (int i = lane; i < nparts; i += 32) M = fmaxf(M, pm[i]);
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  float L = 0.f;
+  for (int i = lane; i < nparts; i += 32)
+    L += (M == -INFINITY || pm[i] == -INFINITY) ? 0.f : expf(pm[i] - M) * pl[i];
+  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+  const float inv = 1.f / (L + 1e-6f);
+  const float* po = p.part_out + (int64_t)seq * p.part_out_seq_stride + (int64_t)head * p.part_out_head_stride;
+  if (VEC) {
+    for (int v4 = lane; v4 < head_size / 4; v4 += 32) {
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int i = 0; i < nparts; ++i) {
+        const float w = (M == -INFINITY || pm[i] == -INFINITY) ? 0.f : expf(pm[i] - M);
+        const float4 x = reinterpret_cast<const float4*>(po + (int64_t)i * p.part_out_part_stride)[v4];
+        a.x += w * x.x;
+        a.y += w * x.y;
+        a.z += w * x.z;
+        a.w += w * x.w;
+      }
+      out[4 * v4 + 0] = from_float<T>(a.x * inv);
+      out[4 * v4 + 1] = from_float<T>(a.y * inv);
+      out[4 * v4 + 2] = from_float<T>(a.z * inv);
+      out[4 * v4 + 3] = from_float<T>(a.w * inv);
+    }
+  } else {
+    for (int d = lane; d < head_size; d += 32) {
+      float a = 0.f;
+      for (int i = 0; i < nparts; ++i) {
+        const float w = (M == -INFINITY || pm[i] == -INFINITY) ? 0.f : expf(pm[i] - M);
+        a += w * po[(int64_t)i * p.part_out_part_stride + d];
+      }
+      out[d] = from_float<T>(a * inv);
+    }
+  }
+}
+
+template <typename KERN>
+static cudaError_t launch_pdl(KERN kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              const DecodeParams& p, int D) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)p.num_heads, (unsigned)p.num_seqs);
-  cfg.blockDim = dim3(kReduceWarps * 32);
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -448,6 +501,22 @@ static cudaError_t launch_reduce_v(const DecodeParams& p, int D, cudaStream_t st
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, D);
   count_launch();
   return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+template <typename Q_T, bool VEC>
+static cudaError_t launch_reduce_v(const DecodeParams& p, int D, cudaStream_t stream) {
+  if (p.num_partitions <= 32) {
+    dim3 grid((unsigned)((p.num_heads + kReduceHeadsPerCta - 1) / kReduceHeadsPerCta), (unsigned)p.num_seqs);
+    return launch_pdl(splitk_reduce_few_kernel<Q_T, VEC>, grid, dim3(kReduceHeadsPerCta * 32), 0, stream, p, D);
+  }
+  auto kern = splitk_reduce_kernel<Q_T, VEC>;
+  const size_t smem = (size_t)(((p.num_partitions + 3) & ~3) + kReduceWarps * D) * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_pdl(kern, dim3((unsigned)p.num_heads, (unsigned)p.num_seqs), dim3(kReduceWarps * 32), smem, stream,
+                    p, D);
 }
 
 template <typename Q_T>

@@ -11,7 +11,7 @@
 // Data movement: each warp owns a ring of STAGES shared-memory stages.  A stage
 // holds one 32-token group: 32/BS pages of K ([D/8][BS][8] elements, 16-byte
 // rows per token) and of V ([D][BS]).  Pages are contiguous in HBM, so one lane
-// moves each with a single 1-D bulk copy (cp.async.bulk, no multicast) that
+// moves each with a single CTA-local 1-D bulk copy (cp.async.bulk) that
 // completes on the stage's mbarrier; STAGES-1 groups stay in flight while the
 // warp computes on the current one.
 //

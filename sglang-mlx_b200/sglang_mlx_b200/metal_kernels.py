@@ -143,20 +143,43 @@ def paged_attention_v2(
     return out
 
 
+def choose_decode(num_seqs: int, num_kv_heads: int, max_seq_len: int, block_size: int = 16,
+                  sm_count: int = 148) -> int:
+    """0 for the single-pass decode, else the split-K partition size to use.
+
+    The single-pass grid has one CTA per (sequence, kv head); the tensor-core
+    kernel keeps two or three CTAs per SM, and with variable lengths it wants
+    about four waves to hide the tail.  Below that, sequences are split into
+    partitions: the largest power of two (256 ... 2048 tokens, a multiple of the
+    block size) that still yields four waves, counting half of max_seq_len as the
+    typical length."""
+    slots = sm_count * (3 if block_size >= 32 else 2)
+    target = 4 * slots
+    items = num_seqs * num_kv_heads
+    if items >= target or max_seq_len <= 256:
+        return 0
+    for p in (2048, 1024, 512, 256):
+        if p % block_size == 0 and items * max(1, -(-max_seq_len // p)) / 2 >= target:
+            return p
+    return max(256, block_size)
+
+
 def use_split_k(num_seqs: int, num_kv_heads: int, max_seq_len: int, sm_count: int = 148,
-                partition_size: int = DEFAULT_PARTITION_SIZE) -> bool:
-    """Heuristic: split when the single-pass grid cannot fill the GPU and the
-    sequences are long enough to partition."""
-    return num_seqs * num_kv_heads < 2 * sm_count and max_seq_len > 2 * partition_size
+                block_size: int = 16) -> bool:
+    """True when choose_decode picks the split-K form."""
+    return choose_decode(num_seqs, num_kv_heads, max_seq_len, block_size, sm_count) > 0
 
 
 def paged_attention(query, key_cache, value_cache, block_tables, context_lens, num_kv_heads: int, scale: float,
-                    block_size: int, max_seq_len: int, alibi_slopes=None, *, stream=None, out=None):
-    """Picks paged_attention_v1 or paged_attention_v2 by use_split_k."""
+                    block_size: int, max_seq_len: int, alibi_slopes=None, *, stream=None, out=None,
+                    workspace=None):
+    """Single-pass or split-K decode, whichever choose_decode picks for the shape."""
     shape, _, _, _, _ = describe(_dev(query))
-    if use_split_k(shape[0], num_kv_heads, max_seq_len):
+    psize = choose_decode(shape[0], num_kv_heads, max_seq_len, block_size)
+    if psize:
         return paged_attention_v2(query, key_cache, value_cache, block_tables, context_lens, num_kv_heads, scale,
-                                  block_size, max_seq_len, alibi_slopes, stream=stream, out=out)
+                                  block_size, max_seq_len, alibi_slopes, partition_size=psize, workspace=workspace,
+                                  stream=stream, out=out)
     return paged_attention_v1(query, key_cache, value_cache, block_tables, context_lens, num_kv_heads, scale,
                               block_size, max_seq_len, alibi_slopes, stream=stream, out=out)
 
