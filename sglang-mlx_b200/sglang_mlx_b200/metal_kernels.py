@@ -150,18 +150,24 @@ def choose_decode(num_seqs: int, num_kv_heads: int, max_seq_len: int, block_size
     The single-pass grid has one CTA per (sequence, kv head); the tensor-core
     kernel keeps two or three CTAs per SM, and with variable lengths it wants
     about four waves to hide the tail.  Below that, sequences are split into
-    partitions: the largest power of two (256 ... 2048 tokens, a multiple of the
-    block size) that still yields four waves, counting half of max_seq_len as the
-    typical length."""
+    partitions.  Counting half of max_seq_len as the typical length: 2048-token
+    partitions when they still give four waves, else 1024 when that gives one
+    wave, else 512.  (Measured on 1/2/4/8-way head-sharded Llama-3-8B decode:
+    short partitions lose more to per-CTA pipeline ramp than they gain in
+    balance.)"""
     slots = sm_count * (3 if block_size >= 32 else 2)
-    target = 4 * slots
     items = num_seqs * num_kv_heads
-    if items >= target or max_seq_len <= 256:
+    if items >= 4 * slots or max_seq_len <= 512:
         return 0
-    for p in (2048, 1024, 512, 256):
-        if p % block_size == 0 and items * max(1, -(-max_seq_len // p)) / 2 >= target:
-            return p
-    return max(256, block_size)
+
+    def ctas(p):
+        return items * max(1, -(-max_seq_len // p)) / 2
+
+    if ctas(2048) >= 4 * slots:
+        return 2048
+    if ctas(1024) >= slots:
+        return 1024
+    return 512
 
 
 def use_split_k(num_seqs: int, num_kv_heads: int, max_seq_len: int, sm_count: int = 148,
