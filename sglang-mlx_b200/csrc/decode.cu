@@ -290,27 +290,30 @@ __global__ void __launch_bounds__(kGenericWarps * 32) paged_decode_generic_kerne
 
 // ---------------------------------------------------------------------------
 // Split-K reduce: out = sum_p e^{m_p - M} o_p / (sum_p e^{m_p - M} l_p + 1e-6)
-// over the partitions that hold tokens of the sequence.  CTA = (head, seq);
-// warp w accumulates partitions w, w + 8, ... with 16-byte loads (lane = 4
-// dims), then the 8 partial rows are summed through shared memory.  Launched
-// as a programmatic dependent of the partition kernel: it may start during
-// that kernel's tail and waits (griddepcontrol.wait) before reading partials.
+// over the partitions that hold tokens of the sequence, for many partitions
+// (long contexts).  CTA = (head, seq, 32-dim slice): lane = dim, warp w
+// accumulates partitions w, w + 8, ... (four rows in flight), then the 8
+// partial rows are summed through shared memory.  Every CTA recomputes M and
+// the weights from the (max, sum) pairs, which are small and L2-resident.
+// Launched as a programmatic dependent of the partition kernel: it may start
+// during that kernel's tail and waits (griddepcontrol.wait) before reading.
 // ---------------------------------------------------------------------------
 constexpr int kReduceWarps = 8;
+constexpr int kReduceSlice = 32;
 
-
-template <typename T, bool VEC>
+template <typename T>
 __global__ void __launch_bounds__(kReduceWarps * 32) splitk_reduce_kernel(DecodeParams p, int head_size) {
-  extern __shared__ float smem_f[];  // w[num_partitions] then acc[kReduceWarps][head_size]
+  extern __shared__ float smem_f[];  // w[num_partitions] then acc[kReduceWarps][kReduceSlice]
   __shared__ float red[kReduceWarps];
   __shared__ float s_M, s_inv;
   grid_dependency_wait();
   const int head = blockIdx.x, seq = blockIdx.y;
+  const int d = blockIdx.z * kReduceSlice + (threadIdx.x & 31);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t ctx = p.context_lens[seq];
   T* out = reinterpret_cast<T*>(p.out) + (int64_t)seq * p.out_seq_stride + (int64_t)head * p.out_head_stride;
   if (ctx == 0 || ctx > (uint32_t)p.max_seq_len) {
-    for (int d = threadIdx.x; d < head_size; d += blockDim.x) out[d] = from_float<T>(0.f);
+    if (warp == 0 && d < head_size) out[d] = from_float<T>(0.f);
     return;
   }
   const int nparts = (int)((ctx + p.partition_size - 1) / p.partition_size);
@@ -338,7 +341,7 @@ __global__ void __launch_bounds__(kReduceWarps * 32) splitk_reduce_kernel(Decode
     L += wt * pl[i];
   }
   for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-  __syncthreads();  // red[] reuse
+  __syncthreads();  // red[] reuse, w[] complete
   if (lane == 0) red[warp] = L;
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -347,51 +350,28 @@ __global__ void __launch_bounds__(kReduceWarps * 32) splitk_reduce_kernel(Decode
     s_inv = 1.f / (v + 1e-6f);
   }
   const float* po = p.part_out + (int64_t)seq * p.part_out_seq_stride + (int64_t)head * p.part_out_head_stride;
-  if (VEC) {
-    const int nv = head_size / 4;
-    for (int v4 = lane; v4 < nv; v4 += 32) {
-      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-      int i = warp;
-      for (; i + 3 * kReduceWarps < nparts; i += 4 * kReduceWarps) {
-        float4 x[4];
-        float ww[4];
+  float a = 0.f;
+  if (d < head_size) {
+    int i = warp;
+    for (; i + 3 * kReduceWarps < nparts; i += 4 * kReduceWarps) {
+      float x[4], ww[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          x[u] = reinterpret_cast<const float4*>(po + (int64_t)(i + u * kReduceWarps) * p.part_out_part_stride)[v4];
-          ww[u] = w[i + u * kReduceWarps];
-        }
+      for (int u = 0; u < 4; ++u) {
+        x[u] = po[(int64_t)(i + u * kReduceWarps) * p.part_out_part_stride + d];
+        ww[u] = w[i + u * kReduceWarps];
+      }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          a.x += ww[u] * x[u].x;
-          a.y += ww[u] * x[u].y;
-          a.z += ww[u] * x[u].z;
-          a.w += ww[u] * x[u].w;
-        }
-      }
-      for (; i < nparts; i += kReduceWarps) {
-        const float4 x = reinterpret_cast<const float4*>(po + (int64_t)i * p.part_out_part_stride)[v4];
-        const float ww = w[i];
-        a.x += ww * x.x;
-        a.y += ww * x.y;
-        a.z += ww * x.z;
-        a.w += ww * x.w;
-      }
-      reinterpret_cast<float4*>(acc_s + warp * head_size)[v4] = a;
+      for (int u = 0; u < 4; ++u) a += ww[u] * x[u];
     }
-  } else {
-    for (int d = lane; d < head_size; d += 32) {
-      float a = 0.f;
-      for (int i = warp; i < nparts; i += kReduceWarps) a += w[i] * po[(int64_t)i * p.part_out_part_stride + d];
-      acc_s[warp * head_size + d] = a;
-    }
+    for (; i < nparts; i += kReduceWarps) a += w[i] * po[(int64_t)i * p.part_out_part_stride + d];
   }
+  acc_s[warp * kReduceSlice + lane] = a;
   __syncthreads();
-  const float inv = s_inv;
-  for (int d = threadIdx.x; d < head_size; d += blockDim.x) {
-    float a = 0.f;
+  if (warp == 0 && d < head_size) {
+    float sum = 0.f;
 #pragma unroll
-    for (int k = 0; k < kReduceWarps; ++k) a += acc_s[k * head_size + d];
-    out[d] = from_float<T>(a * inv);
+    for (int k = 0; k < kReduceWarps; ++k) sum += acc_s[k * kReduceSlice + lane];
+    out[d] = from_float<T>(sum * s_inv);
   }
 }
 
@@ -509,14 +489,14 @@ static cudaError_t launch_reduce_v(const DecodeParams& p, int D, cudaStream_t st
     dim3 grid((unsigned)((p.num_heads + kReduceHeadsPerCta - 1) / kReduceHeadsPerCta), (unsigned)p.num_seqs);
     return launch_pdl(splitk_reduce_few_kernel<Q_T, VEC>, grid, dim3(kReduceHeadsPerCta * 32), 0, stream, p, D);
   }
-  auto kern = splitk_reduce_kernel<Q_T, VEC>;
-  const size_t smem = (size_t)(((p.num_partitions + 3) & ~3) + kReduceWarps * D) * sizeof(float);
+  auto kern = splitk_reduce_kernel<Q_T>;
+  const size_t smem = (size_t)(((p.num_partitions + 3) & ~3) + kReduceWarps * kReduceSlice) * sizeof(float);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  return launch_pdl(kern, dim3((unsigned)p.num_heads, (unsigned)p.num_seqs), dim3(kReduceWarps * 32), smem, stream,
-                    p, D);
+  return launch_pdl(kern, dim3((unsigned)p.num_heads, (unsigned)p.num_seqs, (unsigned)((D + kReduceSlice - 1) / kReduceSlice)),
+                    dim3(kReduceWarps * 32), smem, stream, p, D);
 }
 
 template <typename Q_T>

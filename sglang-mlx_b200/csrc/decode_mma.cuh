@@ -27,6 +27,12 @@
 // product (the only rounding the reference's fp32 path does not have).
 #pragma once
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <type_traits>
+
 namespace kvc {
 namespace mma_detail {
 
@@ -95,6 +101,26 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Tiled tensor copies global -> shared (this CTA only), completion counted on
+// `bar`.  Coordinates are innermost first.
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            int c4, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, %7}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -140,26 +166,50 @@ constexpr float kLn2 = 0.6931471805599453f;
 
 }  // namespace mma_detail
 
-template <int D, int BS, int NW, int STAGES, int GT_ = 32>
+// How a group's K and V reach shared memory, in "boxes" of VBS tokens:
+//  kBulk      1-D bulk copies of whole pages (VBS = BS, so GT >= BS).
+//  kTiles     tiled tensor copies of VBS = min(GT, BS) tokens: a 16-token box
+//             of a 32-token page lands densely as [D/8][16][8] (K) and [D][16]
+//             (V); the V box carries the 32/64-byte swizzle.
+//  kSwizzledV K by 1-D bulk copy; V as a whole page through a tensor map that
+//             views it as 128-byte rows, written with the 128-byte swizzle.
+// A swizzled V box makes the ldmatrix reads of V rows (VBS * 2 bytes apart)
+// hit distinct banks.
+constexpr int kBulk = 0, kTiles = 1, kSwizzledV = 2;
+
+template <int D, int BS, int NW, int STAGES, int GT_ = 32, int MODE = kBulk>
 struct MmaGeom {
-  static constexpr int GT = GT_;                   // tokens per group (16, 32 or 64)
-  static constexpr int PPG = GT / BS;              // pages per group
-  static_assert(GT % 16 == 0 && GT >= BS, "a group is whole pages and whole 16-token k-steps");
-  static constexpr int PAGE = D * BS * 2;          // bytes of one K (or V) page
-  static constexpr int STAGE = PPG * 2 * PAGE;     // K pages then V pages
+  static constexpr int GT = GT_;                          // tokens per group (16, 32 or 64)
+  static constexpr int VBS = MODE == kTiles ? (GT < BS ? GT : BS) : BS;  // tokens per box
+  static constexpr int NBOX = GT / VBS;                   // boxes per group (K and V each)
+  static_assert(GT % 16 == 0 && GT % VBS == 0, "a group is whole boxes and whole 16-token k-steps");
+  static constexpr int BOX = D * VBS * 2;                 // bytes of one K (or V) box
+  static constexpr int VSWZ = MODE == kSwizzledV ? 128 : (MODE == kTiles && VBS * 2 >= 32 ? VBS * 2 : 0);
+  static constexpr int STAGE = NBOX * 2 * BOX;            // K boxes then V boxes
+  static constexpr int ALIGN = MODE != kBulk ? 1024 : 0;  // ring base alignment slack (swizzle atoms)
   static constexpr int RING = NW * STAGES * STAGE;
-  static constexpr int BAR_OFF = RING;             // NW*STAGES mbarriers
+  static constexpr int BAR_OFF = ALIGN + RING;            // NW*STAGES mbarriers
   static constexpr int MASK_OFF = BAR_OFF + NW * STAGES * 8;
   static constexpr int COMBINE = NW * 16 * D * 4 + NW * 16 * 2 * 4;  // reuses the ring
   static constexpr int SMEM = MASK_OFF + NW * STAGES * 4;
   static_assert(COMBINE <= RING, "combine buffer must fit in the ring");
 };
 
-template <typename T, int D, int BS, int NW, int STAGES, int GTOK>
-__global__ void __launch_bounds__(NW * 32) paged_decode_mma_kernel(DecodeParams p) {
+// Tensor maps of one launch (tensor-copy modes only).  kTiles: K as
+// [nb][H][D/8][BS][8] and V as [nb][H][D][BS]; kSwizzledV: V as
+// [nb][H][D*BS/64][64] (128-byte rows); innermost last in these brackets.
+struct TmaMaps {
+  CUtensorMap k;
+  CUtensorMap v;
+};
+
+template <typename T, int D, int BS, int NW, int STAGES, int GTOK, int MODE>
+__global__ void __launch_bounds__(NW * 32)
+    paged_decode_mma_kernel(DecodeParams p, const __grid_constant__ TmaMaps tm) {
   using namespace mma_detail;
-  using Geo = MmaGeom<D, BS, NW, STAGES, GTOK>;
-  constexpr int GT = Geo::GT, PPG = Geo::PPG, PAGE = Geo::PAGE;
+  using Geo = MmaGeom<D, BS, NW, STAGES, GTOK, MODE>;
+  constexpr int GT = Geo::GT, NBOX = Geo::NBOX, BOX = Geo::BOX, VBS = Geo::VBS;
+  constexpr uint32_t VSW_MASK = Geo::VSWZ ? (uint32_t)(Geo::VSWZ / 16 - 1) : 0u;
   constexpr int KS = D / 16;    // k-steps of Q.K^T
   constexpr int NT = D / 8;     // n-tiles of P.V
   constexpr int ST = GT / 8;    // 8-token S tiles per group
@@ -183,7 +233,15 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_mma_kernel(DecodeParams 
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Geo::BAR_OFF) + warp * STAGES;
   uint32_t* masks = reinterpret_cast<uint32_t*>(smem + Geo::MASK_OFF) + warp * STAGES;
-  uint8_t* ring = smem + (size_t)warp * STAGES * Geo::STAGE;
+  // Tensor-copy modes: the ring starts on a 1024-byte boundary of the shared window, so the
+  // swizzle pattern TMA applies (address bits 4.. ^= bits 7..) is the one the
+  // ldmatrix addressing below undoes.
+  uint8_t* ring_base = smem;
+  if constexpr (Geo::ALIGN > 0) {
+    constexpr uint32_t A = (uint32_t)Geo::ALIGN;
+    ring_base += (A - (smem_u32(smem) & (A - 1u))) & (A - 1u);
+  }
+  uint8_t* ring = ring_base + (size_t)warp * STAGES * Geo::STAGE;
   if (lane == 0) {
     for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
     mbar_fence_init();
@@ -226,30 +284,30 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_mma_kernel(DecodeParams 
   const int n_mine = warp < ngroups ? (ngroups - warp + NW - 1) / NW : 0;
   const int page_end = (end + BS - 1) / BS;  // first page past the context
 
-  // Lane i < PPG fetches the block id of page i of group `k` of this warp.
+  // Lane i < NBOX fetches the block id of box i of group `k` of this warp.
   auto load_block = [&](int k) -> uint32_t {
     uint32_t b = 0xffffffffu;
-    if (lane < PPG && k < n_mine) {
-      const int pg = (begin + (warp + k * NW) * GT) / BS + lane;
+    if (lane < NBOX && k < n_mine) {
+      const int pg = (begin + (warp + k * NW) * GT + lane * VBS) / BS;
       if (pg < page_end) b = __ldg(table + pg);
     }
     return b;
   };
   // Lane 0 issues the copies of group `k` into stage `s`; `blk` holds lane
-  // i's block id (from load_block).  Records which pages were loaded.
+  // i's block id (from load_block).  Records which boxes were loaded.
   auto issue = [&](int k, int s, uint32_t blk) {
-    uint32_t ids[PPG];
+    uint32_t ids[NBOX];
 #pragma unroll
-    for (int i = 0; i < PPG; ++i) ids[i] = __shfl_sync(0xffffffffu, blk, i);
+    for (int i = 0; i < NBOX; ++i) ids[i] = __shfl_sync(0xffffffffu, blk, i);
     if (lane == 0) {
-      const int pg0 = (begin + (warp + k * NW) * GT) / BS;
+      const int t0 = begin + (warp + k * NW) * GT;
       uint32_t mask = 0, bytes = 0;
 #pragma unroll
-      for (int i = 0; i < PPG; ++i) {
-        if (pg0 + i < page_end) {
+      for (int i = 0; i < NBOX; ++i) {
+        if ((t0 + i * VBS) / BS < page_end) {
           if ((int64_t)ids[i] < p.num_blocks) {
             mask |= 1u << i;
-            bytes += 2 * PAGE;
+            bytes += 2 * BOX;
           } else {
             set_status(&g_decode_status, KVC_STATUS_BLOCK_OOB);
           }
@@ -260,11 +318,24 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_mma_kernel(DecodeParams 
       if (bytes) {
         mbar_arrive_expect_tx(&bars[s], bytes);
 #pragma unroll
-        for (int i = 0; i < PPG; ++i) {
+        for (int i = 0; i < NBOX; ++i) {
           if (mask & (1u << i)) {
-            const int64_t b = (int64_t)ids[i];
-            bulk_g2s(st + i * PAGE, kbase + b * p.k_block_stride, PAGE, &bars[s]);
-            bulk_g2s(st + (PPG + i) * PAGE, vbase + b * p.v_block_stride, PAGE, &bars[s]);
+            if constexpr (MODE == kTiles) {
+              // token offset of the box inside its page: 0 or a multiple of 16
+              // (16 tokens * 2 bytes = 32 B, so the innermost V coordinate is
+              // 16-byte aligned as tiled copies require)
+              const int toff = (t0 + i * VBS) % BS;
+              tma_load_5d(st + i * BOX, &tm.k, 0, toff, 0, kvh, (int)ids[i], &bars[s]);
+              tma_load_4d(st + (NBOX + i) * BOX, &tm.v, toff, 0, kvh, (int)ids[i], &bars[s]);
+            } else if constexpr (MODE == kSwizzledV) {
+              const int64_t b = (int64_t)ids[i];
+              bulk_g2s(st + i * BOX, kbase + b * p.k_block_stride, BOX, &bars[s]);
+              tma_load_4d(st + (NBOX + i) * BOX, &tm.v, 0, 0, kvh, (int)ids[i], &bars[s]);
+            } else {
+              const int64_t b = (int64_t)ids[i];
+              bulk_g2s(st + i * BOX, kbase + b * p.k_block_stride, BOX, &bars[s]);
+              bulk_g2s(st + (NBOX + i) * BOX, vbase + b * p.v_block_stride, BOX, &bars[s]);
+            }
           }
         }
       } else {
@@ -295,10 +366,10 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_mma_kernel(DecodeParams 
     }
     const uint8_t* st = ring + (size_t)s * Geo::STAGE;
     const uint32_t kst = smem_u32(st);
-    const uint32_t vst = smem_u32(st + PPG * PAGE);
+    const uint32_t vst = smem_u32(st + NBOX * BOX);
     const int tok0 = begin + (warp + k * NW) * GT;  // first token of the group
     const uint32_t pmask = masks[s];
-    const bool tail = (tok0 + GT > end) || (pmask != (1u << PPG) - 1u);
+    const bool tail = (tok0 + GT > end) || (pmask != (1u << NBOX) - 1u);
 
     // ---- S = Q K^T : ST tiles of 8 tokens
     float sacc[ST][4];
@@ -308,11 +379,11 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_mma_kernel(DecodeParams 
     for (int j = 0; j < ST; ++j) {
       // lane -> matrix (lane >> 3): chunk 2*ks + (lane>>3); row (lane & 7): token 8j + (lane & 7)
       const int tok = 8 * j + (lane & 7);
-      const int pg = tok / BS, off = tok % BS;
+      const int bx = tok / VBS, off = tok % VBS;
 #pragma unroll
       for (int ks = 0; ks < KS; ks += 2) {
         const int chunk = 2 * ks + (lane >> 3);
-        const uint32_t addr = kst + pg * PAGE + (chunk * BS + off) * 16;
+        const uint32_t addr = kst + bx * BOX + (chunk * VBS + off) * 16;
         uint32_t b0, b1, b2, b3;
         ldmatrix_x4(addr, b0, b1, b2, b3);
         MmaOp<T>::run(sacc[j], qa[ks], b0, b1);
@@ -335,7 +406,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_mma_kernel(DecodeParams 
           x_hi += slope_hi * pos;
         }
         if (tail) {
-          const bool ok = (tok0 + t < end) && ((pmask >> (t / BS)) & 1u);
+          const bool ok = (tok0 + t < end) && ((pmask >> (t / VBS)) & 1u);
           x_lo = ok ? x_lo : -INFINITY;
           x_hi = ok ? x_hi : -INFINITY;
         }
@@ -389,21 +460,25 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_mma_kernel(DecodeParams 
       // lane -> matrix mi = lane >> 3: dims 8*(nt + mi/2) + (lane & 7), tokens 16kk + 8*(mi & 1) ..+7
       const int mi = lane >> 3;
       const int vtok = 16 * kk + 8 * (mi & 1);
-      const int vpg = vtok / BS, voff = vtok % BS;
+      const int vbx = vtok / VBS, voff = vtok % VBS;
       // tokens this lane holds in the B fragments: 16kk + 2*q4 + e (b0/b2) and +8 (b1/b3)
       const int t_lo = tok0 + 16 * kk + 2 * q4;
       bool ok_lo0 = true, ok_lo1 = true, ok_hi0 = true, ok_hi1 = true;
       if (tail) {
         const int tl = 16 * kk + 2 * q4;
-        ok_lo0 = (t_lo < end) && ((pmask >> (tl / BS)) & 1u);
-        ok_lo1 = (t_lo + 1 < end) && ((pmask >> ((tl + 1) / BS)) & 1u);
-        ok_hi0 = (t_lo + 8 < end) && ((pmask >> ((tl + 8) / BS)) & 1u);
-        ok_hi1 = (t_lo + 9 < end) && ((pmask >> ((tl + 9) / BS)) & 1u);
+        ok_lo0 = (t_lo < end) && ((pmask >> (tl / VBS)) & 1u);
+        ok_lo1 = (t_lo + 1 < end) && ((pmask >> ((tl + 1) / VBS)) & 1u);
+        ok_hi0 = (t_lo + 8 < end) && ((pmask >> ((tl + 8) / VBS)) & 1u);
+        ok_hi1 = (t_lo + 9 < end) && ((pmask >> ((tl + 9) / VBS)) & 1u);
       }
 #pragma unroll
       for (int nt = 0; nt < NT; nt += 2) {
         const int dim = 8 * (nt + (mi >> 1)) + (lane & 7);
-        const uint32_t addr = vst + vpg * PAGE + (dim * BS + voff) * 2;
+        // byte offset of (dim, voff) in the V box; with a swizzled box the
+        // 16-byte chunk index (bits 4..) is XORed with address bits 7..
+        uint32_t voffb = (uint32_t)(dim * VBS + voff) * 2;
+        if (VSW_MASK) voffb ^= ((voffb >> 7) & VSW_MASK) << 4;
+        const uint32_t addr = vst + vbx * BOX + voffb;
         uint32_t b0, b1, b2, b3;
         ldmatrix_x4(addr, b0, b1, b2, b3);
         if (tail) {
@@ -507,10 +582,121 @@ static bool mma_supported(const DecodeArgs& a) {
   return true;
 }
 
-template <typename T, int D, int BS, int NW, int STAGES, int GT>
+// ---- tensor maps ---------------------------------------------------------------
+// cuTensorMapEncodeTiled is a driver entry point; it is looked up through the
+// runtime so the library needs no link against libcuda.
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+struct MapKey {
+  const void* k;
+  const void* v;
+  int64_t nb, hkv, ks[2], vs[2];
+  int d, bs, vbs, swz, dt, dev, mode;
+  bool operator==(const MapKey& o) const { return memcmp(this, &o, sizeof(*this)) == 0; }
+};
+
+// Encodes (or finds in a small cache) the maps of one launch.  kTiles: K is
+// [nb][H][D/8][BS][8] (box 8 x VBS x D/8: VBS tokens of every 16-byte chunk
+// row) and V is [nb][H][D][BS] (box VBS x D, swizzled by `swz` bytes).
+// kSwizzledV: only V, as [nb][H][D*BS/64][64] with one whole page per box and
+// the 128-byte swizzle.
+static bool make_tensor_maps(const DecodeParams& p, ElemType et, int D, int BS, int VBS, int swz, int mode,
+                             TmaMaps* out) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  MapKey key;
+  memset(&key, 0, sizeof(key));
+  key.k = p.k_cache;
+  key.v = p.v_cache;
+  key.nb = p.num_blocks;
+  key.hkv = p.num_kv_heads;
+  key.ks[0] = p.k_head_stride;
+  key.ks[1] = p.k_block_stride;
+  key.vs[0] = p.v_head_stride;
+  key.vs[1] = p.v_block_stride;
+  key.d = D;
+  key.bs = BS;
+  key.vbs = VBS;
+  key.swz = swz;
+  key.dt = (int)et;
+  key.mode = mode;
+  cudaGetDevice(&key.dev);
+  static std::mutex mu;
+  static MapKey keys[32];
+  static TmaMaps maps[32];
+  static int used = 0, next = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (keys[i] == key) {
+      *out = maps[i];
+      return true;
+    }
+  const CUtensorMapDataType dt = et == ElemType::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const cuuint64_t es = 2;
+  TmaMaps m;
+  memset(&m, 0, sizeof(m));
+  cuuint32_t ones[5] = {1, 1, 1, 1, 1};
+  if (mode == kSwizzledV) {
+    const cuuint64_t rows = (cuuint64_t)D * BS / 64;  // 128-byte rows per page
+    cuuint64_t vdim[4] = {64, rows, (cuuint64_t)p.num_kv_heads, (cuuint64_t)p.num_blocks};
+    cuuint64_t vstr[3] = {128, (cuuint64_t)p.v_head_stride * es, (cuuint64_t)p.v_block_stride * es};
+    cuuint32_t vbox[4] = {64, (cuuint32_t)rows, 1, 1};
+    if (rows > 256 ||
+        enc(&m.v, dt, 4, const_cast<void*>(p.v_cache), vdim, vstr, vbox, ones, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+            CUDA_SUCCESS)
+      return false;
+    keys[next] = key;
+    maps[next] = m;
+    next = (next + 1) % 32;
+    if (used < 32) ++used;
+    *out = m;
+    return true;
+  }
+  cuuint64_t kdim[5] = {8, (cuuint64_t)BS, (cuuint64_t)(D / 8), (cuuint64_t)p.num_kv_heads, (cuuint64_t)p.num_blocks};
+  cuuint64_t kstr[4] = {16, (cuuint64_t)BS * 16, (cuuint64_t)p.k_head_stride * es, (cuuint64_t)p.k_block_stride * es};
+  cuuint32_t kbox[5] = {8, (cuuint32_t)VBS, (cuuint32_t)(D / 8), 1, 1};
+  if (enc(&m.k, dt, 5, const_cast<void*>(p.k_cache), kdim, kstr, kbox, ones, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+      CUDA_SUCCESS)
+    return false;
+  cuuint64_t vdim[4] = {(cuuint64_t)BS, (cuuint64_t)D, (cuuint64_t)p.num_kv_heads, (cuuint64_t)p.num_blocks};
+  cuuint64_t vstr[3] = {(cuuint64_t)BS * es, (cuuint64_t)p.v_head_stride * es, (cuuint64_t)p.v_block_stride * es};
+  cuuint32_t vbox[4] = {(cuuint32_t)VBS, (cuuint32_t)D, 1, 1};
+  const CUtensorMapSwizzle sw = swz == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                          : (swz == 32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (enc(&m.v, dt, 4, const_cast<void*>(p.v_cache), vdim, vstr, vbox, ones, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  keys[next] = key;
+  maps[next] = m;
+  next = (next + 1) % 32;
+  if (used < 32) ++used;
+  *out = m;
+  return true;
+}
+
+template <typename T, int D, int BS, int NW, int STAGES, int GT, int MODE = kBulk>
 static cudaError_t launch_mma_nw(const DecodeParams& p, cudaStream_t stream) {
-  using Geo = MmaGeom<D, BS, NW, STAGES, GT>;
-  auto kern = paged_decode_mma_kernel<T, D, BS, NW, STAGES, GT>;
+  using Geo = MmaGeom<D, BS, NW, STAGES, GT, MODE>;
+  auto kern = paged_decode_mma_kernel<T, D, BS, NW, STAGES, GT, MODE>;
+  TmaMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  if (MODE != kBulk) {
+    const ElemType et = std::is_same<T, __nv_bfloat16>::value ? ElemType::BF16 : ElemType::F16;
+    if (!make_tensor_maps(p, et, D, BS, Geo::VBS, Geo::VSWZ, MODE, &maps)) return cudaErrorNotSupported;
+  }
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -520,19 +706,22 @@ static cudaError_t launch_mma_nw(const DecodeParams& p, cudaStream_t stream) {
     configured[dev] = true;
   }
   dim3 grid((unsigned)p.num_kv_heads, (unsigned)p.num_seqs, (unsigned)p.num_partitions);
-  kern<<<grid, NW * 32, Geo::SMEM, stream>>>(p);
+  kern<<<grid, NW * 32, Geo::SMEM, stream>>>(p, maps);
   count_launch();
   return cudaGetLastError();
 }
 
-// Variant id = warps * 1000 + stages * 100 + group tokens.
+// Variant id = warps * 1000 + stages * 100 + group tokens, + 100000 for tiled
+// tensor copies ("<warps>x<stages>x<group>t"), + 200000 for bulk K with the
+// swizzled whole-page V ("<warps>x<stages>x<group>s").
 static int mma_variant() {
   const char* v = getenv("KVC_MMA_CONFIG");
   if (!v) return 0;
   int w = 0, s = 0, g = 32;
-  const int n = sscanf(v, "%dx%dx%d", &w, &s, &g);
+  char t = 0;
+  const int n = sscanf(v, "%dx%dx%d%c", &w, &s, &g, &t);
   if (n < 2) return 0;
-  return w * 1000 + s * 100 + g;
+  return (t == 't' ? 100000 : (t == 's' ? 200000 : 0)) + w * 1000 + s * 100 + g;
 }
 
 template <typename T, int D, int BS>
@@ -540,29 +729,37 @@ static cudaError_t launch_mma_typed(const DecodeParams& p, cudaStream_t stream) 
   const int v = mma_variant();
   const int g = v % 100;
   const bool part_ok = p.num_partitions == 1 || (g > 0 && p.partition_size % g == 0);
-  if (D == 128 && v && part_ok && g >= BS) {
+  if (D == 128 && v && part_ok) {
+    cudaError_t e = cudaErrorNotSupported;
     switch (v) {
-      case 2332: return launch_mma_nw<T, D, BS, 2, 3, 32>(p, stream);
-      case 4332: return launch_mma_nw<T, D, BS, 4, 3, 32>(p, stream);
-      case 1232: return launch_mma_nw<T, D, BS, 1, 2, 32>(p, stream);
-      case 2232: return launch_mma_nw<T, D, BS, 2, 2, 32>(p, stream);
-      case 3232: return launch_mma_nw<T, D, BS, 3, 2, 32>(p, stream);
-      case 6232: return launch_mma_nw<T, D, BS, 6, 2, 32>(p, stream);
-      case 1332: return launch_mma_nw<T, D, BS, 1, 3, 32>(p, stream);
-      case 4316: if constexpr (BS <= 16) return launch_mma_nw<T, D, BS, 4, 3, 16>(p, stream); break;
-      case 8316: if constexpr (BS <= 16) return launch_mma_nw<T, D, BS, 8, 3, 16>(p, stream); break;
-      case 2416: if constexpr (BS <= 16) return launch_mma_nw<T, D, BS, 2, 4, 16>(p, stream); break;
-      case 4416: if constexpr (BS <= 16) return launch_mma_nw<T, D, BS, 4, 4, 16>(p, stream); break;
+      case 2332: e = launch_mma_nw<T, D, BS, 2, 3, 32>(p, stream); break;
+      case 2232: e = launch_mma_nw<T, D, BS, 2, 2, 32>(p, stream); break;
+      case 4316: if constexpr (BS <= 16) e = launch_mma_nw<T, D, BS, 4, 3, 16>(p, stream); break;
+      case 104316: e = launch_mma_nw<T, D, BS, 4, 3, 16, kTiles>(p, stream); break;
+      case 102232: e = launch_mma_nw<T, D, BS, 2, 2, 32, kTiles>(p, stream); break;
+      case 204316: if constexpr (BS <= 16) e = launch_mma_nw<T, D, BS, 4, 3, 16, kSwizzledV>(p, stream); break;
+      case 202232: e = launch_mma_nw<T, D, BS, 2, 2, 32, kSwizzledV>(p, stream); break;
+      case 203232: e = launch_mma_nw<T, D, BS, 3, 2, 32, kSwizzledV>(p, stream); break;
+      case 202332: e = launch_mma_nw<T, D, BS, 2, 3, 32, kSwizzledV>(p, stream); break;
       default: break;
     }
+    if (e != cudaErrorNotSupported) return e;
   }
-  // Defaults from sweeps on B200 (config 2 / config 3 shapes): 16-token
-  // groups, 4 warps x 3 stages (96 KB, two CTAs and 8 warps per SM) where the
+  // Defaults from sweeps on B200: 16-token groups, 4 warps x 3 stages (96 KB,
+  // two CTAs and 8 warps per SM) with whole-page 1-D bulk copies where the
   // block size allows (98% of copy bandwidth on config 2, against 81% for
-  // 32-token groups); 32-token groups with 2 warps x 2 stages (64 KB, three
-  // CTAs per SM) for 32-token blocks.
+  // 32-token groups).  32-token blocks: 32-token groups, 2 warps x 2 stages
+  // (64 KB, three CTAs per SM), K by bulk copy and V through the 128-byte
+  // swizzled tensor map (config 3: 77.7% against 73.9% with the 4-way bank
+  // conflicts of unswizzled 64-byte V rows; config 5: 91% against 89%).
+  // Tiled 16-token boxes of 32-token pages measured slower: such a box is
+  // hundreds of 16-32 byte rows.  If no tensor map can be encoded for the
+  // cache, plain bulk copies are used.
   if constexpr (BS <= 16) {
     if (p.num_partitions == 1 || p.partition_size % 16 == 0) return launch_mma_nw<T, D, BS, 4, 3, 16>(p, stream);
+  } else {
+    cudaError_t e = launch_mma_nw<T, D, BS, 2, 2, 32, kSwizzledV>(p, stream);
+    if (e != cudaErrorNotSupported) return e;
   }
   return launch_mma_nw<T, D, BS, 2, 2, 32>(p, stream);
 }

@@ -154,10 +154,12 @@ def choose_decode(num_seqs: int, num_kv_heads: int, max_seq_len: int, block_size
     partitions when they still give four waves, else 1024 when that gives one
     wave, else 512.  (Measured on 1/2/4/8-way head-sharded Llama-3-8B decode:
     short partitions lose more to per-CTA pipeline ramp than they gain in
-    balance.)"""
+    balance.)  Batches allowed to hold sequences of 8192+ tokens are split
+    too: one such sequence alone in the last wave would set the launch time
+    (lognormal continuous batch: 63% single pass, 91% split)."""
     slots = sm_count * (3 if block_size >= 32 else 2)
     items = num_seqs * num_kv_heads
-    if items >= 4 * slots or max_seq_len <= 512:
+    if max_seq_len <= 512 or (items >= 4 * slots and max_seq_len < 8192):
         return 0
 
     def ctas(p):

@@ -138,3 +138,97 @@ def config1(seed: int = 11, dtype: str = "float16") -> dict:
     rng = np.random.default_rng(seed)
     lens = rng.integers(1, 1025, size=8)
     return paged_batch(seed + 1, dtype, 8, 32, 8, 128, 16, lens)
+
+
+# ---------------------------------------------------------------------------
+# BASELINE.json workloads (configs 2-5) for the bench and the large parity tests.
+# Only the host-side structure is built here (lengths, block tables, slots);
+# K/V contents are drawn on the device by the caller.
+# ---------------------------------------------------------------------------
+BASELINE = {
+    2: dict(name="llama3-8b-batched-decode", layers=32, batch=256, hq=32, hkv=8, d=128, bs=16, partition=0),
+    3: dict(name="128k-batch1-splitk-decode", layers=1, batch=1, hq=64, hkv=8, d=128, bs=32, partition=512),
+    4: dict(name="radix-shared-prefix-decode", layers=1, batch=64, hq=64, hkv=8, d=128, bs=16, partition=0,
+            prefix=2048, tail=256, l2_flush=True),
+    5: dict(name="mixed-continuous-batch-step", layers=1, batch=512, hq=28, hkv=4, d=128, bs=32, partition=0,
+            prefill_chunks=16, chunk=512, lognormal_median=1500.0, lognormal_sigma=1.0, clip=(16, 32768)),
+}
+
+
+def _tables_from_free_list(n_blocks_per_seq, free_list):
+    mb = max(max(n_blocks_per_seq), 1)
+    tables = np.zeros((len(n_blocks_per_seq), mb), np.int32)
+    o = 0
+    for b, n in enumerate(n_blocks_per_seq):
+        tables[b, :n] = free_list[o:o + n]
+        tables[b, n:] = free_list[o] if n else 0  # padding, never read
+        o += n
+    return tables, o
+
+
+def baseline_workload(config: int, batch: int | None = None) -> dict:
+    """One decode step of BASELINE config `config`.
+
+    Returns the sequences' context length before the step (`lens`), their block
+    tables covering lens + 1 tokens, the slot each sequence's new token is
+    appended to (`decode_slots`), the pool size, and for config 5 the slots of
+    the step's prefill-chunk tokens.  `batch` shrinks the batch (profiling)."""
+    cfg = dict(BASELINE[config])
+    if batch:
+        cfg["batch"] = batch
+    B, bs = cfg["batch"], cfg["bs"]
+    prefill_slots = np.zeros(0, np.int32)
+    if config == 2:
+        lens = np.random.default_rng(2024).integers(512, 4096 + 1, size=B).astype(np.int64)
+        nblk = [(-(-int(c + 1) // bs)) for c in lens]
+        free = np.random.default_rng(7).permutation(int(sum(nblk))).astype(np.int32)
+        tables, used = _tables_from_free_list(nblk, free)
+        num_blocks = used
+    elif config == 3:
+        lens = np.full(B, 131072 - 1, np.int64)
+        nblk = [(-(-int(c + 1) // bs)) for c in lens]
+        free = np.random.default_rng(8).permutation(int(sum(nblk))).astype(np.int32)
+        tables, num_blocks = _tables_from_free_list(nblk, free)
+    elif config == 4:
+        pre_blocks = cfg["prefix"] // bs
+        tail_blocks = cfg["tail"] // bs
+        num_blocks = pre_blocks + B * tail_blocks
+        free = np.random.default_rng(9).permutation(num_blocks).astype(np.int32)
+        prefix = free[:pre_blocks]
+        tables = np.zeros((B, pre_blocks + tail_blocks), np.int32)
+        for b in range(B):
+            tables[b, :pre_blocks] = prefix
+            tables[b, pre_blocks:] = free[pre_blocks + b * tail_blocks: pre_blocks + (b + 1) * tail_blocks]
+        lens = np.full(B, cfg["prefix"] + cfg["tail"] - 1, np.int64)
+    elif config == 5:
+        rng = np.random.default_rng(10)
+        lo, hi = cfg["clip"]
+        lens = np.clip(rng.lognormal(np.log(cfg["lognormal_median"]), cfg["lognormal_sigma"], B), lo, hi)
+        lens = lens.astype(np.int64)
+        nblk = [(-(-int(c + 1) // bs)) for c in lens]
+        chunk_blocks = cfg["chunk"] // bs
+        num_blocks = int(sum(nblk)) + cfg["prefill_chunks"] * chunk_blocks
+        free = rng.permutation(num_blocks).astype(np.int32)  # seeded shuffled block free list
+        tables, used = _tables_from_free_list(nblk, free)
+        pre = free[used:used + cfg["prefill_chunks"] * chunk_blocks].astype(np.int64)
+        t = np.arange(cfg["prefill_chunks"] * cfg["chunk"])
+        prefill_slots = (pre[t // bs] * bs + t % bs).astype(np.int32)
+    else:
+        raise ValueError(config)
+    decode_slots = (tables[np.arange(B), lens // bs].astype(np.int64) * bs + lens % bs).astype(np.int32)
+    return dict(cfg=cfg, lens=lens, tables=tables, num_blocks=int(num_blocks), decode_slots=decode_slots,
+                prefill_slots=prefill_slots, max_seq_len=int(tables.shape[1] * bs))
+
+
+def unique_kv_bytes(tables, lens_after, hkv, d, bs, elem=2):
+    """K+V bytes a decode must read when shared blocks are read once: every
+    distinct block counts its largest used prefix of tokens once."""
+    used = {}
+    for b, c in enumerate(lens_after):
+        nb = -(-int(c) // bs)
+        for i in range(nb):
+            blk = int(tables[b, i])
+            toks = min(bs, int(c) - i * bs)
+            if toks > used.get(blk, 0):
+                used[blk] = toks
+    return sum(used.values()) * hkv * d * elem * 2
