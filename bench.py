@@ -184,8 +184,8 @@ def workload(args):
     cfg = dict(w["cfg"])
     if args.layers:
         cfg["layers"] = args.layers
-    if args.layers or args.batch:
-        cfg["name"] += f" (reduced: {cfg['layers']} layers, batch {cfg['batch']})"
+    if args.layers or args.batch or args.kv_heads:
+        cfg["name"] += f" (reduced: {cfg['layers']} layers, batch {cfg['batch']}, kv heads {args.kv_heads or cfg['hkv']})"
     return w, cfg
 
 
@@ -249,7 +249,7 @@ def run_ours(args, rank, world, local_rank):
 
     from sglang_mlx_b200 import _lib, sharding
     from sglang_mlx_b200 import metal_kernels as mk
-    from sglang_mlx_b200.device_array import DeviceArray, Event, HostBuffer
+    from sglang_mlx_b200.device_array import DeviceArray, Event, Graph, HostBuffer, Stream
 
     dev = local_rank
     _lib.set_device(dev)
@@ -258,6 +258,9 @@ def run_ours(args, rank, world, local_rank):
 
     w, cfg = workload(args)
     L, B_all, HQ, HKV, D, BS = cfg["layers"], cfg["batch"], cfg["hq"], cfg["hkv"], cfg["d"], cfg["bs"]
+    if args.kv_heads:  # profiling: one rank's share of a head-sharded run, on one GPU
+        HQ, HKV = HQ * args.kv_heads // HKV, args.kv_heads
+        cfg["hq"], cfg["hkv"] = HQ, HKV
     plan = sharding.plan(HQ, HKV, world, rank, w["lens"] + 1)
     hkv, hq = plan.num_kv_heads, plan.num_q_heads
     lens = w["lens"][plan.seqs]
@@ -312,25 +315,27 @@ def run_ours(args, rank, world, local_rank):
     split = psize > 0
     ws = mk.splitk_workspace(B, hq, D, max_seq_len, psize, dev) if split else None
     torch.cuda.synchronize()
+    st = Stream()  # all work of the step runs on this stream (graph-capturable)
 
     def decode(i):
         if split:
             return mk.paged_attention_v2(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, BS, max_seq_len,
-                                         partition_size=psize, workspace=ws, out=out[i])
-        return mk.paged_attention_v1(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, BS, max_seq_len, out=out[i])
+                                         partition_size=psize, workspace=ws, out=out[i], stream=st)
+        return mk.paged_attention_v1(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, BS, max_seq_len, out=out[i],
+                                     stream=st)
 
     def step(ev=None):
         for i in range(L):
-            mk.reshape_and_cache(kn[i], vn[i], kc[i], vc[i], slots_d)
+            mk.reshape_and_cache(kn[i], vn[i], kc[i], vc[i], slots_d, stream=st)
             if ev is not None:
-                ev[i][0].record()
+                ev[i][0].record(st)
             decode(i)
             if ev is not None:
-                ev[i][1].record()
+                ev[i][1].record(st)
 
     def l2_flush():
         if flush is not None:
-            flush.fill_zero()
+            flush.fill_zero(stream=st)
 
     dist = None
     if world > 1:
@@ -343,25 +348,47 @@ def run_ours(args, rank, world, local_rank):
     for _ in range(args.warmup):
         l2_flush()
         step()
-    _lib.synchronize()
+    st.synchronize()
 
     # ---- timed region (device-resident inputs); L2 flushed between steps, outside the events ----
     evs = [[[Event(), Event()] for _ in range(L)] for _ in range(args.steps)]
     sev = [[Event(), Event()] for _ in range(args.steps)]
+
+    graph = None
+    if args.graph:
+        # one step (all layers) as one CUDA graph; replayed between events below
+        launches0 = _lib.launch_count()
+        graph = Graph.capture(st, step)
+        graph_launches = _lib.launch_count() - launches0
+        for _ in range(args.warmup):
+            l2_flush()
+            graph.replay(st)
+        st.synchronize()
+
+    def timed_region(with_layer_events):
+        for s in range(args.steps):
+            l2_flush()
+            sev[s][0].record(st)
+            if graph is not None and not with_layer_events:
+                graph.replay(st)
+            else:
+                step(evs[s] if with_layer_events else None)
+            sev[s][1].record(st)
+
     sampler = ClockSampler(dev)
     barrier()
     _lib.synchronize()
     sampler.start()
     launches0 = _lib.launch_count()
-    for s in range(args.steps):
-        l2_flush()
-        sev[s][0].record()
-        step(evs[s])
-        sev[s][1].record()
-    _lib.synchronize()
-    launches = _lib.launch_count() - launches0
+    timed_region(with_layer_events=graph is None)
+    st.synchronize()
+    launches = (_lib.launch_count() - launches0) if graph is None else graph_launches * args.steps
     clocks = sampler.stop()
     total_ms = sum(a.elapsed_ms(b) for a, b in sev)
+    if graph is not None:
+        # per-launch decode times come from an eager pass of the same launches
+        timed_region(with_layer_events=True)
+        st.synchronize()
     dec_ms = [evs[s][i][0].elapsed_ms(evs[s][i][1]) for s in range(args.steps) for i in range(L)]
     barrier()
 
@@ -383,28 +410,28 @@ def run_ours(args, rank, world, local_rank):
         h_slots.array[...] = slots
 
         def e2e_step():
-            lens_d.copy_from_host(h_lens)
-            slots_d.copy_from_host(h_slots)
+            lens_d.copy_from_host(h_lens, stream=st)
+            slots_d.copy_from_host(h_slots, stream=st)
             for i in range(L):
-                q[i].copy_from_host(h_q[i])
-                kn[i].copy_from_host(h_k[i])
-                vn[i].copy_from_host(h_v[i])
-                mk.reshape_and_cache(kn[i], vn[i], kc[i], vc[i], slots_d)
+                q[i].copy_from_host(h_q[i], stream=st)
+                kn[i].copy_from_host(h_k[i], stream=st)
+                vn[i].copy_from_host(h_v[i], stream=st)
+                mk.reshape_and_cache(kn[i], vn[i], kc[i], vc[i], slots_d, stream=st)
                 decode(i)
-                out[i].copy_to_host(h_o[i])
+                out[i].copy_to_host(h_o[i], stream=st)
 
         for _ in range(max(1, args.warmup)):
             l2_flush()
             e2e_step()
-        _lib.synchronize()
+        st.synchronize()
         barrier()
         eev = [[Event(), Event()] for _ in range(args.steps)]
         for s in range(args.steps):
             l2_flush()
-            eev[s][0].record()
+            eev[s][0].record(st)
             e2e_step()
-            eev[s][1].record()
-        _lib.synchronize()
+            eev[s][1].record(st)
+        st.synchronize()
         e2e_ms = sum(a.elapsed_ms(b) for a, b in eev)
         h2d = B * 4 + T_new * 4 + L * (B * hq * D * 2 + 2 * T_new * hkv * D * 2)
         d2h = L * B * hq * D * 2
@@ -426,11 +453,12 @@ def run_ours(args, rank, world, local_rank):
         return
     alg_all, logical_all, h2d_all, d2h_all = sums
     peak, peak_kind = load_peaks()
-    traffic = TRAFFIC_PER_LAUNCH.get(args.config) if (world == 1 and not (args.layers or args.batch)) else None
+    traffic = (TRAFFIC_PER_LAUNCH.get(args.config)
+               if (world == 1 and not (args.layers or args.batch or args.kv_heads)) else None)
     achieved = alg / (mean_dec_ms * 1e-3) / 1e9
     toks = B_all / (step_ms * 1e-3)
     kernel = f"split-K v2, {psize}-token partitions" if split else "paged_attention_v1"
-    extra = {"kernel": kernel,
+    extra = {"kernel": kernel, "launch": "one CUDA graph per step (decode timing from an eager pass)" if graph is not None else "eager",
              "l2": ("flushed between steps (unique KV fits in L2)" if flush is not None else
                     f"inputs larger than L2 (KV per layer {logical_all / 1e9:.2f} GB); no flush")}
     line = {
@@ -495,6 +523,10 @@ def main():
     ap.add_argument("--partition", type=int, default=0, help="split-K partition size (tokens) when split")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (profiling cases only)")
     ap.add_argument("--batch", type=int, default=0, help="override the batch (profiling cases only)")
+    ap.add_argument("--kv-heads", type=int, default=0,
+                    help="override the KV head count, keeping the group size (profiling cases only)")
+    ap.add_argument("--graph", action=argparse.BooleanOptionalAction, default=True,
+                    help="replay each timed step as one CUDA graph (removes host launch overhead)")
     args = ap.parse_args()
     if args.impl == "ours":
         args.warmup = max(args.warmup, 3)

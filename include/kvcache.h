@@ -199,6 +199,15 @@ int kvc_event_synchronize(void* event);
 int kvc_event_elapsed_ms(void* start, void* end, float* ms);
 /* Writes `bytes` of garbage over a device buffer to evict it from L2. */
 int kvc_l2_flush(void* scratch, size_t bytes, void* stream);
+/* CUDA graphs for launch-bound loops (a decode step is two launches per layer):
+ * begin/end capture on a non-default stream, then replay the instantiated
+ * graph.  Every entry point above is capturable once it has run once on the
+ * device (first calls set kernel attributes).  The capture is thread-local
+ * (cudaStreamCaptureModeThreadLocal). */
+int kvc_stream_begin_capture(void* stream);
+int kvc_stream_end_capture(void* stream, void** graph_exec);
+int kvc_graph_launch(void* graph_exec, void* stream);
+int kvc_graph_destroy(void* graph_exec);
 /* Number of kernels this library has launched in this process. */
 uint64_t kvc_launch_count(void);
 

@@ -659,6 +659,36 @@ int kvc_event_elapsed_ms(void* start, void* end, float* ms) {
   return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaEventElapsedTime");
 }
 
+int kvc_stream_begin_capture(void* stream) {
+  if (!stream) return fail(KVC_EINVAL, "capture needs a non-default stream");
+  cudaError_t e = cudaStreamBeginCapture(static_cast<cudaStream_t>(stream), cudaStreamCaptureModeThreadLocal);
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaStreamBeginCapture");
+}
+
+int kvc_stream_end_capture(void* stream, void** graph_exec) {
+  if (!graph_exec) return fail(KVC_EINVAL, "graph_exec is null");
+  *graph_exec = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(static_cast<cudaStream_t>(stream), &graph);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+  cudaGraphExec_t exec = nullptr;
+  e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+  *graph_exec = exec;
+  return KVC_OK;
+}
+
+int kvc_graph_launch(void* graph_exec, void* stream) {
+  cudaError_t e = cudaGraphLaunch(static_cast<cudaGraphExec_t>(graph_exec), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaGraphLaunch");
+}
+
+int kvc_graph_destroy(void* graph_exec) {
+  cudaError_t e = cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(graph_exec));
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaGraphExecDestroy");
+}
+
 int kvc_l2_flush(void* scratch, size_t bytes, void* stream) {
   if (bytes == 0) return KVC_OK;
   cudaError_t e = cudaMemsetAsync(scratch, 0x5a, bytes, static_cast<cudaStream_t>(stream));

@@ -75,6 +75,10 @@ SIGNATURES: dict[str, tuple] = {
     "kvc_event_synchronize": (_i, [_p]),
     "kvc_event_elapsed_ms": (_i, [_p, _p, ctypes.POINTER(_f)]),
     "kvc_l2_flush": (_i, [_p, _sz, _p]),
+    "kvc_stream_begin_capture": (_i, [_p]),
+    "kvc_stream_end_capture": (_i, [_p, ctypes.POINTER(_p)]),
+    "kvc_graph_launch": (_i, [_p, _p]),
+    "kvc_graph_destroy": (_i, [_p]),
     "kvc_launch_count": (ctypes.c_uint64, []),
 }
 

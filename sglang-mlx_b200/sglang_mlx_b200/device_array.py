@@ -362,6 +362,34 @@ class Stream:
         _lib.check(_lib_ref.kvc_stream_synchronize(ctypes.c_void_p(self.handle)))
 
 
+class Graph:
+    """A captured sequence of libkvcache work, replayed with one launch.
+
+        g = Graph.capture(stream, fn)   # runs fn() under stream capture
+        g.replay(stream)
+
+    Every call inside `fn` must pass `stream=stream`; arrays it touches must be
+    allocated beforehand and stay alive as long as the graph."""
+
+    def __init__(self, handle: int):
+        self.handle = handle
+        weakref.finalize(self, _lib_ref.kvc_graph_destroy, ctypes.c_void_p(handle))
+
+    @classmethod
+    def capture(cls, stream: "Stream", fn) -> "Graph":
+        _lib.check(_lib_ref.kvc_stream_begin_capture(ctypes.c_void_p(stream.handle)))
+        try:
+            fn()
+        finally:
+            h = ctypes.c_void_p()
+            rc = _lib_ref.kvc_stream_end_capture(ctypes.c_void_p(stream.handle), ctypes.byref(h))
+        _lib.check(rc)
+        return cls(h.value)
+
+    def replay(self, stream: "Stream") -> None:
+        _lib.check(_lib_ref.kvc_graph_launch(ctypes.c_void_p(self.handle), ctypes.c_void_p(stream.handle)))
+
+
 class Event:
     """A CUDA event for device-side timing."""
 

@@ -369,3 +369,38 @@ def test_ring_variants(gpu, monkeypatch, variant, bs):
                                        c["max_seq_len"])
     assert_close(run_v1(d, c).to_numpy(), ref, ATOL_NS, RTOL_NS, f"{variant} v1")
     assert_close(run_v2(d, c, partition_size=256).to_numpy(), ref, ATOL_NS, RTOL_NS, f"{variant} v2")
+
+
+def test_decode_step_replays_as_cuda_graph(gpu):
+    """append + single-pass + split-K decode captured once, replayed twice: same results as eager."""
+    from sglang_mlx_b200.device_array import Graph, Stream
+
+    c = cases.paged_batch(1234, "bfloat16", 4, 32, 8, 128, 16, [100, 700, 33, 1500])
+    d = upload_case(c)
+    fill_cache(d)
+    st = Stream()
+    o1 = DeviceArray.empty(d["q"].shape, "bfloat16")
+    o2 = DeviceArray.empty(d["q"].shape, "bfloat16")
+    ws = mk.splitk_workspace(4, 32, 128, c["max_seq_len"], 256)
+    k_new = DeviceArray.from_numpy(np.ones((4, 8, 128), np.float32), dtype="bfloat16")
+    slots = DeviceArray.from_numpy(np.array([c["block_tables"][i, 0] * 16 for i in range(4)], np.int32))
+
+    def work():
+        mk.reshape_and_cache(k_new, k_new, d["k_cache"], d["v_cache"], slots, stream=st)
+        mk.paged_attention_v1(d["q"], d["k_cache"], d["v_cache"], d["block_tables"], d["context_lens"], 8,
+                              c["scale"], 16, c["max_seq_len"], out=o1, stream=st)
+        mk.paged_attention_v2(d["q"], d["k_cache"], d["v_cache"], d["block_tables"], d["context_lens"], 8,
+                              c["scale"], 16, c["max_seq_len"], partition_size=256, workspace=ws, out=o2, stream=st)
+
+    work()  # eager first (sets kernel attributes)
+    st.synchronize()
+    e1, e2 = o1.to_numpy(), o2.to_numpy()
+    g = Graph.capture(st, work)
+    for _ in range(2):
+        o1.fill_zero(stream=st)
+        o2.fill_zero(stream=st)
+        g.replay(st)
+        st.synchronize()
+        np.testing.assert_array_equal(o1.to_numpy(), e1)
+        np.testing.assert_array_equal(o2.to_numpy(), e2)
+    assert_close(e2, e1, ATOL_NS, RTOL_NS, "split vs single pass")
