@@ -23,8 +23,9 @@
 //   O[head][d] += P[head][tok] V[tok][d]        A = P taken straight from the S
 //       accumulators (two 8-token tiles form one 16-token k-step), B = V via
 //       ldmatrix on the [D][BS] page: 8 dims x 16 B (8 tokens) rows.
-// fp32 accumulation everywhere; P is rounded to the cache type for the second
-// product (the only rounding the reference's fp32 path does not have).
+// fp32 accumulation everywhere.  P enters the second product as f16, or for
+// bf16 as a hi + lo pair of bf16 values (about 16 bits), close to the
+// reference's fp32 P.
 #pragma once
 
 #include <cuda.h>
@@ -140,6 +141,15 @@ template <> struct MmaOp<__nv_bfloat16> {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
   }
+  // (x0, x1) = hi + lo with hi = bf16(x) and lo = bf16(x - hi).
+  static constexpr bool kSplitP = true;
+  __device__ __forceinline__ static void pack_split(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+  }
 };
 template <> struct MmaOp<__half> {
   __device__ __forceinline__ static void run(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
@@ -152,6 +162,11 @@ template <> struct MmaOp<__half> {
   __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
     __half2 v = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
+  }
+  static constexpr bool kSplitP = false;
+  __device__ __forceinline__ static void pack_split(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    hi = pack(x0, x1);
+    lo = 0u;
   }
 };
 
@@ -203,17 +218,190 @@ struct TmaMaps {
   CUtensorMap v;
 };
 
+// Online-softmax state of one warp over the rows r (lo) and r + 8 (hi) of its
+// 16-row tile: running max (log2 units), this lane's share of the row sums,
+// and the unnormalised output accumulators (the P.V C fragments).
+template <int D>
+struct GroupState {
+  float m_lo, m_hi, l_lo, l_hi;
+  float o[D / 8][4];
+  __device__ __forceinline__ void reset() {
+    m_lo = m_hi = -INFINITY;
+    l_lo = l_hi = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < D / 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+  }
+  // Row sums completed across the quad of lanes that share a row.
+  __device__ __forceinline__ float quad_sum_lo() const {
+    float v = l_lo + __shfl_xor_sync(0xffffffffu, l_lo, 1);
+    return v + __shfl_xor_sync(0xffffffffu, v, 2);
+  }
+  __device__ __forceinline__ float quad_sum_hi() const {
+    float v = l_hi + __shfl_xor_sync(0xffffffffu, l_hi, 1);
+    return v + __shfl_xor_sync(0xffffffffu, v, 2);
+  }
+};
+
+// One GT-token group staged in shared memory (K boxes at `kst`, V boxes at
+// `vst`): S = Q K^T on the tensor cores, the online-softmax update of `gs`,
+// and O += P V.  Tokens at or past `end`, and boxes whose bit in `pmask` is
+// clear (page not loaded), are masked.  `ctx` is the sequence's context
+// length (ALiBi positions).
+template <typename T, typename Geo, int D>
+__device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa)[D / 16][4], uint32_t kst,
+                                          uint32_t vst, int tok0, int end, uint32_t pmask, int ctx, float qk_scale,
+                                          bool alibi, float slope_lo, float slope_hi, int lane) {
+  using namespace mma_detail;
+  constexpr int GT = Geo::GT, NBOX = Geo::NBOX, BOX = Geo::BOX, VBS = Geo::VBS;
+  constexpr uint32_t VSW_MASK = Geo::VSWZ ? (uint32_t)(Geo::VSWZ / 16 - 1) : 0u;
+  constexpr int KS = D / 16;
+  constexpr int NT = D / 8;
+  constexpr int ST = GT / 8;
+  constexpr int PK = GT / 16;
+  const int q4 = lane & 3;
+  const bool tail = (tok0 + GT > end) || (pmask != (1u << NBOX) - 1u);
+  (void)KS;
+
+  // ---- S = Q K^T : ST tiles of 8 tokens
+  float sacc[ST][4];
+#pragma unroll
+  for (int j = 0; j < ST; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+#pragma unroll
+  for (int j = 0; j < ST; ++j) {
+    // lane -> matrix (lane >> 3): chunk 2*ks + (lane>>3); row (lane & 7): token 8j + (lane & 7)
+    const int tok = 8 * j + (lane & 7);
+    const int bx = tok / VBS, off = tok % VBS;
+#pragma unroll
+    for (int ks = 0; ks < KS; ks += 2) {
+      const int chunk = 2 * ks + (lane >> 3);
+      const uint32_t addr = kst + bx * BOX + (chunk * VBS + off) * 16;
+      uint32_t b0, b1, b2, b3;
+      ldmatrix_x4(addr, b0, b1, b2, b3);
+      MmaOp<T>::run(sacc[j], qa[ks], b0, b1);
+      MmaOp<T>::run(sacc[j], qa[ks + 1], b2, b3);
+    }
+  }
+
+  // ---- online softmax (log2 domain).  Lane holds tokens 8j + 2*q4 + e.
+  float mx_lo = -INFINITY, mx_hi = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < ST; ++j) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int t = 8 * j + 2 * q4 + e;
+      float x_lo = sacc[j][e] * qk_scale;
+      float x_hi = sacc[j][2 + e] * qk_scale;
+      if (alibi) {
+        const float pos = (float)(tok0 + t - ctx + 1);
+        x_lo += slope_lo * pos;
+        x_hi += slope_hi * pos;
+      }
+      if (tail) {
+        const bool ok = (tok0 + t < end) && ((pmask >> (t / VBS)) & 1u);
+        x_lo = ok ? x_lo : -INFINITY;
+        x_hi = ok ? x_hi : -INFINITY;
+      }
+      sacc[j][e] = x_lo;
+      sacc[j][2 + e] = x_hi;
+      mx_lo = fmaxf(mx_lo, x_lo);
+      mx_hi = fmaxf(mx_hi, x_hi);
+    }
+  }
+  mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
+  mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
+  mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
+  mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
+  const float mn_lo = fmaxf(gs.m_lo, mx_lo), mn_hi = fmaxf(gs.m_hi, mx_hi);
+  // A row whose every token so far is masked keeps max -inf: use 0 as the
+  // reference so exp2 sees -inf - 0 = -inf (never -inf - -inf = NaN).
+  const float ref_lo = mn_lo == -INFINITY ? 0.f : mn_lo;
+  const float ref_hi = mn_hi == -INFINITY ? 0.f : mn_hi;
+  const float a_lo = fast_exp2(gs.m_lo - ref_lo), a_hi = fast_exp2(gs.m_hi - ref_hi);
+  gs.m_lo = mn_lo;
+  gs.m_hi = mn_hi;
+  float ps_lo = 0.f, ps_hi = 0.f;
+#pragma unroll
+  for (int j = 0; j < ST; ++j) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      sacc[j][e] = fast_exp2(sacc[j][e] - ref_lo);
+      sacc[j][2 + e] = fast_exp2(sacc[j][2 + e] - ref_hi);
+      ps_lo += sacc[j][e];
+      ps_hi += sacc[j][2 + e];
+    }
+  }
+  gs.l_lo = gs.l_lo * a_lo + ps_lo;
+  gs.l_hi = gs.l_hi * a_hi + ps_hi;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    gs.o[nt][0] *= a_lo;
+    gs.o[nt][1] *= a_lo;
+    gs.o[nt][2] *= a_hi;
+    gs.o[nt][3] *= a_hi;
+  }
+
+  // ---- O += P V : PK k-steps of 16 tokens x NT tiles of 8 dims
+#pragma unroll
+  for (int kk = 0; kk < PK; ++kk) {
+    // A = P.  bf16 keeps 8 mantissa bits, so P is carried as hi + lo bf16
+    // parts (two products into the same accumulators, ~16 bits of P); f16's
+    // 11 bits are used as they are.
+    uint32_t pa[4], pl[4];
+    MmaOp<T>::pack_split(sacc[2 * kk][0], sacc[2 * kk][1], pa[0], pl[0]);
+    MmaOp<T>::pack_split(sacc[2 * kk][2], sacc[2 * kk][3], pa[1], pl[1]);
+    MmaOp<T>::pack_split(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1], pa[2], pl[2]);
+    MmaOp<T>::pack_split(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3], pa[3], pl[3]);
+    // lane -> matrix mi = lane >> 3: dims 8*(nt + mi/2) + (lane & 7), tokens 16kk + 8*(mi & 1) ..+7
+    const int mi = lane >> 3;
+    const int vtok = 16 * kk + 8 * (mi & 1);
+    const int vbx = vtok / VBS, voff = vtok % VBS;
+    // tokens this lane holds in the B fragments: 16kk + 2*q4 + e (b0/b2) and +8 (b1/b3)
+    const int t_lo = tok0 + 16 * kk + 2 * q4;
+    bool ok_lo0 = true, ok_lo1 = true, ok_hi0 = true, ok_hi1 = true;
+    if (tail) {
+      const int tl = 16 * kk + 2 * q4;
+      ok_lo0 = (t_lo < end) && ((pmask >> (tl / VBS)) & 1u);
+      ok_lo1 = (t_lo + 1 < end) && ((pmask >> ((tl + 1) / VBS)) & 1u);
+      ok_hi0 = (t_lo + 8 < end) && ((pmask >> ((tl + 8) / VBS)) & 1u);
+      ok_hi1 = (t_lo + 9 < end) && ((pmask >> ((tl + 9) / VBS)) & 1u);
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; nt += 2) {
+      const int dim = 8 * (nt + (mi >> 1)) + (lane & 7);
+      // byte offset of (dim, voff) in the V box; with a swizzled box the
+      // 16-byte chunk index (bits 4..) is XORed with address bits 7..
+      uint32_t voffb = (uint32_t)(dim * VBS + voff) * 2;
+      if (VSW_MASK) voffb ^= ((voffb >> 7) & VSW_MASK) << 4;
+      const uint32_t addr = vst + vbx * BOX + voffb;
+      uint32_t b0, b1, b2, b3;
+      ldmatrix_x4(addr, b0, b1, b2, b3);
+      if (tail) {
+        // zero V of masked tokens: their slots may hold anything (NaN * 0 = NaN)
+        const uint32_t m_lo_bits = (ok_lo0 ? 0x0000ffffu : 0u) | (ok_lo1 ? 0xffff0000u : 0u);
+        const uint32_t m_hi_bits = (ok_hi0 ? 0x0000ffffu : 0u) | (ok_hi1 ? 0xffff0000u : 0u);
+        b0 &= m_lo_bits;
+        b2 &= m_lo_bits;
+        b1 &= m_hi_bits;
+        b3 &= m_hi_bits;
+      }
+      MmaOp<T>::run(gs.o[nt], pa, b0, b1);
+      MmaOp<T>::run(gs.o[nt + 1], pa, b2, b3);
+      if constexpr (MmaOp<T>::kSplitP) {
+        MmaOp<T>::run(gs.o[nt], pl, b0, b1);
+        MmaOp<T>::run(gs.o[nt + 1], pl, b2, b3);
+      }
+    }
+  }
+}
+
 template <typename T, int D, int BS, int NW, int STAGES, int GTOK, int MODE>
 __global__ void __launch_bounds__(NW * 32)
     paged_decode_mma_kernel(DecodeParams p, const __grid_constant__ TmaMaps tm) {
   using namespace mma_detail;
   using Geo = MmaGeom<D, BS, NW, STAGES, GTOK, MODE>;
   constexpr int GT = Geo::GT, NBOX = Geo::NBOX, BOX = Geo::BOX, VBS = Geo::VBS;
-  constexpr uint32_t VSW_MASK = Geo::VSWZ ? (uint32_t)(Geo::VSWZ / 16 - 1) : 0u;
   constexpr int KS = D / 16;    // k-steps of Q.K^T
   constexpr int NT = D / 8;     // n-tiles of P.V
-  constexpr int ST = GT / 8;    // 8-token S tiles per group
-  constexpr int PK = GT / 16;   // 16-token k-steps of P.V per group
   extern __shared__ __align__(128) uint8_t smem[];
 
   const int kvh = blockIdx.x, seq = blockIdx.y, part = blockIdx.z;
@@ -350,11 +538,8 @@ __global__ void __launch_bounds__(NW * 32)
     if (s < n_mine) issue(s, s, load_block(s));
   }
 
-  float m_lo = -INFINITY, m_hi = -INFINITY;  // running max (log2 units), rows r / r+8
-  float l_lo = 0.f, l_hi = 0.f;              // this lane's share of the row sums
-  float o[NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+  GroupState<D> gs;
+  gs.reset();
   int k_fail = -1;  // group whose wait gave up
 
   for (int k = 0; k < n_mine; ++k) {
@@ -369,131 +554,8 @@ __global__ void __launch_bounds__(NW * 32)
     const uint32_t vst = smem_u32(st + NBOX * BOX);
     const int tok0 = begin + (warp + k * NW) * GT;  // first token of the group
     const uint32_t pmask = masks[s];
-    const bool tail = (tok0 + GT > end) || (pmask != (1u << NBOX) - 1u);
-
-    // ---- S = Q K^T : ST tiles of 8 tokens
-    float sacc[ST][4];
-#pragma unroll
-    for (int j = 0; j < ST; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
-#pragma unroll
-    for (int j = 0; j < ST; ++j) {
-      // lane -> matrix (lane >> 3): chunk 2*ks + (lane>>3); row (lane & 7): token 8j + (lane & 7)
-      const int tok = 8 * j + (lane & 7);
-      const int bx = tok / VBS, off = tok % VBS;
-#pragma unroll
-      for (int ks = 0; ks < KS; ks += 2) {
-        const int chunk = 2 * ks + (lane >> 3);
-        const uint32_t addr = kst + bx * BOX + (chunk * VBS + off) * 16;
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(addr, b0, b1, b2, b3);
-        MmaOp<T>::run(sacc[j], qa[ks], b0, b1);
-        MmaOp<T>::run(sacc[j], qa[ks + 1], b2, b3);
-      }
-    }
-
-    // ---- online softmax (log2 domain).  Lane holds tokens 8j + 2*q4 + e.
-    float mx_lo = -INFINITY, mx_hi = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < ST; ++j) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int t = 8 * j + 2 * q4 + e;
-        float x_lo = sacc[j][e] * qk_scale;
-        float x_hi = sacc[j][2 + e] * qk_scale;
-        if (p.alibi) {
-          const float pos = (float)(tok0 + t - (int)ctx + 1);
-          x_lo += slope_lo * pos;
-          x_hi += slope_hi * pos;
-        }
-        if (tail) {
-          const bool ok = (tok0 + t < end) && ((pmask >> (t / VBS)) & 1u);
-          x_lo = ok ? x_lo : -INFINITY;
-          x_hi = ok ? x_hi : -INFINITY;
-        }
-        sacc[j][e] = x_lo;
-        sacc[j][2 + e] = x_hi;
-        mx_lo = fmaxf(mx_lo, x_lo);
-        mx_hi = fmaxf(mx_hi, x_hi);
-      }
-    }
-    mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
-    mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
-    mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
-    mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
-    const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
-    // A row whose every token so far is masked keeps max -inf: use 0 as the
-    // reference so exp2 sees -inf - 0 = -inf (never -inf - -inf = NaN).
-    const float ref_lo = mn_lo == -INFINITY ? 0.f : mn_lo;
-    const float ref_hi = mn_hi == -INFINITY ? 0.f : mn_hi;
-    const float a_lo = fast_exp2(m_lo - ref_lo), a_hi = fast_exp2(m_hi - ref_hi);
-    m_lo = mn_lo;
-    m_hi = mn_hi;
-    float ps_lo = 0.f, ps_hi = 0.f;
-#pragma unroll
-    for (int j = 0; j < ST; ++j) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        sacc[j][e] = fast_exp2(sacc[j][e] - ref_lo);
-        sacc[j][2 + e] = fast_exp2(sacc[j][2 + e] - ref_hi);
-        ps_lo += sacc[j][e];
-        ps_hi += sacc[j][2 + e];
-      }
-    }
-    l_lo = l_lo * a_lo + ps_lo;
-    l_hi = l_hi * a_hi + ps_hi;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      o[nt][0] *= a_lo;
-      o[nt][1] *= a_lo;
-      o[nt][2] *= a_hi;
-      o[nt][3] *= a_hi;
-    }
-
-    // ---- O += P V : PK k-steps of 16 tokens x NT tiles of 8 dims
-#pragma unroll
-    for (int kk = 0; kk < PK; ++kk) {
-      uint32_t pa[4];
-      pa[0] = MmaOp<T>::pack(sacc[2 * kk][0], sacc[2 * kk][1]);
-      pa[1] = MmaOp<T>::pack(sacc[2 * kk][2], sacc[2 * kk][3]);
-      pa[2] = MmaOp<T>::pack(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1]);
-      pa[3] = MmaOp<T>::pack(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]);
-      // lane -> matrix mi = lane >> 3: dims 8*(nt + mi/2) + (lane & 7), tokens 16kk + 8*(mi & 1) ..+7
-      const int mi = lane >> 3;
-      const int vtok = 16 * kk + 8 * (mi & 1);
-      const int vbx = vtok / VBS, voff = vtok % VBS;
-      // tokens this lane holds in the B fragments: 16kk + 2*q4 + e (b0/b2) and +8 (b1/b3)
-      const int t_lo = tok0 + 16 * kk + 2 * q4;
-      bool ok_lo0 = true, ok_lo1 = true, ok_hi0 = true, ok_hi1 = true;
-      if (tail) {
-        const int tl = 16 * kk + 2 * q4;
-        ok_lo0 = (t_lo < end) && ((pmask >> (tl / VBS)) & 1u);
-        ok_lo1 = (t_lo + 1 < end) && ((pmask >> ((tl + 1) / VBS)) & 1u);
-        ok_hi0 = (t_lo + 8 < end) && ((pmask >> ((tl + 8) / VBS)) & 1u);
-        ok_hi1 = (t_lo + 9 < end) && ((pmask >> ((tl + 9) / VBS)) & 1u);
-      }
-#pragma unroll
-      for (int nt = 0; nt < NT; nt += 2) {
-        const int dim = 8 * (nt + (mi >> 1)) + (lane & 7);
-        // byte offset of (dim, voff) in the V box; with a swizzled box the
-        // 16-byte chunk index (bits 4..) is XORed with address bits 7..
-        uint32_t voffb = (uint32_t)(dim * VBS + voff) * 2;
-        if (VSW_MASK) voffb ^= ((voffb >> 7) & VSW_MASK) << 4;
-        const uint32_t addr = vst + vbx * BOX + voffb;
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(addr, b0, b1, b2, b3);
-        if (tail) {
-          // zero V of masked tokens: their slots may hold anything (NaN * 0 = NaN)
-          const uint32_t m_lo_bits = (ok_lo0 ? 0x0000ffffu : 0u) | (ok_lo1 ? 0xffff0000u : 0u);
-          const uint32_t m_hi_bits = (ok_hi0 ? 0x0000ffffu : 0u) | (ok_hi1 ? 0xffff0000u : 0u);
-          b0 &= m_lo_bits;
-          b2 &= m_lo_bits;
-          b1 &= m_hi_bits;
-          b3 &= m_hi_bits;
-        }
-        MmaOp<T>::run(o[nt], pa, b0, b1);
-        MmaOp<T>::run(o[nt + 1], pa, b2, b3);
-      }
-    }
+    mma_group<T, Geo, D>(gs, qa, kst, vst, tok0, end, pmask, (int)ctx, qk_scale, p.alibi != nullptr, slope_lo,
+                         slope_hi, lane);
 
     // ---- recycle the stage
     __syncwarp();
@@ -512,10 +574,8 @@ __global__ void __launch_bounds__(NW * 32)
   }
 
   // ---- merge: quad sums of l, then across warps through shared memory.
-  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
-  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
-  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
-  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
+  const float l_lo = gs.quad_sum_lo(), l_hi = gs.quad_sum_hi();
+  const float m_lo = gs.m_lo, m_hi = gs.m_hi;
   __syncthreads();  // every warp is done with its ring
   float* red_o = reinterpret_cast<float*>(smem);          // [NW][16][D]
   float* red_ml = red_o + NW * 16 * D;                     // [NW][16][2] (max, sum)
@@ -524,10 +584,10 @@ __global__ void __launch_bounds__(NW * 32)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int d = 8 * nt + 2 * q4;
-      ow[r * D + d] = o[nt][0];
-      ow[r * D + d + 1] = o[nt][1];
-      ow[(r + 8) * D + d] = o[nt][2];
-      ow[(r + 8) * D + d + 1] = o[nt][3];
+      ow[r * D + d] = gs.o[nt][0];
+      ow[r * D + d + 1] = gs.o[nt][1];
+      ow[(r + 8) * D + d] = gs.o[nt][2];
+      ow[(r + 8) * D + d + 1] = gs.o[nt][3];
     }
     if (q4 == 0) {
       red_ml[(warp * 16 + r) * 2 + 0] = m_lo;

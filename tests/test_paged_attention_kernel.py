@@ -224,6 +224,19 @@ def test_mixed_lengths_and_zero_rows_in_one_batch(gpu):
         assert_close(out, ref, ATOL_NS, RTOL_NS, "mixed")
 
 
+def test_short_bf16_sequences_meet_the_tolerance(gpu):
+    """64 sequences of 1..64 tokens: with few tokens and nearly cancelling V
+    rows the output is sensitive to how P is rounded for the P.V product."""
+    c = cases.paged_batch(2501, "bfloat16", 64, 32, 2, 128, 16, list(range(1, 65)))
+    d = upload_case(c)
+    fill_cache(d)
+    kc, vc = oracle_fill(c, "bfloat16")
+    ref = kv_oracle.paged_attention_v1(c["q"], kc, vc, c["block_tables"], c["context_lens"], 2, c["scale"], 16,
+                                       c["max_seq_len"])
+    for fn in (run_v1, lambda d_, c_: run_v2(d_, c_, partition_size=32)):
+        assert_close(fn(d, c).to_numpy(), ref, ATOL_NS, RTOL_NS, "short bf16")
+
+
 def test_nan_garbage_beyond_context_is_never_used(gpu):
     """Tokens past context_len in the last block hold NaN: they must not leak."""
     c = cases.paged_batch(88, "float16", 2, 8, 2, 128, 16, [20, 40])
