@@ -169,6 +169,31 @@ int kvc_reshape_and_cache_flash(const kvc_dltensor* key, const kvc_dltensor* val
 int kvc_gather_kv(kvc_dltensor* k_out, kvc_dltensor* v_out, const kvc_dltensor* k_buffer,
                   const kvc_dltensor* v_buffer, const kvc_dltensor* indices, void* stream);
 
+/* Replaces `_ext.copy_blocks` (bindings.cpp:97-113, mlx_cache.cpp:302-346,
+ * kernel copy_blocks.metal:9-44): for every layer i and every pair
+ * (src, dst) of block_mapping, block dst of key_caches[i] and value_caches[i]
+ * is overwritten with block src, in place.
+ *   key_caches, value_caches  arrays of num_*_caches tensors, each dense with a
+ *                             leading block dimension (any dtype; K and V of a
+ *                             layer share dtype and elements per block)
+ *   block_mapping             [num_pairs, 2] int32 / uint32 / int64, on the
+ *                             caches' device or in host memory
+ * Pairs run in parallel (a block both written and read by one call gives an
+ * unspecified result, as on Metal).  Out-of-range block ids are skipped and
+ * flagged with KVC_STATUS_INDEX_OOB. */
+int kvc_copy_blocks(kvc_dltensor* key_caches, int num_key_caches, kvc_dltensor* value_caches,
+                    int num_value_caches, const kvc_dltensor* block_mapping, void* stream);
+
+/* Replaces `_ext.swap_blocks` (bindings.cpp:115-123, mlx_cache.cpp:348-370,
+ * kernel copy_blocks.metal:60-75): block dst of `dst` is overwritten with block
+ * src of `src` for every pair.  src and dst are dense with a leading block
+ * dimension, equal dtype and elements per block; each may live on a CUDA device
+ * or in host memory (kDLCPU, or pinned kDLCUDAHost for asynchronous copies).
+ * Device-to-device on one GPU runs a kernel; otherwise one cudaMemcpyAsync per
+ * run of consecutive pairs (out-of-range pairs are then rejected with
+ * KVC_EINVAL before anything is copied). */
+int kvc_swap_blocks(const kvc_dltensor* src, kvc_dltensor* dst, const kvc_dltensor* block_mapping, void* stream);
+
 /* ---- device attributes (paged_attention/mlx_device.cpp) -------------------- */
 /* mlx_device.cpp:16-20: max shared memory per block (opt-in) of `device`. */
 int kvc_get_max_shared_memory_per_block_device_attribute(int device, int64_t* out);

@@ -113,6 +113,29 @@ def pool_fetch(k_buffer, v_buffer, indices):
 
 
 # ---------------------------------------------------------------------------
+# copy_blocks / swap_blocks — copy_blocks.metal:9-75 (host: mlx_cache.cpp:302-370)
+# ---------------------------------------------------------------------------
+def copy_blocks(key_caches, value_caches, block_mapping):
+    """In place, for every layer and pair (src, dst): block dst of the key and
+    value caches := block src (a block is everything behind the leading index,
+    copy_blocks.metal:21-43).  Pairs are applied in order; the kernel runs them
+    in parallel, which agrees whenever no block is both read and written."""
+    pairs = np.asarray(block_mapping, dtype=np.int64).reshape(-1, 2)
+    for kc, vc in zip(key_caches, value_caches):
+        for s, d in pairs:
+            kc[d] = kc[s]
+            vc[d] = vc[s]
+    return key_caches, value_caches
+
+
+def swap_blocks(src, dst, block_mapping):
+    """dst[d] := src[s] for every pair (copy_blocks.metal:60-75); returns dst."""
+    for s, d in np.asarray(block_mapping, dtype=np.int64).reshape(-1, 2):
+        dst[d] = src[s]
+    return dst
+
+
+# ---------------------------------------------------------------------------
 # paged attention decode — paged_attention_kernels.metal:37-168
 # ---------------------------------------------------------------------------
 def gather_seq(key_cache, value_cache, block_table, n_tokens, kv_head):

@@ -8,6 +8,7 @@
 
 #include <atomic>
 #include <string>
+#include <vector>
 
 #include "kvc_tensor.h"
 #include "kvcache.h"
@@ -38,6 +39,7 @@ static ElemType decode_dtype(const kvc_dldtype& d) {
   if (d.code == 0 && d.bits == 32) return ElemType::I32;
   if (d.code == 1 && d.bits == 32) return ElemType::U32;
   if (d.code == 0 && d.bits == 64) return ElemType::I64;
+  if (d.code == 1 && d.bits == 8) return ElemType::U8;
   return ElemType::INVALID;
 }
 
@@ -69,6 +71,7 @@ bool parse(const kvc_dltensor* t, const char* name, View* v) {
   }
   v->data = static_cast<char*>(t->data) + t->byte_offset;
   v->on_cuda = (t->device.device_type == 2 || t->device.device_type == 13);
+  v->on_host = (t->device.device_type == 1 || t->device.device_type == 3);
   v->device = t->device.device_id;
   return true;
 }
@@ -221,6 +224,59 @@ static int prepare_decode(kvc_dltensor* out, const kvc_dltensor* query, const kv
   return KVC_OK;
 }
 
+// block_mapping of copy_blocks / swap_blocks: [num_pairs, 2] of int32, uint32
+// or int64 (mlx_cache.cpp:309-310,356-357 for the shape rule and message).
+static int parse_block_mapping(const kvc_dltensor* t, View* m) {
+  if (!parse(t, "block_mapping", m)) return KVC_EINVAL;
+  if (m->ndim != 2 || m->shape[1] != 2) return fail(KVC_EINVAL, "block_mapping must have shape [num_pairs, 2]");
+  if (m->dtype != ElemType::I32 && m->dtype != ElemType::U32 && m->dtype != ElemType::I64)
+    return fail(KVC_EINVAL, "block_mapping must be int32, uint32 or int64");
+  if (!m->dense_from(0)) return fail(KVC_EINVAL, "block_mapping must be contiguous");
+  if (!m->on_cuda && !m->on_host) return fail(KVC_EINVAL, "block_mapping must live on a CUDA device or the host");
+  return KVC_OK;
+}
+
+// The mapping's pairs as int64 on the host (a device mapping is copied back
+// synchronously; only the host-memory paths need this).
+static int read_block_mapping(const View& m, std::vector<int64_t>* out) {
+  const int64_t n = 2 * m.shape[0];
+  out->resize((size_t)n);
+  std::vector<int32_t> tmp32;
+  const void* src = m.data;
+  if (m.on_cuda) {
+    DeviceGuard g(m.device);
+    if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+    const size_t bytes = (size_t)n * elem_size(m.dtype);
+    if (m.dtype == ElemType::I64) {
+      cudaError_t e = cudaMemcpy(out->data(), m.data, bytes, cudaMemcpyDeviceToHost);
+      if (e != cudaSuccess) return cuda_fail(e, "block_mapping copy");
+      return KVC_OK;
+    }
+    tmp32.resize((size_t)n);
+    cudaError_t e = cudaMemcpy(tmp32.data(), m.data, bytes, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "block_mapping copy");
+    src = tmp32.data();
+  }
+  for (int64_t i = 0; i < n; ++i) {
+    if (m.dtype == ElemType::I64) (*out)[i] = static_cast<const int64_t*>(src)[i];
+    else if (m.dtype == ElemType::U32) (*out)[i] = (int64_t) static_cast<const uint32_t*>(src)[i];
+    else (*out)[i] = static_cast<const int32_t*>(src)[i];
+  }
+  return KVC_OK;
+}
+
+// Pairs for the kernel: a device mapping on the launch device is read by the
+// kernel itself; anything else is handed over as host values.
+static int attach_mapping(const View& m, int device, BlockCopyArgs* a) {
+  a->num_pairs = m.shape[0];
+  if (m.on_cuda && m.device == device && m.dtype != ElemType::U32) {
+    a->device_mapping = m.data;
+    a->mapping_i64 = m.dtype == ElemType::I64;
+    return KVC_OK;
+  }
+  return read_block_mapping(m, &a->host_mapping);
+}
+
 }  // namespace kvc
 
 using namespace kvc;
@@ -238,9 +294,12 @@ int kvc_get_status(int device, uint32_t* flags, int clear) {
   DeviceGuard g(device);
   if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
   cudaError_t e1 = cudaSuccess, e2 = cudaSuccess;
-  unsigned int f = kvc_cache_ops_status(clear, &e1) | kvc_decode_status(clear, &e2);
+  cudaError_t e3 = cudaSuccess;
+  unsigned int f =
+      kvc_cache_ops_status(clear, &e1) | kvc_decode_status(clear, &e2) | kvc_block_ops_status(clear, &e3);
   if (e1 != cudaSuccess) return cuda_fail(e1, "kvc_get_status");
   if (e2 != cudaSuccess) return cuda_fail(e2, "kvc_get_status");
+  if (e3 != cudaSuccess) return cuda_fail(e3, "kvc_get_status");
   *flags = f;
   return KVC_OK;
 }
@@ -339,6 +398,107 @@ int kvc_paged_attention_v2_noalloc(kvc_dltensor* out, const kvc_dltensor* query,
   if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
   cudaError_t e = launch_paged_decode_noalloc(a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "paged_attention_v2_noalloc launch");
+  return KVC_OK;
+}
+
+// ---- copy_blocks / swap_blocks (copy_blocks.metal:9-88, mlx_cache.cpp:302-370) ----
+
+int kvc_copy_blocks(kvc_dltensor* key_caches, int num_key_caches, kvc_dltensor* value_caches,
+                    int num_value_caches, const kvc_dltensor* block_mapping, void* stream) {
+  if (num_key_caches != num_value_caches) return fail(KVC_EINVAL, "key_caches and value_caches size mismatch");
+  View m;
+  if (int rc = parse_block_mapping(block_mapping, &m)) return rc;
+  if (num_key_caches < 0) return fail(KVC_EINVAL, "key_caches and value_caches size mismatch");
+  if (num_key_caches > 0 && (key_caches == nullptr || value_caches == nullptr))
+    return fail(KVC_EINVAL, "key_caches/value_caches is null");
+  // Layers with equal block sizes share launches.
+  std::vector<BlockCopyArgs> groups;
+  int device = -1;
+  for (int i = 0; i < num_key_caches; ++i) {
+    View kc, vc;
+    const std::string kn = "key_caches[" + std::to_string(i) + "]", vn = "value_caches[" + std::to_string(i) + "]";
+    if (!parse(&key_caches[i], kn.c_str(), &kc) || !parse(&value_caches[i], vn.c_str(), &vc)) return KVC_EINVAL;
+    if (kc.ndim == 0 || vc.ndim == 0 || kc.shape[0] == 0 || vc.shape[0] == 0 || kc.shape[0] != vc.shape[0])
+      return fail(KVC_EINVAL, "key/value caches must have matching block counts");
+    if (kc.dtype != vc.dtype || kc.numel() / kc.shape[0] != vc.numel() / vc.shape[0])
+      return fail(KVC_EINVAL, "key/value cache block layouts must match");
+    if (!kc.dense_from(0) || !vc.dense_from(0)) return fail(KVC_EINVAL, "key/value caches must be contiguous");
+    int layer_dev = -1;
+    if (int rc = check_all_cuda({&kc, &vc}, &layer_dev)) return rc;
+    if (device >= 0 && layer_dev != device) return fail(KVC_EINVAL, "all tensors must live on the same CUDA device");
+    device = layer_dev;
+    const int64_t bb = kc.numel() / kc.shape[0] * elem_size(kc.dtype);
+    BlockCopyArgs* g = nullptr;
+    for (auto& x : groups)
+      if (x.block_bytes == bb) g = &x;
+    if (!g) {
+      groups.emplace_back();
+      g = &groups.back();
+      g->block_bytes = bb;
+    }
+    g->planes.push_back({kc.data, kc.data, kc.shape[0], kc.shape[0]});
+    g->planes.push_back({vc.data, vc.data, vc.shape[0], vc.shape[0]});
+  }
+  if (groups.empty() || m.shape[0] == 0) return KVC_OK;
+  if (m.on_cuda && m.device != device) return fail(KVC_EINVAL, "all tensors must live on the same CUDA device");
+  for (auto& g : groups)
+    if (int rc = attach_mapping(m, device, &g)) return rc;
+  DeviceGuard guard(device);
+  if (!guard.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  for (auto& g : groups) {
+    cudaError_t e = launch_block_copies(g, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "copy_blocks launch");
+  }
+  return KVC_OK;
+}
+
+int kvc_swap_blocks(const kvc_dltensor* src, kvc_dltensor* dst, const kvc_dltensor* block_mapping, void* stream) {
+  View s, d;
+  if (!parse(src, "src", &s) || !parse(dst, "dst", &d)) return KVC_EINVAL;
+  if (s.ndim == 0 || d.ndim == 0 || s.shape[0] == 0 || d.shape[0] == 0)
+    return fail(KVC_EINVAL, "src and dst must have a leading block dimension");
+  if (s.dtype != d.dtype || s.numel() / s.shape[0] != d.numel() / d.shape[0])
+    return fail(KVC_EINVAL, "src and dst block layouts must match");
+  View m;
+  if (int rc = parse_block_mapping(block_mapping, &m)) return rc;
+  if (!s.dense_from(0) || !d.dense_from(0)) return fail(KVC_EINVAL, "src and dst must be contiguous");
+  if ((!s.on_cuda && !s.on_host) || (!d.on_cuda && !d.on_host))
+    return fail(KVC_EINVAL, "src and dst must live on a CUDA device or in host memory");
+  if (m.shape[0] == 0) return KVC_OK;
+  const int64_t bb = s.numel() / s.shape[0] * elem_size(s.dtype);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (s.on_cuda && d.on_cuda && s.device == d.device) {
+    BlockCopyArgs a;
+    a.block_bytes = bb;
+    a.planes.push_back({s.data, d.data, s.shape[0], d.shape[0]});
+    if (m.on_cuda && m.device != s.device) return fail(KVC_EINVAL, "all tensors must live on the same CUDA device");
+    if (int rc = attach_mapping(m, s.device, &a)) return rc;
+    DeviceGuard guard(s.device);
+    if (!guard.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+    cudaError_t e = launch_block_copies(a, st);
+    if (e != cudaSuccess) return cuda_fail(e, "swap_blocks launch");
+    return KVC_OK;
+  }
+  // Host memory on either side (or two devices): one cudaMemcpyAsync per run
+  // of consecutive pairs, on the stream's device.
+  std::vector<int64_t> pairs;
+  if (int rc = read_block_mapping(m, &pairs)) return rc;
+  const int64_t n = m.shape[0];
+  for (int64_t i = 0; i < n; ++i) {
+    if (pairs[2 * i] < 0 || pairs[2 * i] >= s.shape[0] || pairs[2 * i + 1] < 0 || pairs[2 * i + 1] >= d.shape[0])
+      return fail(KVC_EINVAL, "block_mapping entry " + std::to_string(i) + " is out of range");
+  }
+  DeviceGuard guard(s.on_cuda ? s.device : (d.on_cuda ? d.device : -1));
+  if (!guard.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  for (int64_t i = 0; i < n;) {
+    int64_t run = 1;
+    while (i + run < n && pairs[2 * (i + run)] == pairs[2 * i] + run && pairs[2 * (i + run) + 1] == pairs[2 * i + 1] + run)
+      ++run;
+    cudaError_t e = cudaMemcpyAsync(d.data + pairs[2 * i + 1] * bb, s.data + pairs[2 * i] * bb, (size_t)(run * bb),
+                                    cudaMemcpyDefault, st);
+    if (e != cudaSuccess) return cuda_fail(e, "swap_blocks copy");
+    i += run;
+  }
   return KVC_OK;
 }
 

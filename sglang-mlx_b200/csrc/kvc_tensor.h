@@ -6,18 +6,20 @@
 #include <stdint.h>
 
 #include <string>
+#include <vector>
 
 #include "kvcache.h"
 
 namespace kvc {
 
-enum class ElemType : int { F32 = 0, F16 = 1, BF16 = 2, I32 = 3, U32 = 4, I64 = 5, INVALID = -1 };
+enum class ElemType : int { F32 = 0, F16 = 1, BF16 = 2, I32 = 3, U32 = 4, I64 = 5, U8 = 6, INVALID = -1 };
 
 inline int elem_size(ElemType t) {
   switch (t) {
     case ElemType::F32: case ElemType::I32: case ElemType::U32: return 4;
     case ElemType::F16: case ElemType::BF16: return 2;
     case ElemType::I64: return 8;
+    case ElemType::U8: return 1;
     default: return 0;
   }
 }
@@ -30,6 +32,7 @@ inline const char* elem_name(ElemType t) {
     case ElemType::I32: return "int32";
     case ElemType::U32: return "uint32";
     case ElemType::I64: return "int64";
+    case ElemType::U8: return "uint8";
     default: return "invalid";
   }
 }
@@ -41,7 +44,8 @@ struct View {
   int64_t shape[8] = {0};
   int64_t strides[8] = {0};  // elements
   int device = -1;
-  bool on_cuda = false;
+  bool on_cuda = false;  // kDLCUDA or kDLCUDAManaged
+  bool on_host = false;  // kDLCPU or kDLCUDAHost (pinned)
 
   int64_t size(int i) const { return shape[i < 0 ? i + ndim : i]; }
   int64_t stride(int i) const { return strides[i < 0 ? i + ndim : i]; }
@@ -130,6 +134,23 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream);
 // Split-K decode with its partials in the library's static scratch array
 // (kvc_paged_attention_v2_noalloc).  `a` carries no workspace pointers.
 cudaError_t launch_paged_decode_noalloc(DecodeArgs a, cudaStream_t stream);
+// Whole-block copies (copy_blocks / swap_blocks).  A plane is one buffer
+// pair; every plane of one launch has the same block size in bytes.
+constexpr int kMaxBlockPlanes = 32;
+struct BlockPlane {
+  const void* src;
+  void* dst;
+  int64_t src_blocks, dst_blocks;
+};
+struct BlockCopyArgs {
+  std::vector<BlockPlane> planes;
+  int64_t block_bytes = 0;
+  int64_t num_pairs = 0;
+  const void* device_mapping = nullptr;  // [num_pairs, 2] on the launch device, or null
+  bool mapping_i64 = false;
+  std::vector<int64_t> host_mapping;     // the pairs, when device_mapping is null
+};
+cudaError_t launch_block_copies(const BlockCopyArgs& a, cudaStream_t stream);
 cudaError_t launch_reshape_and_cache(const ReshapeArgs& a, cudaStream_t stream);
 cudaError_t launch_reshape_and_cache_flash(const ReshapeArgs& a, cudaStream_t stream);
 cudaError_t launch_gather_kv(const GatherArgs& a, cudaStream_t stream);
@@ -139,3 +160,4 @@ cudaError_t launch_gather_kv(const GatherArgs& a, cudaStream_t stream);
 // Host accessors of each translation unit's sticky status word.
 unsigned int kvc_cache_ops_status(int clear, cudaError_t* err);
 unsigned int kvc_decode_status(int clear, cudaError_t* err);
+unsigned int kvc_block_ops_status(int clear, cudaError_t* err);

@@ -51,6 +51,8 @@ SIGNATURES: dict[str, tuple] = {
     "kvc_reshape_and_cache": (_i, [_p, _p, _p, _p, _p, _p]),
     "kvc_reshape_and_cache_flash": (_i, [_p, _p, _p, _p, _p, _p]),
     "kvc_gather_kv": (_i, [_p, _p, _p, _p, _p, _p]),
+    "kvc_copy_blocks": (_i, [_p, _i, _p, _i, _p, _p]),
+    "kvc_swap_blocks": (_i, [_p, _p, _p, _p]),
     "kvc_get_max_shared_memory_per_block_device_attribute": (
         _i,
         [_i, ctypes.POINTER(ctypes.c_int64)],

@@ -63,6 +63,12 @@ class HostBuffer:
             dtypes.storage_dtype(self.dtype)).reshape(self.shape)
         weakref.finalize(self, _lib_ref.kvc_free_host, ctypes.c_void_p(self.ptr))
 
+    def _dltensor(self):
+        """(DLTensor, keepalive) describing this buffer as pinned host memory (kDLCUDAHost)."""
+        from .dlpack import KDL_CUDA_HOST, make_dltensor
+
+        return make_dltensor(self.ptr, self.shape, _contiguous_strides(self.shape), self.dtype, 0, KDL_CUDA_HOST)
+
 
 def _contiguous_strides(shape) -> tuple:
     acc, st = 1, []

@@ -1,9 +1,9 @@
 """DLPack structs (restated from the public DLPack specification) and the
 conversion of Python array objects into `DLTensor*` arguments for libkvcache.
 
-Accepted inputs: this package's DeviceArray (descriptor built directly, no
-capsule), or any object implementing the DLPack protocol (`__dlpack__`,
-e.g. a CUDA torch tensor or a CuPy array).
+Accepted inputs: this package's DeviceArray and HostBuffer (descriptors built
+directly, no capsule), or any object implementing the DLPack protocol
+(`__dlpack__`, e.g. a CUDA torch tensor, a CuPy array or a NumPy array).
 """
 
 from __future__ import annotations
@@ -102,13 +102,16 @@ class _ForeignView:
 
 def as_dltensor(obj, name: str = "tensor"):
     """Returns (ctypes pointer to a DLTensor, keepalive) for `obj`."""
-    from .device_array import DeviceArray
+    from .device_array import DeviceArray, HostBuffer
 
     if obj is None:
         return None, None
     if isinstance(obj, DeviceArray):
         t = obj._dltensor()
         return ctypes.pointer(t), obj
+    if isinstance(obj, HostBuffer):
+        t, keep = obj._dltensor()
+        return ctypes.pointer(t), (obj, keep)
     if hasattr(obj, "__dlpack__"):
         view = _ForeignView(obj)
         return ctypes.pointer(view.managed.dl_tensor), view

@@ -14,6 +14,7 @@ bfloat16 = "bfloat16"
 int32 = "int32"
 uint32 = "uint32"
 int64 = "int64"
+uint8 = "uint8"
 
 # name -> (DLPack code, bits, itemsize, numpy storage dtype)
 _TABLE = {
@@ -23,6 +24,7 @@ _TABLE = {
     int32: (0, 32, 4, np.dtype(np.int32)),
     uint32: (1, 32, 4, np.dtype(np.uint32)),
     int64: (0, 64, 8, np.dtype(np.int64)),
+    uint8: (1, 8, 1, np.dtype(np.uint8)),
 }
 _FROM_DL = {(c, b): n for n, (c, b, _, _) in _TABLE.items()}
 

@@ -19,8 +19,8 @@ import ctypes
 import numpy as np
 
 from . import _lib, dtypes
-from .device_array import DeviceArray, _stream, asarray
-from .dlpack import as_dltensor, describe
+from .device_array import DeviceArray, HostBuffer, _stream, asarray
+from .dlpack import DLTensor, as_dltensor, describe
 
 _L = _lib.lib
 
@@ -232,14 +232,48 @@ def gather_kv(k_buffer, v_buffer, indices, *, k_out=None, v_out=None, stream=Non
     return k_out, v_out
 
 
-def copy_blocks(key_caches, value_caches, block_mapping):
-    """Copy blocks within the cache (metal_kernels.py:77-85)."""
-    raise NotImplementedError("copy_blocks is not part of the B200 hot path yet")
+def _mapping(block_mapping):
+    """A block mapping as an array libkvcache accepts: device arrays and
+    DLPack producers pass through, anything else becomes a host int64 array."""
+    if isinstance(block_mapping, DeviceArray) or hasattr(block_mapping, "__dlpack__"):
+        if isinstance(block_mapping, np.ndarray):
+            return np.ascontiguousarray(block_mapping)
+        return block_mapping
+    return np.ascontiguousarray(np.asarray(block_mapping, dtype=np.int64))
 
 
-def swap_blocks(src, dst, block_mapping):
-    """Blit blocks between two buffers (metal_kernels.py:88-96)."""
-    raise NotImplementedError("swap_blocks is not part of the B200 hot path yet")
+def copy_blocks(key_caches, value_caches, block_mapping, *, stream=None):
+    """Copy blocks within the cache (metal_kernels.py:77-85): for every layer and
+    every pair (src, dst) of `block_mapping` ([num_pairs, 2]), block dst of the
+    layer's key and value caches is overwritten with block src.  The caches are
+    updated in place; returns (key_caches, value_caches) as the reference does."""
+    keys, vals = [_dev(x) for x in key_caches], [_dev(x) for x in value_caches]
+    kd = [as_dltensor(x, f"key_caches[{i}]") for i, x in enumerate(keys)]
+    vd = [as_dltensor(x, f"value_caches[{i}]") for i, x in enumerate(vals)]
+    karr = (DLTensor * max(1, len(kd)))(*[p.contents for p, _ in kd])
+    varr = (DLTensor * max(1, len(vd)))(*[p.contents for p, _ in vd])
+    m, mkeep = as_dltensor(_mapping(block_mapping), "block_mapping")
+    _lib.check(_L.kvc_copy_blocks(ctypes.cast(karr, ctypes.c_void_p), len(kd), ctypes.cast(varr, ctypes.c_void_p),
+                                  len(vd), m, _stream(stream)))
+    del kd, vd, mkeep
+    return keys, vals
+
+
+def swap_blocks(src, dst, block_mapping, *, stream=None):
+    """Blit blocks between two buffers (metal_kernels.py:88-96): block dst of
+    `dst` is overwritten with block src of `src` for every pair.  Either side
+    may be device memory or host memory (a HostBuffer, pinned, or a NumPy
+    array); returns `dst`, updated in place."""
+    def side(x):
+        return x if isinstance(x, (HostBuffer, np.ndarray)) else _dev(x)
+
+    dst = side(dst)
+    s, skeep = as_dltensor(side(src), "src")
+    d, dkeep = as_dltensor(dst, "dst")
+    m, mkeep = as_dltensor(_mapping(block_mapping), "block_mapping")
+    _lib.check(_L.kvc_swap_blocks(s, d, m, _stream(stream)))
+    del skeep, dkeep, mkeep
+    return dst
 
 
 def get_max_shared_memory_per_block_device_attribute(device_id: int = 0) -> int:

@@ -188,3 +188,49 @@ def test_python_shim_raises_value_error_with_reference_text():
     with pytest.raises(ValueError, match="is null"):
         _lib.check(_lib.KVC_EINVAL)
     assert metal_kernels.use_split_k(1, 8, 131072) and not metal_kernels.use_split_k(256, 8, 4096)
+
+
+# ---- copy_blocks / swap_blocks argument checks (mlx_cache.cpp:306-359 messages) ----
+
+def _layers(*shapes, dtype="float16"):
+    arr = (dlpack.DLTensor * max(1, len(shapes)))(*[fake(sh, dtype).contents for sh in shapes])
+    return ctypes.cast(arr, ctypes.c_void_p), arr
+
+
+def test_copy_blocks_rejects_layer_count_mismatch():
+    k, _ka = _layers((4, 6))
+    v, _va = _layers((4, 6), (4, 6))
+    expect(_lib.lib.kvc_copy_blocks(k, 1, v, 2, fake((1, 2), "int64"), None), "key_caches and value_caches size mismatch")
+
+
+def test_copy_blocks_rejects_mapping_shape():
+    k, _ka = _layers((4, 6))
+    v, _va = _layers((4, 6))
+    expect(_lib.lib.kvc_copy_blocks(k, 1, v, 1, fake((2, 3), "int64"), None), "block_mapping must have shape [num_pairs, 2]")
+
+
+def test_copy_blocks_rejects_block_count_mismatch():
+    k, _ka = _layers((4, 6))
+    v, _va = _layers((5, 6))
+    expect(_lib.lib.kvc_copy_blocks(k, 1, v, 1, fake((1, 2), "int64"), None), "key/value caches must have matching block counts")
+
+
+def test_copy_blocks_rejects_block_layout_mismatch():
+    k, _ka = _layers((4, 6))
+    v, _va = _layers((4, 8))
+    expect(_lib.lib.kvc_copy_blocks(k, 1, v, 1, fake((1, 2), "int64"), None), "key/value cache block layouts must match")
+
+
+def test_swap_blocks_rejects_missing_block_dim():
+    expect(_lib.lib.kvc_swap_blocks(fake(()), fake((4, 6)), fake((1, 2), "int64"), None),
+           "src and dst must have a leading block dimension")
+
+
+def test_swap_blocks_rejects_layout_mismatch():
+    expect(_lib.lib.kvc_swap_blocks(fake((4, 6)), fake((4, 6), "float32"), fake((1, 2), "int64"), None),
+           "src and dst block layouts must match")
+
+
+def test_swap_blocks_rejects_mapping_shape():
+    expect(_lib.lib.kvc_swap_blocks(fake((4, 6)), fake((4, 6)), fake((2,), "int64"), None),
+           "block_mapping must have shape [num_pairs, 2]")

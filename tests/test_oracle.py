@@ -133,3 +133,28 @@ def test_bf16_rounding_is_nearest_even():
     # 1 + 2^-8 is a tie between 1 and 1 + 2^-7: rounds to even (1.0)
     assert back[1] == 1.0 and back[3] == np.float32(1.015625)
     assert np.isinf(back[5])
+
+
+def test_copy_blocks_oracle_matches_reference_test():
+    """test_paged_attention_kernel.py:400-425 restated on the oracle."""
+    keys = [np.arange(24, dtype=np.float32).reshape(4, 2, 3) + layer * 100 for layer in range(2)]
+    vals = [k + 1000 for k in keys]
+    before_k = [k.copy() for k in keys]
+    before_v = [v.copy() for v in vals]
+    kv_oracle.copy_blocks(keys, vals, [[0, 2], [1, 3]])
+    for layer in range(2):
+        ek, ev = before_k[layer].copy(), before_v[layer].copy()
+        ek[2], ek[3] = before_k[layer][0], before_k[layer][1]
+        ev[2], ev[3] = before_v[layer][0], before_v[layer][1]
+        np.testing.assert_array_equal(keys[layer], ek)
+        np.testing.assert_array_equal(vals[layer], ev)
+
+
+def test_swap_blocks_oracle_matches_reference_test():
+    """test_paged_attention_kernel.py:427-438 restated on the oracle."""
+    src = np.arange(24, dtype=np.float32).reshape(4, 2, 3)
+    dst = np.full((4, 2, 3), -1, dtype=np.float32)
+    expected = dst.copy()
+    expected[2] = src[0]
+    expected[1] = src[3]
+    np.testing.assert_array_equal(kv_oracle.swap_blocks(src, dst, [[0, 2], [3, 1]]), expected)
