@@ -76,12 +76,14 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
-def decode_bytes(tables, lens_after, hq, hkv, d, bs, shared: bool, s=2):
+def decode_bytes(tables, lens_after, hq, hkv, d, bs, shared: bool, s=2, s_kv=None):
     """Algorithmic bytes of one decode launch: K/V read (distinct blocks once when
     blocks are shared), q read, output write, table entries, lengths.  Also
-    returns the logical K/V bytes (every sequence's tokens counted)."""
-    logical = int(np.sum(lens_after)) * hkv * d * s * 2
-    kv = cases.unique_kv_bytes(tables, lens_after, hkv, d, bs, s) if shared else logical
+    returns the logical K/V bytes (every sequence's tokens counted).  `s_kv` is
+    the cache element size (1 for FP8 caches), `s` that of q and out."""
+    s_kv = s if s_kv is None else s_kv
+    logical = int(np.sum(lens_after)) * hkv * d * s_kv * 2
+    kv = cases.unique_kv_bytes(tables, lens_after, hkv, d, bs, s_kv) if shared else logical
     qo = len(lens_after) * hq * d * (s + s)
     tab = int(np.sum(-(-np.asarray(lens_after) // bs))) * 4 + len(lens_after) * 4
     return kv + qo + tab, logical
@@ -279,14 +281,38 @@ def run_ours(args, rank, world, local_rank):
     slots = np.concatenate([pre, w["decode_slots"][plan.seqs]]).astype(np.int32)
     T_new = len(slots)
     shared = args.config == 4
+    pool = args.layout == "pool"
+    fp8 = args.kv_dtype.startswith("fp8")
+    fmt = args.kv_dtype[4:] if fp8 else None
+    if fp8 and (pool or args.decode == "cascade"):
+        raise SystemExit("--kv-dtype fp8 runs on the paged layout with the single-pass / split-K decode")
+    if pool:
+        # MHATokenPool layout: block b's tokens are slots b*BS+1 .. b*BS+BS (slot 0 is
+        # the pool's padding slot); the block tables become per-token slot lists
+        t = np.arange(tables.shape[1] * BS)
+        blk = tables[:, t // BS].astype(np.int64)
+        tables = np.ascontiguousarray(np.where(blk >= 0, blk * BS + t % BS + 1, 0).astype(np.int32))
+        slots = (slots.astype(np.int64) + 1).astype(np.int32)
+    tab_bs = 1 if pool else BS
 
     g = torch.Generator(device=tdev)
     g.manual_seed(1234 + rank)
     tdt = torch.bfloat16
     kc_t, vc_t, kc, vc = [], [], [], []
     for _ in range(L):
-        k = torch.randn((num_blocks, hkv, D // 8, BS, 8), generator=g, device=tdev, dtype=tdt)
-        v = torch.randn((num_blocks, hkv, D, BS), generator=g, device=tdev, dtype=tdt)
+        if pool:
+            k = torch.randn((num_blocks * BS + 1, hkv, D), generator=g, device=tdev, dtype=tdt)
+            v = torch.randn((num_blocks * BS + 1, hkv, D), generator=g, device=tdev, dtype=tdt)
+        elif fp8:
+            # finite codes only (exponent field below all-ones), random sign
+            top = 0x78 if fmt == "e4m3" else 0x7C
+            k = (torch.randint(0, top, (num_blocks, hkv, D // 16, BS, 16), generator=g, device=tdev, dtype=torch.int32)
+                 | (torch.randint(0, 2, (1,), generator=g, device=tdev, dtype=torch.int32) << 7)).to(torch.uint8)
+            v = (torch.randint(0, top, (num_blocks, hkv, D, BS), generator=g, device=tdev, dtype=torch.int32)
+                 | (torch.randint(0, 2, (1,), generator=g, device=tdev, dtype=torch.int32) << 7)).to(torch.uint8)
+        else:
+            k = torch.randn((num_blocks, hkv, D // 8, BS, 8), generator=g, device=tdev, dtype=tdt)
+            v = torch.randn((num_blocks, hkv, D, BS), generator=g, device=tdev, dtype=tdt)
         kc_t.append(k)
         vc_t.append(v)
         kc.append(DeviceArray.from_dlpack(k))
@@ -305,19 +331,47 @@ def run_ours(args, rank, world, local_rank):
     scale = 1.0 / math.sqrt(D)
 
     # decode form: config 3 fixes 512-token partitions; otherwise the shim's heuristic
-    psize = cfg["partition"] or mk.choose_decode(B, hkv, max_seq_len, BS)
+    # (the token-pool kernel runs 16-token groups, two CTAs per SM)
+    psize = cfg["partition"] or mk.choose_decode(B, hkv, max_seq_len, 16 if pool else BS)
     if args.decode == "v1":
         psize = 0
     elif args.decode == "v2":
         psize = args.partition or psize or 512
     if args.partition and psize:
         psize = args.partition
+    # config 4 is a radix-cache hit: every table starts with the same prefix, which
+    # the serving stack knows, so the default decode is the shared-prefix (cascade) one
+    cascade = (args.decode == "cascade" or (args.decode == "auto" and shared)) and not pool
+    if cascade:
+        prefix = cfg["prefix"]
+        pp, pt = mk.cascade_partitions(B, hq, hkv, max_seq_len, prefix, BS)
+        pp, pt = args.partition_prefix or pp, args.partition or pt
+        cws = mk.cascade_workspace(B, hq, D, max_seq_len, prefix, pp, pt, dev)
+        psize = 0
     split = psize > 0
     ws = mk.splitk_workspace(B, hq, D, max_seq_len, psize, dev) if split else None
     torch.cuda.synchronize()
     st = Stream()  # all work of the step runs on this stream (graph-capturable)
 
+    def append(i):
+        if fp8:
+            return mk.reshape_and_cache_fp8(kn[i], vn[i], kc[i], vc[i], slots_d, 0.05, 0.05, fmt, stream=st)
+        if pool:
+            return mk.reshape_and_cache_flash(kn[i], vn[i], kc[i], vc[i], slots_d, stream=st)
+        return mk.reshape_and_cache(kn[i], vn[i], kc[i], vc[i], slots_d, stream=st)
+
     def decode(i):
+        if fp8:
+            return mk.paged_attention_fp8(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, BS, max_seq_len,
+                                          k_scale=0.05, v_scale=0.05, fp8_format=fmt, partition_size=psize,
+                                          workspace=ws, out=out[i], stream=st)
+        if cascade:
+            return mk.paged_attention_cascade(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, BS, max_seq_len, prefix,
+                                              prefix_partition_size=pp, partition_size=pt, workspace=cws, out=out[i],
+                                              stream=st)
+        if pool:
+            return mk.paged_attention_flash(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, 1, max_seq_len,
+                                            partition_size=psize, workspace=ws, out=out[i], stream=st)
         if split:
             return mk.paged_attention_v2(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, BS, max_seq_len,
                                          partition_size=psize, workspace=ws, out=out[i], stream=st)
@@ -326,7 +380,7 @@ def run_ours(args, rank, world, local_rank):
 
     def step(ev=None):
         for i in range(L):
-            mk.reshape_and_cache(kn[i], vn[i], kc[i], vc[i], slots_d, stream=st)
+            append(i)
             if ev is not None:
                 ev[i][0].record(st)
             decode(i)
@@ -416,7 +470,7 @@ def run_ours(args, rank, world, local_rank):
                 q[i].copy_from_host(h_q[i], stream=st)
                 kn[i].copy_from_host(h_k[i], stream=st)
                 vn[i].copy_from_host(h_v[i], stream=st)
-                mk.reshape_and_cache(kn[i], vn[i], kc[i], vc[i], slots_d, stream=st)
+                append(i)
                 decode(i)
                 out[i].copy_to_host(h_o[i], stream=st)
 
@@ -440,7 +494,7 @@ def run_ours(args, rank, world, local_rank):
     step_ms = total_ms / args.steps
     e2e_step_ms = e2e_ms / args.steps
     mean_dec_ms = float(np.mean(dec_ms))
-    alg, logical = decode_bytes(tables, lens_after, hq, hkv, D, BS, shared)
+    alg, logical = decode_bytes(tables, lens_after, hq, hkv, D, tab_bs, shared, s_kv=1 if fp8 else 2)
     sums = np.array([float(alg), float(logical), float(h2d), float(d2h)])
     if dist is not None:
         t = torch.tensor([step_ms, e2e_step_ms, mean_dec_ms], dtype=torch.float64)
@@ -454,10 +508,18 @@ def run_ours(args, rank, world, local_rank):
     alg_all, logical_all, h2d_all, d2h_all = sums
     peak, peak_kind = load_peaks()
     traffic = (TRAFFIC_PER_LAUNCH.get(args.config)
-               if (world == 1 and not (args.layers or args.batch or args.kv_heads)) else None)
+               if (world == 1 and not pool and not cascade and not fp8 and not (args.layers or args.batch or args.kv_heads))
+               else None)
     achieved = alg / (mean_dec_ms * 1e-3) / 1e9
     toks = B_all / (step_ms * 1e-3)
     kernel = f"split-K v2, {psize}-token partitions" if split else "paged_attention_v1"
+    if pool:
+        kernel = "token-pool decode (paged_attention_flash, slot lists" + (
+            f", {psize}-token partitions)" if split else ", single pass)")
+    if fp8:
+        kernel = f"FP8 ({fmt}) cache decode, " + (f"{psize}-token partitions" if split else "single pass")
+    if cascade:
+        kernel = f"shared-prefix cascade ({prefix}-token prefix in {pp}-token chunks, tail partitions of {pt})"
     extra = {"kernel": kernel, "launch": "one CUDA graph per step (decode timing from an eager pass)" if graph is not None else "eager",
              "l2": ("flushed between steps (unique KV fits in L2)" if flush is not None else
                     f"inputs larger than L2 (KV per layer {logical_all / 1e9:.2f} GB); no flush")}
@@ -472,7 +534,7 @@ def run_ours(args, rank, world, local_rank):
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "bf16",
+        "dtype": f"{args.kv_dtype} cache, f16 products" if fp8 else "bf16",
         "data": "synthetic",
         "config": config_json(cfg, args, world, extra),
         "kv_gbs": L * alg_all / (step_ms * 1e-3) / 1e9,
@@ -491,7 +553,9 @@ def run_ours(args, rank, world, local_rank):
         line["roofline"]["note"] = "achieved counts each shared prefix block once (unique bytes)"
     if len(w["prefill_slots"]):
         line["prefill_tokens_per_s"] = len(w["prefill_slots"]) / (step_ms * 1e-3)
-    if not args.no_cpu_baseline and world == 1:
+    if pool:
+        extra["layout"] = "MHATokenPool buffers [slots, kv_heads, head_dim], slot-list tables"
+    if not args.no_cpu_baseline and world == 1 and not pool:
         n_seq = min(8, B)
         blocks, t2 = compact_sample(tables, lens_after, BS, n_seq)
 
@@ -518,9 +582,16 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=sorted(cases.BASELINE))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
-    ap.add_argument("--decode", default="auto", choices=["auto", "v1", "v2"],
-                    help="decode form: the shim's choice (default), single pass, or split-K")
+    ap.add_argument("--kv-dtype", default="bf16", choices=["bf16", "fp8-e4m3", "fp8-e5m2"],
+                    help="cache element type: bf16 (default) or one-byte FP8 codes (half the KV bytes)")
+    ap.add_argument("--layout", default="paged", choices=["paged", "pool"],
+                    help="cache layout: the vLLM paged layout (default) or the MHATokenPool token pool")
+    ap.add_argument("--decode", default="auto", choices=["auto", "v1", "v2", "cascade"],
+                    help="decode form: the shim's choice (default; shared-prefix cascade for config 4), single pass, "
+                         "split-K, or cascade")
     ap.add_argument("--partition", type=int, default=0, help="split-K partition size (tokens) when split")
+    ap.add_argument("--partition-prefix", type=int, default=0,
+                    help="cascade: shared-prefix chunk size (tokens); default from cascade_partitions")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (profiling cases only)")
     ap.add_argument("--batch", type=int, default=0, help="override the batch (profiling cases only)")
     ap.add_argument("--kv-heads", type=int, default=0,

@@ -67,6 +67,7 @@ typedef struct {
 #define KVC_STATUS_BLOCK_OOB 0x2u   /* a block-table entry beyond the cache was skipped */
 #define KVC_STATUS_WAIT_TIMEOUT 0x4u /* a bounded pipeline wait gave up */
 #define KVC_STATUS_INDEX_OOB 0x8u   /* a gather/copy index beyond its buffer was skipped */
+#define KVC_STATUS_PREFIX_MISMATCH 0x10u /* a sequence's table did not start with the shared prefix blocks */
 
 /* ---- errors / info --------------------------------------------------------- */
 /* Thread-local message of the last failing call ("" if none). */
@@ -111,6 +112,47 @@ int kvc_paged_attention_v2(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltens
                            const kvc_dltensor* block_tables, const kvc_dltensor* context_lens,
                            int num_kv_heads, float scale, int block_size, int max_seq_len,
                            const kvc_dltensor* alibi_slopes, int partition_size, void* stream);
+
+/* Paged decode over token-major caches: the reshape_and_cache_flash layout
+ * [num_blocks, block_size, num_kv_heads, head_size], or the MHATokenPool
+ * buffers [slots, num_kv_heads, head_size] (pool_size + 1 slots, slot 0 the
+ * padding slot) with block_size 1, where a block table row is the sequence's
+ * slot list.  This is the decode the reference leaves as a TODO over its pool
+ * (memory_pool.py:110-112: attention straight on scattered pool slots instead
+ * of the per-layer gather behind PooledKVCache.update_and_fetch,
+ * memory_pool.py:206-234).  Same math and edge rules as
+ * kvc_paged_attention_v1; partition_size 0 runs the single pass, otherwise
+ * exp_sums / max_logits / tmp_out are the split-K workspace of
+ * kvc_paged_attention_v2.  float16/bfloat16 query and caches of one dtype,
+ * head_size 64 or 128, up to 16 query heads per KV head (else
+ * KVC_EUNSUPPORTED); token rows must start on 16-byte boundaries. */
+int kvc_paged_attention_flash(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltensor* max_logits,
+                              kvc_dltensor* tmp_out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                              const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                              const kvc_dltensor* context_lens, int num_kv_heads, float scale, int block_size,
+                              int max_seq_len, const kvc_dltensor* alibi_slopes, int partition_size, void* stream);
+
+/* Shared-prefix ("cascade") decode.  No counterpart in the reference; the
+ * workload is BASELINE config 4 (a radix-cache hit shared by a whole batch,
+ * radix_cache.py).  Precondition: the first shared_prefix_len / block_size
+ * entries of every row of block_tables equal those of row 0 (checked on the
+ * device: a sequence that breaks it sets KVC_STATUS_PREFIX_MISMATCH and its
+ * output is not meaningful).  The prefix is attended once per KV head for all
+ * sequences (chunks of prefix_partition_size tokens), the tokens after it by
+ * split-K partitions of partition_size tokens, and a log-sum-exp reduce merges
+ * them; sequences shorter than the prefix attend to their own length only.
+ * Result = kvc_paged_attention_v1 on the same inputs, within floating-point
+ * reassociation.  Workspace as kvc_paged_attention_v2 with
+ * P = ceil(shared_prefix_len / prefix_partition_size)
+ *   + ceil((max_seq_len - shared_prefix_len) / partition_size).
+ * float16/bfloat16 query and cache of one dtype, head_size 64 or 128, up to 16
+ * query heads per KV head, no ALiBi (else KVC_EUNSUPPORTED). */
+int kvc_paged_attention_cascade(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltensor* max_logits,
+                                kvc_dltensor* tmp_out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                                const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                                const kvc_dltensor* context_lens, int num_kv_heads, float scale, int block_size,
+                                int max_seq_len, const kvc_dltensor* alibi_slopes, int shared_prefix_len,
+                                int prefix_partition_size, int partition_size, void* stream);
 
 /* Split-K decode for callers that cannot allocate device memory.  No
  * counterpart in the reference: sglang-mlx has no split-K decode at all.
@@ -193,6 +235,45 @@ int kvc_copy_blocks(kvc_dltensor* key_caches, int num_key_caches, kvc_dltensor* 
  * run of consecutive pairs (out-of-range pairs are then rejected with
  * KVC_EINVAL before anything is copied). */
 int kvc_swap_blocks(const kvc_dltensor* src, kvc_dltensor* dst, const kvc_dltensor* block_mapping, void* stream);
+
+/* ---- FP8 (one-byte) KV cache ----------------------------------------------
+ * The reference ships FP8 codecs (float8.metal:13-125) and an elementwise
+ * converter (convert_fp8.metal:13-80) but no cache kernel stores one-byte
+ * values (memory_pool.py:85, TODO(quant)).  Here the codes live in uint8
+ * caches of the vLLM layout with x = 16: K [num_blocks, H, D/16, bs, 16],
+ * V [num_blocks, H, D, bs]; a value is stored as encode(x / scale) and reads
+ * back as decode(code) * scale, with one scale for K and one for V.
+ * fp8_format 0 = E4M3 as float8.metal defines it (all-ones exponent kept for
+ * Inf/NaN, largest finite 240), 1 = E5M2.  Encoding rounds to nearest even,
+ * saturates to +-Inf past the largest finite value and underflows gradually
+ * (the behaviour float8.metal:65-68 states; its code sends exponents past the
+ * last finite one down the subnormal branch and drops a subnormal's carry into
+ * the smallest normal, which this encoder does not). */
+
+/* reshape_and_cache into one-byte caches; key/value f32/f16/bf16, head_size a
+ * multiple of 16, slot < 0 skips the token. */
+int kvc_reshape_and_cache_fp8(const kvc_dltensor* key, const kvc_dltensor* value, kvc_dltensor* key_cache,
+                              kvc_dltensor* value_cache, const kvc_dltensor* slot_mapping, float k_scale,
+                              float v_scale, int fp8_format, void* stream);
+
+/* Decode over one-byte caches: kvc_paged_attention_v1 semantics on the
+ * dequantised cache (f16/bf16 query, head_size 64 or 128, block_size 8/16/32,
+ * up to 16 query heads per KV head).  partition_size 0 runs the single pass,
+ * otherwise exp_sums / max_logits / tmp_out are the split-K workspace of
+ * kvc_paged_attention_v2.  The codes are converted to f16 in registers (exact)
+ * and the products run as f16 with fp32 accumulation; k_scale scales the
+ * logits and v_scale the output. */
+int kvc_paged_attention_fp8(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltensor* max_logits,
+                            kvc_dltensor* tmp_out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                            const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                            const kvc_dltensor* context_lens, int num_kv_heads, float scale, int block_size,
+                            int max_seq_len, const kvc_dltensor* alibi_slopes, float k_scale, float v_scale,
+                            int fp8_format, int partition_size, void* stream);
+
+/* convert_fp8_kernel (convert_fp8.metal:13-80) on dense arrays of one shape:
+ * float -> uint8 quantises (encode(x / scale)), uint8 -> float dequantises
+ * (decode(code) * scale), uint8 -> uint8 rescales, float -> float scales. */
+int kvc_convert_fp8(kvc_dltensor* dst, const kvc_dltensor* src, float scale, int fp8_format, void* stream);
 
 /* ---- device attributes (paged_attention/mlx_device.cpp) -------------------- */
 /* mlx_device.cpp:16-20: max shared memory per block (opt-in) of `device`. */

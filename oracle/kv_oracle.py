@@ -113,6 +113,90 @@ def pool_fetch(k_buffer, v_buffer, indices):
 
 
 # ---------------------------------------------------------------------------
+# FP8 codecs — float8.metal:13-125 (used by convert_fp8.metal:13-80)
+# ---------------------------------------------------------------------------
+def fp8_to_float(v, fmt: str = "e4m3"):
+    """Decodes uint8 codes (float8.metal:13-63).  Both formats keep the
+    all-ones exponent for Inf (mantissa 0) and NaN, IEEE style: E4M3's largest
+    finite value is 240 here, not OCP E4M3FN's 448."""
+    v = np.asarray(v, dtype=np.uint8).astype(np.int64)
+    eb, mb, bias = (4, 3, 7) if fmt == "e4m3" else (5, 2, 15)
+    s = v >> 7
+    e = (v >> mb) & ((1 << eb) - 1)
+    m = v & ((1 << mb) - 1)
+    sub = np.ldexp(m / float(1 << mb), 1 - bias)
+    nor = np.ldexp(1.0 + m / float(1 << mb), e - bias)
+    out = np.where(e == 0, sub, nor)
+    top = e == (1 << eb) - 1
+    out = np.where(top, np.where(m == 0, np.inf, np.nan), out)
+    return np.where(s == 1, -out, out).astype(np.float32)
+
+
+def float_to_fp8(f, fmt: str = "e4m3"):
+    """Encodes float32 values with the behaviour float8.metal:65-68 states:
+    round to nearest even in the normal range, saturation to Inf above the
+    last finite exponent, NaN kept, gradual underflow (the shifted mantissa
+    rounded half up, as :110-117 does).  Two departures from the code of
+    :69-118, both outside its stated behaviour: values whose exponent is past
+    the last finite one go down its subnormal branch there (garbage codes)
+    and are saturated to Inf here; a subnormal that rounds up to the smallest
+    normal keeps the carry here (the code masks it away and returns zero)."""
+    eb, mb, bias = (4, 3, 7) if fmt == "e4m3" else (5, 2, 15)
+    bits = np.ascontiguousarray(np.asarray(f, dtype=np.float32)).view(np.uint32).astype(np.int64)
+    s = bits >> 31
+    a = bits & 0x7FFFFFFF
+    top = ((1 << eb) - 1) << mb
+    e = ((a >> 23) & 0xFF) - 127
+    m = a & 0x7FFFFF
+    exp_max = (1 << eb) - 2
+    ef = e + bias
+    shift = 23 - mb
+    mant = m >> shift
+    lsb = mant & 1
+    rnd = (m >> (shift - 1)) & 1
+    sticky = (m & ((1 << (shift - 1)) - 1)) != 0
+    mant = mant + (rnd & (sticky | lsb))
+    carry = (mant >> mb) != 0
+    ef_n = np.where(carry, ef + 1, ef)
+    mant = np.where(carry, 0, mant)
+    normal = np.where(ef_n > exp_max, (s << 7) | top, (s << 7) | (ef_n << mb) | (mant & ((1 << mb) - 1)))
+    rshift = np.clip((1 - ef) + (23 - mb), 1, 62)
+    rounded = ((0x800000 | m) + (np.int64(1) << (rshift - 1))) >> rshift
+    sub = np.where((ef < 1 - mb) | (rounded == 0), s << 7, (s << 7) | rounded)  # rounded <= 1 << mb
+    out = np.where(ef > exp_max, (s << 7) | top, np.where(ef >= 1, normal, sub))
+    nan_inf = a >= 0x7F800000
+    out = np.where(nan_inf, (s << 7) | top | (a != 0x7F800000), out)
+    return out.astype(np.uint8)
+
+
+def quantize(x, scale: float, fmt: str = "e4m3"):
+    """Higher precision -> FP8: encode(x / scale) (convert_fp8.metal:33-36)."""
+    return float_to_fp8(np.asarray(x, dtype=np.float32) / np.float32(scale), fmt)
+
+
+def dequantize(q, scale: float, fmt: str = "e4m3"):
+    """FP8 -> float: decode(q) * scale (convert_fp8.metal:28-31)."""
+    return fp8_to_float(q, fmt) * np.float32(scale)
+
+
+def reshape_and_cache_fp8(key, value, key_cache, value_cache, slot_mapping, k_scale, v_scale, fmt="e4m3"):
+    """Quantising append into uint8 caches of the vLLM layout with x = 16 (the
+    index math of reshape_and_cache.metal:41-65 on quantize(x, scale) codes)."""
+    kq = quantize(np.asarray(key, dtype=np.float32), k_scale, fmt)
+    vq = quantize(np.asarray(value, dtype=np.float32), v_scale, fmt)
+    return reshape_and_cache(kq, vq, key_cache, value_cache, slot_mapping)
+
+
+def paged_attention_fp8(query, key_cache, value_cache, block_tables, context_lens, num_kv_heads, scale, block_size,
+                        max_seq_len, k_scale, v_scale, fmt="e4m3", alibi_slopes=None):
+    """paged_attention_v1 (float64) over the dequantised one-byte caches."""
+    kc = dequantize(key_cache, k_scale, fmt)
+    vc = dequantize(value_cache, v_scale, fmt)
+    return paged_attention_v1(query, kc, vc, block_tables, context_lens, num_kv_heads, scale, block_size,
+                              max_seq_len, alibi_slopes)
+
+
+# ---------------------------------------------------------------------------
 # copy_blocks / swap_blocks — copy_blocks.metal:9-75 (host: mlx_cache.cpp:302-370)
 # ---------------------------------------------------------------------------
 def copy_blocks(key_caches, value_caches, block_mapping):
@@ -192,6 +276,40 @@ def paged_attention_v1(query, key_cache, value_cache, block_tables, context_lens
             continue
         for kvh in range(num_kv_heads):
             k, v = gather_seq(key_cache, value_cache, block_tables[b], C, kvh)
+            hs = slice(kvh * G, (kvh + 1) * G)
+            slope = 0.0 if alibi_slopes is None else np.asarray(alibi_slopes, dtype=np.float64)[hs]
+            out[b, hs] = attend(q[b, hs], k, v, scale, slope, C)
+    return out
+
+
+def gather_seq_flash(key_cache, value_cache, block_table, n_tokens, kv_head):
+    """(n_tokens, D) K and V of one sequence and KV head from token-major caches:
+    [nb, bs, H, D] (reshape_and_cache.metal:115-136 layout) or the pool's
+    [slots, H, D] (memory_pool.py:102-108), where the table row is the slot list."""
+    if key_cache.ndim == 3:
+        key_cache = key_cache[:, None]
+        value_cache = value_cache[:, None]
+    bs = key_cache.shape[1]
+    t = np.arange(n_tokens)
+    blocks = np.asarray(block_table).astype(np.uint32).astype(np.int64)[t // bs]
+    return key_cache[blocks, t % bs, kv_head], value_cache[blocks, t % bs, kv_head]
+
+
+def paged_attention_flash(query, key_cache, value_cache, block_tables, context_lens, num_kv_heads, scale,
+                          max_seq_len, alibi_slopes=None):
+    """paged_attention_v1's result over token-major caches (same edge rules:
+    zeros when context_len == 0 or > max_seq_len; kv_head = h // G)."""
+    q = np.asarray(query, dtype=np.float64)
+    B, Hq, D = q.shape
+    G = Hq // num_kv_heads
+    out = np.zeros((B, Hq, D), dtype=np.float64)
+    lens = np.asarray(context_lens).astype(np.uint32)
+    for b in range(B):
+        C = int(lens[b])
+        if C == 0 or C > max_seq_len:
+            continue
+        for kvh in range(num_kv_heads):
+            k, v = gather_seq_flash(key_cache, value_cache, block_tables[b], C, kvh)
             hs = slice(kvh * G, (kvh + 1) * G)
             slope = 0.0 if alibi_slopes is None else np.asarray(alibi_slopes, dtype=np.float64)[hs]
             out[b, hs] = attend(q[b, hs], k, v, scale, slope, C)

@@ -9,6 +9,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "kvc_common.cuh"
 
 namespace kvc {
@@ -378,6 +380,173 @@ cudaError_t launch_gather_kv(const GatherArgs& a, cudaStream_t stream) {
   p.index_i64 = a.index_type == ElemType::I64;
   p.store = false;
   return launch_row_copy(p, stream);
+}
+
+// ---------------------------------------------------------------------------
+// FP8 (one-byte) KV cache: quantising append and the elementwise codec.
+// Encoding follows the behaviour float8.metal:65-68 states: round to nearest
+// even in the normal range, +-Inf past the last finite exponent (E4M3: 240,
+// its all-ones exponent is kept for Inf/NaN), NaN kept, gradual underflow
+// with the shifted mantissa rounded half up (float8.metal:110-117).  Values
+// are quantised as code = encode(x / scale) and read back as decode(code) *
+// scale (convert_fp8.metal:28-36).
+// ---------------------------------------------------------------------------
+template <int EB, int MB, int BIAS>
+__device__ __forceinline__ uint8_t encode_fp8(float f) {
+  const uint32_t bits = __float_as_uint(f);
+  const uint32_t s = (bits >> 31) << 7;
+  const uint32_t a = bits & 0x7FFFFFFFu;
+  const uint32_t top = ((1u << EB) - 1u) << MB;
+  if (a >= 0x7F800000u) return (uint8_t)(s | top | (a != 0x7F800000u ? 1u : 0u));
+  const int exp_max = (1 << EB) - 2;
+  const int ef = (int)((a >> 23) & 0xFFu) - 127 + BIAS;
+  const uint32_t m = a & 0x7FFFFFu;
+  if (ef > exp_max) return (uint8_t)(s | top);
+  if (ef >= 1) {
+    constexpr int SH = 23 - MB;
+    uint32_t mant = m >> SH;
+    const uint32_t rnd = (m >> (SH - 1)) & 1u;
+    const uint32_t sticky = (m & ((1u << (SH - 1)) - 1u)) != 0u;
+    mant += rnd & (sticky | (mant & 1u));
+    int e = ef;
+    if (mant >> MB) {
+      mant = 0;
+      if (++e > exp_max) return (uint8_t)(s | top);
+    }
+    return (uint8_t)(s | ((uint32_t)e << MB) | (mant & ((1u << MB) - 1u)));
+  }
+  if (ef < 1 - MB) return (uint8_t)s;
+  const int rshift = (1 - ef) + (23 - MB);
+  const uint32_t rounded = ((0x800000u | m) + (1u << (rshift - 1))) >> rshift;  // <= 1 << MB: carry kept
+  return (uint8_t)(s | rounded);
+}
+
+template <int EB, int MB, int BIAS>
+__device__ __forceinline__ float decode_fp8(uint32_t c) {
+  const uint32_t e = (c >> MB) & ((1u << EB) - 1u), m = c & ((1u << MB) - 1u);
+  float v;
+  if (e == 0) v = ldexpf((float)m / (float)(1u << MB), 1 - BIAS);
+  else if (e == (1u << EB) - 1u) v = m ? __int_as_float(0x7FC00000) : __int_as_float(0x7F800000);
+  else v = ldexpf(1.f + (float)m / (float)(1u << MB), (int)e - BIAS);
+  return (c & 0x80u) ? -v : v;
+}
+
+template <int FMT>
+__device__ __forceinline__ uint8_t fp8_encode(float f) {
+  if constexpr (FMT == 0) return encode_fp8<4, 3, 7>(f);
+  else return encode_fp8<5, 2, 15>(f);
+}
+template <int FMT>
+__device__ __forceinline__ float fp8_decode(uint32_t c) {
+  if constexpr (FMT == 0) return decode_fp8<4, 3, 7>(c);
+  else return decode_fp8<5, 2, 15>(c);
+}
+
+// Append into one-byte caches in the vLLM layout (x = 16): K [nb, H, D/16, bs,
+// 16], V [nb, H, D, bs].  Thread = (token, head, 16-dim chunk): it quantises
+// the chunk of K (one 16-byte store) and of V (16 bytes at a stride of bs).
+template <typename KV_T, int FMT>
+__global__ void __launch_bounds__(256) reshape_and_cache_fp8_kernel(ReshapeArgs a) {
+  const int chunks = a.head_size / 16;
+  const int64_t total = a.num_tokens * a.num_heads * chunks;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int c = (int)(i % chunks);
+  const int h = (int)((i / chunks) % a.num_heads);
+  const int64_t t = i / ((int64_t)chunks * a.num_heads);
+  const int64_t slot = a.slot_type == ElemType::I64 ? static_cast<const int64_t*>(a.slots)[t]
+                                                     : (int64_t) static_cast<const int32_t*>(a.slots)[t];
+  if (slot < 0) return;  // reshape_and_cache.metal:36-39
+  const int64_t blk = slot / a.block_size, off = slot % a.block_size;
+  if (blk >= a.num_blocks) {
+    set_status(&g_cache_ops_status, KVC_STATUS_SLOT_OOB);
+    return;
+  }
+  const KV_T* k = static_cast<const KV_T*>(a.key) + t * a.key_tok_stride + h * a.key_head_stride + 16 * c;
+  const KV_T* v = static_cast<const KV_T*>(a.value) + t * a.value_tok_stride + h * a.value_head_stride + 16 * c;
+  uint32_t kw[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int e = 0; e < 16; ++e)
+    kw[e >> 2] |= (uint32_t)fp8_encode<FMT>(to_float(k[e]) / a.k_scale) << (8 * (e & 3));
+  uint8_t* kc = static_cast<uint8_t*>(a.key_cache) + blk * a.kc_block_stride + h * a.kc_head_stride +
+                (int64_t)c * a.block_size * 16 + off * 16;
+  *reinterpret_cast<uint4*>(kc) = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+  uint8_t* vc = static_cast<uint8_t*>(a.value_cache) + blk * a.vc_block_stride + h * a.vc_head_stride +
+                (int64_t)(16 * c) * a.block_size + off;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) vc[(int64_t)e * a.block_size] = fp8_encode<FMT>(to_float(v[e]) / a.v_scale);
+}
+
+template <typename KV_T>
+static cudaError_t launch_fp8_append_t(const ReshapeArgs& a, cudaStream_t stream) {
+  const int64_t total = a.num_tokens * a.num_heads * (a.head_size / 16);
+  if (total == 0) return cudaSuccess;
+  const unsigned grid = (unsigned)((total + 255) / 256);
+  if (a.fp8_format == 1) reshape_and_cache_fp8_kernel<KV_T, 1><<<grid, 256, 0, stream>>>(a);
+  else reshape_and_cache_fp8_kernel<KV_T, 0><<<grid, 256, 0, stream>>>(a);
+  count_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_reshape_and_cache_fp8(const ReshapeArgs& a, cudaStream_t stream) {
+  if (a.kv_type == ElemType::F32) return launch_fp8_append_t<float>(a, stream);
+  if (a.kv_type == ElemType::F16) return launch_fp8_append_t<__half>(a, stream);
+  return launch_fp8_append_t<__nv_bfloat16>(a, stream);
+}
+
+// convert_fp8.metal:13-80: quantise (float types -> codes), dequantise (codes
+// -> float types), rescale codes, or scale between float types; dense arrays.
+template <typename SRC, typename DST, int FMT>
+__global__ void __launch_bounds__(256) convert_fp8_kernel(const SRC* src, DST* dst, float scale, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    if constexpr (std::is_same<SRC, uint8_t>::value && std::is_same<DST, uint8_t>::value) {
+      dst[i] = fp8_encode<FMT>(fp8_decode<FMT>(src[i]) * scale);
+    } else if constexpr (std::is_same<SRC, uint8_t>::value) {
+      dst[i] = from_float<DST>(fp8_decode<FMT>(src[i]) * scale);
+    } else if constexpr (std::is_same<DST, uint8_t>::value) {
+      dst[i] = fp8_encode<FMT>(to_float(src[i]) / scale);
+    } else {
+      dst[i] = from_float<DST>(to_float(src[i]) * scale);
+    }
+  }
+}
+
+template <typename SRC, typename DST>
+static cudaError_t launch_convert_t(const void* src, void* dst, float scale, int64_t n, int fmt, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  const int64_t want = (n + 255) / 256;
+  const unsigned grid = (unsigned)(want < 65535 * 8 ? want : 65535 * 8);
+  if (fmt == 1)
+    convert_fp8_kernel<SRC, DST, 1><<<grid, 256, 0, stream>>>(static_cast<const SRC*>(src), static_cast<DST*>(dst),
+                                                              scale, n);
+  else
+    convert_fp8_kernel<SRC, DST, 0><<<grid, 256, 0, stream>>>(static_cast<const SRC*>(src), static_cast<DST*>(dst),
+                                                              scale, n);
+  count_launch();
+  return cudaGetLastError();
+}
+
+template <typename SRC>
+static cudaError_t launch_convert_src(ElemType dt, const void* src, void* dst, float scale, int64_t n, int fmt,
+                                      cudaStream_t stream) {
+  switch (dt) {
+    case ElemType::U8: return launch_convert_t<SRC, uint8_t>(src, dst, scale, n, fmt, stream);
+    case ElemType::F32: return launch_convert_t<SRC, float>(src, dst, scale, n, fmt, stream);
+    case ElemType::F16: return launch_convert_t<SRC, __half>(src, dst, scale, n, fmt, stream);
+    case ElemType::BF16: return launch_convert_t<SRC, __nv_bfloat16>(src, dst, scale, n, fmt, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_convert_fp8(ElemType src_type, ElemType dst_type, const void* src, void* dst, float scale,
+                               int64_t n, int fmt, cudaStream_t stream) {
+  switch (src_type) {
+    case ElemType::U8: return launch_convert_src<uint8_t>(dst_type, src, dst, scale, n, fmt, stream);
+    case ElemType::F32: return launch_convert_src<float>(dst_type, src, dst, scale, n, fmt, stream);
+    case ElemType::F16: return launch_convert_src<__half>(dst_type, src, dst, scale, n, fmt, stream);
+    case ElemType::BF16: return launch_convert_src<__nv_bfloat16>(dst_type, src, dst, scale, n, fmt, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace kvc

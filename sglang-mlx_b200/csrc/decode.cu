@@ -45,6 +45,12 @@ struct DecodeParams {
   int64_t num_blocks;
   int64_t q_seq_stride, q_head_stride, out_seq_stride, out_head_stride;
   int64_t k_block_stride, k_head_stride, v_block_stride, v_head_stride;
+  int64_t k_tok_stride, v_tok_stride;  // token-major caches: elements between a block's tokens
+  // shared-prefix decode: partitions [0, prefix_parts) are chunks of prefix_part_size tokens of the shared
+  // prefix (the cascade kernel writes them); partition prefix_parts + i covers tokens
+  // prefix_len + i * partition_size onwards.  part_offset is added to blockIdx.z by the partition kernels.
+  int prefix_len, prefix_parts, prefix_part_size, part_offset;
+  float k_scale, v_scale;  // one-byte caches: dequantisation scales (value = code * scale)
   int64_t table_stride;
   int64_t part_seq_stride, part_head_stride;
   int64_t part_out_seq_stride, part_out_head_stride, part_out_part_stride;
@@ -68,6 +74,15 @@ __device__ __forceinline__ bool partition_range(const DecodeParams& p, int seq, 
     // Single pass: this CTA writes the zeros.  Split: the reduce does.
     *zero_out = (p.num_partitions == 1);
     return false;
+  }
+  if (p.prefix_len > 0) {
+    // shared-prefix decode: this kernel only runs the partitions after the prefix
+    const int64_t b = (int64_t)p.prefix_len + (int64_t)(part - p.prefix_parts) * p.partition_size;
+    if (part < p.prefix_parts || b >= (int64_t)ctx) return false;
+    *begin = (int)b;
+    const int64_t e = b + p.partition_size;
+    *end = (int)((int64_t)ctx < e ? (int64_t)ctx : e);
+    return true;
   }
   if (p.num_partitions == 1) {
     *begin = 0;
@@ -140,7 +155,7 @@ __global__ void __launch_bounds__(kGenericWarps * 32) paged_decode_generic_kerne
   const int h0 = kvh * G + hc * GC;
   const int nh = min(GC, G - hc * GC);
   const int seq = blockIdx.y;
-  const int part = blockIdx.z;
+  const int part = blockIdx.z + p.part_offset;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bs = p.block_size;
   grid_dependents_launch();  // lets the split-K reduce get scheduled during our tail
@@ -316,7 +331,11 @@ __global__ void __launch_bounds__(kReduceWarps * 32) splitk_reduce_kernel(Decode
     if (warp == 0 && d < head_size) out[d] = from_float<T>(0.f);
     return;
   }
-  const int nparts = (int)((ctx + p.partition_size - 1) / p.partition_size);
+  const int nparts = p.prefix_len > 0
+                         ? p.prefix_parts + ((int)ctx > p.prefix_len
+                                                 ? (int)((ctx - p.prefix_len + p.partition_size - 1) / p.partition_size)
+                                                 : 0)
+                         : (int)((ctx + p.partition_size - 1) / p.partition_size);
   const float* pm = p.part_max + (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride;
   const float* pl = p.part_sum + (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride;
   float* w = smem_f;
@@ -378,6 +397,7 @@ __global__ void __launch_bounds__(kReduceWarps * 32) splitk_reduce_kernel(Decode
 }  // namespace kvc
 
 #include "decode_mma.cuh"
+#include "cascade.cuh"
 
 namespace kvc {
 
@@ -385,7 +405,7 @@ template <typename Q_T, typename CACHE_T, int D>
 static cudaError_t launch_generic(const DecodeParams& p, cudaStream_t stream) {
   const int G = p.num_heads / p.num_kv_heads;
   const int chunks = (G + kGenericGC - 1) / kGenericGC;
-  dim3 grid((unsigned)(p.num_kv_heads * chunks), (unsigned)p.num_seqs, (unsigned)p.num_partitions);
+  dim3 grid((unsigned)(p.num_kv_heads * chunks), (unsigned)p.num_seqs, (unsigned)(p.num_partitions - p.part_offset));
   paged_decode_generic_kernel<Q_T, CACHE_T, D><<<grid, kGenericWarps * 32, 0, stream>>>(p);
   count_launch();
   return cudaGetLastError();
@@ -425,7 +445,11 @@ __global__ void __launch_bounds__(kReduceHeadsPerCta * 32) splitk_reduce_few_ker
     for (int d = lane; d < head_size; d += 32) out[d] = from_float<T>(0.f);
     return;
   }
-  const int nparts = (int)((ctx + p.partition_size - 1) / p.partition_size);
+  const int nparts = p.prefix_len > 0
+                         ? p.prefix_parts + ((int)ctx > p.prefix_len
+                                                 ? (int)((ctx - p.prefix_len + p.partition_size - 1) / p.partition_size)
+                                                 : 0)
+                         : (int)((ctx + p.partition_size - 1) / p.partition_size);
   const float* pm = p.part_max + (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride;
   const float* pl = p.part_sum + (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride;
   float M = -INFINITY;
@@ -536,6 +560,14 @@ static DecodeParams to_params(const DecodeArgs& a) {
   p.k_head_stride = a.k_head_stride;
   p.v_block_stride = a.v_block_stride;
   p.v_head_stride = a.v_head_stride;
+  p.k_tok_stride = a.k_tok_stride;
+  p.v_tok_stride = a.v_tok_stride;
+  p.prefix_len = a.prefix_len;
+  p.prefix_parts = a.prefix_parts;
+  p.prefix_part_size = a.prefix_part_size;
+  p.part_offset = 0;
+  p.k_scale = a.cache_type == ElemType::U8 ? a.k_scale : 1.f;
+  p.v_scale = a.cache_type == ElemType::U8 ? a.v_scale : 1.f;
   p.table_stride = a.table_stride;
   p.part_seq_stride = a.part_seq_stride;
   p.part_head_stride = a.part_head_stride;
@@ -548,6 +580,12 @@ static DecodeParams to_params(const DecodeArgs& a) {
 
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
+static bool pages_aligned(const DecodeArgs& a) {
+  const int cs = elem_size(a.cache_type);
+  return aligned16(a.k_cache) && aligned16(a.v_cache) && (a.k_block_stride * cs) % 16 == 0 &&
+         (a.k_head_stride * cs) % 16 == 0 && (a.v_block_stride * cs) % 16 == 0 && (a.v_head_stride * cs) % 16 == 0;
+}
+
 cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   if (a.num_seqs > 65535) return cudaErrorInvalidValue;
   DecodeParams p = to_params(a);
@@ -557,8 +595,11 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   const int cs = elem_size(a.cache_type);
   const bool pages_aligned = aligned16(a.k_cache) && aligned16(a.v_cache) && (a.k_block_stride * cs) % 16 == 0 &&
                              (a.k_head_stride * cs) % 16 == 0 && (a.v_block_stride * cs) % 16 == 0 &&
-                             (a.v_head_stride * cs) % 16 == 0;
+                             (a.v_head_stride * cs) % 16 == 0 &&
+                             (!a.flash || ((a.k_tok_stride * cs) % 16 == 0 && (a.v_tok_stride * cs) % 16 == 0));
   if (!pages_aligned) return cudaErrorMisalignedAddress;
+  if ((a.flash || a.cache_type == ElemType::U8) && !mma_supported(a))
+    return cudaErrorNotSupported;  // no CUDA-core kernel for these caches
   if (mma_supported(a)) {
     e = launch_mma(p, a, stream);
   } else if (a.q_type == ElemType::F32) {
@@ -574,6 +615,77 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   if (a.q_type == ElemType::F32) return launch_reduce<float>(p, D, stream);
   if (a.q_type == ElemType::F16) return launch_reduce<__half>(p, D, stream);
   return launch_reduce<__nv_bfloat16>(p, D, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Shared-prefix decode (cascade.cuh): the partitions after the prefix (the
+// ordinary split-K partition kernel, offset past the prefix partitions), then
+// the prefix kernel as a programmatic dependent that waits for them before it
+// exits, then the reduce.  Stage ring: 16-token groups (32 for 32-token
+// blocks), 6 stages (4 for 32-token blocks) of K and V pages.
+// ---------------------------------------------------------------------------
+template <typename T, int D, int BS>
+static cudaError_t launch_cascade_prefix(const DecodeParams& p, cudaStream_t stream, bool after_tail) {
+  constexpr int GT = BS <= 16 ? 16 : 32;
+  constexpr int STAGES = BS <= 16 ? 6 : 4;
+  using CG = CascadeGeom<D, BS, STAGES, GT>;
+  auto kern = cascade_prefix_kernel<T, D, BS, STAGES, GT>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, CG::SMEM);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  const int G = p.num_heads / p.num_kv_heads;
+  const int64_t rows = (int64_t)p.num_seqs * G;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((rows + kCascadeRows - 1) / kCascadeRows), (unsigned)p.prefix_parts,
+                     (unsigned)p.num_kv_heads);
+  cfg.blockDim = dim3((kCascadeConsumers + 1) * 32);
+  cfg.dynamicSmemBytes = CG::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = after_tail ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+  count_launch();
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_cascade_prefix_t(const DecodeParams& p, int D, cudaStream_t stream, bool after_tail) {
+  if (D == 128) {
+    if (p.block_size == 8) return launch_cascade_prefix<T, 128, 8>(p, stream, after_tail);
+    if (p.block_size == 16) return launch_cascade_prefix<T, 128, 16>(p, stream, after_tail);
+    return launch_cascade_prefix<T, 128, 32>(p, stream, after_tail);
+  }
+  if (p.block_size == 8) return launch_cascade_prefix<T, 64, 8>(p, stream, after_tail);
+  if (p.block_size == 16) return launch_cascade_prefix<T, 64, 16>(p, stream, after_tail);
+  return launch_cascade_prefix<T, 64, 32>(p, stream, after_tail);
+}
+
+cudaError_t launch_paged_decode_cascade(const DecodeArgs& a, cudaStream_t stream) {
+  if (a.num_seqs > 65535 || a.prefix_len <= 0 || a.prefix_parts <= 0) return cudaErrorInvalidValue;
+  if (!mma_supported(a) || a.alibi != nullptr || a.flash) return cudaErrorNotSupported;
+  if (!pages_aligned(a)) return cudaErrorMisalignedAddress;
+  DecodeParams p = to_params(a);
+  cudaError_t e = cudaSuccess;
+  const bool tail = p.num_partitions > p.prefix_parts;
+  if (tail) {
+    p.part_offset = p.prefix_parts;
+    e = launch_mma(p, a, stream);
+    if (e != cudaSuccess) return e;
+    p.part_offset = 0;
+  }
+  e = a.q_type == ElemType::BF16 ? launch_cascade_prefix_t<__nv_bfloat16>(p, a.head_size, stream, tail)
+                                 : launch_cascade_prefix_t<__half>(p, a.head_size, stream, tail);
+  if (e != cudaSuccess) return e;
+  if (a.q_type == ElemType::BF16) return launch_reduce<__nv_bfloat16>(p, a.head_size, stream);
+  return launch_reduce<__half>(p, a.head_size, stream);
 }
 
 // ---------------------------------------------------------------------------

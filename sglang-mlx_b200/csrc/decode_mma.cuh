@@ -128,6 +128,15 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_
                : "r"(addr));
 }
 
+// Transposing form: each lane's address is a row of 8 consecutive 16-bit
+// elements; every 8x8 matrix is delivered transposed.
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                                  uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
 template <typename T> struct MmaOp;
 template <> struct MmaOp<__nv_bfloat16> {
   __device__ __forceinline__ static void run(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
@@ -188,20 +197,33 @@ constexpr float kLn2 = 0.6931471805599453f;
 //             (V); the V box carries the 32/64-byte swizzle.
 //  kSwizzledV K by 1-D bulk copy; V as a whole page through a tensor map that
 //             views it as 128-byte rows, written with the 128-byte swizzle.
+//  kFlash     token-major caches ([nb, bs, H, D], the MHATokenPool buffers
+//             being bs = 1): every token's K row and V row (D * 2 bytes) is
+//             its own 1-D bulk copy, landing in a shared row of D * 2 + 16
+//             bytes (the 16-byte pad spreads the ldmatrix rows of 8 tokens
+//             over all banks); V is read with ldmatrix.trans.  A "box" is one
+//             token, so the stage mask has a bit per token.
 // A swizzled V box makes the ldmatrix reads of V rows (VBS * 2 bytes apart)
 // hit distinct banks.
-constexpr int kBulk = 0, kTiles = 1, kSwizzledV = 2;
+//  kFp8E4M3 / kFp8E5M2  one-byte caches in the paged layout (K pages
+//             [D/16][bs][16], V pages [D][bs] bytes), 1-D bulk copies of whole
+//             pages; mma_group_fp8 converts codes to f16 in registers.
+constexpr int kBulk = 0, kTiles = 1, kSwizzledV = 2, kFlash = 3, kFp8E4M3 = 4, kFp8E5M2 = 5;
 
 template <int D, int BS, int NW, int STAGES, int GT_ = 32, int MODE = kBulk>
 struct MmaGeom {
   static constexpr int GT = GT_;                          // tokens per group (16, 32 or 64)
-  static constexpr int VBS = MODE == kTiles ? (GT < BS ? GT : BS) : BS;  // tokens per box
+  static constexpr bool FLASH = MODE == kFlash;           // token-major K/V rows
+  static constexpr bool FP8 = MODE == kFp8E4M3 || MODE == kFp8E5M2;  // one-byte caches
+  static constexpr int VBS = MODE == kFlash ? 1 : (MODE == kTiles ? (GT < BS ? GT : BS) : BS);  // tokens per box
   static constexpr int NBOX = GT / VBS;                   // boxes per group (K and V each)
   static_assert(GT % 16 == 0 && GT % VBS == 0, "a group is whole boxes and whole 16-token k-steps");
-  static constexpr int BOX = D * VBS * 2;                 // bytes of one K (or V) box
+  static_assert(MODE != kFlash || GT == 16, "token-major groups are 16 tokens (one bit per token)");
+  static constexpr int ROWB = D * 2;                      // bytes of one token row (kFlash)
+  static constexpr int BOX = MODE == kFlash ? ROWB + 16 : D * VBS * (FP8 ? 1 : 2);  // bytes (stride) of one K (or V) box
   static constexpr int VSWZ = MODE == kSwizzledV ? 128 : (MODE == kTiles && VBS * 2 >= 32 ? VBS * 2 : 0);
   static constexpr int STAGE = NBOX * 2 * BOX;            // K boxes then V boxes
-  static constexpr int ALIGN = MODE != kBulk ? 1024 : 0;  // ring base alignment slack (swizzle atoms)
+  static constexpr int ALIGN = (MODE == kTiles || MODE == kSwizzledV) ? 1024 : 0;  // ring alignment (swizzle atoms)
   static constexpr int RING = NW * STAGES * STAGE;
   static constexpr int BAR_OFF = ALIGN + RING;            // NW*STAGES mbarriers
   static constexpr int MASK_OFF = BAR_OFF + NW * STAGES * 8;
@@ -246,11 +268,14 @@ struct GroupState {
 // `vst`): S = Q K^T on the tensor cores, the online-softmax update of `gs`,
 // and O += P V.  Tokens at or past `end`, and boxes whose bit in `pmask` is
 // clear (page not loaded), are masked.  `ctx` is the sequence's context
-// length (ALiBi positions).
+// length (ALiBi positions).  When the tile's rows belong to different
+// sequences (the shared-prefix kernel), `end_lo` / `end_hi` further end the
+// scores of this lane's rows r and r + 8; `end` still bounds the V data.
 template <typename T, typename Geo, int D>
 __device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa)[D / 16][4], uint32_t kst,
                                           uint32_t vst, int tok0, int end, uint32_t pmask, int ctx, float qk_scale,
-                                          bool alibi, float slope_lo, float slope_hi, int lane) {
+                                          bool alibi, float slope_lo, float slope_hi, int lane,
+                                          int end_lo = 2147483647, int end_hi = 2147483647) {
   using namespace mma_detail;
   constexpr int GT = Geo::GT, NBOX = Geo::NBOX, BOX = Geo::BOX, VBS = Geo::VBS;
   constexpr uint32_t VSW_MASK = Geo::VSWZ ? (uint32_t)(Geo::VSWZ / 16 - 1) : 0u;
@@ -259,7 +284,8 @@ __device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa
   constexpr int ST = GT / 8;
   constexpr int PK = GT / 16;
   const int q4 = lane & 3;
-  const bool tail = (tok0 + GT > end) || (pmask != (1u << NBOX) - 1u);
+  const int row_end = end_lo < end_hi ? end_lo : end_hi;
+  const bool tail = (tok0 + GT > end) || (tok0 + GT > row_end) || (pmask != (1u << NBOX) - 1u);
   (void)KS;
 
   // ---- S = Q K^T : ST tiles of 8 tokens
@@ -298,8 +324,8 @@ __device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa
       }
       if (tail) {
         const bool ok = (tok0 + t < end) && ((pmask >> (t / VBS)) & 1u);
-        x_lo = ok ? x_lo : -INFINITY;
-        x_hi = ok ? x_hi : -INFINITY;
+        x_lo = (ok && tok0 + t < end_lo) ? x_lo : -INFINITY;
+        x_hi = (ok && tok0 + t < end_hi) ? x_hi : -INFINITY;
       }
       sacc[j][e] = x_lo;
       sacc[j][2 + e] = x_hi;
@@ -372,9 +398,16 @@ __device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa
       // 16-byte chunk index (bits 4..) is XORed with address bits 7..
       uint32_t voffb = (uint32_t)(dim * VBS + voff) * 2;
       if (VSW_MASK) voffb ^= ((voffb >> 7) & VSW_MASK) << 4;
-      const uint32_t addr = vst + vbx * BOX + voffb;
       uint32_t b0, b1, b2, b3;
-      ldmatrix_x4(addr, b0, b1, b2, b3);
+      if constexpr (Geo::FLASH) {
+        // token-major V rows: lane -> token 16kk + 8*(mi & 1) + (lane & 7),
+        // 16-byte dim chunk nt + mi/2; transposed on load
+        const uint32_t row = (uint32_t)(vtok + (lane & 7));
+        ldmatrix_x4_trans(vst + row * BOX + (uint32_t)(nt + (mi >> 1)) * 16, b0, b1, b2, b3);
+        (void)voffb;
+      } else {
+        ldmatrix_x4(vst + vbx * BOX + voffb, b0, b1, b2, b3);
+      }
       if (tail) {
         // zero V of masked tokens: their slots may hold anything (NaN * 0 = NaN)
         const uint32_t m_lo_bits = (ok_lo0 ? 0x0000ffffu : 0u) | (ok_lo1 ? 0xffff0000u : 0u);
@@ -394,6 +427,175 @@ __device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa
   }
 }
 
+namespace mma_detail {
+
+// Two codes (low byte first) -> f16x2; every E4M3 / E5M2 value is exact in f16.
+template <int MODE>
+__device__ __forceinline__ uint32_t fp8x2_to_f16x2(uint32_t two) {
+  uint32_t d;
+  const uint16_t v = (uint16_t)two;
+  if constexpr (MODE == kFp8E4M3) {
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(v));
+  } else {
+    asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(d) : "h"(v));
+  }
+  return d;
+}
+
+// Four codes of `w` -> lo (bytes 0, 1) and hi (bytes 2, 3) as f16x2.  The
+// hardware's E4M3 is the OCP E4M3FN variant; the KV cache's E4M3 keeps the
+// all-ones exponent for Inf (mantissa 0) and NaN, so such codes (written only
+// for Inf, NaN or out-of-range inputs) are patched on a rarely taken path.
+template <int MODE>
+__device__ __forceinline__ void fp8x4_to_f16(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  lo = fp8x2_to_f16x2<MODE>(w);
+  hi = fp8x2_to_f16x2<MODE>(w >> 16);
+  if constexpr (MODE == kFp8E4M3) {
+    const uint32_t z = (w & 0x78787878u) ^ 0x78787878u;  // zero byte <=> exponent all ones
+    if ((z - 0x01010101u) & ~z & 0x80808080u) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t c = (w >> (8 * i)) & 0xFFu;
+        if ((c & 0x78u) == 0x78u) {
+          const uint32_t h = ((c & 0x80u) << 8) | ((c & 0x07u) ? 0x7E00u : 0x7C00u);
+          uint32_t& dst = i < 2 ? lo : hi;
+          const int sh = 16 * (i & 1);
+          dst = (dst & ~(0xFFFFu << sh)) | (h << sh);
+        }
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+}  // namespace mma_detail
+
+// mma_group for one-byte caches: S = Q K^T and O += P V as f16 products.
+// Permutations make plain 32-bit shared loads produce the fragments:
+//  * K: column c of S tile j is token 16*(j/2) + 4*(c/2) + 2*(j%2) + c%2, and
+//    the k index 2*q4 + e (+ 8) of a 16-dim step is dim 4*q4 + e (+ 2), so a
+//    lane's 4 bytes (4 consecutive dims of one token) are its b0 / b1 and the
+//    query fragments are loaded in the same dim order (the kernel does it);
+//  * P: with that token order the S accumulators of tiles 2kk and 2kk + 1 are
+//    exactly the A fragment of the 16-token step kk (tokens 4*q4 + 0..3), and
+//    a lane's 4 bytes of a V row (dim, tokens 4*q4 .. 4*q4 + 3) are its b0 / b1.
+// k_scale is folded into qk_scale by the caller and v_scale applied to O.
+template <typename Geo, int D, int MODE>
+__device__ __forceinline__ void mma_group_fp8(GroupState<D>& gs, const uint32_t (&qa)[D / 16][4], uint32_t kst,
+                                              uint32_t vst, int tok0, int end, uint32_t pmask, int ctx,
+                                              float qk_scale, bool alibi, float slope_lo, float slope_hi, int lane) {
+  using namespace mma_detail;
+  constexpr int GT = Geo::GT, NBOX = Geo::NBOX, BOX = Geo::BOX, VBS = Geo::VBS;
+  constexpr int KS = D / 16;
+  constexpr int NT = D / 8;
+  constexpr int ST = GT / 8;
+  constexpr int PK = GT / 16;
+  const int q4 = lane & 3, n = lane >> 2;
+  const bool tail = (tok0 + GT > end) || (pmask != (1u << NBOX) - 1u);
+
+  // ---- S = Q K^T
+  float sacc[ST][4];
+#pragma unroll
+  for (int j = 0; j < ST; ++j) {
+    sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+    const int tok = 16 * (j >> 1) + 4 * (n >> 1) + 2 * (j & 1) + (n & 1);  // this lane's K row
+    const uint32_t krow = kst + (uint32_t)((tok / VBS) * BOX + (tok % VBS) * 16 + 4 * q4);
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      uint32_t b0, b1;
+      fp8x4_to_f16<MODE>(lds32(krow + (uint32_t)(ks * VBS * 16)), b0, b1);
+      MmaOp<__half>::run(sacc[j], qa[ks], b0, b1);
+    }
+  }
+
+  // ---- online softmax (log2 domain); element (j, e) of a lane is token
+  // 16*(j/2) + 4*q4 + 2*(j%2) + e
+  float mx_lo = -INFINITY, mx_hi = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < ST; ++j) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int t = 16 * (j >> 1) + 4 * q4 + 2 * (j & 1) + e;
+      float x_lo = sacc[j][e] * qk_scale;
+      float x_hi = sacc[j][2 + e] * qk_scale;
+      if (alibi) {
+        const float pos = (float)(tok0 + t - ctx + 1);
+        x_lo += slope_lo * pos;
+        x_hi += slope_hi * pos;
+      }
+      if (tail) {
+        const bool ok = (tok0 + t < end) && ((pmask >> (t / VBS)) & 1u);
+        x_lo = ok ? x_lo : -INFINITY;
+        x_hi = ok ? x_hi : -INFINITY;
+      }
+      sacc[j][e] = x_lo;
+      sacc[j][2 + e] = x_hi;
+      mx_lo = fmaxf(mx_lo, x_lo);
+      mx_hi = fmaxf(mx_hi, x_hi);
+    }
+  }
+  mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
+  mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
+  mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
+  mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
+  const float mn_lo = fmaxf(gs.m_lo, mx_lo), mn_hi = fmaxf(gs.m_hi, mx_hi);
+  const float ref_lo = mn_lo == -INFINITY ? 0.f : mn_lo;
+  const float ref_hi = mn_hi == -INFINITY ? 0.f : mn_hi;
+  const float a_lo = fast_exp2(gs.m_lo - ref_lo), a_hi = fast_exp2(gs.m_hi - ref_hi);
+  gs.m_lo = mn_lo;
+  gs.m_hi = mn_hi;
+  float ps_lo = 0.f, ps_hi = 0.f;
+#pragma unroll
+  for (int j = 0; j < ST; ++j) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      sacc[j][e] = fast_exp2(sacc[j][e] - ref_lo);
+      sacc[j][2 + e] = fast_exp2(sacc[j][2 + e] - ref_hi);
+      ps_lo += sacc[j][e];
+      ps_hi += sacc[j][2 + e];
+    }
+  }
+  gs.l_lo = gs.l_lo * a_lo + ps_lo;
+  gs.l_hi = gs.l_hi * a_hi + ps_hi;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    gs.o[nt][0] *= a_lo;
+    gs.o[nt][1] *= a_lo;
+    gs.o[nt][2] *= a_hi;
+    gs.o[nt][3] *= a_hi;
+  }
+
+  // ---- O += P V
+#pragma unroll
+  for (int kk = 0; kk < PK; ++kk) {
+    uint32_t pa[4];
+    pa[0] = MmaOp<__half>::pack(sacc[2 * kk][0], sacc[2 * kk][1]);
+    pa[1] = MmaOp<__half>::pack(sacc[2 * kk][2], sacc[2 * kk][3]);
+    pa[2] = MmaOp<__half>::pack(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1]);
+    pa[3] = MmaOp<__half>::pack(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]);
+    const int t4 = 16 * kk + 4 * q4;  // this lane's 4 tokens of the step
+    const uint32_t vcol = vst + (uint32_t)((t4 / VBS) * BOX + t4 % VBS);
+    uint32_t keep_lo = 0xFFFFFFFFu, keep_hi = 0xFFFFFFFFu;
+    if (tail) {
+      // zero V of masked tokens: their slots may hold anything (NaN * 0 = NaN)
+      auto ok = [&](int t) { return (tok0 + t < end) && ((pmask >> (t / VBS)) & 1u); };
+      keep_lo = (ok(t4) ? 0x0000FFFFu : 0u) | (ok(t4 + 1) ? 0xFFFF0000u : 0u);
+      keep_hi = (ok(t4 + 2) ? 0x0000FFFFu : 0u) | (ok(t4 + 3) ? 0xFFFF0000u : 0u);
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      uint32_t b0, b1;
+      fp8x4_to_f16<MODE>(lds32(vcol + (uint32_t)((8 * nt + n) * VBS)), b0, b1);
+      MmaOp<__half>::run(gs.o[nt], pa, b0 & keep_lo, b1 & keep_hi);
+    }
+  }
+}
+
 template <typename T, int D, int BS, int NW, int STAGES, int GTOK, int MODE>
 __global__ void __launch_bounds__(NW * 32)
     paged_decode_mma_kernel(DecodeParams p, const __grid_constant__ TmaMaps tm) {
@@ -404,7 +606,7 @@ __global__ void __launch_bounds__(NW * 32)
   constexpr int NT = D / 8;     // n-tiles of P.V
   extern __shared__ __align__(128) uint8_t smem[];
 
-  const int kvh = blockIdx.x, seq = blockIdx.y, part = blockIdx.z;
+  const int kvh = blockIdx.x, seq = blockIdx.y, part = blockIdx.z + p.part_offset;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, q4 = lane & 3;
   const int G = p.num_heads / p.num_kv_heads;
@@ -437,8 +639,33 @@ __global__ void __launch_bounds__(NW * 32)
   __syncwarp();
 
   // ---- Q as A fragments (natural dim order), rows = heads of the group.
+  // One-byte caches: f16 fragments in mma_group_fp8's dim order (the k index
+  // 2*q4 + e (+ 8) of a 16-dim step is dim 4*q4 + e (+ 2)).
   uint32_t qa[KS][4];
-  {
+  if constexpr (Geo::FP8) {
+    const T* qp = reinterpret_cast<const T*>(p.q) + (int64_t)seq * p.q_seq_stride;
+    auto pair = [&](const T* row, int d) -> uint32_t {
+      if constexpr (std::is_same<T, __half>::value) return *reinterpret_cast<const uint32_t*>(row + d);
+      else return MmaOp<__half>::pack(to_float(row[d]), to_float(row[d + 1]));
+    };
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      const int d0 = ks * 16 + 4 * q4;
+      uint32_t v[4] = {0u, 0u, 0u, 0u};
+      if (r < G) {
+        const T* row = qp + (int64_t)(h0 + r) * p.q_head_stride;
+        v[0] = pair(row, d0);
+        v[2] = pair(row, d0 + 2);
+      }
+      if (r + 8 < G) {
+        const T* row = qp + (int64_t)(h0 + r + 8) * p.q_head_stride;
+        v[1] = pair(row, d0);
+        v[3] = pair(row, d0 + 2);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) qa[ks][i] = v[i];
+    }
+  } else {
     const T* qp = reinterpret_cast<const T*>(p.q) + (int64_t)seq * p.q_seq_stride;
 #pragma unroll
     for (int ks = 0; ks < KS; ++ks) {
@@ -458,76 +685,109 @@ __global__ void __launch_bounds__(NW * 32)
       for (int i = 0; i < 4; ++i) qa[ks][i] = v[i];
     }
   }
-  const float qk_scale = p.scale * kLog2e;
+  const float qk_scale = p.scale * kLog2e * (Geo::FP8 ? p.k_scale : 1.f);
   float slope_lo = 0.f, slope_hi = 0.f;  // ALiBi slopes of rows r and r + 8 (log2 units)
   if (p.alibi) {
     if (r < G) slope_lo = p.alibi[h0 + r] * kLog2e;
     if (r + 8 < G) slope_hi = p.alibi[h0 + r + 8] * kLog2e;
   }
 
-  const T* kbase = reinterpret_cast<const T*>(p.k_cache) + (int64_t)kvh * p.k_head_stride;
-  const T* vbase = reinterpret_cast<const T*>(p.v_cache) + (int64_t)kvh * p.v_head_stride;
+  using CT = typename std::conditional<Geo::FP8, uint8_t, T>::type;  // cache element
+  const CT* kbase = reinterpret_cast<const CT*>(p.k_cache) + (int64_t)kvh * p.k_head_stride;
+  const CT* vbase = reinterpret_cast<const CT*>(p.v_cache) + (int64_t)kvh * p.v_head_stride;
   const uint32_t* table = p.block_tables + (int64_t)seq * p.table_stride;
   const int ngroups = (end - begin + GT - 1) / GT;
   const int n_mine = warp < ngroups ? (ngroups - warp + NW - 1) / NW : 0;
   const int page_end = (end + BS - 1) / BS;  // first page past the context
 
   // Lane i < NBOX fetches the block id of box i of group `k` of this warp.
+  // Token-major caches: lane i < GT fetches the block id of token i of the
+  // group (block size p.block_size, 1 for the token pool).
   auto load_block = [&](int k) -> uint32_t {
     uint32_t b = 0xffffffffu;
-    if (lane < NBOX && k < n_mine) {
-      const int pg = (begin + (warp + k * NW) * GT + lane * VBS) / BS;
-      if (pg < page_end) b = __ldg(table + pg);
+    if constexpr (Geo::FLASH) {
+      if (lane < GT && k < n_mine) {
+        const int tt = begin + (warp + k * NW) * GT + lane;
+        if (tt < end) b = __ldg(table + tt / p.block_size);
+      }
+    } else {
+      if (lane < NBOX && k < n_mine) {
+        const int pg = (begin + (warp + k * NW) * GT + lane * VBS) / BS;
+        if (pg < page_end) b = __ldg(table + pg);
+      }
     }
     return b;
   };
   // Lane 0 issues the copies of group `k` into stage `s`; `blk` holds lane
   // i's block id (from load_block).  Records which boxes were loaded.
+  // Token-major caches: every lane with a token copies that token's K and V
+  // rows (lane 0 first posts the byte count), the mask has a bit per token.
   auto issue = [&](int k, int s, uint32_t blk) {
-    uint32_t ids[NBOX];
-#pragma unroll
-    for (int i = 0; i < NBOX; ++i) ids[i] = __shfl_sync(0xffffffffu, blk, i);
-    if (lane == 0) {
-      const int t0 = begin + (warp + k * NW) * GT;
-      uint32_t mask = 0, bytes = 0;
-#pragma unroll
-      for (int i = 0; i < NBOX; ++i) {
-        if ((t0 + i * VBS) / BS < page_end) {
-          if ((int64_t)ids[i] < p.num_blocks) {
-            mask |= 1u << i;
-            bytes += 2 * BOX;
-          } else {
-            set_status(&g_decode_status, KVC_STATUS_BLOCK_OOB);
-          }
-        }
-      }
-      masks[s] = mask;
+    if constexpr (Geo::FLASH) {
+      const int tt = begin + (warp + k * NW) * GT + lane;
+      const bool in_ctx = lane < GT && tt < end;
+      const bool ok = in_ctx && (int64_t)blk < p.num_blocks;
+      if (in_ctx && !ok) set_status(&g_decode_status, KVC_STATUS_BLOCK_OOB);
+      const uint32_t mask = __ballot_sync(0xffffffffu, ok);
       uint8_t* st = ring + (size_t)s * Geo::STAGE;
-      if (bytes) {
-        mbar_arrive_expect_tx(&bars[s], bytes);
+      if (lane == 0) {
+        masks[s] = mask;
+        if (mask) mbar_arrive_expect_tx(&bars[s], (uint32_t)__popc(mask) * 2u * (uint32_t)Geo::ROWB);
+        else mbar_arrive(&bars[s]);
+      }
+      __syncwarp();
+      if (ok) {
+        const int64_t off = (int64_t)blk * p.k_block_stride + (int64_t)(tt % p.block_size) * p.k_tok_stride;
+        const int64_t voff = (int64_t)blk * p.v_block_stride + (int64_t)(tt % p.block_size) * p.v_tok_stride;
+        bulk_g2s(st + lane * BOX, kbase + off, Geo::ROWB, &bars[s]);
+        bulk_g2s(st + (NBOX + lane) * BOX, vbase + voff, Geo::ROWB, &bars[s]);
+      }
+    } else {
+      uint32_t ids[NBOX];
+#pragma unroll
+      for (int i = 0; i < NBOX; ++i) ids[i] = __shfl_sync(0xffffffffu, blk, i);
+      if (lane == 0) {
+        const int t0 = begin + (warp + k * NW) * GT;
+        uint32_t mask = 0, bytes = 0;
 #pragma unroll
         for (int i = 0; i < NBOX; ++i) {
-          if (mask & (1u << i)) {
-            if constexpr (MODE == kTiles) {
-              // token offset of the box inside its page: 0 or a multiple of 16
-              // (16 tokens * 2 bytes = 32 B, so the innermost V coordinate is
-              // 16-byte aligned as tiled copies require)
-              const int toff = (t0 + i * VBS) % BS;
-              tma_load_5d(st + i * BOX, &tm.k, 0, toff, 0, kvh, (int)ids[i], &bars[s]);
-              tma_load_4d(st + (NBOX + i) * BOX, &tm.v, toff, 0, kvh, (int)ids[i], &bars[s]);
-            } else if constexpr (MODE == kSwizzledV) {
-              const int64_t b = (int64_t)ids[i];
-              bulk_g2s(st + i * BOX, kbase + b * p.k_block_stride, BOX, &bars[s]);
-              tma_load_4d(st + (NBOX + i) * BOX, &tm.v, 0, 0, kvh, (int)ids[i], &bars[s]);
+          if ((t0 + i * VBS) / BS < page_end) {
+            if ((int64_t)ids[i] < p.num_blocks) {
+              mask |= 1u << i;
+              bytes += 2 * BOX;
             } else {
-              const int64_t b = (int64_t)ids[i];
-              bulk_g2s(st + i * BOX, kbase + b * p.k_block_stride, BOX, &bars[s]);
-              bulk_g2s(st + (NBOX + i) * BOX, vbase + b * p.v_block_stride, BOX, &bars[s]);
+              set_status(&g_decode_status, KVC_STATUS_BLOCK_OOB);
             }
           }
         }
-      } else {
-        mbar_arrive(&bars[s]);
+        masks[s] = mask;
+        uint8_t* st = ring + (size_t)s * Geo::STAGE;
+        if (bytes) {
+          mbar_arrive_expect_tx(&bars[s], bytes);
+#pragma unroll
+          for (int i = 0; i < NBOX; ++i) {
+            if (mask & (1u << i)) {
+              if constexpr (MODE == kTiles) {
+                // token offset of the box inside its page: 0 or a multiple of 16
+                // (16 tokens * 2 bytes = 32 B, so the innermost V coordinate is
+                // 16-byte aligned as tiled copies require)
+                const int toff = (t0 + i * VBS) % BS;
+                tma_load_5d(st + i * BOX, &tm.k, 0, toff, 0, kvh, (int)ids[i], &bars[s]);
+                tma_load_4d(st + (NBOX + i) * BOX, &tm.v, toff, 0, kvh, (int)ids[i], &bars[s]);
+              } else if constexpr (MODE == kSwizzledV) {
+                const int64_t b = (int64_t)ids[i];
+                bulk_g2s(st + i * BOX, kbase + b * p.k_block_stride, BOX, &bars[s]);
+                tma_load_4d(st + (NBOX + i) * BOX, &tm.v, 0, 0, kvh, (int)ids[i], &bars[s]);
+              } else {
+                const int64_t b = (int64_t)ids[i];
+                bulk_g2s(st + i * BOX, kbase + b * p.k_block_stride, BOX, &bars[s]);
+                bulk_g2s(st + (NBOX + i) * BOX, vbase + b * p.v_block_stride, BOX, &bars[s]);
+              }
+            }
+          }
+        } else {
+          mbar_arrive(&bars[s]);
+        }
       }
     }
   };
@@ -554,8 +814,13 @@ __global__ void __launch_bounds__(NW * 32)
     const uint32_t vst = smem_u32(st + NBOX * BOX);
     const int tok0 = begin + (warp + k * NW) * GT;  // first token of the group
     const uint32_t pmask = masks[s];
-    mma_group<T, Geo, D>(gs, qa, kst, vst, tok0, end, pmask, (int)ctx, qk_scale, p.alibi != nullptr, slope_lo,
-                         slope_hi, lane);
+    if constexpr (Geo::FP8) {
+      mma_group_fp8<Geo, D, MODE>(gs, qa, kst, vst, tok0, end, pmask, (int)ctx, qk_scale, p.alibi != nullptr,
+                                  slope_lo, slope_hi, lane);
+    } else {
+      mma_group<T, Geo, D>(gs, qa, kst, vst, tok0, end, pmask, (int)ctx, qk_scale, p.alibi != nullptr, slope_lo,
+                           slope_hi, lane);
+    }
 
     // ---- recycle the stage
     __syncwarp();
@@ -571,6 +836,12 @@ __global__ void __launch_bounds__(NW * 32)
     if (lane == 0) set_status(&g_decode_status, KVC_STATUS_WAIT_TIMEOUT);
     for (int kk = k_fail; kk < n_mine && kk < k_fail + STAGES; ++kk)
       mbar_wait_bounded(&bars[kk % STAGES], (uint32_t)((kk / STAGES) & 1));
+  }
+
+  if constexpr (Geo::FP8) {  // dequantisation scale of V, applied once to the accumulators
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+      for (int i = 0; i < 4; ++i) gs.o[nt][i] *= p.v_scale;
   }
 
   // ---- merge: quad sums of l, then across warps through shared memory.
@@ -629,14 +900,23 @@ static bool mma_disabled_by_env() {
 }
 
 static bool mma_supported(const DecodeArgs& a) {
+  if (a.cache_type == ElemType::U8) {  // one-byte caches have no other kernel
+    const int G = a.num_heads / a.num_kv_heads;
+    return (a.q_type == ElemType::F16 || a.q_type == ElemType::BF16) && (a.head_size == 64 || a.head_size == 128) &&
+           (a.block_size == 8 || a.block_size == 16 || a.block_size == 32) && G >= 1 && G <= 16 && !a.flash &&
+           (a.num_partitions == 1 || a.partition_size % 32 == 0) && (reinterpret_cast<uintptr_t>(a.q) & 3u) == 0 &&
+           (a.q_seq_stride & 1) == 0 && (a.q_head_stride & 1) == 0;
+  }
   if (mma_disabled_by_env()) return false;
   if (a.q_type != a.cache_type) return false;
   if (a.q_type != ElemType::F16 && a.q_type != ElemType::BF16) return false;
   if (!(a.head_size == 64 || a.head_size == 128)) return false;
-  if (a.block_size != 8 && a.block_size != 16 && a.block_size != 32) return false;
+  if (!a.flash && a.block_size != 8 && a.block_size != 16 && a.block_size != 32) return false;
   const int G = a.num_heads / a.num_kv_heads;
   if (G < 1 || G > 16) return false;
   if (a.num_partitions > 1 && a.partition_size % 32 != 0) return false;
+  if (a.flash) return (reinterpret_cast<uintptr_t>(a.q) & 3u) == 0 && (a.q_seq_stride & 1) == 0 &&
+                      (a.q_head_stride & 1) == 0;
   // q rows are read as 4-byte pairs
   if ((reinterpret_cast<uintptr_t>(a.q) & 3u) || (a.q_seq_stride & 1) || (a.q_head_stride & 1)) return false;
   return true;
@@ -753,7 +1033,7 @@ static cudaError_t launch_mma_nw(const DecodeParams& p, cudaStream_t stream) {
   auto kern = paged_decode_mma_kernel<T, D, BS, NW, STAGES, GT, MODE>;
   TmaMaps maps;
   memset(&maps, 0, sizeof(maps));
-  if (MODE != kBulk) {
+  if (MODE == kTiles || MODE == kSwizzledV) {
     const ElemType et = std::is_same<T, __nv_bfloat16>::value ? ElemType::BF16 : ElemType::F16;
     if (!make_tensor_maps(p, et, D, BS, Geo::VBS, Geo::VSWZ, MODE, &maps)) return cudaErrorNotSupported;
   }
@@ -765,7 +1045,7 @@ static cudaError_t launch_mma_nw(const DecodeParams& p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  dim3 grid((unsigned)p.num_kv_heads, (unsigned)p.num_seqs, (unsigned)p.num_partitions);
+  dim3 grid((unsigned)p.num_kv_heads, (unsigned)p.num_seqs, (unsigned)(p.num_partitions - p.part_offset));
   kern<<<grid, NW * 32, Geo::SMEM, stream>>>(p, maps);
   count_launch();
   return cudaGetLastError();
@@ -824,8 +1104,32 @@ static cudaError_t launch_mma_typed(const DecodeParams& p, cudaStream_t stream) 
   return launch_mma_nw<T, D, BS, 2, 2, 32>(p, stream);
 }
 
+// One-byte caches: 16-token groups, 4 warps x 4 stages of 4 KB (three CTAs per
+// SM) for blocks of up to 16 tokens; 32-token groups, 4 warps x 3 stages of
+// 8 KB for 32-token blocks.
+template <typename T, int D, int MODE>
+static cudaError_t launch_mma_fp8(const DecodeParams& p, int block_size, cudaStream_t stream) {
+  if (block_size == 8) return launch_mma_nw<T, D, 8, 4, 4, 16, MODE>(p, stream);
+  if (block_size == 16) return launch_mma_nw<T, D, 16, 4, 4, 16, MODE>(p, stream);
+  return launch_mma_nw<T, D, 32, 4, 3, 32, MODE>(p, stream);
+}
+
 template <typename T>
 static cudaError_t launch_mma_t(const DecodeParams& p, const DecodeArgs& a, cudaStream_t stream) {
+  if (a.cache_type == ElemType::U8) {
+    const bool e5m2 = a.fp8_format == 1;
+    if (a.head_size == 128)
+      return e5m2 ? launch_mma_fp8<T, 128, kFp8E5M2>(p, a.block_size, stream)
+                  : launch_mma_fp8<T, 128, kFp8E4M3>(p, a.block_size, stream);
+    return e5m2 ? launch_mma_fp8<T, 64, kFp8E5M2>(p, a.block_size, stream)
+                : launch_mma_fp8<T, 64, kFp8E4M3>(p, a.block_size, stream);
+  }
+  if (a.flash) {
+    // token-major caches: 16-token groups, 4 warps x 3 stages (104 KB for
+    // D = 128, two CTAs per SM); the block size is read at run time
+    if (a.head_size == 128) return launch_mma_nw<T, 128, 16, 4, 3, 16, kFlash>(p, stream);
+    return launch_mma_nw<T, 64, 16, 4, 3, 16, kFlash>(p, stream);
+  }
   if (a.head_size == 128) {
     if (a.block_size == 8) return launch_mma_typed<T, 128, 8>(p, stream);
     if (a.block_size == 16) return launch_mma_typed<T, 128, 16>(p, stream);

@@ -7,6 +7,7 @@
 #include <string.h>
 
 #include <atomic>
+#include <cmath>
 #include <string>
 #include <vector>
 
@@ -138,7 +139,8 @@ static int check_index_type(const View& v, const char* name, bool allow_i64) {
 static int prepare_decode(kvc_dltensor* out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
                           const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
                           const kvc_dltensor* context_lens, int num_kv_heads, float scale, int block_size,
-                          int max_seq_len, const kvc_dltensor* alibi_slopes, DecodeArgs* a, int* device) {
+                          int max_seq_len, const kvc_dltensor* alibi_slopes, DecodeArgs* a, int* device,
+                          bool fp8 = false) {
   View q, kc, vc, bt, cl, o, al;
   if (!parse(query, "query", &q) || !parse(key_cache, "key_cache", &kc) ||
       !parse(value_cache, "value_cache", &vc) || !parse(block_tables, "block_tables", &bt) ||
@@ -172,7 +174,11 @@ static int prepare_decode(kvc_dltensor* out, const kvc_dltensor* query, const kv
     return fail(KVC_EINVAL, "Unsupported head_size/block_size for paged_attention");
 
   // Checks the Metal path leaves to kernel lookup or to luck.
-  if (!is_float(q.dtype) || !is_float(kc.dtype) || kc.dtype != vc.dtype || !is_supported_pair(q.dtype, kc.dtype))
+  if (fp8) {
+    if ((q.dtype != ElemType::F16 && q.dtype != ElemType::BF16) || kc.dtype != ElemType::U8 || vc.dtype != ElemType::U8)
+      return fail(KVC_EINVAL, "paged_attention_fp8 needs a float16/bfloat16 query and uint8 caches");
+  } else if (!is_float(q.dtype) || !is_float(kc.dtype) || kc.dtype != vc.dtype ||
+             !is_supported_pair(q.dtype, kc.dtype))
     return fail(KVC_EINVAL, std::string("Unsupported dtype combination for paged_attention: query ") +
                                 elem_name(q.dtype) + ", cache " + elem_name(kc.dtype) + "/" + elem_name(vc.dtype));
   const int x = 16 / elem_size(kc.dtype);
@@ -221,6 +227,8 @@ static int prepare_decode(kvc_dltensor* out, const kvc_dltensor* query, const kv
   a->scale = scale;
   a->num_partitions = 1;
   a->partition_size = 0;
+  a->k_scale = 1.f;
+  a->v_scale = 1.f;
   return KVC_OK;
 }
 
@@ -277,6 +285,142 @@ static int attach_mapping(const View& m, int device, BlockCopyArgs* a) {
   return read_block_mapping(m, &a->host_mapping);
 }
 
+// Split-K workspace of the v2-style entry points: exp_sums / max_logits
+// [B, Hq, P] and tmp_out [B, Hq, P, D] (f32), P = ceil(max_seq_len / partition_size).
+static int attach_splitk_workspace(kvc_dltensor* exp_sums, kvc_dltensor* max_logits, kvc_dltensor* tmp_out,
+                                   int partition_size, int block_size, int max_seq_len, int device, DecodeArgs* a,
+                                   int parts_override = 0) {
+  if (partition_size <= 0 || partition_size % 32 != 0 || partition_size % block_size != 0)
+    return fail(KVC_EINVAL, "partition_size must be a positive multiple of 32 and of block_size");
+  View es, ml, to;
+  if (!parse(exp_sums, "exp_sums", &es) || !parse(max_logits, "max_logits", &ml) || !parse(tmp_out, "tmp_out", &to))
+    return KVC_EINVAL;
+  const int parts = parts_override > 0 ? parts_override : (max_seq_len + partition_size - 1) / partition_size;
+  if (es.dtype != ElemType::F32 || ml.dtype != ElemType::F32 || to.dtype != ElemType::F32)
+    return fail(KVC_EINVAL, "exp_sums, max_logits and tmp_out must be float32");
+  if (es.ndim != 3 || ml.ndim != 3 || to.ndim != 4 || es.shape[0] != a->num_seqs || es.shape[1] != a->num_heads ||
+      es.shape[2] < parts || ml.shape[0] != a->num_seqs || ml.shape[1] != a->num_heads || ml.shape[2] < parts ||
+      to.shape[0] != a->num_seqs || to.shape[1] != a->num_heads || to.shape[2] < parts || to.shape[3] != a->head_size)
+    return fail(KVC_EINVAL,
+                "split-K workspace must be exp_sums/max_logits [num_seqs, num_heads, P] and tmp_out "
+                "[num_seqs, num_heads, P, head_size] with P >= " +
+                    std::string(parts_override > 0 ? "the partition count " : "ceil(max_seq_len / partition_size) = ") +
+                    std::to_string(parts));
+  if (es.stride(2) != 1 || ml.stride(2) != 1 || to.stride(3) != 1 || es.stride(0) != ml.stride(0) ||
+      es.stride(1) != ml.stride(1))
+    return fail(KVC_EINVAL, "exp_sums and max_logits must share strides with a contiguous last dimension");
+  int dev2 = -1;
+  if (int rc = check_all_cuda({&es, &ml, &to}, &dev2)) return rc;
+  if (dev2 != device) return fail(KVC_EINVAL, "all tensors must live on the same CUDA device");
+  a->part_sum = reinterpret_cast<float*>(es.data);
+  a->part_max = reinterpret_cast<float*>(ml.data);
+  a->part_out = reinterpret_cast<float*>(to.data);
+  a->part_seq_stride = es.stride(0);
+  a->part_head_stride = es.stride(1);
+  a->part_out_seq_stride = to.stride(0);
+  a->part_out_head_stride = to.stride(1);
+  a->part_out_part_stride = to.stride(2);
+  a->partition_size = partition_size;
+  a->num_partitions = parts;
+  return KVC_OK;
+}
+
+// Validation + packing of the token-major decode (kvc_paged_attention_flash).
+// Caches are [num_blocks, block_size, num_kv_heads, head_size] (the
+// reshape_and_cache_flash layout) or [slots, num_kv_heads, head_size] with
+// block_size 1 (the MHATokenPool buffers); every token row is dense.
+static int prepare_flash(kvc_dltensor* out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                         const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                         const kvc_dltensor* context_lens, int num_kv_heads, float scale, int block_size,
+                         int max_seq_len, const kvc_dltensor* alibi_slopes, DecodeArgs* a, int* device) {
+  View q, kc, vc, bt, cl, o, al;
+  if (!parse(query, "query", &q) || !parse(key_cache, "key_cache", &kc) ||
+      !parse(value_cache, "value_cache", &vc) || !parse(block_tables, "block_tables", &bt) ||
+      !parse(context_lens, "context_lens", &cl) || !parse(out, "out", &o))
+    return KVC_EINVAL;
+  if (alibi_slopes && !parse(alibi_slopes, "alibi_slopes", &al)) return KVC_EINVAL;
+  if (q.ndim != 3) return fail(KVC_EINVAL, "query must have shape [num_seqs, num_heads, head_size]");
+  const bool pool = kc.ndim == 3;
+  if (!((kc.ndim == 4 || kc.ndim == 3) && vc.ndim == kc.ndim))
+    return fail(KVC_EINVAL, "key_cache/value_cache must be [num_blocks, block_size, num_kv_heads, head_size] "
+                            "or [slots, num_kv_heads, head_size]");
+  if (bt.ndim != 2 || cl.ndim != 1) return fail(KVC_EINVAL, "block_tables must be 2D and context_lens must be 1D");
+  if (q.shape[0] != bt.shape[0] || q.shape[0] != cl.shape[0])
+    return fail(KVC_EINVAL, "query, block_tables, and context_lens sequence counts differ");
+  if (num_kv_heads <= 0 || q.shape[1] % num_kv_heads != 0)
+    return fail(KVC_EINVAL, "num_heads must be divisible by num_kv_heads");
+  const int hd = pool ? 1 : 2;  // head dimension of the cache
+  if (kc.shape[hd] != num_kv_heads || vc.shape[hd] != num_kv_heads)
+    return fail(KVC_EINVAL, "cache KV-head count does not match num_kv_heads");
+  if (kc.shape[hd + 1] != q.shape[2] || vc.shape[hd + 1] != q.shape[2])
+    return fail(KVC_EINVAL, "cache head size does not match query head size");
+  const int64_t cache_bs = pool ? 1 : kc.shape[1];
+  if (kc.shape[0] != vc.shape[0] || (!pool && vc.shape[1] != cache_bs) || block_size != cache_bs)
+    return fail(KVC_EINVAL, "cache block dimensions do not match block_size");
+  if (alibi_slopes && (al.ndim != 1 || al.shape[0] != q.shape[1]))
+    return fail(KVC_EINVAL, "alibi_slopes must have shape [num_heads]");
+  if (max_seq_len <= 0) return fail(KVC_EINVAL, "max_seq_len must be positive");
+  if ((int64_t)max_seq_len > bt.shape[1] * (int64_t)block_size)
+    return fail(KVC_EINVAL, "max_seq_len exceeds block table capacity");
+  const int head_size = (int)q.shape[2];
+  if (!(q.dtype == ElemType::F16 || q.dtype == ElemType::BF16) || kc.dtype != q.dtype || vc.dtype != q.dtype ||
+      !(head_size == 64 || head_size == 128) || q.shape[1] / num_kv_heads > 16)
+    return fail(KVC_EUNSUPPORTED,
+                std::string("paged_attention_flash supports float16/bfloat16 query and caches of one dtype, "
+                            "head_size 64 or 128 and up to 16 query heads per KV head (got query ") +
+                    elem_name(q.dtype) + ", cache " + elem_name(kc.dtype) + ", head_size " +
+                    std::to_string(head_size) + ")");
+  if (int rc = check_index_type(bt, "block_tables", false)) return rc;
+  if (int rc = check_index_type(cl, "context_lens", false)) return rc;
+  if (alibi_slopes && al.dtype != ElemType::F32) return fail(KVC_EINVAL, "alibi_slopes must be float32");
+  if (o.ndim != 3 || o.shape[0] != q.shape[0] || o.shape[1] != q.shape[1] || o.shape[2] != q.shape[2] ||
+      o.dtype != q.dtype)
+    return fail(KVC_EINVAL, "out must have the shape and dtype of query");
+  if (q.stride(2) != 1 || o.stride(2) != 1) return fail(KVC_EINVAL, "query/out head_size dimension must be contiguous");
+  if (kc.stride(-1) != 1 || vc.stride(-1) != 1)
+    return fail(KVC_EINVAL, "key_cache/value_cache rows (head_size) must be contiguous");
+  if (bt.stride(1) != 1 || cl.stride(0) != 1 || (alibi_slopes && al.stride(0) != 1))
+    return fail(KVC_EINVAL, "block_tables rows, context_lens and alibi_slopes must be contiguous");
+  if (int rc = check_all_cuda({&q, &kc, &vc, &bt, &cl, &o, alibi_slopes ? &al : nullptr}, device)) return rc;
+
+  memset(a, 0, sizeof(*a));
+  a->out = o.data;
+  a->q = q.data;
+  a->k_cache = kc.data;
+  a->v_cache = vc.data;
+  a->block_tables = reinterpret_cast<const uint32_t*>(bt.data);
+  a->context_lens = reinterpret_cast<const uint32_t*>(cl.data);
+  a->alibi = alibi_slopes ? reinterpret_cast<const float*>(al.data) : nullptr;
+  a->q_type = q.dtype;
+  a->cache_type = kc.dtype;
+  a->num_seqs = (int)q.shape[0];
+  a->num_heads = (int)q.shape[1];
+  a->num_kv_heads = num_kv_heads;
+  a->head_size = head_size;
+  a->block_size = block_size;
+  a->max_blocks_per_seq = (int)bt.shape[1];
+  a->max_seq_len = max_seq_len;
+  a->num_blocks = kc.shape[0];
+  a->q_seq_stride = q.stride(0);
+  a->q_head_stride = q.stride(1);
+  a->out_seq_stride = o.stride(0);
+  a->out_head_stride = o.stride(1);
+  a->k_block_stride = kc.stride(0);
+  a->v_block_stride = vc.stride(0);
+  a->k_tok_stride = pool ? 0 : kc.stride(1);
+  a->v_tok_stride = pool ? 0 : vc.stride(1);
+  a->k_head_stride = kc.stride(hd);
+  a->v_head_stride = vc.stride(hd);
+  a->flash = true;
+  a->table_stride = bt.stride(0);
+  a->scale = scale;
+  a->num_partitions = 1;
+  a->partition_size = 0;
+  a->k_scale = 1.f;
+  a->v_scale = 1.f;
+  return KVC_OK;
+}
+
 }  // namespace kvc
 
 using namespace kvc;
@@ -331,42 +475,81 @@ int kvc_paged_attention_v2(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltens
   if (int rc = prepare_decode(out, query, key_cache, value_cache, block_tables, context_lens, num_kv_heads, scale,
                               block_size, max_seq_len, alibi_slopes, &a, &device))
     return rc;
-  if (partition_size <= 0 || partition_size % 32 != 0 || partition_size % block_size != 0)
-    return fail(KVC_EINVAL, "partition_size must be a positive multiple of 32 and of block_size");
-  View es, ml, to;
-  if (!parse(exp_sums, "exp_sums", &es) || !parse(max_logits, "max_logits", &ml) || !parse(tmp_out, "tmp_out", &to))
-    return KVC_EINVAL;
-  const int parts = (max_seq_len + partition_size - 1) / partition_size;
-  if (es.dtype != ElemType::F32 || ml.dtype != ElemType::F32 || to.dtype != ElemType::F32)
-    return fail(KVC_EINVAL, "exp_sums, max_logits and tmp_out must be float32");
-  if (es.ndim != 3 || ml.ndim != 3 || to.ndim != 4 || es.shape[0] != a.num_seqs || es.shape[1] != a.num_heads ||
-      es.shape[2] < parts || ml.shape[0] != a.num_seqs || ml.shape[1] != a.num_heads || ml.shape[2] < parts ||
-      to.shape[0] != a.num_seqs || to.shape[1] != a.num_heads || to.shape[2] < parts || to.shape[3] != a.head_size)
-    return fail(KVC_EINVAL,
-                "split-K workspace must be exp_sums/max_logits [num_seqs, num_heads, P] and tmp_out "
-                "[num_seqs, num_heads, P, head_size] with P >= ceil(max_seq_len / partition_size) = " +
-                    std::to_string(parts));
-  if (es.stride(2) != 1 || ml.stride(2) != 1 || to.stride(3) != 1 || es.stride(0) != ml.stride(0) ||
-      es.stride(1) != ml.stride(1))
-    return fail(KVC_EINVAL, "exp_sums and max_logits must share strides with a contiguous last dimension");
-  int dev2 = -1;
-  if (int rc = check_all_cuda({&es, &ml, &to}, &dev2)) return rc;
-  if (dev2 != device) return fail(KVC_EINVAL, "all tensors must live on the same CUDA device");
+  if (int rc = attach_splitk_workspace(exp_sums, max_logits, tmp_out, partition_size, block_size, max_seq_len,
+                                       device, &a))
+    return rc;
   if (a.num_seqs == 0) return KVC_OK;
-  a.part_sum = reinterpret_cast<float*>(es.data);
-  a.part_max = reinterpret_cast<float*>(ml.data);
-  a.part_out = reinterpret_cast<float*>(to.data);
-  a.part_seq_stride = es.stride(0);
-  a.part_head_stride = es.stride(1);
-  a.part_out_seq_stride = to.stride(0);
-  a.part_out_head_stride = to.stride(1);
-  a.part_out_part_stride = to.stride(2);
-  a.partition_size = partition_size;
-  a.num_partitions = parts;
   DeviceGuard g(device);
   if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
   cudaError_t e = launch_paged_decode(a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "paged_attention_v2 launch");
+  return KVC_OK;
+}
+
+int kvc_paged_attention_flash(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltensor* max_logits,
+                              kvc_dltensor* tmp_out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                              const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                              const kvc_dltensor* context_lens, int num_kv_heads, float scale, int block_size,
+                              int max_seq_len, const kvc_dltensor* alibi_slopes, int partition_size, void* stream) {
+  DecodeArgs a;
+  int device = -1;
+  if (int rc = prepare_flash(out, query, key_cache, value_cache, block_tables, context_lens, num_kv_heads, scale,
+                             block_size, max_seq_len, alibi_slopes, &a, &device))
+    return rc;
+  if (partition_size != 0) {
+    if (int rc = attach_splitk_workspace(exp_sums, max_logits, tmp_out, partition_size, block_size, max_seq_len,
+                                         device, &a))
+      return rc;
+  }
+  if (a.num_seqs == 0) return KVC_OK;
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_paged_decode(a, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorMisalignedAddress)
+    return fail(KVC_EINVAL, "key_cache/value_cache rows, blocks and heads must start on 16-byte boundaries");
+  if (e != cudaSuccess) return cuda_fail(e, "paged_attention_flash launch");
+  return KVC_OK;
+}
+
+int kvc_paged_attention_cascade(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltensor* max_logits,
+                                kvc_dltensor* tmp_out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                                const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                                const kvc_dltensor* context_lens, int num_kv_heads, float scale, int block_size,
+                                int max_seq_len, const kvc_dltensor* alibi_slopes, int shared_prefix_len,
+                                int prefix_partition_size, int partition_size, void* stream) {
+  DecodeArgs a;
+  int device = -1;
+  if (int rc = prepare_decode(out, query, key_cache, value_cache, block_tables, context_lens, num_kv_heads, scale,
+                              block_size, max_seq_len, alibi_slopes, &a, &device))
+    return rc;
+  if (alibi_slopes) return fail(KVC_EUNSUPPORTED, "paged_attention_cascade does not take alibi_slopes");
+  const int G = a.num_heads / a.num_kv_heads;
+  if (a.q_type != a.cache_type || (a.q_type != ElemType::F16 && a.q_type != ElemType::BF16) ||
+      !(a.head_size == 64 || a.head_size == 128) || G > 16)
+    return fail(KVC_EUNSUPPORTED, "paged_attention_cascade supports float16/bfloat16 query and cache of one dtype, "
+                                  "head_size 64 or 128 and up to 16 query heads per KV head");
+  if (shared_prefix_len <= 0 || shared_prefix_len % block_size != 0 || shared_prefix_len > max_seq_len)
+    return fail(KVC_EINVAL, "shared_prefix_len must be a positive multiple of block_size, at most max_seq_len");
+  if (prefix_partition_size <= 0 || prefix_partition_size % 32 != 0 || prefix_partition_size % block_size != 0)
+    return fail(KVC_EINVAL, "prefix_partition_size must be a positive multiple of 32 and of block_size");
+  const int prefix_parts = (shared_prefix_len + prefix_partition_size - 1) / prefix_partition_size;
+  const int tail_parts = partition_size > 0 && max_seq_len > shared_prefix_len
+                             ? (max_seq_len - shared_prefix_len + partition_size - 1) / partition_size
+                             : 0;
+  if (int rc = attach_splitk_workspace(exp_sums, max_logits, tmp_out, partition_size, block_size, max_seq_len,
+                                       device, &a, prefix_parts + tail_parts))
+    return rc;
+  a.prefix_len = shared_prefix_len;
+  a.prefix_parts = prefix_parts;
+  a.prefix_part_size = prefix_partition_size;
+  a.num_partitions = prefix_parts + tail_parts;
+  if (a.num_seqs == 0) return KVC_OK;
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_paged_decode_cascade(a, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorMisalignedAddress)
+    return fail(KVC_EINVAL, "key_cache/value_cache pages must start on 16-byte boundaries");
+  if (e != cudaSuccess) return cuda_fail(e, "paged_attention_cascade launch");
   return KVC_OK;
 }
 
@@ -505,7 +688,7 @@ int kvc_swap_blocks(const kvc_dltensor* src, kvc_dltensor* dst, const kvc_dltens
 // Shared validation of the two append layouts.
 static int prepare_reshape(const kvc_dltensor* key, const kvc_dltensor* value, kvc_dltensor* key_cache,
                            kvc_dltensor* value_cache, const kvc_dltensor* slot_mapping, bool flash,
-                           ReshapeArgs* a, int* device) {
+                           ReshapeArgs* a, int* device, bool fp8 = false) {
   View k, v, kc, vc, sm;
   if (!parse(key, "key", &k) || !parse(value, "value", &v) || !parse(key_cache, "key_cache", &kc) ||
       !parse(value_cache, "value_cache", &vc) || !parse(slot_mapping, "slot_mapping", &sm))
@@ -518,7 +701,10 @@ static int prepare_reshape(const kvc_dltensor* key, const kvc_dltensor* value, k
   if (sm.ndim != 1 || sm.shape[0] < k.shape[0])
     return fail(KVC_EINVAL, "slot_mapping must have shape [num_tokens]");
   if (int rc = check_index_type(sm, "slot_mapping", true)) return rc;
-  if (k.dtype != v.dtype || kc.dtype != vc.dtype || !is_supported_pair(k.dtype, kc.dtype))
+  if (fp8) {
+    if (k.dtype != v.dtype || !is_float(k.dtype) || kc.dtype != ElemType::U8 || vc.dtype != ElemType::U8)
+      return fail(KVC_EINVAL, "reshape_and_cache_fp8 needs float32/float16/bfloat16 key/value and uint8 caches");
+  } else if (k.dtype != v.dtype || kc.dtype != vc.dtype || !is_supported_pair(k.dtype, kc.dtype))
     return fail(KVC_EINVAL, std::string("Unsupported dtype combination for reshape_and_cache: kv ") +
                                 elem_name(k.dtype) + "/" + elem_name(v.dtype) + ", cache " + elem_name(kc.dtype) +
                                 "/" + elem_name(vc.dtype));
@@ -672,6 +858,89 @@ int kvc_gather_kv(kvc_dltensor* k_out, kvc_dltensor* v_out, const kvc_dltensor* 
   if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
   cudaError_t e = launch_gather_kv(a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "gather_kv launch");
+  return KVC_OK;
+}
+
+// ---- FP8 (one-byte) KV cache -------------------------------------------------
+
+static int check_fp8_args(float k_scale, float v_scale, int fp8_format) {
+  if (!(k_scale > 0.f) || !(v_scale > 0.f) || !std::isfinite(k_scale) || !std::isfinite(v_scale))
+    return fail(KVC_EINVAL, "k_scale and v_scale must be positive and finite");
+  if (fp8_format != 0 && fp8_format != 1) return fail(KVC_EINVAL, "fp8_format must be 0 (e4m3) or 1 (e5m2)");
+  return KVC_OK;
+}
+
+int kvc_reshape_and_cache_fp8(const kvc_dltensor* key, const kvc_dltensor* value, kvc_dltensor* key_cache,
+                              kvc_dltensor* value_cache, const kvc_dltensor* slot_mapping, float k_scale,
+                              float v_scale, int fp8_format, void* stream) {
+  if (int rc = check_fp8_args(k_scale, v_scale, fp8_format)) return rc;
+  ReshapeArgs a;
+  int device = -1;
+  if (int rc = prepare_reshape(key, value, key_cache, value_cache, slot_mapping, false, &a, &device, true)) return rc;
+  if (a.head_size % 16 != 0) return fail(KVC_EINVAL, "head_size must be a multiple of 16 for one-byte caches");
+  if ((reinterpret_cast<uintptr_t>(a.key_cache) & 15u) || (a.kc_block_stride & 15) || (a.kc_head_stride & 15))
+    return fail(KVC_EINVAL, "key_cache pages must start on 16-byte boundaries");
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  a.fp8_format = fp8_format;
+  if (a.num_tokens == 0) return KVC_OK;
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_reshape_and_cache_fp8(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "reshape_and_cache_fp8 launch");
+  return KVC_OK;
+}
+
+int kvc_paged_attention_fp8(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltensor* max_logits,
+                            kvc_dltensor* tmp_out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                            const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                            const kvc_dltensor* context_lens, int num_kv_heads, float scale, int block_size,
+                            int max_seq_len, const kvc_dltensor* alibi_slopes, float k_scale, float v_scale,
+                            int fp8_format, int partition_size, void* stream) {
+  if (int rc = check_fp8_args(k_scale, v_scale, fp8_format)) return rc;
+  DecodeArgs a;
+  int device = -1;
+  if (int rc = prepare_decode(out, query, key_cache, value_cache, block_tables, context_lens, num_kv_heads, scale,
+                              block_size, max_seq_len, alibi_slopes, &a, &device, true))
+    return rc;
+  const int G = a.num_heads / a.num_kv_heads;
+  if (!(a.head_size == 64 || a.head_size == 128) || G > 16)
+    return fail(KVC_EUNSUPPORTED, "paged_attention_fp8 supports head_size 64 or 128 and up to 16 query heads per "
+                                  "KV head");
+  if (partition_size != 0) {
+    if (int rc = attach_splitk_workspace(exp_sums, max_logits, tmp_out, partition_size, block_size, max_seq_len,
+                                         device, &a))
+      return rc;
+  }
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  a.fp8_format = fp8_format;
+  if (a.num_seqs == 0) return KVC_OK;
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_paged_decode(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "paged_attention_fp8 launch");
+  return KVC_OK;
+}
+
+int kvc_convert_fp8(kvc_dltensor* dst, const kvc_dltensor* src, float scale, int fp8_format, void* stream) {
+  if (int rc = check_fp8_args(scale, 1.f, fp8_format)) return rc;
+  View d, s;
+  if (!parse(dst, "dst", &d) || !parse(src, "src", &s)) return KVC_EINVAL;
+  if (d.ndim != s.ndim) return fail(KVC_EINVAL, "src and dst shapes differ");
+  for (int i = 0; i < d.ndim; ++i)
+    if (d.shape[i] != s.shape[i]) return fail(KVC_EINVAL, "src and dst shapes differ");
+  auto ok_type = [](ElemType t) { return t == ElemType::U8 || is_float(t); };
+  if (!ok_type(d.dtype) || !ok_type(s.dtype))
+    return fail(KVC_EINVAL, "convert_fp8 converts between uint8 codes and float32/float16/bfloat16");
+  if (!d.dense_from(0) || !s.dense_from(0)) return fail(KVC_EINVAL, "src and dst must be contiguous");
+  int device = -1;
+  if (int rc = check_all_cuda({&d, &s}, &device)) return rc;
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_convert_fp8(s.dtype, d.dtype, s.data, d.data, scale, s.numel(), fp8_format,
+                                     static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "convert_fp8 launch");
   return KVC_OK;
 }
 

@@ -89,6 +89,11 @@ struct DecodeArgs {
   int64_t out_seq_stride, out_head_stride;    // elements
   int64_t k_block_stride, k_head_stride;      // elements
   int64_t v_block_stride, v_head_stride;      // elements
+  int64_t k_tok_stride, v_tok_stride;         // token-major caches: elements between a block's tokens
+  bool flash;                                 // token-major caches ([nb, bs, H, D] / [slots, H, D])
+  int prefix_len, prefix_parts, prefix_part_size;  // shared-prefix decode (0 = off)
+  float k_scale, v_scale;                     // one-byte (FP8) caches: value = code * scale
+  int fp8_format;                             // 0 = E4M3, 1 = E5M2
   int64_t table_stride;                       // elements
   int partition_size;                         // tokens per partition (split-K)
   int num_partitions;                         // 1 = single pass
@@ -109,6 +114,8 @@ struct ReshapeArgs {
   int64_t num_blocks;
   int64_t key_tok_stride, key_head_stride;      // elements
   int64_t value_tok_stride, value_head_stride;  // elements
+  float k_scale, v_scale;                       // one-byte caches: code = encode(x / scale)
+  int fp8_format;                               // 0 = E4M3, 1 = E5M2
   int64_t kc_block_stride, kc_head_stride;      // vLLM: [nb, H, D/x, bs, x]; flash: [nb, bs, H, D]
   int64_t vc_block_stride, vc_head_stride;
   int64_t kc_tok_stride, vc_tok_stride;         // flash layout only
@@ -134,6 +141,8 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream);
 // Split-K decode with its partials in the library's static scratch array
 // (kvc_paged_attention_v2_noalloc).  `a` carries no workspace pointers.
 cudaError_t launch_paged_decode_noalloc(DecodeArgs a, cudaStream_t stream);
+// Shared-prefix decode: tail partitions, the cascade prefix kernel, the reduce.
+cudaError_t launch_paged_decode_cascade(const DecodeArgs& a, cudaStream_t stream);
 // Whole-block copies (copy_blocks / swap_blocks).  A plane is one buffer
 // pair; every plane of one launch has the same block size in bytes.
 constexpr int kMaxBlockPlanes = 32;
@@ -152,6 +161,11 @@ struct BlockCopyArgs {
 };
 cudaError_t launch_block_copies(const BlockCopyArgs& a, cudaStream_t stream);
 cudaError_t launch_reshape_and_cache(const ReshapeArgs& a, cudaStream_t stream);
+// Quantising append into one-byte caches (vLLM layout, x = 16).
+cudaError_t launch_reshape_and_cache_fp8(const ReshapeArgs& a, cudaStream_t stream);
+// Elementwise codec of convert_fp8.metal (U8 <-> F32/F16/BF16, U8 -> U8, float -> float).
+cudaError_t launch_convert_fp8(ElemType src_type, ElemType dst_type, const void* src, void* dst, float scale,
+                               int64_t n, int fmt, cudaStream_t stream);
 cudaError_t launch_reshape_and_cache_flash(const ReshapeArgs& a, cudaStream_t stream);
 cudaError_t launch_gather_kv(const GatherArgs& a, cudaStream_t stream);
 

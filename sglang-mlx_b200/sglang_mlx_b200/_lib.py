@@ -31,6 +31,7 @@ STATUS_SLOT_OOB = 0x1
 STATUS_BLOCK_OOB = 0x2
 STATUS_WAIT_TIMEOUT = 0x4
 STATUS_INDEX_OOB = 0x8
+STATUS_PREFIX_MISMATCH = 0x10
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int
@@ -48,10 +49,24 @@ SIGNATURES: dict[str, tuple] = {
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _i, _p],
     ),
     "kvc_paged_attention_v2_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _i, _p]),
+    "kvc_paged_attention_cascade": (
+        _i,
+        [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _i, _i, _i, _p],
+    ),
+    "kvc_paged_attention_flash": (
+        _i,
+        [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _i, _p],
+    ),
     "kvc_reshape_and_cache": (_i, [_p, _p, _p, _p, _p, _p]),
     "kvc_reshape_and_cache_flash": (_i, [_p, _p, _p, _p, _p, _p]),
     "kvc_gather_kv": (_i, [_p, _p, _p, _p, _p, _p]),
     "kvc_copy_blocks": (_i, [_p, _i, _p, _i, _p, _p]),
+    "kvc_reshape_and_cache_fp8": (_i, [_p, _p, _p, _p, _p, _f, _f, _i, _p]),
+    "kvc_paged_attention_fp8": (
+        _i,
+        [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _f, _f, _i, _i, _p],
+    ),
+    "kvc_convert_fp8": (_i, [_p, _p, _f, _i, _p]),
     "kvc_swap_blocks": (_i, [_p, _p, _p, _p]),
     "kvc_get_max_shared_memory_per_block_device_attribute": (
         _i,

@@ -15,6 +15,7 @@ stream) and is asynchronous like an unevaluated mx.array; `to_numpy()` or
 from __future__ import annotations
 
 import ctypes
+import math
 
 import numpy as np
 
@@ -143,6 +144,127 @@ def paged_attention_v2(
     return out
 
 
+def paged_attention_flash(
+    query,
+    key_cache,
+    value_cache,
+    block_tables,
+    context_lens,
+    num_kv_heads: int,
+    scale: float,
+    block_size: int,
+    max_seq_len: int,
+    alibi_slopes=None,
+    *,
+    partition_size: int | None = None,
+    workspace=None,
+    out=None,
+    stream=None,
+):
+    """Decode over token-major caches: [num_blocks, block_size, kv_heads, D]
+    (the reshape_and_cache_flash layout) or a token pool [slots, kv_heads, D]
+    with block_size 1, whose block table rows are slot lists.  Same math and
+    edge rules as paged_attention_v1.  partition_size None lets choose_decode
+    pick (0 = single pass)."""
+    query, key_cache, value_cache = _dev(query), _dev(key_cache), _dev(value_cache)
+    block_tables, context_lens, alibi_slopes = _dev(block_tables), _dev(context_lens), _dev(alibi_slopes)
+    shape, _, _, _, dev = describe(query)
+    if partition_size is None:
+        # the token-major kernel keeps two CTAs per SM (16-token groups)
+        partition_size = choose_decode(shape[0], num_kv_heads, max_seq_len, 16)
+    if out is None:
+        out = _out_like_query(query)
+    ws = (None, None, None)
+    if partition_size:
+        ws = workspace if workspace is not None else splitk_workspace(shape[0], shape[1], shape[2], max_seq_len,
+                                                                      partition_size, dev)
+    ptrs = [as_dltensor(a, n) for a, n in ((out, "out"), (ws[0], "exp_sums"), (ws[1], "max_logits"),
+                                           (ws[2], "tmp_out"), (query, "query"), (key_cache, "key_cache"),
+                                           (value_cache, "value_cache"), (block_tables, "block_tables"),
+                                           (context_lens, "context_lens"), (alibi_slopes, "alibi_slopes"))]
+    rc = _L.kvc_paged_attention_flash(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ptrs[4][0], ptrs[5][0],
+                                      ptrs[6][0], ptrs[7][0], ptrs[8][0], int(num_kv_heads), float(scale),
+                                      int(block_size), int(max_seq_len), ptrs[9][0], int(partition_size),
+                                      _stream(stream))
+    _lib.check(rc)
+    return out
+
+
+def cascade_partitions(num_seqs: int, num_heads: int, num_kv_heads: int, max_seq_len: int, shared_prefix_len: int,
+                       block_size: int = 16, sm_count: int = 148) -> tuple[int, int]:
+    """(prefix_partition_size, partition_size) for paged_attention_cascade.
+
+    The prefix kernel's grid is (64-row tiles of the B*G query rows) x (prefix
+    chunks) x (kv heads); chunks are sized for about two CTAs per SM.  The
+    tokens after the prefix form one partition when there are at most 1024 of
+    them, else 1024-token partitions."""
+    unit = 32 * block_size // math.gcd(32, block_size)
+    tiles = -(-num_seqs * (num_heads // num_kv_heads) // 64)
+    chunks = max(1, -(-2 * sm_count // max(1, tiles * num_kv_heads)))
+    pp = -(-shared_prefix_len // chunks)
+    pp = max(unit, -(-pp // unit) * unit)
+    tail = max(0, max_seq_len - shared_prefix_len)
+    pt = 1024 if tail > 1024 else max(unit, -(-tail // unit) * unit)
+    return pp, pt
+
+
+def cascade_workspace(num_seqs: int, num_heads: int, head_size: int, max_seq_len: int, shared_prefix_len: int,
+                      prefix_partition_size: int, partition_size: int, device: int | None = None):
+    """(exp_sums, max_logits, tmp_out) for paged_attention_cascade."""
+    parts = -(-shared_prefix_len // prefix_partition_size)
+    if max_seq_len > shared_prefix_len:
+        parts += -(-(max_seq_len - shared_prefix_len) // partition_size)
+    es = DeviceArray.empty((num_seqs, num_heads, parts), dtypes.float32, device)
+    ml = DeviceArray.empty((num_seqs, num_heads, parts), dtypes.float32, device)
+    to = DeviceArray.empty((num_seqs, num_heads, parts, head_size), dtypes.float32, device)
+    return es, ml, to
+
+
+def paged_attention_cascade(
+    query,
+    key_cache,
+    value_cache,
+    block_tables,
+    context_lens,
+    num_kv_heads: int,
+    scale: float,
+    block_size: int,
+    max_seq_len: int,
+    shared_prefix_len: int,
+    *,
+    prefix_partition_size: int | None = None,
+    partition_size: int | None = None,
+    workspace=None,
+    out=None,
+    stream=None,
+):
+    """Decode of a batch whose block tables all start with the same
+    shared_prefix_len tokens (a radix-cache hit shared by every sequence): the
+    prefix is attended once per KV head for all sequences together, the rest
+    per sequence, merged by log-sum-exp.  Same arguments and result as
+    paged_attention_v1 (no ALiBi), plus the prefix length."""
+    query, key_cache, value_cache = _dev(query), _dev(key_cache), _dev(value_cache)
+    block_tables, context_lens = _dev(block_tables), _dev(context_lens)
+    shape, _, _, _, dev = describe(query)
+    pp, pt = cascade_partitions(shape[0], shape[1], num_kv_heads, max_seq_len, shared_prefix_len, block_size)
+    pp = prefix_partition_size or pp
+    pt = partition_size or pt
+    if out is None:
+        out = _out_like_query(query)
+    if workspace is None:
+        workspace = cascade_workspace(shape[0], shape[1], shape[2], max_seq_len, shared_prefix_len, pp, pt, dev)
+    es, ml, to = workspace
+    ptrs = [as_dltensor(a, n) for a, n in ((out, "out"), (es, "exp_sums"), (ml, "max_logits"), (to, "tmp_out"),
+                                           (query, "query"), (key_cache, "key_cache"), (value_cache, "value_cache"),
+                                           (block_tables, "block_tables"), (context_lens, "context_lens"))]
+    rc = _L.kvc_paged_attention_cascade(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ptrs[4][0], ptrs[5][0],
+                                        ptrs[6][0], ptrs[7][0], ptrs[8][0], int(num_kv_heads), float(scale),
+                                        int(block_size), int(max_seq_len), None, int(shared_prefix_len), int(pp),
+                                        int(pt), _stream(stream))
+    _lib.check(rc)
+    return out
+
+
 def choose_decode(num_seqs: int, num_kv_heads: int, max_seq_len: int, block_size: int = 16,
                   sm_count: int = 148) -> int:
     """0 for the single-pass decode, else the split-K partition size to use.
@@ -240,6 +362,62 @@ def _mapping(block_mapping):
             return np.ascontiguousarray(block_mapping)
         return block_mapping
     return np.ascontiguousarray(np.asarray(block_mapping, dtype=np.int64))
+
+
+_FP8 = {"e4m3": 0, "e5m2": 1}
+
+
+def reshape_and_cache_fp8(key, value, key_cache, value_cache, slot_mapping, k_scale: float = 1.0,
+                          v_scale: float = 1.0, fp8_format: str = "e4m3", *, stream=None):
+    """reshape_and_cache into one-byte (uint8) caches: each value is stored as
+    encode(x / scale) in the float8.metal code of `fp8_format`.  Caches are
+    [nb, kv_heads, D/16, bs, 16] and [nb, kv_heads, D, bs]."""
+    ptrs = [as_dltensor(_dev(a), n) for a, n in ((key, "key"), (value, "value"), (key_cache, "key_cache"),
+                                                 (value_cache, "value_cache"), (slot_mapping, "slot_mapping"))]
+    _lib.check(_L.kvc_reshape_and_cache_fp8(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ptrs[4][0],
+                                            float(k_scale), float(v_scale), _FP8[fp8_format], _stream(stream)))
+    return [key_cache, value_cache]
+
+
+def paged_attention_fp8(query, key_cache, value_cache, block_tables, context_lens, num_kv_heads: int, scale: float,
+                        block_size: int, max_seq_len: int, alibi_slopes=None, *, k_scale: float = 1.0,
+                        v_scale: float = 1.0, fp8_format: str = "e4m3", partition_size: int | None = None,
+                        workspace=None, out=None, stream=None):
+    """paged_attention_v1 over one-byte caches written by reshape_and_cache_fp8
+    (values decode(code) * scale).  partition_size None lets choose_decode pick
+    (0 = single pass)."""
+    query, key_cache, value_cache = _dev(query), _dev(key_cache), _dev(value_cache)
+    block_tables, context_lens, alibi_slopes = _dev(block_tables), _dev(context_lens), _dev(alibi_slopes)
+    shape, _, _, _, dev = describe(query)
+    if partition_size is None:
+        partition_size = choose_decode(shape[0], num_kv_heads, max_seq_len, 16 if block_size <= 16 else 32)
+    if out is None:
+        out = _out_like_query(query)
+    ws = (None, None, None)
+    if partition_size:
+        ws = workspace if workspace is not None else splitk_workspace(shape[0], shape[1], shape[2], max_seq_len,
+                                                                      partition_size, dev)
+    ptrs = [as_dltensor(a, n) for a, n in ((out, "out"), (ws[0], "exp_sums"), (ws[1], "max_logits"),
+                                           (ws[2], "tmp_out"), (query, "query"), (key_cache, "key_cache"),
+                                           (value_cache, "value_cache"), (block_tables, "block_tables"),
+                                           (context_lens, "context_lens"), (alibi_slopes, "alibi_slopes"))]
+    rc = _L.kvc_paged_attention_fp8(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ptrs[4][0], ptrs[5][0],
+                                    ptrs[6][0], ptrs[7][0], ptrs[8][0], int(num_kv_heads), float(scale),
+                                    int(block_size), int(max_seq_len), ptrs[9][0], float(k_scale), float(v_scale),
+                                    _FP8[fp8_format], int(partition_size), _stream(stream))
+    _lib.check(rc)
+    return out
+
+
+def convert_fp8(dst, src, scale: float = 1.0, fp8_format: str = "e4m3", *, stream=None):
+    """convert_fp8_kernel (convert_fp8.metal:13-80): uint8 codes <-> float
+    arrays of the same shape (quantise encode(x / scale), dequantise
+    decode(code) * scale, rescale codes, or scale floats).  Returns dst."""
+    d, dk = as_dltensor(_dev(dst), "dst")
+    s, sk = as_dltensor(_dev(src), "src")
+    _lib.check(_L.kvc_convert_fp8(d, s, float(scale), _FP8[fp8_format], _stream(stream)))
+    del dk, sk
+    return dst
 
 
 def copy_blocks(key_caches, value_caches, block_mapping, *, stream=None):

@@ -9,6 +9,12 @@ sglang_mlx/srt/mem_cache/memory_pool.py.
   gather launch writing (1, H, T, D) (memory_pool.py:117-159).
 - PooledKVCache: the per-request adapter (memory_pool.py:167-269), unchanged
   in behaviour.
+
+Beyond the reference: the decode its pool leaves as a TODO
+(memory_pool.py:110-112) — attention straight on the scattered pool slots,
+with no per-layer gather.  MHATokenPool.decode runs it for a batch of slot
+lists; PooledKVCache.update_and_attend is update_and_fetch followed by the
+attention, for single-token decode, in two launches (append, decode).
 """
 
 from __future__ import annotations
@@ -142,6 +148,31 @@ class MHATokenPool:
         _lib.check(_L.kvc_gather_kv(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ptrs[4][0], _stream(stream)))
         return k_out, v_out
 
+    def decode(self, layer_idx: int, queries, slot_tables, context_lens, scale: float | None = None, *,
+               max_seq_len: int | None = None, alibi_slopes=None, partition_size: int | None = None,
+               out=None, stream=None):
+        """Single-token attention of a batch straight on the pool's slots.
+
+        Args:
+            queries: ``(B, n_heads, head_dim)``, n_heads a multiple of n_kv_heads.
+            slot_tables: ``(B, max_len)`` int32 slot lists (sequence b attends
+                to slots ``slot_tables[b, :context_lens[b]]``, in order).
+            context_lens: ``(B,)`` int32.
+            scale: softmax scale, default ``head_dim ** -0.5``.
+        Returns ``(B, n_heads, head_dim)`` in the pool dtype.
+        """
+        from ... import metal_kernels as mk
+
+        tshape = describe(slot_tables)[0] if not isinstance(slot_tables, (list, np.ndarray)) \
+            else np.asarray(slot_tables).shape
+        if max_seq_len is None:
+            max_seq_len = max(1, int(tshape[1]))
+        if scale is None:
+            scale = self.head_dim ** -0.5
+        return mk.paged_attention_flash(queries, self.k_buffer[layer_idx], self.v_buffer[layer_idx], slot_tables,
+                                        context_lens, self.n_kv_heads, scale, 1, max_seq_len, alibi_slopes,
+                                        partition_size=partition_size, out=out, stream=stream)
+
 
 class PooledKVCache:
     """Adapter that makes the shared KV pool look like a per-request KV cache.
@@ -172,16 +203,58 @@ class PooledKVCache:
     def _all_indices(self) -> list[int]:
         return self._prefix_indices + self._new_indices[: self._store_offset]
 
-    def _store_new(self, keys, values) -> None:
+    def _store_new(self, keys, values, stream=None) -> None:
         n_new = describe(keys)[0][2]
         store_indices = self._new_indices[self._store_offset: self._store_offset + n_new]
         self._store_offset += n_new
-        self._pool.store(self._layer_idx, store_indices, keys, values)
+        self._pool.store(self._layer_idx, store_indices, keys, values, stream=stream)
 
     def update_and_fetch(self, keys, values):
         """Stores new KV and gathers all (prefix + new) KV (memory_pool.py:206-234)."""
         self._store_new(keys, values)
         return self._pool.fetch(self._layer_idx, self._all_indices())
+
+    def update_and_attend(self, queries, keys, values, scale: float | None = None, *, stream=None):
+        """Stores the new token's KV and attends over prefix + new slots on the
+        pool itself (no gather).  Single-token decode only.
+
+        Args:
+            queries: ``(1, n_heads, 1, head_dim)``; keys, values:
+                ``(1, n_kv_heads, 1, head_dim)`` (mlx-lm format).
+        Returns ``(1, n_heads, 1, head_dim)``.
+        """
+        qshape, qstr, qdt, _, qdev = describe(queries)
+        if len(qshape) != 4 or qshape[0] != 1 or qshape[2] != 1 or describe(keys)[0][2] != 1:
+            raise ValueError("update_and_attend handles single-token decode: queries (1, H, 1, D) and keys/values "
+                             "(1, H_kv, 1, D); use update_and_fetch for prefill")
+        self._store_new(keys, values, stream=stream)
+        slots = np.asarray(self._all_indices(), dtype=np.int32)[None, :]
+        qptr, qkeep = as_dltensor(queries, "queries")
+        qt, qk = make_dltensor(qptr.contents.data + qptr.contents.byte_offset, (1, qshape[1], qshape[3]),
+                               (qstr[0], qstr[1], qstr[3]), qdt, qptr.contents.device.device_id)
+
+        out = DeviceArray.empty((1, qshape[1], qshape[3]), qdt, qdev)
+        lens = DeviceArray.from_numpy(np.array([slots.shape[1]], dtype=np.int32), device=qdev)
+        tables = DeviceArray.from_numpy(slots, device=qdev)
+        from ... import metal_kernels as mk
+
+        ws = (None, None, None)
+        T = slots.shape[1]
+        psize = mk.choose_decode(1, self._pool.n_kv_heads, T, 16)
+        if psize:
+            ws = mk.splitk_workspace(1, qshape[1], qshape[3], T, psize, qdev)
+        if scale is None:
+            scale = self._pool.head_dim ** -0.5
+        ptrs = [as_dltensor(a, n) for a, n in ((out, "out"), (ws[0], "exp_sums"), (ws[1], "max_logits"),
+                                               (ws[2], "tmp_out"), (self._pool.k_buffer[self._layer_idx], "k"),
+                                               (self._pool.v_buffer[self._layer_idx], "v"), (tables, "tables"),
+                                               (lens, "lens"))]
+        _lib.check(_L.kvc_paged_attention_flash(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ctypes.pointer(qt),
+                                                ptrs[4][0], ptrs[5][0], ptrs[6][0], ptrs[7][0],
+                                                self._pool.n_kv_heads, float(scale), 1, T, None, int(psize),
+                                                _stream(stream)))
+        del qkeep, qk, ptrs
+        return out.reshape(1, qshape[1], 1, qshape[3])
 
     @property
     def state(self):

@@ -1,0 +1,251 @@
+"""GPU parity tests of the token-major decode (kvc_paged_attention_flash): the
+reshape_and_cache_flash layout [nb, bs, H, D] and the MHATokenPool buffers
+[slots, H, D] (block size 1, slot lists as block tables), through
+metal_kernels.paged_attention_flash, MHATokenPool.decode and
+PooledKVCache.update_and_attend.  Oracle: kv_oracle.paged_attention_flash
+(float64), itself pinned to the golden-pinned paged_attention_v1
+restatement in tests/test_oracle.py."""
+
+import numpy as np
+import pytest
+
+import cases
+from helpers import ATOL_NS, RTOL_NS, assert_close, fill_cache, upload_case
+from oracle import kv_oracle
+from sglang_mlx_b200 import _lib
+from sglang_mlx_b200 import metal_kernels as mk
+from sglang_mlx_b200.device_array import DeviceArray
+from sglang_mlx_b200.srt.mem_cache.memory_pool import MHATokenPool, PooledKVCache, TokenPoolAllocator
+
+pytestmark = pytest.mark.gpu
+
+
+def flash_case(seed, dtype, num_seqs, hq, hkv, d, bs, lens):
+    """A batch in token-major caches.  bs = 1 gives a token pool: caches
+    [slots, H, D] and block tables that are slot lists."""
+    c = cases.paged_batch(seed, dtype, num_seqs, hq, hkv, d, 16, lens)
+    nb16 = c["k_cache"].shape[0]
+    slots = c["slot_mapping"].astype(np.int64)
+    T = len(slots)
+    if bs == 1:
+        shape = (nb16 * 16 + 1, hkv, d)  # + the pool's padding slot 0
+        slots = slots + 1
+        t = np.arange(c["block_tables"].shape[1] * 16)
+        tables = np.where(c["block_tables"][:, t // 16] >= 0, c["block_tables"][:, t // 16] * 16 + t % 16 + 1, 0)
+    else:
+        # re-block the same tokens into bs-token blocks of a permuted pool
+        rng = np.random.default_rng(seed + 5)
+        nbb = -(-nb16 * 16 // bs) + 2
+        perm = rng.permutation(nbb)
+        maxb = -(-c["block_tables"].shape[1] * 16 // bs)
+        tables = np.full((num_seqs, maxb), -1, np.int64)
+        pos = 0
+        off = 0
+        slots = np.empty(T, np.int64)
+        for b, n in enumerate(c["context_lens"]):
+            nb = -(-int(n) // bs)
+            tables[b, :nb] = perm[pos:pos + nb]
+            tt = np.arange(int(n))
+            slots[off:off + n] = tables[b, tt // bs] * bs + tt % bs
+            pos += nb
+            off += int(n)
+        shape = (nbb, bs, hkv, d)
+    store = np.float16 if dtype == "float16" else np.float32
+    return dict(c=c, shape=shape, tables=tables.astype(np.int32), slots=slots.astype(np.int32), bs=bs, store=store)
+
+
+def upload_flash(fc):
+    c = fc["c"]
+    dt = c["dtype"]
+    q = DeviceArray.from_numpy(c["q"], dtype=dt)
+    k = DeviceArray.from_numpy(c["k"], dtype=dt)
+    v = DeviceArray.from_numpy(c["v"], dtype=dt)
+    kc = DeviceArray.zeros(fc["shape"], dt)
+    vc = DeviceArray.zeros(fc["shape"], dt)
+    mk.reshape_and_cache_flash(k, v, kc, vc, DeviceArray.from_numpy(fc["slots"]))
+    return dict(q=q, kc=kc, vc=vc, tables=DeviceArray.from_numpy(fc["tables"]),
+                lens=DeviceArray.from_numpy(c["context_lens"].astype(np.int32)))
+
+
+def oracle_flash(fc, alibi=None, max_seq_len=None):
+    c = fc["c"]
+    fk = np.zeros(fc["shape"], np.float32)
+    fv = np.zeros(fc["shape"], np.float32)
+    kv_oracle.reshape_and_cache_flash(kv_oracle.round_to(c["k"], c["dtype"]), kv_oracle.round_to(c["v"], c["dtype"]),
+                                      fk, fv, fc["slots"])
+    return kv_oracle.paged_attention_flash(kv_oracle.round_to(c["q"], c["dtype"]), fk, fv, fc["tables"],
+                                           c["context_lens"], c["num_kv_heads"], c["scale"],
+                                           max_seq_len or c["max_seq_len"], alibi)
+
+
+def run_flash(fc, d, partition_size=0, alibi=None, max_seq_len=None):
+    c = fc["c"]
+    return mk.paged_attention_flash(d["q"], d["kc"], d["vc"], d["tables"], d["lens"], c["num_kv_heads"], c["scale"],
+                                    fc["bs"], max_seq_len or c["max_seq_len"], alibi,
+                                    partition_size=partition_size).to_numpy()
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("bs", [1, 8, 16, 32])
+def test_layouts_dtypes_head_sizes(gpu, dtype, D, bs):
+    fc = flash_case(4000 + D + bs, dtype, 3, 8, 2, D, bs, [1, 37, 300])
+    d = upload_flash(fc)
+    ref = oracle_flash(fc)
+    assert_close(run_flash(fc, d), ref, ATOL_NS, RTOL_NS, f"{dtype} D{D} bs{bs}")
+    assert_close(run_flash(fc, d, partition_size=64), ref, ATOL_NS, RTOL_NS, f"{dtype} D{D} bs{bs} split")
+    assert gpu.get_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(4, 4), (8, 4), (16, 4), (28, 4), (32, 4), (32, 2), (16, 1), (64, 2)])
+def test_group_sizes(gpu, Hq, Hkv):
+    fc = flash_case(4100 + Hq + Hkv, "bfloat16", 3, Hq, Hkv, 128, 1, [200, 33, 1500])
+    d = upload_flash(fc)
+    if Hq // Hkv > 16:  # one tensor-core tile holds at most 16 query heads of a group
+        with pytest.raises(NotImplementedError, match="16 query heads"):
+            run_flash(fc, d)
+        return
+    assert_close(run_flash(fc, d), oracle_flash(fc), ATOL_NS, RTOL_NS, f"G={Hq // Hkv}")
+
+
+def test_alibi_and_split(gpu):
+    fc = flash_case(4200, "float16", 3, 8, 2, 128, 16, [17, 2000, 64])
+    d = upload_flash(fc)
+    slopes = (2.0 ** -np.arange(1, 9)).astype(np.float32)
+    ref = oracle_flash(fc, alibi=slopes)
+    al = DeviceArray.from_numpy(slopes)
+    assert_close(run_flash(fc, d, alibi=al), ref, ATOL_NS, RTOL_NS, "alibi")
+    assert_close(run_flash(fc, d, partition_size=256, alibi=al), ref, ATOL_NS, RTOL_NS, "alibi split")
+
+
+def test_mixed_lengths_zero_rows_and_max_seq_len(gpu):
+    lens = [0, 1, 15, 16, 17, 511, 512, 513, 1000, 0, 3000]
+    fc = flash_case(4300, "bfloat16", len(lens), 16, 4, 128, 1, [max(x, 1) for x in lens])
+    fc["c"]["context_lens"] = np.array(lens, np.int32)
+    d = upload_flash(fc)
+    for psize in (0, 256):
+        out = run_flash(fc, d, partition_size=psize)
+        assert not out[0].any() and not out[9].any()
+        assert_close(out, oracle_flash(fc), ATOL_NS, RTOL_NS, f"mixed P={psize}")
+    out = run_flash(fc, d, max_seq_len=1000)
+    assert not out[10].any()
+    assert_close(out, oracle_flash(fc, max_seq_len=1000), ATOL_NS, RTOL_NS, "max_seq_len")
+
+
+def test_nan_in_unused_slots_never_leaks(gpu):
+    fc = flash_case(4400, "float16", 2, 8, 2, 128, 1, [20, 40])
+    d = upload_flash(fc)
+    # poison every slot no sequence uses
+    used = set(fc["slots"].tolist())
+    kc = d["kc"].to_numpy()
+    vc = d["vc"].to_numpy()
+    unused = np.array([i for i in range(kc.shape[0]) if i not in used])
+    kc[unused] = np.nan
+    vc[unused] = np.nan
+    d["kc"] = DeviceArray.from_numpy(kc)
+    d["vc"] = DeviceArray.from_numpy(vc)
+    out = run_flash(fc, d)
+    assert np.isfinite(out).all()
+    assert_close(out, oracle_flash(fc), ATOL_NS, RTOL_NS, "nan neighbours")
+
+
+def test_out_of_range_slot_is_skipped_and_flagged(gpu):
+    fc = flash_case(4500, "float16", 2, 8, 2, 128, 1, [40, 40])
+    d = upload_flash(fc)
+    t = fc["tables"].copy()
+    t[1, 5] = 10_000_000
+    d["tables"] = DeviceArray.from_numpy(t)
+    gpu.get_status(clear=True)
+    out = run_flash(fc, d)
+    assert np.isfinite(out).all()
+    assert gpu.get_status(clear=True) & _lib.STATUS_BLOCK_OOB
+
+
+def test_unsupported_dtype_is_refused(gpu):
+    fc = flash_case(4600, "float32", 2, 8, 2, 128, 1, [4, 5])
+    d = upload_flash(fc)
+    with pytest.raises(NotImplementedError, match="float16/bfloat16"):
+        run_flash(fc, d)
+
+
+def test_matches_paged_layout_at_scale(gpu):
+    """Config 2's shape (32 sequences here, U[512, 4096] tokens, 32/8 heads, bf16):
+    the same tokens through the vLLM layout (paged_attention_v1) and the token pool."""
+    rng = np.random.default_rng(2024)
+    lens = rng.integers(512, 4097, size=32)
+    fc = flash_case(4700, "bfloat16", 32, 32, 8, 128, 1, lens)
+    d = upload_flash(fc)
+    c = fc["c"]
+    pd = upload_case(c)
+    fill_cache(pd)
+    v1 = mk.paged_attention_v1(pd["q"], pd["k_cache"], pd["v_cache"], pd["block_tables"], pd["context_lens"], 8,
+                               c["scale"], 16, c["max_seq_len"]).to_numpy()
+    for psize in (0, 1024):
+        assert_close(run_flash(fc, d, partition_size=psize), v1.astype(np.float64), ATOL_NS, RTOL_NS,
+                     f"pool vs paged P={psize}")
+
+
+# ---- the pool API ----------------------------------------------------------------
+
+def _pool_batch(seed, dtype, hq, hkv, d, prompt_lens, pool_size=6000):
+    rng = np.random.default_rng(seed)
+    pool = MHATokenPool(pool_size, 2, hkv, d, dtype)
+    alloc = TokenPoolAllocator(pool_size)
+    slots, keys = [], []
+    for n in prompt_lens:
+        idx = alloc.alloc(int(n))
+        kv = [kv_oracle.round_to(rng.standard_normal((1, hkv, n, d)).astype(np.float32), dtype) for _ in range(2)]
+        for layer in range(2):
+            pool.store(layer, idx, DeviceArray.from_numpy(kv[0], dtype=dtype), DeviceArray.from_numpy(kv[1],
+                                                                                                      dtype=dtype))
+        slots.append(idx)
+        keys.append(kv)
+    return pool, alloc, slots, keys, rng
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+def test_pool_decode_matches_oracle(gpu, dtype):
+    prompt_lens = [1, 17, 300, 1234]
+    pool, _, slots, keys, rng = _pool_batch(4800, dtype, 32, 8, 128, prompt_lens)
+    B, T = len(prompt_lens), max(prompt_lens)
+    tables = np.zeros((B, T), np.int32)
+    for b, idx in enumerate(slots):
+        tables[b, :len(idx)] = idx
+    q = kv_oracle.round_to(rng.standard_normal((B, 32, 128)).astype(np.float32), dtype)
+    out = pool.decode(1, DeviceArray.from_numpy(q, dtype=dtype), tables, np.array(prompt_lens, np.int32)).to_numpy()
+    ref = np.zeros((B, 32, 128))
+    for b in range(B):
+        k = keys[b][0][0].transpose(1, 0, 2)  # (S, H, D)
+        v = keys[b][1][0].transpose(1, 0, 2)
+        for h in range(8):
+            ref[b, 4 * h:4 * h + 4] = kv_oracle.attend(q[b, 4 * h:4 * h + 4], k[:, h], v[:, h], 128 ** -0.5)
+    assert_close(out, ref, ATOL_NS, RTOL_NS, f"pool decode {dtype}")
+
+
+def test_pooled_cache_update_and_attend_equals_gather_path(gpu):
+    """update_and_attend (append + decode on the pool) against update_and_fetch
+    (append + gather) followed by the oracle's attention, over several steps."""
+    dtype = "bfloat16"
+    pool, alloc, slots, keys, rng = _pool_batch(4900, dtype, 16, 4, 128, [700])
+    prefix = list(slots[0])
+    for step in range(3):
+        new = alloc.alloc(1)
+        caches = [PooledKVCache(pool, 0), PooledKVCache(pool, 1)]
+        q = kv_oracle.round_to(rng.standard_normal((1, 16, 1, 128)).astype(np.float32), dtype)
+        kn = kv_oracle.round_to(rng.standard_normal((1, 4, 1, 128)).astype(np.float32), dtype)
+        vn = kv_oracle.round_to(rng.standard_normal((1, 4, 1, 128)).astype(np.float32), dtype)
+        caches[0].set_indices(prefix, new)
+        caches[1].set_indices(prefix, new)
+        out = caches[0].update_and_attend(DeviceArray.from_numpy(q, dtype=dtype), DeviceArray.from_numpy(kn, dtype=dtype),
+                                          DeviceArray.from_numpy(vn, dtype=dtype))
+        assert out.shape == (1, 16, 1, 128)
+        kf, vf = caches[1].update_and_fetch(DeviceArray.from_numpy(kn, dtype=dtype),
+                                            DeviceArray.from_numpy(vn, dtype=dtype))
+        kf, vf = kf.to_numpy()[0], vf.to_numpy()[0]  # (H, T, D)
+        ref = np.stack([kv_oracle.attend(q[0, 4 * h:4 * h + 4, 0], kf[h], vf[h], 128 ** -0.5) for h in range(4)])
+        assert_close(out.to_numpy()[0, :, 0], ref.reshape(16, 128), ATOL_NS, RTOL_NS, f"step {step}")
+        prefix = prefix + new
+    with pytest.raises(ValueError, match="single-token"):
+        caches[0].update_and_attend(DeviceArray.from_numpy(np.zeros((1, 16, 2, 128), np.float32), dtype=dtype),
+                                    DeviceArray.from_numpy(np.zeros((1, 4, 2, 128), np.float32), dtype=dtype),
+                                    DeviceArray.from_numpy(np.zeros((1, 4, 2, 128), np.float32), dtype=dtype))

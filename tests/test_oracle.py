@@ -158,3 +158,63 @@ def test_swap_blocks_oracle_matches_reference_test():
     expected[2] = src[0]
     expected[1] = src[3]
     np.testing.assert_array_equal(kv_oracle.swap_blocks(src, dst, [[0, 2], [3, 1]]), expected)
+
+
+@pytest.mark.parametrize("bs", [1, 16])
+def test_flash_oracle_equals_paged_oracle(bs):
+    """The token-major restatement (paged_attention_flash) on caches filled with
+    the same tokens as the vLLM-layout caches gives the same float64 result as
+    the golden-pinned paged_attention_v1 restatement."""
+    c = cases.paged_batch(77, "float16", 3, 8, 2, 64, 16, [5, 40, 130])
+    kc, vc = kv_oracle.reshape_and_cache(c["k"].astype(np.float32), c["v"].astype(np.float32),
+                                         c["k_cache"].astype(np.float32), c["v_cache"].astype(np.float32),
+                                         c["slot_mapping"])
+    ref = kv_oracle.paged_attention_v1(c["q"], kc, vc, c["block_tables"], c["context_lens"], 2, c["scale"], 16,
+                                       c["max_seq_len"])
+    nb = c["k_cache"].shape[0]
+    if bs == 1:
+        fk = np.zeros((nb * 16, 2, 64), np.float32)
+        fv = np.zeros_like(fk)
+        kv_oracle.reshape_and_cache_flash(c["k"], c["v"], fk, fv, c["slot_mapping"])
+        t = np.arange(c["block_tables"].shape[1] * 16)
+        tables = c["block_tables"][:, t // 16].astype(np.int64) * 16 + t % 16
+    else:
+        fk = np.zeros((nb, 16, 2, 64), np.float32)
+        fv = np.zeros_like(fk)
+        kv_oracle.reshape_and_cache_flash(c["k"], c["v"], fk, fv, c["slot_mapping"])
+        tables = c["block_tables"]
+    got = kv_oracle.paged_attention_flash(c["q"], fk, fv, tables, c["context_lens"], 2, c["scale"], c["max_seq_len"])
+    np.testing.assert_array_equal(got, ref)
+
+
+def test_fp8_codec_restatement():
+    """float8.metal's codecs restated in kv_oracle: checked against torch's OCP
+    formats where the formats coincide (every E5M2 code; E4M3 codes below the
+    all-ones exponent, which the reference keeps for Inf/NaN) and on known
+    answers of the reference's IEEE-style E4M3 (max finite 240, Inf above)."""
+    import torch
+
+    codes = np.arange(256, dtype=np.uint8)
+    t5 = torch.from_numpy(codes.copy()).view(torch.float8_e5m2).float().numpy()
+    d5 = kv_oracle.fp8_to_float(codes, "e5m2")
+    assert np.array_equal(np.isnan(t5), np.isnan(d5)) and np.array_equal(t5[~np.isnan(t5)], d5[~np.isnan(d5)])
+    t4 = torch.from_numpy(codes.copy()).view(torch.float8_e4m3fn).float().numpy()
+    d4 = kv_oracle.fp8_to_float(codes, "e4m3")
+    low = ((codes >> 3) & 0xF) != 15
+    assert np.array_equal(t4[low], d4[low])
+    assert np.isposinf(d4[0x78]) and np.isneginf(d4[0xF8]) and np.isnan(d4[0x79])
+    for fmt, dec in (("e4m3", d4), ("e5m2", d5)):  # every finite code survives encode(decode(c))
+        fin = np.isfinite(dec)
+        assert np.array_equal(kv_oracle.float_to_fp8(dec[fin], fmt), codes[fin])
+    rng = np.random.default_rng(0)
+    x = (rng.standard_normal(50000) * 20).astype(np.float32)
+    x = x[(np.abs(x) > 2.0 ** -5) & (np.abs(x) < 240)]  # normal range: round to nearest even, as torch
+    assert np.array_equal(kv_oracle.float_to_fp8(x, "e4m3"),
+                          torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy())
+    enc = lambda v, f="e4m3": int(kv_oracle.float_to_fp8(np.array([v], np.float32), f)[0])
+    assert enc(1.0) == 0x38 and enc(240.0) == 0x77 and enc(-240.0) == 0xF7
+    assert enc(300.0) == 0x78 and enc(np.inf) == 0x78 and enc(np.nan) == 0x79  # saturates to Inf / keeps NaN
+    assert enc(2.0 ** -9) == 0x01 and enc(-0.0) == 0x80 and enc(2.0 ** -11) == 0x00
+    assert enc(2.0 ** -6 * (1 - 2.0 ** -10)) == 0x08  # subnormal rounding up into the smallest normal
+    assert enc(1e6) == 0x78 and enc(-1e6) == 0xF8 and enc(250.0) == 0x78  # past 240: +-Inf
+    assert enc(57344.0, "e5m2") == 0x7B and enc(65536.0, "e5m2") == 0x7C
