@@ -22,9 +22,12 @@
 //    output) of its own rows for partition `chunk`; the tokens after the
 //    prefix are partitions prefix_parts.. of the ordinary split-K kernel, and
 //    the split-K reduce merges both.
-//  * Launch order: tail partitions, then this kernel as a programmatic
-//    dependent (it needs nothing from them and overlaps their tail), which
-//    waits for them (griddepcontrol.wait) before exiting, then the reduce.
+//  * Launch order: this kernel (tensor-core bound), then the tail partitions
+//    (HBM bound) as a programmatic dependent so the two run side by side —
+//    every tail CTA waits for this grid (griddepcontrol.wait) before it exits
+//    — then the reduce, which waits for the tail grid.
+//  * P enters the P.V product as one bf16 value (no hi + lo split): over a
+//    long shared prefix the rounding of the many terms averages out.
 // Every wait is bounded; a timeout sets KVC_STATUS_WAIT_TIMEOUT and an abort
 // flag that ends every loop of the CTA.
 #pragma once
@@ -140,7 +143,6 @@ __global__ void __launch_bounds__((kCascadeConsumers + 1) * 32)
       }
       if (bad) set_status(&g_decode_status, KVC_STATUS_PREFIX_MISMATCH);
     }
-    grid_dependency_wait();
     return;
   }
 
@@ -190,8 +192,8 @@ __global__ void __launch_bounds__((kCascadeConsumers + 1) * 32)
       break;
     }
     const uint8_t* st = smem + (size_t)s * Geo::STAGE;
-    mma_group<T, Geo, D>(gs, qa, smem_u32(st), smem_u32(st + NBOX * BOX), c_begin + k * GT, c_end, masks[s], 0,
-                         qk_scale, false, 0.f, 0.f, lane, end_lo, end_hi);
+    mma_group<T, Geo, D, false>(gs, qa, smem_u32(st), smem_u32(st + NBOX * BOX), c_begin + k * GT, c_end, masks[s],
+                                0, qk_scale, false, 0.f, 0.f, lane, end_lo, end_hi);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
@@ -217,7 +219,6 @@ __global__ void __launch_bounds__((kCascadeConsumers + 1) * 32)
   };
   write_row(R_lo, seq_lo, g_lo, gs.m_lo, l_lo, 0);
   write_row(R_hi, seq_hi, g_hi, gs.m_hi, l_hi, 1);
-  grid_dependency_wait();
 }
 
 }  // namespace kvc

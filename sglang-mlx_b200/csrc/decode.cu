@@ -51,6 +51,7 @@ struct DecodeParams {
   // prefix_len + i * partition_size onwards.  part_offset is added to blockIdx.z by the partition kernels.
   int prefix_len, prefix_parts, prefix_part_size, part_offset;
   float k_scale, v_scale;  // one-byte caches: dequantisation scales (value = code * scale)
+  int wait_prior_at_end;   // partition kernel: griddepcontrol.wait before exiting (shared-prefix launch order)
   int64_t table_stride;
   int64_t part_seq_stride, part_head_stride;
   int64_t part_out_seq_stride, part_out_head_stride, part_out_part_stride;
@@ -566,6 +567,7 @@ static DecodeParams to_params(const DecodeArgs& a) {
   p.prefix_parts = a.prefix_parts;
   p.prefix_part_size = a.prefix_part_size;
   p.part_offset = 0;
+  p.wait_prior_at_end = 0;
   p.k_scale = a.cache_type == ElemType::U8 ? a.k_scale : 1.f;
   p.v_scale = a.cache_type == ElemType::U8 ? a.v_scale : 1.f;
   p.table_stride = a.table_stride;
@@ -625,7 +627,7 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
 // blocks), 6 stages (4 for 32-token blocks) of K and V pages.
 // ---------------------------------------------------------------------------
 template <typename T, int D, int BS>
-static cudaError_t launch_cascade_prefix(const DecodeParams& p, cudaStream_t stream, bool after_tail) {
+static cudaError_t launch_cascade_prefix(const DecodeParams& p, cudaStream_t stream, bool pdl) {
   constexpr int GT = BS <= 16 ? 16 : 32;
   constexpr int STAGES = BS <= 16 ? 6 : 4;
   using CG = CascadeGeom<D, BS, STAGES, GT>;
@@ -650,22 +652,22 @@ static cudaError_t launch_cascade_prefix(const DecodeParams& p, cudaStream_t str
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = after_tail ? 1 : 0;
+  cfg.numAttrs = pdl ? 1 : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
   count_launch();
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <typename T>
-static cudaError_t launch_cascade_prefix_t(const DecodeParams& p, int D, cudaStream_t stream, bool after_tail) {
+static cudaError_t launch_cascade_prefix_t(const DecodeParams& p, int D, cudaStream_t stream, bool pdl) {
   if (D == 128) {
-    if (p.block_size == 8) return launch_cascade_prefix<T, 128, 8>(p, stream, after_tail);
-    if (p.block_size == 16) return launch_cascade_prefix<T, 128, 16>(p, stream, after_tail);
-    return launch_cascade_prefix<T, 128, 32>(p, stream, after_tail);
+    if (p.block_size == 8) return launch_cascade_prefix<T, 128, 8>(p, stream, pdl);
+    if (p.block_size == 16) return launch_cascade_prefix<T, 128, 16>(p, stream, pdl);
+    return launch_cascade_prefix<T, 128, 32>(p, stream, pdl);
   }
-  if (p.block_size == 8) return launch_cascade_prefix<T, 64, 8>(p, stream, after_tail);
-  if (p.block_size == 16) return launch_cascade_prefix<T, 64, 16>(p, stream, after_tail);
-  return launch_cascade_prefix<T, 64, 32>(p, stream, after_tail);
+  if (p.block_size == 8) return launch_cascade_prefix<T, 64, 8>(p, stream, pdl);
+  if (p.block_size == 16) return launch_cascade_prefix<T, 64, 16>(p, stream, pdl);
+  return launch_cascade_prefix<T, 64, 32>(p, stream, pdl);
 }
 
 cudaError_t launch_paged_decode_cascade(const DecodeArgs& a, cudaStream_t stream) {
@@ -673,17 +675,18 @@ cudaError_t launch_paged_decode_cascade(const DecodeArgs& a, cudaStream_t stream
   if (!mma_supported(a) || a.alibi != nullptr || a.flash) return cudaErrorNotSupported;
   if (!pages_aligned(a)) return cudaErrorMisalignedAddress;
   DecodeParams p = to_params(a);
-  cudaError_t e = cudaSuccess;
   const bool tail = p.num_partitions > p.prefix_parts;
+  cudaError_t e = a.q_type == ElemType::BF16 ? launch_cascade_prefix_t<__nv_bfloat16>(p, a.head_size, stream, false)
+                                             : launch_cascade_prefix_t<__half>(p, a.head_size, stream, false);
+  if (e != cudaSuccess) return e;
   if (tail) {
     p.part_offset = p.prefix_parts;
+    p.wait_prior_at_end = 1;
     e = launch_mma(p, a, stream);
     if (e != cudaSuccess) return e;
     p.part_offset = 0;
+    p.wait_prior_at_end = 0;
   }
-  e = a.q_type == ElemType::BF16 ? launch_cascade_prefix_t<__nv_bfloat16>(p, a.head_size, stream, tail)
-                                 : launch_cascade_prefix_t<__half>(p, a.head_size, stream, tail);
-  if (e != cudaSuccess) return e;
   if (a.q_type == ElemType::BF16) return launch_reduce<__nv_bfloat16>(p, a.head_size, stream);
   return launch_reduce<__half>(p, a.head_size, stream);
 }

@@ -89,6 +89,18 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// 16-byte global -> shared copy (L2 only); completion is reported to an
+// mbarrier by cp_async_arrive.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+// One arrival on `bar` once every cp.async this thread issued before has
+// completed (the barrier's expected count includes it).
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -228,7 +240,12 @@ struct MmaGeom {
   static constexpr int BAR_OFF = ALIGN + RING;            // NW*STAGES mbarriers
   static constexpr int MASK_OFF = BAR_OFF + NW * STAGES * 8;
   static constexpr int COMBINE = NW * 16 * D * 4 + NW * 16 * 2 * 4;  // reuses the ring
-  static constexpr int SMEM = MASK_OFF + NW * STAGES * 4;
+  // kFlash: per warp, the block ids of two chunks of IDC groups (one id per
+  // token), filled a chunk ahead of the copies that use them
+  static constexpr int IDC = 8;
+  static constexpr int IDS_OFF = (MASK_OFF + NW * STAGES * 4 + 15) / 16 * 16;
+  static constexpr int SMEM = IDS_OFF + (FLASH ? NW * 2 * IDC * GT * 4 : 0);
+  static_assert(!FLASH || (STAGES <= IDC && (IDC * GT) % 32 == 0), "id chunks cover the ring");
   static_assert(COMBINE <= RING, "combine buffer must fit in the ring");
 };
 
@@ -271,7 +288,7 @@ struct GroupState {
 // length (ALiBi positions).  When the tile's rows belong to different
 // sequences (the shared-prefix kernel), `end_lo` / `end_hi` further end the
 // scores of this lane's rows r and r + 8; `end` still bounds the V data.
-template <typename T, typename Geo, int D>
+template <typename T, typename Geo, int D, bool SPLIT_P = true>
 __device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa)[D / 16][4], uint32_t kst,
                                           uint32_t vst, int tok0, int end, uint32_t pmask, int ctx, float qk_scale,
                                           bool alibi, float slope_lo, float slope_hi, int lane,
@@ -371,7 +388,8 @@ __device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa
   for (int kk = 0; kk < PK; ++kk) {
     // A = P.  bf16 keeps 8 mantissa bits, so P is carried as hi + lo bf16
     // parts (two products into the same accumulators, ~16 bits of P); f16's
-    // 11 bits are used as they are.
+    // 11 bits are used as they are.  SPLIT_P = false (long shared prefixes,
+    // where the rounding of many terms averages out) keeps only the hi part.
     uint32_t pa[4], pl[4];
     MmaOp<T>::pack_split(sacc[2 * kk][0], sacc[2 * kk][1], pa[0], pl[0]);
     MmaOp<T>::pack_split(sacc[2 * kk][2], sacc[2 * kk][3], pa[1], pl[1]);
@@ -419,7 +437,7 @@ __device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa
       }
       MmaOp<T>::run(gs.o[nt], pa, b0, b1);
       MmaOp<T>::run(gs.o[nt + 1], pa, b2, b3);
-      if constexpr (MmaOp<T>::kSplitP) {
+      if constexpr (MmaOp<T>::kSplitP && SPLIT_P) {
         MmaOp<T>::run(gs.o[nt], pl, b0, b1);
         MmaOp<T>::run(gs.o[nt + 1], pl, b2, b3);
       }
@@ -443,26 +461,34 @@ __device__ __forceinline__ uint32_t fp8x2_to_f16x2(uint32_t two) {
 }
 
 // Four codes of `w` -> lo (bytes 0, 1) and hi (bytes 2, 3) as f16x2.  The
-// hardware's E4M3 is the OCP E4M3FN variant; the KV cache's E4M3 keeps the
-// all-ones exponent for Inf (mantissa 0) and NaN, so such codes (written only
-// for Inf, NaN or out-of-range inputs) are patched on a rarely taken path.
+// hardware's E4M3 is the OCP E4M3FN variant (exponent 15 holds the finite
+// values 256..448 and NaN); the KV cache's E4M3 keeps the all-ones exponent for
+// Inf (mantissa 0) and NaN.  Such codes are written only for Inf, NaN or
+// out-of-range inputs, so the group math converts every code the E4M3FN way,
+// ORs e4m3_special_bits of its words into a flag, and when a warp vote finds
+// one adds e4m3_specials' correction in one more product: (the FN value) + Inf
+// = Inf and + NaN = NaN, the values the cache's format gives.
 template <int MODE>
 __device__ __forceinline__ void fp8x4_to_f16(uint32_t w, uint32_t& lo, uint32_t& hi) {
   lo = fp8x2_to_f16x2<MODE>(w);
   hi = fp8x2_to_f16x2<MODE>(w >> 16);
-  if constexpr (MODE == kFp8E4M3) {
-    const uint32_t z = (w & 0x78787878u) ^ 0x78787878u;  // zero byte <=> exponent all ones
-    if ((z - 0x01010101u) & ~z & 0x80808080u) {
+}
+
+// Bit 7 of byte i is set iff code i of `w` has the all-ones exponent (the
+// exponent field plus one carries into bit 7 only from 1111; no byte carries
+// into the next).
+__device__ __forceinline__ uint32_t e4m3_special_bits(uint32_t w) { return (w & 0x78787878u) + 0x08080808u; }
+
+// f16 pairs holding, for each code of `w` with the all-ones exponent, its value
+// in the cache's E4M3 (+-Inf for mantissa 0, NaN otherwise) and +0 elsewhere.
+__device__ __forceinline__ void e4m3_specials(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  lo = hi = 0u;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t c = (w >> (8 * i)) & 0xFFu;
-        if ((c & 0x78u) == 0x78u) {
-          const uint32_t h = ((c & 0x80u) << 8) | ((c & 0x07u) ? 0x7E00u : 0x7C00u);
-          uint32_t& dst = i < 2 ? lo : hi;
-          const int sh = 16 * (i & 1);
-          dst = (dst & ~(0xFFFFu << sh)) | (h << sh);
-        }
-      }
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t c = (w >> (8 * i)) & 0xFFu;
+    if ((c & 0x78u) == 0x78u) {
+      const uint32_t h = ((c & 0x80u) << 8) | ((c & 0x07u) ? 0x7E00u : 0x7C00u);
+      (i < 2 ? lo : hi) |= h << (16 * (i & 1));
     }
   }
 }
@@ -498,19 +524,42 @@ __device__ __forceinline__ void mma_group_fp8(GroupState<D>& gs, const uint32_t 
   const int q4 = lane & 3, n = lane >> 2;
   const bool tail = (tok0 + GT > end) || (pmask != (1u << NBOX) - 1u);
 
+  constexpr bool E4M3 = MODE == kFp8E4M3;
+  auto k_row = [&](int j) -> uint32_t {  // this lane's K row of S tile j
+    const int tok = 16 * (j >> 1) + 4 * (n >> 1) + 2 * (j & 1) + (n & 1);
+    return kst + (uint32_t)((tok / VBS) * BOX + (tok % VBS) * 16 + 4 * q4);
+  };
+
   // ---- S = Q K^T
   float sacc[ST][4];
+  uint32_t special = 0u;  // E4M3: e4m3_special_bits of every word read
 #pragma unroll
   for (int j = 0; j < ST; ++j) {
     sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
-    const int tok = 16 * (j >> 1) + 4 * (n >> 1) + 2 * (j & 1) + (n & 1);  // this lane's K row
-    const uint32_t krow = kst + (uint32_t)((tok / VBS) * BOX + (tok % VBS) * 16 + 4 * q4);
+    const uint32_t krow = k_row(j);
 #pragma unroll
     for (int ks = 0; ks < KS; ++ks) {
       uint32_t b0, b1;
-      fp8x4_to_f16<MODE>(lds32(krow + (uint32_t)(ks * VBS * 16)), b0, b1);
+      const uint32_t w = lds32(krow + (uint32_t)(ks * VBS * 16));
+      if constexpr (E4M3) special |= e4m3_special_bits(w);
+      fp8x4_to_f16<MODE>(w, b0, b1);
       MmaOp<__half>::run(sacc[j], qa[ks], b0, b1);
     }
+  }
+  if constexpr (E4M3) {
+    if (__any_sync(0xffffffffu, (special & 0x80808080u) != 0u)) {  // rare: Inf / NaN codes in K
+#pragma unroll
+      for (int j = 0; j < ST; ++j) {
+        const uint32_t krow = k_row(j);
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+          uint32_t b0, b1;
+          e4m3_specials(lds32(krow + (uint32_t)(ks * VBS * 16)), b0, b1);
+          MmaOp<__half>::run(sacc[j], qa[ks], b0, b1);
+        }
+      }
+    }
+    special = 0u;
   }
 
   // ---- online softmax (log2 domain); element (j, e) of a lane is token
@@ -590,8 +639,21 @@ __device__ __forceinline__ void mma_group_fp8(GroupState<D>& gs, const uint32_t 
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       uint32_t b0, b1;
-      fp8x4_to_f16<MODE>(lds32(vcol + (uint32_t)((8 * nt + n) * VBS)), b0, b1);
+      const uint32_t w = lds32(vcol + (uint32_t)((8 * nt + n) * VBS));
+      if constexpr (E4M3) special |= e4m3_special_bits(w);
+      fp8x4_to_f16<MODE>(w, b0, b1);
       MmaOp<__half>::run(gs.o[nt], pa, b0 & keep_lo, b1 & keep_hi);
+    }
+    if constexpr (E4M3) {
+      if (__any_sync(0xffffffffu, (special & 0x80808080u) != 0u)) {  // rare: Inf / NaN codes in V
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          uint32_t b0, b1;
+          e4m3_specials(lds32(vcol + (uint32_t)((8 * nt + n) * VBS)), b0, b1);
+          MmaOp<__half>::run(gs.o[nt], pa, b0 & keep_lo, b1 & keep_hi);
+        }
+      }
+      special = 0u;
     }
   }
 }
@@ -618,11 +680,14 @@ __global__ void __launch_bounds__(NW * 32)
   bool zero_out = false;
   if (!partition_range(p, seq, part, ctx, &begin, &end, &zero_out)) {
     if (zero_out) write_zero_heads<T>(p, seq, h0, G, D);
+    if (p.wait_prior_at_end) grid_dependency_wait();
     return;
   }
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Geo::BAR_OFF) + warp * STAGES;
   uint32_t* masks = reinterpret_cast<uint32_t*>(smem + Geo::MASK_OFF) + warp * STAGES;
+  constexpr int IDC = Geo::IDC, IDV = IDC * GT / 32;  // groups per id chunk, ids per lane per chunk
+  uint32_t* ids = reinterpret_cast<uint32_t*>(smem + Geo::IDS_OFF) + warp * 2 * IDC * GT;
   // Tensor-copy modes: the ring starts on a 1024-byte boundary of the shared window, so the
   // swizzle pattern TMA applies (address bits 4.. ^= bits 7..) is the one the
   // ldmatrix addressing below undoes.
@@ -633,7 +698,7 @@ __global__ void __launch_bounds__(NW * 32)
   }
   uint8_t* ring = ring_base + (size_t)warp * STAGES * Geo::STAGE;
   if (lane == 0) {
-    for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], Geo::FLASH ? 32 : 1);
     mbar_fence_init();
   }
   __syncwarp();
@@ -703,14 +768,10 @@ __global__ void __launch_bounds__(NW * 32)
   // Lane i < NBOX fetches the block id of box i of group `k` of this warp.
   // Token-major caches: lane i < GT fetches the block id of token i of the
   // group (block size p.block_size, 1 for the token pool).
+  // Token-major caches use the id chunks instead (load_ids / store_ids).
   auto load_block = [&](int k) -> uint32_t {
     uint32_t b = 0xffffffffu;
-    if constexpr (Geo::FLASH) {
-      if (lane < GT && k < n_mine) {
-        const int tt = begin + (warp + k * NW) * GT + lane;
-        if (tt < end) b = __ldg(table + tt / p.block_size);
-      }
-    } else {
+    if constexpr (!Geo::FLASH) {
       if (lane < NBOX && k < n_mine) {
         const int pg = (begin + (warp + k * NW) * GT + lane * VBS) / BS;
         if (pg < page_end) b = __ldg(table + pg);
@@ -718,30 +779,60 @@ __global__ void __launch_bounds__(NW * 32)
     }
     return b;
   };
+  // Token-major caches: the block ids of chunk c (groups c*IDC .. c*IDC +
+  // IDC - 1 of this warp, one id per token; 0xffffffff past the context) are
+  // loaded into registers one chunk before they are stored to the warp's id
+  // buffer, so the table reads (one per token in the pool) overlap a whole
+  // chunk of math instead of one group.
+  auto load_ids = [&](int c, uint32_t (&v)[IDV]) {
+#pragma unroll
+    for (int i = 0; i < IDV; ++i) {
+      const int j = lane + 32 * i, kg = c * IDC + j / GT;
+      const int tt = begin + (warp + kg * NW) * GT + j % GT;
+      v[i] = kg < n_mine && tt < end ? __ldg(table + tt / p.block_size) : 0xffffffffu;
+    }
+  };
+  auto store_ids = [&](int c, const uint32_t (&v)[IDV]) {
+#pragma unroll
+    for (int i = 0; i < IDV; ++i) ids[(c & 1) * IDC * GT + lane + 32 * i] = v[i];
+    __syncwarp();
+  };
   // Lane 0 issues the copies of group `k` into stage `s`; `blk` holds lane
   // i's block id (from load_block).  Records which boxes were loaded.
   // Token-major caches: every lane with a token copies that token's K and V
   // rows (lane 0 first posts the byte count), the mask has a bit per token.
   auto issue = [&](int k, int s, uint32_t blk) {
     if constexpr (Geo::FLASH) {
-      const int tt = begin + (warp + k * NW) * GT + lane;
+      // 16-byte cp.async copies spread over the warp (one copy engine request
+      // per token row was the bottleneck): lane l takes 16-byte column l % CPR
+      // of token rows l / CPR, l / CPR + 32 / CPR, ... of both K and V; every
+      // lane then arrives on the stage's barrier when its copies have landed
+      // (the barrier expects 32 arrivals in this mode).
+      constexpr int CPR = Geo::ROWB / 16;   // 16-byte columns per row
+      constexpr int RPP = 32 / CPR;         // rows per pass of the warp
+      const uint32_t* cid = ids + ((k / IDC) & 1) * IDC * GT + (k % IDC) * GT;  // this group's ids
+      const int t0 = begin + (warp + k * NW) * GT;
+      const int tt = t0 + lane;
       const bool in_ctx = lane < GT && tt < end;
-      const bool ok = in_ctx && (int64_t)blk < p.num_blocks;
+      const bool ok = in_ctx && (int64_t)cid[lane < GT ? lane : 0] < p.num_blocks;
       if (in_ctx && !ok) set_status(&g_decode_status, KVC_STATUS_BLOCK_OOB);
       const uint32_t mask = __ballot_sync(0xffffffffu, ok);
+      if (lane == 0) masks[s] = mask;
       uint8_t* st = ring + (size_t)s * Geo::STAGE;
-      if (lane == 0) {
-        masks[s] = mask;
-        if (mask) mbar_arrive_expect_tx(&bars[s], (uint32_t)__popc(mask) * 2u * (uint32_t)Geo::ROWB);
-        else mbar_arrive(&bars[s]);
+      const int col = lane % CPR;
+#pragma unroll
+      for (int i = 0; i < GT / RPP; ++i) {
+        const int row = lane / CPR + i * RPP;  // token of the group
+        if ((mask >> row) & 1u) {
+          const uint32_t b = cid[row];
+          const int64_t in_blk = (int64_t)((t0 + row) % p.block_size);
+          const CT* ks = kbase + (int64_t)b * p.k_block_stride + in_blk * p.k_tok_stride + col * (16 / (int)sizeof(CT));
+          const CT* vs = vbase + (int64_t)b * p.v_block_stride + in_blk * p.v_tok_stride + col * (16 / (int)sizeof(CT));
+          cp_async16(st + row * BOX + col * 16, ks);
+          cp_async16(st + (NBOX + row) * BOX + col * 16, vs);
+        }
       }
-      __syncwarp();
-      if (ok) {
-        const int64_t off = (int64_t)blk * p.k_block_stride + (int64_t)(tt % p.block_size) * p.k_tok_stride;
-        const int64_t voff = (int64_t)blk * p.v_block_stride + (int64_t)(tt % p.block_size) * p.v_tok_stride;
-        bulk_g2s(st + lane * BOX, kbase + off, Geo::ROWB, &bars[s]);
-        bulk_g2s(st + (NBOX + lane) * BOX, vbase + voff, Geo::ROWB, &bars[s]);
-      }
+      cp_async_arrive(&bars[s]);
     } else {
       uint32_t ids[NBOX];
 #pragma unroll
@@ -793,6 +884,13 @@ __global__ void __launch_bounds__(NW * 32)
   };
 
   // ---- prologue: fill the ring
+  uint32_t ids_next[IDV];  // token-major caches: the chunk after the current one
+  if constexpr (Geo::FLASH) {
+    uint32_t first[IDV];
+    load_ids(0, first);
+    load_ids(1, ids_next);
+    store_ids(0, first);
+  }
 #pragma unroll
   for (int s = 0; s < STAGES; ++s) {
     if (s < n_mine) issue(s, s, load_block(s));
@@ -804,6 +902,14 @@ __global__ void __launch_bounds__(NW * 32)
 
   for (int k = 0; k < n_mine; ++k) {
     const int s = k % STAGES;
+    if constexpr (Geo::FLASH) {
+      // chunk c + 1 (loaded a chunk ago) replaces chunk c - 1, whose last
+      // group was issued STAGES groups before this one; chunk c + 2 is loaded
+      if (k % IDC == 0 && k + STAGES < n_mine) {
+        store_ids(k / IDC + 1, ids_next);
+        load_ids(k / IDC + 2, ids_next);
+      }
+    }
     const uint32_t next_blk = load_block(k + STAGES);  // latency hidden by this group's math
     if (!mbar_wait_bounded(&bars[s], (uint32_t)((k / STAGES) & 1))) {
       k_fail = k;
@@ -886,6 +992,7 @@ __global__ void __launch_bounds__(NW * 32)
     // partial maxima are exchanged in natural-log units (as the generic kernel)
     emit<T>(p, seq, h0 + g, part, d, M * kLn2, L, A, d == 0);
   }
+  if (p.wait_prior_at_end) grid_dependency_wait();
 }
 
 // ---- dispatch -------------------------------------------------------------------
@@ -1046,6 +1153,23 @@ static cudaError_t launch_mma_nw(const DecodeParams& p, cudaStream_t stream) {
     configured[dev] = true;
   }
   dim3 grid((unsigned)p.num_kv_heads, (unsigned)p.num_seqs, (unsigned)(p.num_partitions - p.part_offset));
+  if (p.wait_prior_at_end) {
+    // shared-prefix order: a programmatic dependent of the prefix kernel that
+    // runs beside it and waits for it before exiting
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(NW * 32);
+    cfg.dynamicSmemBytes = Geo::SMEM;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, maps);
+    count_launch();
+    return e != cudaSuccess ? e : cudaGetLastError();
+  }
   kern<<<grid, NW * 32, Geo::SMEM, stream>>>(p, maps);
   count_launch();
   return cudaGetLastError();
