@@ -95,6 +95,13 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 
+// The same with `src_bytes` (0 or 16) read and the rest of the 16 bytes
+// zero-filled: a masked copy without a branch (src must still be mapped).
+__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+
 // One arrival on `bar` once every cp.async this thread issued before has
 // completed (the barrier's expected count includes it).
 __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
@@ -211,28 +218,32 @@ constexpr float kLn2 = 0.6931471805599453f;
 //             views it as 128-byte rows, written with the 128-byte swizzle.
 //  kFlash     token-major caches ([nb, bs, H, D], the MHATokenPool buffers
 //             being bs = 1): every token's K row and V row (D * 2 bytes) is
-//             its own 1-D bulk copy, landing in a shared row of D * 2 + 16
-//             bytes (the 16-byte pad spreads the ldmatrix rows of 8 tokens
-//             over all banks); V is read with ldmatrix.trans.  A "box" is one
-//             token, so the stage mask has a bit per token.
+//             copied by 16-byte cp.async spread over the warp, landing in a
+//             shared row of D * 2 + 16 bytes (the 16-byte pad spreads the
+//             ldmatrix rows of 8 tokens over all banks); V is read with
+//             ldmatrix.trans.  A "box" is one token, so the stage mask has a
+//             bit per token.
+//  kFlashBulk the same rows, each its own 1-D bulk copy issued by the lane of
+//             its token.
 // A swizzled V box makes the ldmatrix reads of V rows (VBS * 2 bytes apart)
 // hit distinct banks.
 //  kFp8E4M3 / kFp8E5M2  one-byte caches in the paged layout (K pages
 //             [D/16][bs][16], V pages [D][bs] bytes), 1-D bulk copies of whole
 //             pages; mma_group_fp8 converts codes to f16 in registers.
-constexpr int kBulk = 0, kTiles = 1, kSwizzledV = 2, kFlash = 3, kFp8E4M3 = 4, kFp8E5M2 = 5;
+constexpr int kBulk = 0, kTiles = 1, kSwizzledV = 2, kFlash = 3, kFp8E4M3 = 4, kFp8E5M2 = 5, kFlashBulk = 6;
 
 template <int D, int BS, int NW, int STAGES, int GT_ = 32, int MODE = kBulk>
 struct MmaGeom {
   static constexpr int GT = GT_;                          // tokens per group (16, 32 or 64)
-  static constexpr bool FLASH = MODE == kFlash;           // token-major K/V rows
+  static constexpr bool FLASH = MODE == kFlash || MODE == kFlashBulk;  // token-major K/V rows
+  static constexpr bool CP_ASYNC = MODE == kFlash;        // stage completion: 32 cp.async arrivals
   static constexpr bool FP8 = MODE == kFp8E4M3 || MODE == kFp8E5M2;  // one-byte caches
-  static constexpr int VBS = MODE == kFlash ? 1 : (MODE == kTiles ? (GT < BS ? GT : BS) : BS);  // tokens per box
+  static constexpr int VBS = FLASH ? 1 : (MODE == kTiles ? (GT < BS ? GT : BS) : BS);  // tokens per box
   static constexpr int NBOX = GT / VBS;                   // boxes per group (K and V each)
   static_assert(GT % 16 == 0 && GT % VBS == 0, "a group is whole boxes and whole 16-token k-steps");
-  static_assert(MODE != kFlash || GT == 16, "token-major groups are 16 tokens (one bit per token)");
+  static_assert(!FLASH || GT == 16, "token-major groups are 16 tokens (one bit per token)");
   static constexpr int ROWB = D * 2;                      // bytes of one token row (kFlash)
-  static constexpr int BOX = MODE == kFlash ? ROWB + 16 : D * VBS * (FP8 ? 1 : 2);  // bytes (stride) of one K (or V) box
+  static constexpr int BOX = FLASH ? ROWB + 16 : D * VBS * (FP8 ? 1 : 2);  // bytes (stride) of one K (or V) box
   static constexpr int VSWZ = MODE == kSwizzledV ? 128 : (MODE == kTiles && VBS * 2 >= 32 ? VBS * 2 : 0);
   static constexpr int STAGE = NBOX * 2 * BOX;            // K boxes then V boxes
   static constexpr int ALIGN = (MODE == kTiles || MODE == kSwizzledV) ? 1024 : 0;  // ring alignment (swizzle atoms)
@@ -375,12 +386,16 @@ __device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa
   }
   gs.l_lo = gs.l_lo * a_lo + ps_lo;
   gs.l_hi = gs.l_hi * a_hi + ps_hi;
+  // Once the row maxima settle most groups leave every factor at exactly 1:
+  // the warp then skips the accumulator rescale.
+  if (__any_sync(0xffffffffu, a_lo != 1.f || a_hi != 1.f)) {
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    gs.o[nt][0] *= a_lo;
-    gs.o[nt][1] *= a_lo;
-    gs.o[nt][2] *= a_hi;
-    gs.o[nt][3] *= a_hi;
+    for (int nt = 0; nt < NT; ++nt) {
+      gs.o[nt][0] *= a_lo;
+      gs.o[nt][1] *= a_lo;
+      gs.o[nt][2] *= a_hi;
+      gs.o[nt][3] *= a_hi;
+    }
   }
 
   // ---- O += P V : PK k-steps of 16 tokens x NT tiles of 8 dims
@@ -611,12 +626,16 @@ __device__ __forceinline__ void mma_group_fp8(GroupState<D>& gs, const uint32_t 
   }
   gs.l_lo = gs.l_lo * a_lo + ps_lo;
   gs.l_hi = gs.l_hi * a_hi + ps_hi;
+  // Once the row maxima settle most groups leave every factor at exactly 1:
+  // the warp then skips the accumulator rescale.
+  if (__any_sync(0xffffffffu, a_lo != 1.f || a_hi != 1.f)) {
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    gs.o[nt][0] *= a_lo;
-    gs.o[nt][1] *= a_lo;
-    gs.o[nt][2] *= a_hi;
-    gs.o[nt][3] *= a_hi;
+    for (int nt = 0; nt < NT; ++nt) {
+      gs.o[nt][0] *= a_lo;
+      gs.o[nt][1] *= a_lo;
+      gs.o[nt][2] *= a_hi;
+      gs.o[nt][3] *= a_hi;
+    }
   }
 
   // ---- O += P V
@@ -698,7 +717,7 @@ __global__ void __launch_bounds__(NW * 32)
   }
   uint8_t* ring = ring_base + (size_t)warp * STAGES * Geo::STAGE;
   if (lane == 0) {
-    for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], Geo::FLASH ? 32 : 1);
+    for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], Geo::CP_ASYNC ? 32 : 1);
     mbar_fence_init();
   }
   __syncwarp();
@@ -784,12 +803,18 @@ __global__ void __launch_bounds__(NW * 32)
   // loaded into registers one chunk before they are stored to the warp's id
   // buffer, so the table reads (one per token in the pool) overlap a whole
   // chunk of math instead of one group.
+  // Token position -> (block, row in block) without a division per copy: the
+  // token pool has one token per block; block sizes that are multiples of 16
+  // hold a whole 16-token group (groups start 16-aligned when `begin` does).
+  const int tbs = p.block_size;
+  const bool tok_blocks = tbs == 1;
+  const bool group_blocks = (tbs & 15) == 0 && (begin & 15) == 0;
   auto load_ids = [&](int c, uint32_t (&v)[IDV]) {
 #pragma unroll
     for (int i = 0; i < IDV; ++i) {
       const int j = lane + 32 * i, kg = c * IDC + j / GT;
       const int tt = begin + (warp + kg * NW) * GT + j % GT;
-      v[i] = kg < n_mine && tt < end ? __ldg(table + tt / p.block_size) : 0xffffffffu;
+      v[i] = kg < n_mine && tt < end ? __ldg(table + (tok_blocks ? tt : tt / tbs)) : 0xffffffffu;
     }
   };
   auto store_ids = [&](int c, const uint32_t (&v)[IDV]) {
@@ -803,11 +828,13 @@ __global__ void __launch_bounds__(NW * 32)
   // rows (lane 0 first posts the byte count), the mask has a bit per token.
   auto issue = [&](int k, int s, uint32_t blk) {
     if constexpr (Geo::FLASH) {
-      // 16-byte cp.async copies spread over the warp (one copy engine request
-      // per token row was the bottleneck): lane l takes 16-byte column l % CPR
-      // of token rows l / CPR, l / CPR + 32 / CPR, ... of both K and V; every
-      // lane then arrives on the stage's barrier when its copies have landed
-      // (the barrier expects 32 arrivals in this mode).
+      // kFlash: 16-byte cp.async copies spread over the warp: lane l takes
+      // 16-byte column l % CPR of the RPL token rows (l / CPR) * RPL .. of both
+      // K and V (rows outside the mask are zero-filled, no branch); every lane
+      // then arrives on the stage's barrier when its copies have landed (the
+      // barrier expects 32 arrivals in this mode).
+      // kFlashBulk: lane l < GT copies token l's K and V rows as two bulk
+      // copies after lane 0 has posted the stage's byte count.
       constexpr int CPR = Geo::ROWB / 16;   // 16-byte columns per row
       constexpr int RPP = 32 / CPR;         // rows per pass of the warp
       const uint32_t* cid = ids + ((k / IDC) & 1) * IDC * GT + (k % IDC) * GT;  // this group's ids
@@ -819,17 +846,47 @@ __global__ void __launch_bounds__(NW * 32)
       const uint32_t mask = __ballot_sync(0xffffffffu, ok);
       if (lane == 0) masks[s] = mask;
       uint8_t* st = ring + (size_t)s * Geo::STAGE;
-      const int col = lane % CPR;
+      const int in0 = tok_blocks ? 0 : (group_blocks ? t0 % tbs : 0);  // row of token t0 in its block
+      if constexpr (!Geo::CP_ASYNC) {
+        if (lane == 0) {
+          if (mask) mbar_arrive_expect_tx(&bars[s], (uint32_t)__popc(mask) * 2u * (uint32_t)Geo::ROWB);
+          else mbar_arrive(&bars[s]);
+        }
+        __syncwarp();
+        if (ok) {
+          const uint32_t b = cid[lane];
+          const int64_t in_blk = tok_blocks ? 0 : (group_blocks ? in0 + lane : tt % tbs);
+          bulk_g2s(st + lane * BOX, kbase + (int64_t)b * p.k_block_stride + in_blk * p.k_tok_stride, Geo::ROWB,
+                   &bars[s]);
+          bulk_g2s(st + (NBOX + lane) * BOX, vbase + (int64_t)b * p.v_block_stride + in_blk * p.v_tok_stride,
+                   Geo::ROWB, &bars[s]);
+        }
+        return;
+      }
+      if (mask) {  // (a set bit means num_blocks > 0: block 0 is mapped for the masked rows)
+        constexpr int RPL = GT / RPP;  // rows per lane
+        const int col = lane % CPR, r0 = (lane / CPR) * RPL;
+        uint32_t rid[RPL];
 #pragma unroll
-      for (int i = 0; i < GT / RPP; ++i) {
-        const int row = lane / CPR + i * RPP;  // token of the group
-        if ((mask >> row) & 1u) {
-          const uint32_t b = cid[row];
-          const int64_t in_blk = (int64_t)((t0 + row) % p.block_size);
-          const CT* ks = kbase + (int64_t)b * p.k_block_stride + in_blk * p.k_tok_stride + col * (16 / (int)sizeof(CT));
-          const CT* vs = vbase + (int64_t)b * p.v_block_stride + in_blk * p.v_tok_stride + col * (16 / (int)sizeof(CT));
-          cp_async16(st + row * BOX + col * 16, ks);
-          cp_async16(st + (NBOX + row) * BOX + col * 16, vs);
+        for (int i = 0; i < RPL; i += 4) {
+          const uint4 v4 = *reinterpret_cast<const uint4*>(cid + r0 + i);
+          rid[i] = v4.x;
+          rid[i + 1] = v4.y;
+          rid[i + 2] = v4.z;
+          rid[i + 3] = v4.w;
+        }
+        const CT* kcol = kbase + col * (16 / (int)sizeof(CT));
+        const CT* vcol = vbase + col * (16 / (int)sizeof(CT));
+#pragma unroll
+        for (int i = 0; i < RPL; ++i) {
+          const int row = r0 + i;  // token of the group
+          const bool on = (mask >> row) & 1u;
+          const int64_t b = on ? rid[i] : 0;
+          const int64_t in_blk = tok_blocks ? 0 : (group_blocks ? in0 + row : (t0 + row) % tbs);
+          cp_async16_zfill(st + row * BOX + col * 16, kcol + b * p.k_block_stride + in_blk * p.k_tok_stride,
+                           on ? 16u : 0u);
+          cp_async16_zfill(st + (NBOX + row) * BOX + col * 16, vcol + b * p.v_block_stride + in_blk * p.v_tok_stride,
+                           on ? 16u : 0u);
         }
       }
       cp_async_arrive(&bars[s]);
@@ -1249,8 +1306,14 @@ static cudaError_t launch_mma_t(const DecodeParams& p, const DecodeArgs& a, cuda
                 : launch_mma_fp8<T, 64, kFp8E4M3>(p, a.block_size, stream);
   }
   if (a.flash) {
-    // token-major caches: 16-token groups, 4 warps x 3 stages (104 KB for
-    // D = 128, two CTAs per SM); the block size is read at run time
+    // token-major caches: 16-token groups, 4 warps x 3 stages (108 KB for
+    // D = 128, two CTAs per SM); the block size is read at run time.
+    // KVC_FLASH_COPY=bulk selects per-row bulk copies (tuning runs).
+    const char* fc = getenv("KVC_FLASH_COPY");
+    if (fc && fc[0] == 'b') {
+      if (a.head_size == 128) return launch_mma_nw<T, 128, 16, 4, 3, 16, kFlashBulk>(p, stream);
+      return launch_mma_nw<T, 64, 16, 4, 3, 16, kFlashBulk>(p, stream);
+    }
     if (a.head_size == 128) return launch_mma_nw<T, 128, 16, 4, 3, 16, kFlash>(p, stream);
     return launch_mma_nw<T, 64, 16, 4, 3, 16, kFlash>(p, stream);
   }
