@@ -573,6 +573,224 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+PREFILL_METRIC = "paged prefill/extend attention TFLOP/s (visible keys only) and prefill tokens/s"
+
+
+def prefill_flops(prefixes, qlens, hq, d):
+    """4 * d FLOPs (Q.K^T and P.V multiply-adds) per (query row, visible key):
+    new token t of a sequence with prefix p sees p + t + 1 keys."""
+    vis = sum(int(n) * int(p) + int(n) * (int(n) + 1) // 2 for p, n in zip(prefixes, qlens))
+    return 4.0 * d * hq * vis
+
+
+def run_prefill(args, rank, world, local_rank):
+    """--mode prefill: the chunked prefill of BASELINE config 5 (16 chunks of 512
+    new tokens, each on a prefix drawn from config 5's seeded lognormal context
+    lengths; 28 q / 4 kv heads, head_dim 128, block 32, bf16) through
+    paged_prefill_attention, per layer.  Tensor-bound: the roofline is TFLOP/s
+    of visible-key FLOPs against the measured bf16 GEMM peak."""
+    import torch
+
+    from sglang_mlx_b200 import _lib, sharding
+    from sglang_mlx_b200 import metal_kernels as mk
+    from sglang_mlx_b200.device_array import DeviceArray, Event, HostBuffer, Stream
+
+    dev = local_rank
+    _lib.set_device(dev)
+    torch.cuda.set_device(dev)
+    tdev = torch.device("cuda", dev)
+    w = cases.baseline_workload(5)
+    cfg = dict(w["cfg"])
+    L = args.layers or cfg["layers"]
+    HQ, HKV, D, BS = cfg["hq"], cfg["hkv"], cfg["d"], cfg["bs"]
+    n_chunks, chunk = cfg["prefill_chunks"], cfg["chunk"]
+    prefixes_all = np.asarray(w["lens"][:n_chunks], np.int64)
+    qlens_all = np.full(n_chunks, chunk, np.int64)
+    plan = sharding.plan(HQ, HKV, world, rank, prefixes_all + qlens_all)
+    hkv, hq = plan.num_kv_heads, plan.num_q_heads
+    prefixes, qlens = prefixes_all[plan.seqs], qlens_all[plan.seqs]
+    B = len(prefixes)
+    kvl = prefixes + qlens
+    pool = args.layout == "pool"
+    rng = np.random.default_rng(77 + rank)
+    nbs = [-(-int(n) // BS) for n in kvl]
+    num_blocks = sum(nbs) + 8
+    perm = rng.permutation(num_blocks)
+    tables = np.zeros((B, max(nbs)), np.int64)
+    o = 0
+    for b, nb in enumerate(nbs):
+        tables[b, :nb] = perm[o:o + nb]
+        o += nb
+    if pool:  # token-pool slot lists (slot 0 is the pool's padding slot)
+        t = np.arange(tables.shape[1] * BS)
+        tables = tables[:, t // BS] * BS + t % BS + 1
+    tables = np.ascontiguousarray(tables.astype(np.int32))
+    indptr = np.concatenate([[0], np.cumsum(qlens)]).astype(np.int32)
+    T = int(indptr[-1])
+    max_q = int(qlens.max())
+
+    g = torch.Generator(device=tdev)
+    g.manual_seed(4321 + rank)
+    tdt = torch.bfloat16
+    kc, vc, q, out, keep = [], [], [], [], []
+    for _ in range(L):
+        if pool:
+            k = torch.randn((num_blocks * BS + 1, hkv, D), generator=g, device=tdev, dtype=tdt)
+            v = torch.randn((num_blocks * BS + 1, hkv, D), generator=g, device=tdev, dtype=tdt)
+        else:
+            k = torch.randn((num_blocks, hkv, D // 8, BS, 8), generator=g, device=tdev, dtype=tdt)
+            v = torch.randn((num_blocks, hkv, D, BS), generator=g, device=tdev, dtype=tdt)
+        qq = torch.randn((T, hq, D), generator=g, device=tdev, dtype=tdt)
+        keep += [k, v, qq]
+        kc.append(DeviceArray.from_dlpack(k))
+        vc.append(DeviceArray.from_dlpack(v))
+        q.append(DeviceArray.from_dlpack(qq))
+        out.append(DeviceArray.empty((T, hq, D), "bfloat16", dev))
+    tables_d = DeviceArray.from_numpy(tables, device=dev)
+    indptr_d = DeviceArray.from_numpy(indptr, device=dev)
+    kvl_d = DeviceArray.from_numpy(kvl.astype(np.int32), device=dev)
+    flush = DeviceArray.empty((L2_FLUSH_BYTES,), "int32", dev)
+    scale = 1.0 / math.sqrt(D)
+    torch.cuda.synchronize()
+    st = Stream()
+    tab_bs = 1 if pool else BS
+
+    def layer(i):
+        mk.paged_prefill_attention(q[i], kc[i], vc[i], tables_d, indptr_d, kvl_d, hkv, scale, tab_bs, max_q_len=max_q,
+                                   out=out[i], stream=st)
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        flush.fill_zero(stream=st)
+        for i in range(L):
+            layer(i)
+    st.synchronize()
+    if _lib.get_status(clear=True):
+        raise SystemExit("prefill kernel status flags set in warm-up")
+    evs = [[[Event(), Event()] for _ in range(L)] for _ in range(args.steps)]
+    sampler = ClockSampler(dev)
+    barrier()
+    _lib.synchronize()
+    sampler.start()
+    launches0 = _lib.launch_count()
+    for s in range(args.steps):
+        flush.fill_zero(stream=st)  # between steps, outside the events
+        for i in range(L):
+            evs[s][i][0].record(st)
+            layer(i)
+            evs[s][i][1].record(st)
+    st.synchronize()
+    launches = _lib.launch_count() - launches0  # prefill kernels (the L2 flush memsets are not counted)
+    clocks = sampler.stop()
+    lay_ms = [evs[s][i][0].elapsed_ms(evs[s][i][1]) for s in range(args.steps) for i in range(L)]
+    step_ms = float(np.sum(lay_ms)) / args.steps
+    mean_ms = float(np.mean(lay_ms))
+
+    # e2e through the public API: queries from pinned host memory, outputs back
+    e2e_ms = float("nan")
+    h2d = d2h = 0
+    if not args.no_e2e:
+        hq_buf = [HostBuffer((T, hq, D), "bfloat16") for _ in range(L)]
+        ho_buf = [HostBuffer((T, hq, D), "bfloat16") for _ in range(L)]
+        for hb in hq_buf:
+            hb.array[...] = rng.integers(0x3c00, 0x4000, size=hb.shape, dtype=np.uint16)
+
+        def e2e_step():
+            for i in range(L):
+                q[i].copy_from_host(hq_buf[i], stream=st)
+                layer(i)
+                out[i].copy_to_host(ho_buf[i], stream=st)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        st.synchronize()
+        eev = [[Event(), Event()] for _ in range(args.steps)]
+        for s in range(args.steps):
+            flush.fill_zero(stream=st)
+            eev[s][0].record(st)
+            e2e_step()
+            eev[s][1].record(st)
+        st.synchronize()
+        e2e_ms = sum(a.elapsed_ms(b) for a, b in eev) / args.steps
+        h2d = d2h = L * T * hq * D * 2
+
+    flops = prefill_flops(prefixes, qlens, hq, D)
+    sums = np.array([flops, float(T), float(h2d), float(d2h)])
+    if dist is not None:
+        t = torch.tensor([step_ms, e2e_ms, mean_ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_ms, e2e_ms, mean_ms = [float(x) for x in t]
+        tt = torch.tensor(sums, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.SUM)
+        sums = tt.numpy()
+    if rank != 0:
+        return
+    flops_all, _, h2d_all, d2h_all = sums
+    peak, peak_kind = load_tensor_peak()
+    achieved = flops / (mean_ms * 1e-3) / 1e12
+    tokens = n_chunks * chunk  # new tokens of the whole job per layer pass
+    line = {
+        "metric": PREFILL_METRIC,
+        "value": L * flops_all / (step_ms * 1e-3) / 1e12,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": step_ms,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "config5-chunked-prefill", "chunks": f"{n_chunks} x {chunk} new tokens",
+                   "prefixes": "config 5 lognormal lengths of sequences 0..15 (seeded)", "layers": L,
+                   "heads": f"{HQ}q/{HKV}kv", "head_dim": D, "block_size": BS,
+                   "layout": "MHATokenPool slot lists" if pool else "paged (vLLM layout)",
+                   "parallelism": f"kv-head-shard{world}", "kernel": "paged_prefill_attention",
+                   "l2": "flushed between steps (512 MB write, outside the events)"},
+        "prefill_tokens_per_s": tokens * 1.0 / (step_ms * 1e-3 / L) if L else None,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "traffic": None, "peak_kind": peak_kind, "kernel": "prefill_kernel, per layer launch",
+                     "algorithmic_flops_per_launch": flops, "mean_launch_ms": mean_ms},
+        "e2e": None if args.no_e2e else {"value": L * flops_all / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                                         "h2d_bytes_per_step": int(h2d_all), "d2h_bytes_per_step": int(d2h_all)},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline and world == 1:
+        from oracle import kv_oracle
+        from threadpoolctl import threadpool_limits
+
+        n_s = min(8, B)
+        kb = keep[0].float().cpu().numpy()
+        vb = keep[1].float().cpu().numpy()
+        qb = keep[2][: int(indptr[n_s])].float().cpu().numpy()
+        with threadpool_limits(1):
+            t0 = time.perf_counter()
+            kv_oracle.paged_prefill(qb, kb, vb, tables[:n_s], indptr[: n_s + 1], kvl[:n_s], hkv, scale)
+            dt = time.perf_counter() - t0
+        sample_flops = prefill_flops(prefixes[:n_s], qlens[:n_s], hq, D)
+        line["cpu_baseline"] = {"value": sample_flops / dt / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+                                "sample": f"{n_s} of {B} sequences x 1 of {L} layers (float64 gather + masked SDPA, "
+                                          f"NumPy, 1 thread), {lscpu_model()}"}
+    print(json.dumps(line), flush=True)
+
+
+def load_tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (burst)"
+    return 1590.0, "fallback"
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -596,6 +814,8 @@ def main():
     ap.add_argument("--batch", type=int, default=0, help="override the batch (profiling cases only)")
     ap.add_argument("--kv-heads", type=int, default=0,
                     help="override the KV head count, keeping the group size (profiling cases only)")
+    ap.add_argument("--mode", default="decode", choices=["decode", "prefill"],
+                    help="decode (the BASELINE metric) or the config-5 chunked prefill through paged_prefill_attention")
     ap.add_argument("--graph", action=argparse.BooleanOptionalAction, default=True,
                     help="replay each timed step as one CUDA graph (removes host launch overhead)")
     args = ap.parse_args()
@@ -612,8 +832,14 @@ def main():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=600))
     try:
-        if args.impl == "reference":
+        if args.impl == "reference" and args.mode == "prefill":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "prefill mode: the reference runs prefill as mlx "
+                                  "SDPA (not installed); the --impl ours line carries the CPU oracle as cpu_baseline"}))
+        elif args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.mode == "prefill":
+            run_prefill(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:

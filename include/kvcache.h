@@ -154,6 +154,37 @@ int kvc_paged_attention_cascade(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_d
                                 int max_seq_len, const kvc_dltensor* alibi_slopes, int shared_prefix_len,
                                 int prefix_partition_size, int partition_size, void* stream);
 
+/* Paged prefill / extend attention.  No kernel counterpart in the reference:
+ * there a prefill stores the new K/V into the pool and gathers prefix + new
+ * tokens back (PooledKVCache.update_and_fetch, memory_pool.py:205-234) for mlx
+ * SDPA under the offset-causal mask of mlx-lm's create_attention_mask
+ * (PooledKVCache.make_mask, memory_pool.py:240-270; model_runner.py:190-258).
+ * This reads the cache in place.
+ *   out, query      [num_tokens, num_heads, head_size]; the new tokens of all
+ *                   sequences, sequence b's at rows qo_indptr[b] ..
+ *                   qo_indptr[b + 1] - 1
+ *   key_cache / value_cache  the paged layout ([nb, H, D/x, bs, x] /
+ *                   [nb, H, D, bs]), the flash layout ([nb, bs, H, D]) or the
+ *                   token pool ([slots, H, D], block_size 1)
+ *   block_tables    [num_seqs, max_blocks] int32 (slot lists for the pool);
+ *                   the new tokens' K/V are already stored
+ *   qo_indptr       [num_seqs + 1] int32, non-decreasing
+ *   kv_lens         [num_seqs] int32: cache tokens of sequence b including its
+ *                   new ones, so its prefix is kv_lens[b] - (qo_indptr[b + 1] -
+ *                   qo_indptr[b])
+ *   max_q_len       at least every sequence's new-token count (sizes the grid)
+ *   window_size     0: causal; w > 0: token t of the new ones sees only cache
+ *                   tokens (prefix + t - w, prefix + t]
+ * New token t of sequence b attends to cache tokens [0, prefix + t].  float16
+ * / bfloat16 query and caches of one dtype, head_size 64 or 128, paged
+ * block_size 8/16/32 (else KVC_EUNSUPPORTED).  Device-side index errors
+ * (kv_lens below the new-token count or past the table, qo_indptr past
+ * num_tokens or a count above max_q_len) set KVC_STATUS_INDEX_OOB. */
+int kvc_paged_prefill(kvc_dltensor* out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                      const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                      const kvc_dltensor* qo_indptr, const kvc_dltensor* kv_lens, int num_kv_heads, float scale,
+                      int block_size, int max_q_len, int window_size, void* stream);
+
 /* Split-K decode for callers that cannot allocate device memory.  No
  * counterpart in the reference: sglang-mlx has no split-K decode at all.
  *

@@ -383,6 +383,69 @@ def gather_sdpa(query, k_contig, v_contig, scale):
     return out
 
 
+# ---------------------------------------------------------------------------
+# prefill / extend attention (the reference runs it as mlx SDPA over the K/V
+# that PooledKVCache.update_and_fetch gathers, memory_pool.py:205-234, under
+# the mask of PooledKVCache.make_mask, memory_pool.py:240-270)
+# ---------------------------------------------------------------------------
+def offset_causal_mask(n_new, kv_len, window=None):
+    """Boolean [n_new, kv_len]: new token t (cache position prefix + t, prefix =
+    kv_len - n_new) sees cache token j iff j <= prefix + t and, with a window w,
+    j > prefix + t - w.  This is what mlx-lm's create_attention_mask(N, offset,
+    window_size) means for make_mask: "causal" with the offset, and the
+    windowed boolean mask the reference pins in tests/test_memory_pool.py:
+    291-320 (N=3, window 2: token 2 sees 1 and 2, not 0)."""
+    prefix = kv_len - n_new
+    pos = prefix + np.arange(n_new)[:, None]
+    j = np.arange(kv_len)[None, :]
+    m = j <= pos
+    if window:
+        m &= j > pos - window
+    return m
+
+
+def sdpa_masked(q, k, v, scale, mask):
+    """softmax(scale * q @ k^T, masked) @ v in float64, no epsilon (mlx SDPA);
+    a row with no visible key is 0.  q [N, D], k/v [T, D], mask [N, T]."""
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    v = np.asarray(v, dtype=np.float64)
+    logits = np.where(mask, (q @ k.T) * float(scale), -np.inf)
+    m = logits.max(axis=1, keepdims=True)
+    m = np.where(np.isfinite(m), m, 0.0)
+    p = np.exp(logits - m)
+    s = p.sum(axis=1, keepdims=True)
+    return np.where(s > 0, (p @ v) / np.where(s > 0, s, 1.0), 0.0)
+
+
+def paged_prefill(query, key_cache, value_cache, block_tables, qo_indptr, kv_lens, num_kv_heads, scale,
+                  window=None):
+    """Float64 [num_tokens, Hq, D] of prefill / extend attention: sequence b's new
+    tokens (rows qo_indptr[b] .. qo_indptr[b+1]-1) attend to its kv_lens[b]
+    cache tokens under offset_causal_mask; GQA as the decode (kv head h // G).
+    Caches in the paged layout (5-D key cache) or token-major ([nb, bs, H, D] /
+    the pool's [slots, H, D])."""
+    q = np.asarray(query, dtype=np.float64)
+    T, Hq, D = q.shape
+    G = Hq // num_kv_heads
+    out = np.zeros((T, Hq, D))
+    ind = np.asarray(qo_indptr).astype(np.int64)
+    lens = np.asarray(kv_lens).astype(np.int64)
+    for b in range(len(lens)):
+        q0, q1, kvl = int(ind[b]), int(ind[b + 1]), int(lens[b])
+        if q1 <= q0:
+            continue
+        mask = offset_causal_mask(q1 - q0, kvl, window)
+        for h in range(num_kv_heads):
+            if key_cache.ndim == 5:
+                k, v = gather_seq(key_cache, value_cache, block_tables[b], kvl, h)
+            else:
+                k, v = gather_seq_flash(key_cache, value_cache, block_tables[b], kvl, h)
+            for g in range(G):
+                out[q0:q1, h * G + g] = sdpa_masked(q[q0:q1, h * G + g], k, v, scale, mask)
+    return out
+
+
 def allclose_report(got, ref, atol, rtol):
     """(ok, max_abs_err, worst_excess) for |got - ref| <= atol + rtol * |ref|."""
     got = np.asarray(got, dtype=np.float64)

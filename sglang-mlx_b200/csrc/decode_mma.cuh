@@ -240,8 +240,9 @@ struct MmaGeom {
   static constexpr bool FP8 = MODE == kFp8E4M3 || MODE == kFp8E5M2;  // one-byte caches
   static constexpr int VBS = FLASH ? 1 : (MODE == kTiles ? (GT < BS ? GT : BS) : BS);  // tokens per box
   static constexpr int NBOX = GT / VBS;                   // boxes per group (K and V each)
+  static constexpr uint32_t FULL_MASK = NBOX >= 32 ? 0xffffffffu : (1u << (NBOX & 31)) - 1u;  // every box loaded
   static_assert(GT % 16 == 0 && GT % VBS == 0, "a group is whole boxes and whole 16-token k-steps");
-  static_assert(!FLASH || GT == 16, "token-major groups are 16 tokens (one bit per token)");
+  static_assert(!FLASH || GT == 16 || GT == 32, "token-major groups are 16 or 32 tokens (one mask bit per token)");
   static constexpr int ROWB = D * 2;                      // bytes of one token row (kFlash)
   static constexpr int BOX = FLASH ? ROWB + 16 : D * VBS * (FP8 ? 1 : 2);  // bytes (stride) of one K (or V) box
   static constexpr int VSWZ = MODE == kSwizzledV ? 128 : (MODE == kTiles && VBS * 2 >= 32 ? VBS * 2 : 0);
@@ -299,13 +300,16 @@ struct GroupState {
 // length (ALiBi positions).  When the tile's rows belong to different
 // sequences (the shared-prefix kernel), `end_lo` / `end_hi` further end the
 // scores of this lane's rows r and r + 8; `end` still bounds the V data.
+// `beg_lo` / `beg_hi` start them (sliding-window prefill); tokens before a
+// row's start are masked like tokens past its end.
 template <typename T, typename Geo, int D, bool SPLIT_P = true>
 __device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa)[D / 16][4], uint32_t kst,
                                           uint32_t vst, int tok0, int end, uint32_t pmask, int ctx, float qk_scale,
                                           bool alibi, float slope_lo, float slope_hi, int lane,
-                                          int end_lo = 2147483647, int end_hi = 2147483647) {
+                                          int end_lo = 2147483647, int end_hi = 2147483647, int beg_lo = 0,
+                                          int beg_hi = 0) {
   using namespace mma_detail;
-  constexpr int GT = Geo::GT, NBOX = Geo::NBOX, BOX = Geo::BOX, VBS = Geo::VBS;
+  constexpr int GT = Geo::GT, BOX = Geo::BOX, VBS = Geo::VBS;
   constexpr uint32_t VSW_MASK = Geo::VSWZ ? (uint32_t)(Geo::VSWZ / 16 - 1) : 0u;
   constexpr int KS = D / 16;
   constexpr int NT = D / 8;
@@ -313,7 +317,8 @@ __device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa
   constexpr int PK = GT / 16;
   const int q4 = lane & 3;
   const int row_end = end_lo < end_hi ? end_lo : end_hi;
-  const bool tail = (tok0 + GT > end) || (tok0 + GT > row_end) || (pmask != (1u << NBOX) - 1u);
+  const bool tail = (tok0 + GT > end) || (tok0 + GT > row_end) || (pmask != Geo::FULL_MASK) ||
+                    (tok0 < (beg_lo > beg_hi ? beg_lo : beg_hi));
   (void)KS;
 
   // ---- S = Q K^T : ST tiles of 8 tokens
@@ -352,8 +357,8 @@ __device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa
       }
       if (tail) {
         const bool ok = (tok0 + t < end) && ((pmask >> (t / VBS)) & 1u);
-        x_lo = (ok && tok0 + t < end_lo) ? x_lo : -INFINITY;
-        x_hi = (ok && tok0 + t < end_hi) ? x_hi : -INFINITY;
+        x_lo = (ok && tok0 + t < end_lo && tok0 + t >= beg_lo) ? x_lo : -INFINITY;
+        x_hi = (ok && tok0 + t < end_hi && tok0 + t >= beg_hi) ? x_hi : -INFINITY;
       }
       sacc[j][e] = x_lo;
       sacc[j][2 + e] = x_hi;
@@ -531,13 +536,13 @@ __device__ __forceinline__ void mma_group_fp8(GroupState<D>& gs, const uint32_t 
                                               uint32_t vst, int tok0, int end, uint32_t pmask, int ctx,
                                               float qk_scale, bool alibi, float slope_lo, float slope_hi, int lane) {
   using namespace mma_detail;
-  constexpr int GT = Geo::GT, NBOX = Geo::NBOX, BOX = Geo::BOX, VBS = Geo::VBS;
+  constexpr int GT = Geo::GT, BOX = Geo::BOX, VBS = Geo::VBS;
   constexpr int KS = D / 16;
   constexpr int NT = D / 8;
   constexpr int ST = GT / 8;
   constexpr int PK = GT / 16;
   const int q4 = lane & 3, n = lane >> 2;
-  const bool tail = (tok0 + GT > end) || (pmask != (1u << NBOX) - 1u);
+  const bool tail = (tok0 + GT > end) || (pmask != Geo::FULL_MASK);
 
   constexpr bool E4M3 = MODE == kFp8E4M3;
   auto k_row = [&](int j) -> uint32_t {  // this lane's K row of S tile j

@@ -108,6 +108,8 @@ static bool is_valid_attention_config(int head_size, int block_size) {
   return ok_hs && ok_bs;
 }
 
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+static bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
 static bool is_float(ElemType t) { return t == ElemType::F32 || t == ElemType::F16 || t == ElemType::BF16; }
 
 // (query dtype, cache dtype) pairs of paged_attention_inst.metal:64-73 and
@@ -550,6 +552,116 @@ int kvc_paged_attention_cascade(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_d
   if (e == cudaErrorMisalignedAddress)
     return fail(KVC_EINVAL, "key_cache/value_cache pages must start on 16-byte boundaries");
   if (e != cudaSuccess) return cuda_fail(e, "paged_attention_cascade launch");
+  return KVC_OK;
+}
+
+// Paged prefill / extend attention: the new tokens of each sequence attend to
+// its cache (prefix + themselves) under the offset-causal rule of mlx-lm's
+// create_attention_mask (memory_pool.py:240-270), reading the cache in place
+// instead of the update_and_fetch gather + SDPA of the reference
+// (memory_pool.py:205-234, model_runner.py:190-258).
+int kvc_paged_prefill(kvc_dltensor* out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                      const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                      const kvc_dltensor* qo_indptr, const kvc_dltensor* kv_lens, int num_kv_heads, float scale,
+                      int block_size, int max_q_len, int window_size, void* stream) {
+  View q, kc, vc, bt, qi, kl, o;
+  if (!parse(query, "query", &q) || !parse(key_cache, "key_cache", &kc) ||
+      !parse(value_cache, "value_cache", &vc) || !parse(block_tables, "block_tables", &bt) ||
+      !parse(qo_indptr, "qo_indptr", &qi) || !parse(kv_lens, "kv_lens", &kl) || !parse(out, "out", &o))
+    return KVC_EINVAL;
+  if (q.ndim != 3) return fail(KVC_EINVAL, "query must have shape [num_tokens, num_heads, head_size]");
+  const bool paged = kc.ndim == 5 && vc.ndim == 4;
+  const bool flash = kc.ndim == 4 && vc.ndim == 4;
+  const bool pool = kc.ndim == 3 && vc.ndim == 3;
+  if (!paged && !flash && !pool)
+    return fail(KVC_EINVAL, "key_cache/value_cache must be [num_blocks, num_kv_heads, head_size/x, block_size, x] / "
+                            "[num_blocks, num_kv_heads, head_size, block_size], [num_blocks, block_size, "
+                            "num_kv_heads, head_size] or [slots, num_kv_heads, head_size]");
+  if (bt.ndim != 2 || qi.ndim != 1 || kl.ndim != 1)
+    return fail(KVC_EINVAL, "block_tables must be 2D, qo_indptr and kv_lens 1D");
+  if (qi.shape[0] != bt.shape[0] + 1 || kl.shape[0] != bt.shape[0])
+    return fail(KVC_EINVAL, "qo_indptr must have num_seqs + 1 entries and kv_lens num_seqs");
+  if (num_kv_heads <= 0 || q.shape[1] % num_kv_heads != 0)
+    return fail(KVC_EINVAL, "num_heads must be divisible by num_kv_heads");
+  const int hd = paged ? 1 : (flash ? 2 : 1);  // KV-head dimension of the caches
+  if (kc.shape[hd] != num_kv_heads || vc.shape[hd] != num_kv_heads)
+    return fail(KVC_EINVAL, "cache KV-head count does not match num_kv_heads");
+  const int64_t D = q.shape[2];
+  if ((paged && (kc.shape[2] * kc.shape[4] != D || vc.shape[2] != D)) ||
+      (!paged && (kc.shape[hd + 1] != D || vc.shape[hd + 1] != D)))
+    return fail(KVC_EINVAL, "cache head size does not match query head size");
+  const int64_t cache_bs = paged ? kc.shape[3] : (flash ? kc.shape[1] : 1);
+  if (kc.shape[0] != vc.shape[0] || block_size != cache_bs || (paged && vc.shape[3] != cache_bs) ||
+      (flash && vc.shape[1] != cache_bs))
+    return fail(KVC_EINVAL, "cache block dimensions do not match block_size");
+  if (max_q_len < 0 || window_size < 0) return fail(KVC_EINVAL, "max_q_len and window_size must be non-negative");
+  if (!(q.dtype == ElemType::F16 || q.dtype == ElemType::BF16) || kc.dtype != q.dtype || vc.dtype != q.dtype ||
+      !(D == 64 || D == 128) || (paged && !(block_size == 8 || block_size == 16 || block_size == 32)))
+    return fail(KVC_EUNSUPPORTED,
+                std::string("paged_prefill supports float16/bfloat16 query and caches of one dtype, head_size 64 or "
+                            "128 and (paged layout) block_size 8, 16 or 32 (got query ") +
+                    elem_name(q.dtype) + ", cache " + elem_name(kc.dtype) + ", head_size " + std::to_string(D) +
+                    ", block_size " + std::to_string(block_size) + ")");
+  if (paged && kc.shape[4] != 16 / elem_size(kc.dtype))
+    return fail(KVC_EINVAL, "key_cache last dimension must be x = 16 / sizeof(cache element)");
+  if (int rc = check_index_type(bt, "block_tables", false)) return rc;
+  if (int rc = check_index_type(qi, "qo_indptr", false)) return rc;
+  if (int rc = check_index_type(kl, "kv_lens", false)) return rc;
+  if (o.ndim != 3 || o.shape[0] != q.shape[0] || o.shape[1] != q.shape[1] || o.shape[2] != D || o.dtype != q.dtype)
+    return fail(KVC_EINVAL, "out must have the shape and dtype of query");
+  if (q.stride(2) != 1 || o.stride(2) != 1) return fail(KVC_EINVAL, "query/out head_size dimension must be contiguous");
+  if ((q.stride(0) | q.stride(1) | o.stride(0) | o.stride(1)) & 1 || !aligned4(q.data) || !aligned4(o.data))
+    return fail(KVC_EINVAL, "query/out rows must start on 4-byte boundaries");
+  if (paged ? (!kc.dense_from(2) || !vc.dense_from(2)) : (kc.stride(-1) != 1 || vc.stride(-1) != 1))
+    return fail(KVC_EINVAL, "key_cache/value_cache pages (paged layout) or rows must be contiguous");
+  if (bt.stride(1) != 1 || qi.stride(0) != 1 || kl.stride(0) != 1)
+    return fail(KVC_EINVAL, "block_tables rows, qo_indptr and kv_lens must be contiguous");
+  const int64_t cs = elem_size(kc.dtype);
+  const int64_t k_tok = paged || pool ? 0 : kc.stride(1), v_tok = paged || pool ? 0 : vc.stride(1);
+  if (!aligned16(kc.data) || !aligned16(vc.data) || (kc.stride(0) * cs) % 16 || (vc.stride(0) * cs) % 16 ||
+      (kc.stride(hd) * cs) % 16 || (vc.stride(hd) * cs) % 16 || (k_tok * cs) % 16 || (v_tok * cs) % 16)
+    return fail(KVC_EINVAL, "key_cache/value_cache pages and rows must start on 16-byte boundaries");
+  int device_of_call = -1;
+  if (int rc = check_all_cuda({&q, &kc, &vc, &bt, &qi, &kl, &o}, &device_of_call)) return rc;
+  PrefillArgs a;
+  memset(&a, 0, sizeof(a));
+  a.out = o.data;
+  a.q = q.data;
+  a.k_cache = kc.data;
+  a.v_cache = vc.data;
+  a.block_tables = reinterpret_cast<const uint32_t*>(bt.data);
+  a.qo_indptr = reinterpret_cast<const uint32_t*>(qi.data);
+  a.kv_lens = reinterpret_cast<const uint32_t*>(kl.data);
+  a.num_seqs = (int)bt.shape[0];
+  a.num_heads = (int)q.shape[1];
+  a.num_kv_heads = num_kv_heads;
+  a.block_size = block_size;
+  a.window = window_size;
+  a.max_q_len = max_q_len;
+  a.num_tokens = q.shape[0];
+  a.num_blocks = kc.shape[0];
+  a.table_len = bt.shape[1];
+  a.table_stride = bt.stride(0);
+  a.q_tok_stride = q.stride(0);
+  a.q_head_stride = q.stride(1);
+  a.out_tok_stride = o.stride(0);
+  a.out_head_stride = o.stride(1);
+  a.k_block_stride = kc.stride(0);
+  a.k_head_stride = kc.stride(hd);
+  a.k_tok_stride = k_tok;
+  a.v_block_stride = vc.stride(0);
+  a.v_head_stride = vc.stride(hd);
+  a.v_tok_stride = v_tok;
+  a.scale = scale;
+  a.q_type = q.dtype;
+  a.head_size = (int)D;
+  a.token_major = !paged;
+  if (a.num_seqs == 0 || a.num_tokens == 0 || max_q_len == 0) return KVC_OK;
+  if (a.num_seqs > 65535) return fail(KVC_EINVAL, "at most 65535 sequences per call");
+  DeviceGuard g(device_of_call);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_paged_prefill(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "paged_prefill launch");
   return KVC_OK;
 }
 

@@ -102,6 +102,26 @@ struct DecodeArgs {
   float scale;
 };
 
+// Paged prefill / extend attention (prefill.cuh).  Strides in elements.
+struct PrefillArgs {
+  void* out;
+  const void* q;
+  const void* k_cache;
+  const void* v_cache;
+  const uint32_t* block_tables;  // [num_seqs][table_stride]: block ids (slot ids for the token pool)
+  const uint32_t* qo_indptr;     // [num_seqs + 1]: rows of sequence b are qo_indptr[b] .. qo_indptr[b + 1] - 1
+  const uint32_t* kv_lens;       // [num_seqs]: cache tokens of sequence b, its new ones included
+  int num_seqs, num_heads, num_kv_heads, block_size, window, max_q_len;
+  int64_t num_tokens, num_blocks, table_len, table_stride;
+  int64_t q_tok_stride, q_head_stride, out_tok_stride, out_head_stride;
+  int64_t k_block_stride, k_head_stride, k_tok_stride;
+  int64_t v_block_stride, v_head_stride, v_tok_stride;
+  float scale;
+  ElemType q_type;   // float16 / bfloat16 (the caches' type too)
+  int head_size;     // 64 or 128
+  bool token_major;  // [nb, bs, H, D] / [slots, H, D] caches; else the paged layout
+};
+
 struct ReshapeArgs {
   const void* key;
   const void* value;
@@ -143,6 +163,8 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream);
 cudaError_t launch_paged_decode_noalloc(DecodeArgs a, cudaStream_t stream);
 // Shared-prefix decode: tail partitions, the cascade prefix kernel, the reduce.
 cudaError_t launch_paged_decode_cascade(const DecodeArgs& a, cudaStream_t stream);
+// Paged prefill / extend attention (prefill.cuh); enqueues one kernel.
+cudaError_t launch_paged_prefill(const PrefillArgs& a, cudaStream_t stream);
 // Whole-block copies (copy_blocks / swap_blocks).  A plane is one buffer
 // pair; every plane of one launch has the same block size in bytes.
 constexpr int kMaxBlockPlanes = 32;

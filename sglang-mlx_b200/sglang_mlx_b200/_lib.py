@@ -53,6 +53,7 @@ SIGNATURES: dict[str, tuple] = {
         _i,
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _i, _i, _i, _p],
     ),
+    "kvc_paged_prefill": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _i, _p]),
     "kvc_paged_attention_flash": (
         _i,
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _i, _p],

@@ -190,6 +190,54 @@ def paged_attention_flash(
     return out
 
 
+def paged_prefill_attention(
+    query,
+    key_cache,
+    value_cache,
+    block_tables,
+    qo_indptr,
+    kv_lens,
+    num_kv_heads: int,
+    scale: float,
+    block_size: int,
+    *,
+    max_q_len: int | None = None,
+    window_size: int | None = None,
+    out=None,
+    stream=None,
+):
+    """Prefill / extend attention over a paged or token-major cache.
+
+    query [num_tokens, num_heads, D] holds the new tokens of every sequence,
+    sequence b's at rows qo_indptr[b] .. qo_indptr[b+1]-1; their K/V are already
+    in the cache, whose sequence b holds kv_lens[b] tokens (prefix + new).  New
+    token t of sequence b attends to cache tokens [0, prefix + t] — the
+    offset-causal mask of mlx-lm's create_attention_mask that
+    PooledKVCache.make_mask returns (memory_pool.py:240-270) — or, with a
+    window w, to (prefix + t - w, prefix + t].  Caches: the paged layout of
+    paged_attention_v1, the flash layout [nb, bs, H, D] or a token pool
+    [slots, H, D] (block_size 1, block_tables rows are slot lists).
+    max_q_len None: read from a host qo_indptr, else num_tokens (an upper
+    bound; extra row tiles exit at once)."""
+    if max_q_len is None:
+        if isinstance(qo_indptr, (np.ndarray, list, tuple)):
+            ind = np.asarray(qo_indptr, dtype=np.int64)
+            max_q_len = int(np.max(np.diff(ind))) if ind.size > 1 else 0
+        else:
+            max_q_len = describe(query)[0][0]
+    query, key_cache, value_cache = _dev(query), _dev(key_cache), _dev(value_cache)
+    block_tables, qo_indptr, kv_lens = _dev(block_tables), _dev(qo_indptr), _dev(kv_lens)
+    if out is None:
+        out = _out_like_query(query)
+    ptrs = [as_dltensor(a, n)[0] for a, n in ((out, "out"), (query, "query"), (key_cache, "key_cache"),
+                                              (value_cache, "value_cache"), (block_tables, "block_tables"),
+                                              (qo_indptr, "qo_indptr"), (kv_lens, "kv_lens"))]
+    rc = _L.kvc_paged_prefill(*ptrs, int(num_kv_heads), float(scale), int(block_size), int(max(0, max_q_len)),
+                              int(window_size or 0), _stream(stream))
+    _lib.check(rc)
+    return out
+
+
 def cascade_partitions(num_seqs: int, num_heads: int, num_kv_heads: int, max_seq_len: int, shared_prefix_len: int,
                        block_size: int = 16, sm_count: int = 148) -> tuple[int, int]:
     """(prefix_partition_size, partition_size) for paged_attention_cascade.

@@ -214,47 +214,63 @@ class PooledKVCache:
         self._store_new(keys, values)
         return self._pool.fetch(self._layer_idx, self._all_indices())
 
-    def update_and_attend(self, queries, keys, values, scale: float | None = None, *, stream=None):
-        """Stores the new token's KV and attends over prefix + new slots on the
-        pool itself (no gather).  Single-token decode only.
+    def update_and_attend(self, queries, keys, values, scale: float | None = None, *, window_size: int | None = None,
+                          stream=None):
+        """Stores the new tokens' KV and attends over prefix + new slots on the
+        pool itself, without the gather of update_and_fetch: the result mlx SDPA
+        gives on update_and_fetch's K/V under make_mask's mask
+        (memory_pool.py:205-270).  One new token runs the decode kernel; more
+        (prefill / extend) or a sliding window run the prefill kernel, where new
+        token t sees slots [0, offset + t] (the last `window_size` of them).
 
         Args:
-            queries: ``(1, n_heads, 1, head_dim)``; keys, values:
-                ``(1, n_kv_heads, 1, head_dim)`` (mlx-lm format).
-        Returns ``(1, n_heads, 1, head_dim)``.
+            queries: ``(1, n_heads, N, head_dim)``; keys, values:
+                ``(1, n_kv_heads, N, head_dim)`` (mlx-lm format).
+        Returns ``(1, n_heads, N, head_dim)``.
         """
         qshape, qstr, qdt, _, qdev = describe(queries)
-        if len(qshape) != 4 or qshape[0] != 1 or qshape[2] != 1 or describe(keys)[0][2] != 1:
-            raise ValueError("update_and_attend handles single-token decode: queries (1, H, 1, D) and keys/values "
-                             "(1, H_kv, 1, D); use update_and_fetch for prefill")
+        kshape = describe(keys)[0]
+        if len(qshape) != 4 or qshape[0] != 1 or len(kshape) != 4 or kshape[2] != qshape[2]:
+            raise ValueError("update_and_attend takes queries (1, H, N, D) and keys/values (1, H_kv, N, D) "
+                             "with the same N")
+        N = qshape[2]
         self._store_new(keys, values, stream=stream)
         slots = np.asarray(self._all_indices(), dtype=np.int32)[None, :]
-        qptr, qkeep = as_dltensor(queries, "queries")
-        qt, qk = make_dltensor(qptr.contents.data + qptr.contents.byte_offset, (1, qshape[1], qshape[3]),
-                               (qstr[0], qstr[1], qstr[3]), qdt, qptr.contents.device.device_id)
-
-        out = DeviceArray.empty((1, qshape[1], qshape[3]), qdt, qdev)
-        lens = DeviceArray.from_numpy(np.array([slots.shape[1]], dtype=np.int32), device=qdev)
-        tables = DeviceArray.from_numpy(slots, device=qdev)
-        from ... import metal_kernels as mk
-
-        ws = (None, None, None)
         T = slots.shape[1]
-        psize = mk.choose_decode(1, self._pool.n_kv_heads, T, 16)
-        if psize:
-            ws = mk.splitk_workspace(1, qshape[1], qshape[3], T, psize, qdev)
+        qptr, qkeep = as_dltensor(queries, "queries")
+        # the queries as [N, H, D] rows (a strided view, no copy)
+        qt, qk = make_dltensor(qptr.contents.data + qptr.contents.byte_offset, (N, qshape[1], qshape[3]),
+                               (qstr[2], qstr[1], qstr[3]), qdt, qptr.contents.device.device_id)
+        out = DeviceArray.empty((N, qshape[1], qshape[3]), qdt, qdev)
+        lens = DeviceArray.from_numpy(np.array([T], dtype=np.int32), device=qdev)
+        tables = DeviceArray.from_numpy(slots, device=qdev)
         if scale is None:
             scale = self._pool.head_dim ** -0.5
-        ptrs = [as_dltensor(a, n) for a, n in ((out, "out"), (ws[0], "exp_sums"), (ws[1], "max_logits"),
-                                               (ws[2], "tmp_out"), (self._pool.k_buffer[self._layer_idx], "k"),
-                                               (self._pool.v_buffer[self._layer_idx], "v"), (tables, "tables"),
-                                               (lens, "lens"))]
-        _lib.check(_L.kvc_paged_attention_flash(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ctypes.pointer(qt),
-                                                ptrs[4][0], ptrs[5][0], ptrs[6][0], ptrs[7][0],
-                                                self._pool.n_kv_heads, float(scale), 1, T, None, int(psize),
-                                                _stream(stream)))
+        from ... import metal_kernels as mk
+
+        kbuf, vbuf = self._pool.k_buffer[self._layer_idx], self._pool.v_buffer[self._layer_idx]
+        if N == 1 and not window_size:
+            ws = (None, None, None)
+            psize = mk.choose_decode(1, self._pool.n_kv_heads, T, 16)
+            if psize:
+                ws = mk.splitk_workspace(1, qshape[1], qshape[3], T, psize, qdev)
+            ptrs = [as_dltensor(a, n) for a, n in ((out, "out"), (ws[0], "exp_sums"), (ws[1], "max_logits"),
+                                                   (ws[2], "tmp_out"), (kbuf, "k"), (vbuf, "v"), (tables, "tables"),
+                                                   (lens, "lens"))]
+            _lib.check(_L.kvc_paged_attention_flash(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0],
+                                                    ctypes.pointer(qt), ptrs[4][0], ptrs[5][0], ptrs[6][0],
+                                                    ptrs[7][0], self._pool.n_kv_heads, float(scale), 1, T, None,
+                                                    int(psize), _stream(stream)))
+        else:
+            indptr = DeviceArray.from_numpy(np.array([0, N], dtype=np.int32), device=qdev)
+            ptrs = [as_dltensor(a, n) for a, n in ((out, "out"), (kbuf, "k"), (vbuf, "v"), (tables, "tables"),
+                                                   (indptr, "qo_indptr"), (lens, "kv_lens"))]
+            _lib.check(_L.kvc_paged_prefill(ptrs[0][0], ctypes.pointer(qt), ptrs[1][0], ptrs[2][0], ptrs[3][0],
+                                            ptrs[4][0], ptrs[5][0], self._pool.n_kv_heads, float(scale), 1, N,
+                                            int(window_size or 0), _stream(stream)))
         del qkeep, qk, ptrs
-        return out.reshape(1, qshape[1], 1, qshape[3])
+        # (N, H, D) -> a (1, H, N, D) view
+        return out.transpose(1, 0, 2).expand_dims(0)
 
     @property
     def state(self):

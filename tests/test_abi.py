@@ -234,3 +234,36 @@ def test_swap_blocks_rejects_layout_mismatch():
 def test_swap_blocks_rejects_mapping_shape():
     expect(_lib.lib.kvc_swap_blocks(fake((4, 6)), fake((4, 6)), fake((2,), "int64"), None),
            "block_mapping must have shape [num_pairs, 2]")
+
+
+# ---- kvc_paged_prefill argument checks (fake CUDA pointers, nothing launches) ------
+
+def call_prefill(q=(10, 8, 64), kc=(20, 4, 8, 16, 8), vc=(20, 4, 64, 16), bt=(2, 4), qi=(3,), kl=(2,), nkv=4, bs=16,
+                 mql=8, win=0, qd="float16", cd="float16", out=None, od=None, device_type=dlpack.KDL_CUDA):
+    out = out or q
+    return _lib.lib.kvc_paged_prefill(
+        fake(out, od or qd), fake(q, qd), fake(kc, cd), fake(vc, cd), fake(bt, "int32", device_type=device_type),
+        fake(qi, "int32"), fake(kl, "int32"), nkv, 0.125, bs, mql, win, None)
+
+
+def test_prefill_rejects_layouts_and_shapes():
+    expect(call_prefill(q=(10, 8)), "query must have shape [num_tokens, num_heads, head_size]")
+    expect(call_prefill(vc=(20, 4, 64)), "key_cache/value_cache must be")
+    expect(call_prefill(qi=(2,)), "qo_indptr must have num_seqs + 1 entries")
+    expect(call_prefill(kl=(3,)), "qo_indptr must have num_seqs + 1 entries and kv_lens num_seqs")
+    expect(call_prefill(nkv=3), "num_heads must be divisible by num_kv_heads")
+    expect(call_prefill(kc=(20, 2, 8, 16, 8), vc=(20, 2, 64, 16)), "cache KV-head count")
+    expect(call_prefill(vc=(20, 4, 32, 16)), "cache head size")
+    expect(call_prefill(bs=8), "cache block dimensions do not match block_size")
+    expect(call_prefill(win=-1), "max_q_len and window_size must be non-negative")
+    expect(call_prefill(out=(10, 8, 32)), "out must have the shape and dtype of query")
+    expect(call_prefill(device_type=dlpack.KDL_CPU), "CUDA device")
+    # token pool: [slots, H, D] with block_size 1
+    expect(call_prefill(kc=(100, 4, 64), vc=(100, 4, 64), bs=16), "cache block dimensions do not match block_size")
+
+
+def test_prefill_refuses_unsupported_types():
+    rc = call_prefill(qd="float32", cd="float32", kc=(20, 4, 16, 16, 4))
+    assert rc == _lib.KVC_EUNSUPPORTED and "paged_prefill supports float16/bfloat16" in _lib.last_error()
+    rc = call_prefill(q=(10, 8, 96), kc=(20, 4, 12, 16, 8), vc=(20, 4, 96, 16))
+    assert rc == _lib.KVC_EUNSUPPORTED

@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 
 import cases
-from helpers import ATOL_NS, RTOL_NS, assert_close, fill_cache, upload_case
+from helpers import ATOL_NS, RTOL_NS, assert_close, fill_cache, flash_case, upload_case, upload_flash
 from oracle import kv_oracle
 from sglang_mlx_b200 import _lib
 from sglang_mlx_b200 import metal_kernels as mk
@@ -18,53 +18,6 @@ from sglang_mlx_b200.device_array import DeviceArray
 from sglang_mlx_b200.srt.mem_cache.memory_pool import MHATokenPool, PooledKVCache, TokenPoolAllocator
 
 pytestmark = pytest.mark.gpu
-
-
-def flash_case(seed, dtype, num_seqs, hq, hkv, d, bs, lens):
-    """A batch in token-major caches.  bs = 1 gives a token pool: caches
-    [slots, H, D] and block tables that are slot lists."""
-    c = cases.paged_batch(seed, dtype, num_seqs, hq, hkv, d, 16, lens)
-    nb16 = c["k_cache"].shape[0]
-    slots = c["slot_mapping"].astype(np.int64)
-    T = len(slots)
-    if bs == 1:
-        shape = (nb16 * 16 + 1, hkv, d)  # + the pool's padding slot 0
-        slots = slots + 1
-        t = np.arange(c["block_tables"].shape[1] * 16)
-        tables = np.where(c["block_tables"][:, t // 16] >= 0, c["block_tables"][:, t // 16] * 16 + t % 16 + 1, 0)
-    else:
-        # re-block the same tokens into bs-token blocks of a permuted pool
-        rng = np.random.default_rng(seed + 5)
-        nbb = -(-nb16 * 16 // bs) + 2
-        perm = rng.permutation(nbb)
-        maxb = -(-c["block_tables"].shape[1] * 16 // bs)
-        tables = np.full((num_seqs, maxb), -1, np.int64)
-        pos = 0
-        off = 0
-        slots = np.empty(T, np.int64)
-        for b, n in enumerate(c["context_lens"]):
-            nb = -(-int(n) // bs)
-            tables[b, :nb] = perm[pos:pos + nb]
-            tt = np.arange(int(n))
-            slots[off:off + n] = tables[b, tt // bs] * bs + tt % bs
-            pos += nb
-            off += int(n)
-        shape = (nbb, bs, hkv, d)
-    store = np.float16 if dtype == "float16" else np.float32
-    return dict(c=c, shape=shape, tables=tables.astype(np.int32), slots=slots.astype(np.int32), bs=bs, store=store)
-
-
-def upload_flash(fc):
-    c = fc["c"]
-    dt = c["dtype"]
-    q = DeviceArray.from_numpy(c["q"], dtype=dt)
-    k = DeviceArray.from_numpy(c["k"], dtype=dt)
-    v = DeviceArray.from_numpy(c["v"], dtype=dt)
-    kc = DeviceArray.zeros(fc["shape"], dt)
-    vc = DeviceArray.zeros(fc["shape"], dt)
-    mk.reshape_and_cache_flash(k, v, kc, vc, DeviceArray.from_numpy(fc["slots"]))
-    return dict(q=q, kc=kc, vc=vc, tables=DeviceArray.from_numpy(fc["tables"]),
-                lens=DeviceArray.from_numpy(c["context_lens"].astype(np.int32)))
 
 
 def oracle_flash(fc, alibi=None, max_seq_len=None):
@@ -245,7 +198,7 @@ def test_pooled_cache_update_and_attend_equals_gather_path(gpu):
         ref = np.stack([kv_oracle.attend(q[0, 4 * h:4 * h + 4, 0], kf[h], vf[h], 128 ** -0.5) for h in range(4)])
         assert_close(out.to_numpy()[0, :, 0], ref.reshape(16, 128), ATOL_NS, RTOL_NS, f"step {step}")
         prefix = prefix + new
-    with pytest.raises(ValueError, match="single-token"):
+    with pytest.raises(ValueError, match="same N"):
         caches[0].update_and_attend(DeviceArray.from_numpy(np.zeros((1, 16, 2, 128), np.float32), dtype=dtype),
-                                    DeviceArray.from_numpy(np.zeros((1, 4, 2, 128), np.float32), dtype=dtype),
-                                    DeviceArray.from_numpy(np.zeros((1, 4, 2, 128), np.float32), dtype=dtype))
+                                    DeviceArray.from_numpy(np.zeros((1, 4, 3, 128), np.float32), dtype=dtype),
+                                    DeviceArray.from_numpy(np.zeros((1, 4, 3, 128), np.float32), dtype=dtype))

@@ -218,3 +218,64 @@ def test_fp8_codec_restatement():
     assert enc(2.0 ** -6 * (1 - 2.0 ** -10)) == 0x08  # subnormal rounding up into the smallest normal
     assert enc(1e6) == 0x78 and enc(-1e6) == 0xF8 and enc(250.0) == 0x78  # past 240: +-Inf
     assert enc(57344.0, "e5m2") == 0x7B and enc(65536.0, "e5m2") == 0x7C
+
+
+# ---- prefill / extend attention oracle --------------------------------------------
+
+def test_prefill_mask_matches_make_mask():
+    """offset_causal_mask is the mask PooledKVCache.make_mask returns (itself
+    checked against the reference's make_mask tests in test_memory_pool.py),
+    including the windowed case the reference pins (N=3, window 2)."""
+    from sglang_mlx_b200.srt.mem_cache.memory_pool import PooledKVCache
+
+    m = kv_oracle.offset_causal_mask(3, 3, 2)
+    assert not m[2, 0] and m[2, 1] and m[2, 2]
+    for prefix, n, w in [(0, 4, None), (3, 2, None), (5, 7, 3), (0, 9, 1), (10, 1, 4), (2, 6, 100)]:
+        pc = PooledKVCache(None, 0)
+        pc.set_indices(list(range(1, prefix + 1)), list(range(prefix + 1, prefix + n + 1)))
+        want = np.asarray(pc.make_mask(N=n, return_array=True, window_size=w)) if n > 1 else None
+        got = kv_oracle.offset_causal_mask(n, prefix + n, w)
+        if want is not None:
+            np.testing.assert_array_equal(got, want)
+        assert got[-1, : prefix + n].sum() == (min(w, prefix + n) if w else prefix + n)
+
+
+def test_sdpa_masked_against_torch():
+    """The float64 masked SDPA against torch's scaled_dot_product_attention, an
+    independent implementation of the same mathematics."""
+    import torch
+
+    rng = np.random.default_rng(61)
+    for n, t, d, w in [(5, 5, 64, None), (7, 40, 128, None), (16, 300, 128, 33), (1, 9, 64, None)]:
+        q = rng.standard_normal((n, d))
+        k = rng.standard_normal((t, d))
+        v = rng.standard_normal((t, d))
+        mask = kv_oracle.offset_causal_mask(n, t, w)
+        got = kv_oracle.sdpa_masked(q, k, v, d ** -0.5, mask)
+        want = torch.nn.functional.scaled_dot_product_attention(
+            torch.from_numpy(q)[None], torch.from_numpy(k)[None], torch.from_numpy(v)[None],
+            attn_mask=torch.from_numpy(mask)[None], scale=d ** -0.5).numpy()[0]
+        np.testing.assert_allclose(got, want, rtol=1e-12, atol=1e-12)
+
+
+def test_prefill_oracle_layouts_agree_and_single_token_is_decode():
+    """paged_prefill reads the paged layout, the flash layout and the token pool
+    alike, and one new token per sequence is the decode oracle (whose softmax
+    denominator carries the kernel's + 1e-6)."""
+    import helpers
+
+    lens = [7, 40, 100]
+    c = cases.paged_batch(62, "float16", 3, 16, 4, 64, 16, lens)
+    kc, vc = _fill(c)
+    q = c["q"].astype(np.float64)  # [3, 16, 64]: one new token per sequence
+    ind = np.arange(4, dtype=np.int32)
+    lens32 = np.asarray(lens, np.int32)
+    paged = kv_oracle.paged_prefill(q, kc, vc, c["block_tables"], ind, lens32, 4, c["scale"])
+    dec = kv_oracle.paged_attention_v1(q, kc, vc, c["block_tables"], lens32, 4, c["scale"], 16, c["max_seq_len"])
+    np.testing.assert_allclose(paged, dec, rtol=1e-5, atol=1e-6)
+    for bs in (1, 16):
+        fc = helpers.flash_case(62, "float16", 3, 16, 4, 64, bs, lens)
+        fk, fv = helpers.oracle_flash_caches(fc)
+        flash = kv_oracle.paged_prefill(fc["c"]["q"].astype(np.float64), fk, fv, fc["tables"], ind, lens32, 4,
+                                        c["scale"])
+        np.testing.assert_allclose(flash, paged, rtol=1e-12, atol=1e-12)
