@@ -400,6 +400,7 @@ __global__ void __launch_bounds__(kReduceWarps * 32) splitk_reduce_kernel(Decode
 #include "decode_mma.cuh"
 #include "cascade.cuh"
 #include "prefill.cuh"
+#include "prefill_umma.cuh"
 
 namespace kvc {
 

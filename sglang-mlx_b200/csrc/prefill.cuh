@@ -336,9 +336,8 @@ static cudaError_t launch_prefill_layout(const PrefillParams& p, bool token_majo
   return cudaErrorNotSupported;
 }
 
-cudaError_t launch_paged_prefill(const PrefillArgs& a, cudaStream_t stream) {
-  if (a.num_seqs <= 0 || a.max_q_len <= 0) return cudaSuccess;
-  if (a.num_seqs > 65535 || a.num_kv_heads > 65535) return cudaErrorInvalidValue;
+// The mma.sync kernel: every layout, head size 64 / 128.
+static cudaError_t launch_prefill_mma_any(const PrefillArgs& a, cudaStream_t stream) {
   if (a.head_size == 128)
     return a.q_type == ElemType::BF16 ? launch_prefill_layout<__nv_bfloat16, 128>(a, a.token_major, stream)
                                       : launch_prefill_layout<__half, 128>(a, a.token_major, stream);

@@ -1,0 +1,535 @@
+// prefill_umma.cuh — tcgen05 (5th-generation tensor core) prefill / extend
+// attention for sm_100a over the paged (vLLM) cache layout.
+//
+// Included by decode.cu after prefill.cuh: same PrefillArgs, same results as
+// prefill_kernel (the offset-causal / window rule of PooledKVCache.make_mask,
+// memory_pool.py:240-270), with the products on the tensor cores' own
+// pipeline instead of mma.sync:
+//
+//  * CTA = 128 query rows (new token, query head of the group) of one
+//    sequence and KV head; row r of the tile is TMEM lane r.
+//  * TMEM (512 columns): two S buffers of 128 fp32 columns (S = Q K^T of a
+//    128-token tile), O (D fp32 columns) and Q (D/2 columns of bf16/f16
+//    pairs).  P overwrites its own S buffer: hi parts in the first 64
+//    columns, lo parts (bf16 only) in the next 64.
+//  * Warp 4 (producer) streams 128-token tiles into a ring of KST stages:
+//    each K page as it is (its [D/8][bs][8] layout is the no-swizzle K-major
+//    operand layout: 8 tokens x 16 bytes per core matrix), each V page
+//    [D][bs] through a tensor map that writes it with the bs*2-byte swizzle,
+//    the K-major operand layout of P.V (tokens are its K).
+//  * Warp 5 (one lane) issues S_j = Q K_j^T (A = Q from TMEM, one chain of
+//    D/16 instructions per page, N = bs), then O += P_{j-1} V_{j-1} (A = P
+//    from TMEM, N = D, 16 tokens per instruction; bf16 P as hi + lo, two
+//    products), committing each to an mbarrier.
+//  * Warps 0-3 (one thread per row) read S_j, mask it (causal end, window
+//    start, context end), keep the running max lazily (O is rescaled only
+//    when a row's max rises by more than 2^8; until then P may exceed 1,
+//    exactly as the final O / l needs), write P, and at the end normalise
+//    O and store the row.
+// Every wait is bounded (KVC_STATUS_WAIT_TIMEOUT and an abort flag end every
+// loop); TMEM is freed only after a final commit shows every product done.
+#pragma once
+
+namespace kvc {
+namespace umma {
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  uint64_t d = (uint64_t)((addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version of sm_100
+  d |= (uint64_t)(layout & 7u) << 61;
+  return d;
+}
+constexpr uint32_t kLayoutNone = 0, kLayoutSw64 = 4, kLayoutSw32 = 6;
+
+// kind::f16 instruction descriptor: fp32 accumulate, A and B both `bf16`
+// (else both f16), K-major A and B, M x N.
+__host__ __device__ constexpr uint32_t instr_desc(bool bf16, int m, int n) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
+}
+
+// D[tmem] (+)= A[tmem] * B[smem descriptor]
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mma_detail::smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 32 consecutive 32-bit columns: this thread's lane, columns c .. c+31
+__device__ __forceinline__ void ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  st16(taddr, r);
+  st16(taddr + 16, r + 16);
+}
+
+}  // namespace umma
+
+constexpr int kUmmaRows = 128;   // query rows per CTA (TMEM lanes)
+constexpr int kUmmaTile = 128;   // tokens per S tile
+constexpr int kUmmaThreads = 192;
+
+template <int D, int BS>
+struct UmmaGeom {
+  static constexpr int PAGES = kUmmaTile / BS;
+  static constexpr int PAGE = D * BS * 2;            // bytes of one K (or V) page of one head
+  static constexpr int STAGE = 2 * PAGES * PAGE;     // K pages, then V pages
+  static constexpr int KST = D == 128 ? 3 : 4;       // ring stages
+  static constexpr int RING = KST * STAGE;
+  static constexpr int BAR_OFF = 1024 + RING;        // (1024: alignment slack of the ring)
+  static constexpr int NBARS = 2 * KST + 2 + 2 + 1 + 1 + 1;  // kv full/empty, s_full, p_full, pv_done, q_ready, done
+  static constexpr int MASK_OFF = BAR_OFF + NBARS * 8;
+  static constexpr int SMEM = MASK_OFF + KST * 4 + 16;
+  static constexpr uint32_t SCOL = 0, OCOL = 256, QCOL = 256 + D;  // TMEM columns
+  static_assert(QCOL + D / 2 <= 512, "TMEM columns");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+template <typename T, int D, int BS>
+__global__ void __launch_bounds__(kUmmaThreads, 1)
+    prefill_umma_kernel(const PrefillArgs p, const __grid_constant__ CUtensorMap vmap) {
+  using namespace mma_detail;
+  using UG = UmmaGeom<D, BS>;
+  constexpr int PAGES = UG::PAGES, PAGE = UG::PAGE, KST = UG::KST, KT = kUmmaTile;
+  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr bool SPLIT = BF16;  // bf16 P as hi + lo; f16 P as it is
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ int s_abort;
+  __shared__ uint32_t s_tmem;
+  uint8_t* ring = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + UG::BAR_OFF);
+  uint64_t* kv_full = bars;
+  uint64_t* kv_empty = bars + KST;
+  uint64_t* s_full = bars + 2 * KST;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* pv_done = p_full + 2;
+  uint64_t* q_ready = pv_done + 1;
+  uint64_t* all_done = q_ready + 1;
+  uint32_t* page_mask = reinterpret_cast<uint32_t*>(smem_raw + UG::MASK_OFF);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int seq = blockIdx.y, kvh = blockIdx.z;
+  const int G = p.num_heads / p.num_kv_heads;
+  const int64_t q0 = p.qo_indptr[seq];
+  const int64_t q1 = p.qo_indptr[seq + 1];
+  const int64_t kvl = p.kv_lens[seq];
+  const int64_t ql = q1 - q0;
+  const int64_t rows = ql * G;
+  const int64_t R0 = (int64_t)(gridDim.x - 1 - blockIdx.x) * kUmmaRows;  // last tiles first
+  if (ql <= 0 || R0 >= rows) return;
+  const bool bad = q1 > p.num_tokens || ql > p.max_q_len || kvl < ql ||
+                   kvl > p.table_len * (int64_t)p.block_size || kvl > 0x7fffffffll - 256;
+  if (bad && threadIdx.x == 0 && blockIdx.x == gridDim.x - 1 && kvh == 0)
+    set_status(&g_decode_status, KVC_STATUS_INDEX_OOB);
+  if (q1 > p.num_tokens) return;
+  const int prefix = bad ? 0 : (int)(kvl - ql);
+  const int64_t R_last = (R0 + kUmmaRows < rows ? R0 + kUmmaRows : rows) - 1;
+  const int t_first = (int)(R0 / G), t_last = (int)(R_last / G);
+  const int kv_end = bad ? 0 : prefix + t_last + 1;
+  int kv_beg = p.window > 0 ? prefix + t_first + 1 - p.window : 0;
+  kv_beg = kv_beg > 0 ? kv_beg / KT * KT : 0;
+  const int ntiles = kv_end > kv_beg ? (kv_end - kv_beg + KT - 1) / KT : 0;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int s = 0; s < KST; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 4);
+    }
+    mbar_init(pv_done, 1);
+    mbar_init(q_ready, 4);
+    mbar_init(all_done, 1);
+    mbar_fence_init();
+  }
+  // stale ring contents are read as V of masked tokens (P = 0): start from zeros
+  for (int i = threadIdx.x; i < UG::RING / 16; i += kUmmaThreads)
+    reinterpret_cast<uint4*>(ring)[i] = make_uint4(0u, 0u, 0u, 0u);
+  fence_proxy_async();
+  if (warp == 5) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  umma::fence_before();
+  __syncthreads();
+  umma::fence_after();
+  const uint32_t tmem = s_tmem;
+  auto abort_now = [&]() -> bool { return *(volatile int*)&s_abort != 0; };
+  auto give_up = [&]() {
+    s_abort = 1;
+    set_status(&g_decode_status, KVC_STATUS_WAIT_TIMEOUT);
+  };
+
+  if (warp == 4) {
+    // ---- producer: 128-token tiles of whole pages
+    const T* kbase = reinterpret_cast<const T*>(p.k_cache) + (int64_t)kvh * p.k_head_stride;
+    const uint32_t* table = p.block_tables + (int64_t)seq * p.table_stride;
+    auto load_id = [&](int j) -> uint32_t {
+      uint32_t id = 0xffffffffu;
+      const int tok = kv_beg + j * KT + lane * BS;
+      if (lane < PAGES && j < ntiles && tok < kv_end) id = __ldg(table + tok / BS);
+      return id;
+    };
+    uint32_t id = load_id(0);
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j % KST;
+      bool ok = true;
+      if (j >= KST && lane == 0) ok = mbar_wait_bounded(&kv_empty[st], (uint32_t)(((j / KST) - 1) & 1));
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) give_up();
+        break;
+      }
+      if (__shfl_sync(0xffffffffu, abort_now() ? 1 : 0, 0)) break;
+      const int t0 = kv_beg + j * KT;
+      const bool in_range = lane < PAGES && t0 + lane * BS < kv_end;
+      const bool valid = in_range && (int64_t)id < p.num_blocks;
+      if (in_range && !valid) set_status(&g_decode_status, KVC_STATUS_BLOCK_OOB);
+      const uint32_t mask = __ballot_sync(0xffffffffu, valid);
+      uint32_t ids[PAGES];
+#pragma unroll
+      for (int i = 0; i < PAGES; ++i) ids[i] = __shfl_sync(0xffffffffu, id, i);
+      id = load_id(j + 1);  // next tile's ids, in flight while this one is issued
+      if (lane == 0) {
+        page_mask[st] = mask;
+        uint8_t* kst = ring + (size_t)st * UG::STAGE;
+        uint8_t* vst = kst + PAGES * PAGE;
+        if (mask) {
+          mbar_arrive_expect_tx(&kv_full[st], (uint32_t)__popc(mask) * 2u * (uint32_t)PAGE);
+#pragma unroll
+          for (int i = 0; i < PAGES; ++i) {
+            if (mask & (1u << i)) {
+              bulk_g2s(kst + i * PAGE, kbase + (int64_t)ids[i] * p.k_block_stride, PAGE, &kv_full[st]);
+              tma_load_4d(vst + i * PAGE, &vmap, 0, 0, kvh, (int)ids[i], &kv_full[st]);
+            }
+          }
+        } else {
+          mbar_arrive(&kv_full[st]);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ---- MMA issue (one lane)
+    if (lane == 0) {
+      const uint32_t idS = umma::instr_desc(BF16, 128, BS), idO = umma::instr_desc(BF16, 128, D);
+      bool o_init = false;
+      bool ok = mbar_wait_bounded(q_ready, 0);
+      umma::fence_after();
+      auto issue_pv = [&](int i) -> bool {
+        const int b = i & 1, st = i % KST;
+        if (!mbar_wait_bounded(&p_full[b], (uint32_t)((i >> 1) & 1))) return false;
+        umma::fence_after();
+        const uint32_t vst = smem_u32(ring + (size_t)st * UG::STAGE + PAGES * PAGE);
+        const int t0 = kv_beg + i * KT;
+#pragma unroll 1
+        for (int ks = 0; ks < KT / 16; ++ks) {
+          if (t0 + 16 * ks >= kv_end) break;
+          const int pg = (16 * ks) / BS, within = (16 * ks) % BS;
+          const uint64_t vd = BS == 32 ? umma::smem_desc(vst + pg * PAGE + within * 2, 16, 512, umma::kLayoutSw64)
+                                       : umma::smem_desc(vst + pg * PAGE, 16, 256, umma::kLayoutSw32);
+          const uint32_t pcol = tmem + UG::SCOL + b * 128 + 8 * ks;
+          umma::mma_ts(tmem + UG::OCOL, pcol, vd, idO, o_init ? 1u : 0u);
+          o_init = true;
+          if (SPLIT) umma::mma_ts(tmem + UG::OCOL, pcol + 64, vd, idO, 1u);
+        }
+        umma::commit(pv_done);
+        umma::commit(&kv_empty[st]);
+        return true;
+      };
+      for (int j = 0; j < ntiles && ok; ++j) {
+        const int st = j % KST, b = j & 1;
+        if (abort_now() || !mbar_wait_bounded(&kv_full[st], (uint32_t)((j / KST) & 1))) {
+          ok = false;
+          break;
+        }
+        umma::fence_after();
+        const uint32_t kst = smem_u32(ring + (size_t)st * UG::STAGE);
+        const int t0 = kv_beg + j * KT;
+#pragma unroll 1
+        for (int pg = 0; pg < PAGES; ++pg) {
+          if (t0 + pg * BS >= kv_end) break;
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks)
+            umma::mma_ts(tmem + UG::SCOL + b * 128 + pg * BS, tmem + UG::QCOL + 8 * ks,
+                         umma::smem_desc(kst + pg * PAGE + ks * 2 * BS * 16, BS * 16, 128, umma::kLayoutNone), idS,
+                         ks > 0 ? 1u : 0u);
+        }
+        umma::commit(&s_full[b]);
+        if (j >= 1 && !issue_pv(j - 1)) ok = false;
+      }
+      if (ok && ntiles > 0 && !abort_now()) ok = issue_pv(ntiles - 1);
+      if (!ok) give_up();
+      // every product issued so far is complete before TMEM can be freed
+      umma::commit(all_done);
+      mbar_wait_bounded(all_done, 0);
+    }
+    __syncwarp();
+  } else {
+    // ---- softmax / epilogue: thread r = row R0 + r = TMEM lane r
+    const int r = threadIdx.x;
+    const int64_t R = R0 + r;
+    const bool in_tile = R < rows;      // a row of the sequence (else padding of the last tile)
+    const bool on = in_tile && !bad;    // a row that sees keys
+    const int t = in_tile ? (int)(R / G) : 0, g = in_tile ? (int)(R - (int64_t)t * G) : 0;
+    const int end_r = on ? prefix + t + 1 : 0;
+    const int beg_r = p.window > 0 ? end_r - p.window : 0;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    // Q row -> TMEM columns QCOL .. QCOL + D/2 - 1 (element pairs)
+    {
+      uint32_t qv[32];
+      const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+          reinterpret_cast<const T*>(p.q) + (q0 + t) * p.q_tok_stride + (int64_t)(kvh * G + g) * p.q_head_stride);
+#pragma unroll
+      for (int c = 0; c < D / 2; c += 32) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) qv[i] = on ? __ldg(qrow + c + i) : 0u;
+        umma::st32(lane_base + UG::QCOL + c, qv);
+      }
+    }
+    umma::wait_st();
+    umma::fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(q_ready);
+
+    const float qk_scale = p.scale * kLog2e;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int b = j & 1, st = j % KST;
+      if (abort_now() || !mbar_wait_bounded(&s_full[b], (uint32_t)((j >> 1) & 1))) {
+        ok = false;
+        break;
+      }
+      umma::fence_after();
+      // (the stage's barrier orders the producer's page mask and the TMA-written
+      // V before this thread reads or clears them; its phase cannot move on
+      // before this tile's P is handed over)
+      if (!mbar_wait_bounded(&kv_full[st], (uint32_t)((j / KST) & 1))) {
+        ok = false;
+        break;
+      }
+      const int t0 = kv_beg + j * KT;
+      const uint32_t pm = page_mask[st];
+      float x[KT];
+#pragma unroll
+      for (int c = 0; c < KT; c += 32) {
+        uint32_t v[32];
+        umma::ld32(lane_base + UG::SCOL + b * 128 + c, v);
+        umma::wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[c + i] = __uint_as_float(v[i]);
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < KT; ++c) {
+        const int tok = t0 + c;
+        const bool vis = tok >= beg_r && tok < end_r && ((pm >> (c / BS)) & 1u);
+        x[c] = vis ? x[c] * qk_scale : -INFINITY;
+        mx = fmaxf(mx, x[c]);
+      }
+      // lazy max: rescale only when the max rises by more than 2^8
+      float alpha = 1.f;
+      if (mx > m_ref + 8.f) {
+        alpha = m_ref == -INFINITY ? 0.f : fast_exp2(m_ref - mx);
+        m_ref = mx;
+      }
+      const float ref = m_ref == -INFINITY ? 0.f : m_ref;
+      float ps = 0.f;
+#pragma unroll
+      for (int c = 0; c < KT; ++c) {
+        x[c] = fast_exp2(x[c] - ref);
+        ps += x[c];
+      }
+      l = l * alpha + ps;
+      // O and the P buffer are free once P.V of the previous tile is done
+      if (j >= 1) {
+        if (!mbar_wait_bounded(pv_done, (uint32_t)((j - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        umma::fence_after();
+      }
+      if (__any_sync(0xffffffffu, alpha != 1.f) && j >= 1) {
+#pragma unroll
+        for (int c = 0; c < D; c += 32) {
+          uint32_t v[32];
+          umma::ld32(lane_base + UG::OCOL + c, v);
+          umma::wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+          umma::st32(lane_base + UG::OCOL + c, v);
+        }
+      }
+      // the last tile's partial page: V of tokens past the context end becomes 0
+      // (its slots may hold anything and 0 * NaN = NaN)
+      if (t0 + KT > kv_end && (kv_end - t0) % BS != 0) {
+        const int pg = (kv_end - t0) / BS, from = (kv_end - t0) % BS;
+        if ((pm >> pg) & 1u) {
+          uint8_t* vpage = ring + (size_t)st * UG::STAGE + PAGES * PAGE + pg * PAGE;
+          const int d = r;  // thread r clears row d of the page
+          if (d < D) {
+            for (int tk = from; tk < BS; ++tk) {
+              const int ch = tk / 8;
+              const int phys = BS == 32 ? (ch ^ ((d >> 1) & 3)) : (ch ^ ((d >> 2) & 1));
+              *reinterpret_cast<uint16_t*>(vpage + d * BS * 2 + phys * 16 + (tk % 8) * 2) = 0;
+            }
+          }
+          fence_proxy_async();
+        }
+      }
+      // P over the S buffer: hi pairs in columns 0..63, lo pairs in 64..127
+#pragma unroll
+      for (int c = 0; c < KT; c += 64) {
+        uint32_t hi[32], lo[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if constexpr (SPLIT) {
+            MmaOp<T>::pack_split(x[c + 2 * i], x[c + 2 * i + 1], hi[i], lo[i]);
+          } else {
+            hi[i] = MmaOp<T>::pack(x[c + 2 * i], x[c + 2 * i + 1]);
+            lo[i] = 0u;
+          }
+        }
+        umma::st32(lane_base + UG::SCOL + b * 128 + c / 2, hi);
+        if constexpr (SPLIT) umma::st32(lane_base + UG::SCOL + b * 128 + 64 + c / 2, lo);
+      }
+      umma::wait_st();
+      umma::fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
+    }
+    if (!ok && lane == 0) give_up();
+    bool have = ok && ntiles > 0;
+    if (have) {
+      have = mbar_wait_bounded(pv_done, (uint32_t)((ntiles - 1) & 1));
+      if (!have && lane == 0) give_up();
+      umma::fence_after();
+    }
+    // ---- epilogue: O / l (a row with no visible key, or after an abort, is 0)
+    const bool nonzero = have && l > 0.f;  // else explicit zeros (this CTA may never have written O)
+    const float inv = nonzero ? 1.f / l : 0.f;
+    T* orow = reinterpret_cast<T*>(p.out) + (q0 + t) * p.out_tok_stride + (int64_t)(kvh * G + g) * p.out_head_stride;
+#pragma unroll
+    for (int c = 0; c < D; c += 32) {
+      uint32_t v[32];
+      umma::ld32(lane_base + UG::OCOL + c, v);
+      umma::wait_ld();
+      if (R < rows) {
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          packed[i] = nonzero ? pack_out<T>(__uint_as_float(v[2 * i]) * inv, __uint_as_float(v[2 * i + 1]) * inv) : 0u;
+#pragma unroll
+        for (int i = 0; i < 16; i += 4)
+          *reinterpret_cast<uint4*>(orow + c + 2 * i) = make_uint4(packed[i], packed[i + 1], packed[i + 2], packed[i + 3]);
+      }
+    }
+  }
+
+  umma::fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    umma::fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
+template <typename T, int D, int BS>
+static cudaError_t launch_prefill_umma(const PrefillArgs& a, cudaStream_t stream) {
+  using UG = UmmaGeom<D, BS>;
+  DecodeParams dp;
+  memset(&dp, 0, sizeof(dp));
+  dp.k_cache = a.k_cache;
+  dp.v_cache = a.v_cache;
+  dp.num_blocks = a.num_blocks;
+  dp.num_kv_heads = a.num_kv_heads;
+  dp.k_head_stride = a.k_head_stride;
+  dp.k_block_stride = a.k_block_stride;
+  dp.v_head_stride = a.v_head_stride;
+  dp.v_block_stride = a.v_block_stride;
+  TmaMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  // the kTiles maps: V as [nb][H][D][BS] pages, one whole page per box, bs*2-byte swizzle
+  if (!make_tensor_maps(dp, std::is_same<T, __nv_bfloat16>::value ? ElemType::BF16 : ElemType::F16, D, BS, BS, BS * 2,
+                        kTiles, &maps))
+    return cudaErrorNotSupported;
+  auto kern = prefill_umma_kernel<T, D, BS>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, UG::SMEM);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  const int G = a.num_heads / a.num_kv_heads;
+  const int64_t tiles = ((int64_t)a.max_q_len * G + kUmmaRows - 1) / kUmmaRows;
+  if (tiles <= 0) return cudaSuccess;
+  if (tiles > 0x7fffffffll) return cudaErrorInvalidValue;
+  kern<<<dim3((unsigned)tiles, (unsigned)a.num_seqs, (unsigned)a.num_kv_heads), kUmmaThreads, UG::SMEM, stream>>>(
+      a, maps.v);
+  count_launch();
+  return cudaGetLastError();
+}
+
+// The tcgen05 kernel serves the paged layout with block size 16 or 32 (pages
+// tile a 128-token S tile; V rows of 32 or 64 bytes match a swizzle mode).
+static bool prefill_umma_supported(const PrefillArgs& a) {
+  if (a.token_major || !(a.block_size == 16 || a.block_size == 32) || !(a.head_size == 64 || a.head_size == 128))
+    return false;
+  // rows are stored as 16-byte vectors
+  if ((reinterpret_cast<uintptr_t>(a.out) & 15u) || (a.out_tok_stride & 7) || (a.out_head_stride & 7)) return false;
+  const char* v = getenv("KVC_PREFILL_KERNEL");
+  return !(v && (v[0] == 'm' || v[0] == 'M'));  // "mma": the mma.sync kernel
+}
+
+static cudaError_t launch_prefill_umma_any(const PrefillArgs& a, cudaStream_t stream) {
+  const bool bf = a.q_type == ElemType::BF16;
+  if (a.head_size == 128) {
+    if (a.block_size == 32)
+      return bf ? launch_prefill_umma<__nv_bfloat16, 128, 32>(a, stream) : launch_prefill_umma<__half, 128, 32>(a, stream);
+    return bf ? launch_prefill_umma<__nv_bfloat16, 128, 16>(a, stream) : launch_prefill_umma<__half, 128, 16>(a, stream);
+  }
+  if (a.block_size == 32)
+    return bf ? launch_prefill_umma<__nv_bfloat16, 64, 32>(a, stream) : launch_prefill_umma<__half, 64, 32>(a, stream);
+  return bf ? launch_prefill_umma<__nv_bfloat16, 64, 16>(a, stream) : launch_prefill_umma<__half, 64, 16>(a, stream);
+}
+
+cudaError_t launch_paged_prefill(const PrefillArgs& a, cudaStream_t stream) {
+  if (a.num_seqs <= 0 || a.max_q_len <= 0) return cudaSuccess;
+  if (a.num_seqs > 65535 || a.num_kv_heads > 65535) return cudaErrorInvalidValue;
+  if (prefill_umma_supported(a)) return launch_prefill_umma_any(a, stream);
+  return launch_prefill_mma_any(a, stream);
+}
+
+}  // namespace kvc
