@@ -60,6 +60,22 @@ __device__ __forceinline__ void commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mma_detail::smem_u32(bar))
                : "memory");
 }
+// Waits for the phase with `parity`, the thread suspended in the barrier
+// (up to 200 us per try, woken when the phase completes) instead of spinning;
+// gives up after ~1 s of wall time (returns false).
+__device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = mma_detail::global_timer_ns();
+  for (;;) {
+    uint32_t done;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(mma_detail::smem_u32(bar)), "r"(parity), "r"(200000u)
+        : "memory");
+    if (done) return true;
+    if (mma_detail::global_timer_ns() - t0 > 1000000000ull) return false;
+  }
+}
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -89,11 +105,24 @@ __device__ __forceinline__ void st32(uint32_t taddr, const uint32_t (&r)[32]) {
   st16(taddr + 16, r + 16);
 }
 
+// Four rows (row0..row3 of a 2-D tensor map whose box is one row high) land
+// one after another at `dst`: a gather of the same chunk of four pages.
+__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, int col, int row0, int row1, int row2,
+                                            int row3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5, %6, %7}], [%2];" ::"r"(mma_detail::smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(mma_detail::smem_u32(bar)), "r"(col), "r"(row0), "r"(row1), "r"(row2),
+      "r"(row3)
+      : "memory");
+}
+
 }  // namespace umma
 
 constexpr int kUmmaRows = 128;   // query rows per CTA (TMEM lanes)
 constexpr int kUmmaTile = 128;   // tokens per S tile
-constexpr int kUmmaThreads = 192;
+constexpr int kUmmaThreads = 320;  // 8 softmax warps, a producer warp, an MMA warp
+constexpr int kProducerWarp = 8, kMmaWarp = 9;
 
 template <int D, int BS>
 struct UmmaGeom {
@@ -103,17 +132,21 @@ struct UmmaGeom {
   static constexpr int KST = D == 128 ? 3 : 4;       // ring stages
   static constexpr int RING = KST * STAGE;
   static constexpr int BAR_OFF = 1024 + RING;        // (1024: alignment slack of the ring)
-  static constexpr int NBARS = 2 * KST + 2 + 2 + 1 + 1 + 1;  // kv full/empty, s_full, p_full, pv_done, q_ready, done
+  static constexpr int NBARS = 2 * KST + 2 + 2 + 1 + 1 + 1 + 1;  // kv full/empty, s_full, p_full, pv_done, q_ready, done, xchg
   static constexpr int MASK_OFF = BAR_OFF + NBARS * 8;
-  static constexpr int SMEM = MASK_OFF + KST * 4 + 16;
+  static constexpr int XBUF_OFF = (MASK_OFF + KST * 4 + 15) / 16 * 16;
+  static constexpr int SMEM = XBUF_OFF + 2 * 2 * 128 * 4;
   static constexpr uint32_t SCOL = 0, OCOL = 256, QCOL = 256 + D;  // TMEM columns
   static_assert(QCOL + D / 2 <= 512, "TMEM columns");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
-template <typename T, int D, int BS>
+// GK: K reaches shared memory as [D/8 chunks][128 tokens][8] through 4-row
+// gathers (a dense K cache, block size 32), so S is one N = 128 product per
+// k-step; else each K page is one bulk copy and S one N = BS chain per page.
+template <typename T, int D, int BS, bool GK>
 __global__ void __launch_bounds__(kUmmaThreads, 1)
-    prefill_umma_kernel(const PrefillArgs p, const __grid_constant__ CUtensorMap vmap) {
+    prefill_umma_kernel(const PrefillArgs p, const __grid_constant__ TmaMaps maps) {
   using namespace mma_detail;
   using UG = UmmaGeom<D, BS>;
   constexpr int PAGES = UG::PAGES, PAGE = UG::PAGE, KST = UG::KST, KT = kUmmaTile;
@@ -131,11 +164,16 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   uint64_t* pv_done = p_full + 2;
   uint64_t* q_ready = pv_done + 1;
   uint64_t* all_done = q_ready + 1;
+  uint64_t* xchg = all_done + 1;
+  float* xbuf = reinterpret_cast<float*>(smem_raw + UG::XBUF_OFF);  // [2 phases][2 halves][128 rows]
   uint32_t* page_mask = reinterpret_cast<uint32_t*>(smem_raw + UG::MASK_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seq = blockIdx.y, kvh = blockIdx.z;
   const int G = p.num_heads / p.num_kv_heads;
+  const CUtensorMap* vmap = &maps.v;
+  const CUtensorMap* kmap = &maps.k;
+  static_assert(!GK || (BS == 32 && PAGES == 4), "the gathered K layout takes four 32-token pages");
   const int64_t q0 = p.qo_indptr[seq];
   const int64_t q1 = p.qo_indptr[seq + 1];
   const int64_t kvl = p.kv_lens[seq];
@@ -164,10 +202,11 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], 4);
+      mbar_init(&p_full[b], 8);
     }
     mbar_init(pv_done, 1);
-    mbar_init(q_ready, 4);
+    mbar_init(q_ready, 8);
+    mbar_init(xchg, 8);
     mbar_init(all_done, 1);
     mbar_fence_init();
   }
@@ -175,7 +214,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   for (int i = threadIdx.x; i < UG::RING / 16; i += kUmmaThreads)
     reinterpret_cast<uint4*>(ring)[i] = make_uint4(0u, 0u, 0u, 0u);
   fence_proxy_async();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
                  "r"(512));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -190,7 +229,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     set_status(&g_decode_status, KVC_STATUS_WAIT_TIMEOUT);
   };
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     // ---- producer: 128-token tiles of whole pages
     const T* kbase = reinterpret_cast<const T*>(p.k_cache) + (int64_t)kvh * p.k_head_stride;
     const uint32_t* table = p.block_tables + (int64_t)seq * p.table_stride;
@@ -204,7 +243,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     for (int j = 0; j < ntiles; ++j) {
       const int st = j % KST;
       bool ok = true;
-      if (j >= KST && lane == 0) ok = mbar_wait_bounded(&kv_empty[st], (uint32_t)(((j / KST) - 1) & 1));
+      if (j >= KST && lane == 0) ok = umma::wait(&kv_empty[st], (uint32_t)(((j / KST) - 1) & 1));
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         if (lane == 0) give_up();
@@ -224,13 +263,28 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         page_mask[st] = mask;
         uint8_t* kst = ring + (size_t)st * UG::STAGE;
         uint8_t* vst = kst + PAGES * PAGE;
+        // few and large requests (the copy engine serves them one by one):
+        // per page one tensor copy of V and one bulk copy of K, or with GK one
+        // 4-row gather per 8-dim chunk for the K of all four pages
         if (mask) {
-          mbar_arrive_expect_tx(&kv_full[st], (uint32_t)__popc(mask) * 2u * (uint32_t)PAGE);
+          if constexpr (GK) {
+            mbar_arrive_expect_tx(&kv_full[st], (uint32_t)(PAGES + __popc(mask)) * (uint32_t)PAGE);
+            const uint32_t any = ids[__ffs(mask) - 1];  // pages without keys gather a loaded page's rows
+            int rb[PAGES];
+#pragma unroll
+            for (int i = 0; i < PAGES; ++i)
+              rb[i] = (int)(((int64_t)((mask >> i) & 1u ? ids[i] : any) * p.num_kv_heads + kvh) * (D / 8));
+#pragma unroll
+            for (int c = 0; c < D / 8; ++c)
+              umma::tma_gather4(kst + c * KT * 16, kmap, 0, rb[0] + c, rb[1] + c, rb[2] + c, rb[3] + c, &kv_full[st]);
+          } else {
+            mbar_arrive_expect_tx(&kv_full[st], (uint32_t)__popc(mask) * 2u * (uint32_t)PAGE);
+          }
 #pragma unroll
           for (int i = 0; i < PAGES; ++i) {
             if (mask & (1u << i)) {
-              bulk_g2s(kst + i * PAGE, kbase + (int64_t)ids[i] * p.k_block_stride, PAGE, &kv_full[st]);
-              tma_load_4d(vst + i * PAGE, &vmap, 0, 0, kvh, (int)ids[i], &kv_full[st]);
+              if constexpr (!GK) bulk_g2s(kst + i * PAGE, kbase + (int64_t)ids[i] * p.k_block_stride, PAGE, &kv_full[st]);
+              tma_load_4d(vst + i * PAGE, vmap, 0, 0, kvh, (int)ids[i], &kv_full[st]);
             }
           }
         } else {
@@ -238,51 +292,69 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ---- MMA issue (one lane)
     if (lane == 0) {
-      const uint32_t idS = umma::instr_desc(BF16, 128, BS), idO = umma::instr_desc(BF16, 128, D);
+      const uint32_t idS = umma::instr_desc(BF16, 128, GK ? KT : BS), idO = umma::instr_desc(BF16, 128, D);
       bool o_init = false;
-      bool ok = mbar_wait_bounded(q_ready, 0);
+      bool ok = umma::wait(q_ready, 0);
       umma::fence_after();
+      // Descriptors of stage 0, advanced by adding (byte offset >> 4) to the
+      // start-address field (shared addresses stay below 256 KB: no carry).
+      const uint32_t ring_addr = smem_u32(ring);
+      const uint64_t k_desc0 = umma::smem_desc(ring_addr, (GK ? KT : BS) * 16, 128, umma::kLayoutNone);
+      const uint64_t v_desc0 = BS == 32 ? umma::smem_desc(ring_addr + PAGES * PAGE, 16, 512, umma::kLayoutSw64)
+                                        : umma::smem_desc(ring_addr + PAGES * PAGE, 16, 256, umma::kLayoutSw32);
       auto issue_pv = [&](int i) -> bool {
         const int b = i & 1, st = i % KST;
-        if (!mbar_wait_bounded(&p_full[b], (uint32_t)((i >> 1) & 1))) return false;
+        if (!umma::wait(&p_full[b], (uint32_t)((i >> 1) & 1))) return false;
         umma::fence_after();
-        const uint32_t vst = smem_u32(ring + (size_t)st * UG::STAGE + PAGES * PAGE);
-        const int t0 = kv_beg + i * KT;
-#pragma unroll 1
+        const uint64_t vd = v_desc0 + (uint64_t)((st * UG::STAGE) >> 4);
+        const int steps = (kv_end - (kv_beg + i * KT) + 15) / 16;  // 16-token k-steps with keys
+        const uint32_t pcol = tmem + UG::SCOL + b * 128;
+#pragma unroll
         for (int ks = 0; ks < KT / 16; ++ks) {
-          if (t0 + 16 * ks >= kv_end) break;
-          const int pg = (16 * ks) / BS, within = (16 * ks) % BS;
-          const uint64_t vd = BS == 32 ? umma::smem_desc(vst + pg * PAGE + within * 2, 16, 512, umma::kLayoutSw64)
-                                       : umma::smem_desc(vst + pg * PAGE, 16, 256, umma::kLayoutSw32);
-          const uint32_t pcol = tmem + UG::SCOL + b * 128 + 8 * ks;
-          umma::mma_ts(tmem + UG::OCOL, pcol, vd, idO, o_init ? 1u : 0u);
-          o_init = true;
-          if (SPLIT) umma::mma_ts(tmem + UG::OCOL, pcol + 64, vd, idO, 1u);
+          if (ks < steps) {
+            // k-step ks: tokens 16ks.. = page (16ks)/BS, byte (16ks % BS) * 2 of its rows
+            const uint64_t d = vd + (uint64_t)((((16 * ks) / BS) * PAGE + ((16 * ks) % BS) * 2) >> 4);
+            umma::mma_ts(tmem + UG::OCOL, pcol + 8 * ks, d, idO, (o_init || ks > 0) ? 1u : 0u);
+            if (SPLIT) umma::mma_ts(tmem + UG::OCOL, pcol + 64 + 8 * ks, d, idO, 1u);
+          }
         }
+        o_init = true;
         umma::commit(pv_done);
         umma::commit(&kv_empty[st]);
         return true;
       };
       for (int j = 0; j < ntiles && ok; ++j) {
         const int st = j % KST, b = j & 1;
-        if (abort_now() || !mbar_wait_bounded(&kv_full[st], (uint32_t)((j / KST) & 1))) {
+        if (abort_now() || !umma::wait(&kv_full[st], (uint32_t)((j / KST) & 1))) {
           ok = false;
           break;
         }
         umma::fence_after();
-        const uint32_t kst = smem_u32(ring + (size_t)st * UG::STAGE);
         const int t0 = kv_beg + j * KT;
-#pragma unroll 1
-        for (int pg = 0; pg < PAGES; ++pg) {
-          if (t0 + pg * BS >= kv_end) break;
+        const int live = (kv_end - t0 + BS - 1) / BS;  // pages with keys
+        const uint64_t kd = k_desc0 + (uint64_t)((st * UG::STAGE) >> 4);
+        if constexpr (GK) {
+          // S = Q K^T as one N = 128 product per 16-dim k-step
 #pragma unroll
           for (int ks = 0; ks < D / 16; ++ks)
-            umma::mma_ts(tmem + UG::SCOL + b * 128 + pg * BS, tmem + UG::QCOL + 8 * ks,
-                         umma::smem_desc(kst + pg * PAGE + ks * 2 * BS * 16, BS * 16, 128, umma::kLayoutNone), idS,
-                         ks > 0 ? 1u : 0u);
+            umma::mma_ts(tmem + UG::SCOL + b * 128, tmem + UG::QCOL + 8 * ks, kd + (uint64_t)((ks * 2 * KT * 16) >> 4),
+                         idS, ks > 0 ? 1u : 0u);
+          (void)live;
+        } else {
+          // S = Q K^T: per page a chain of D/16 products (N = BS); k-step outer
+          // so consecutive products go to different pages' accumulators
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks) {
+#pragma unroll
+            for (int pg = 0; pg < PAGES; ++pg) {
+              if (pg < live)
+                umma::mma_ts(tmem + UG::SCOL + b * 128 + pg * BS, tmem + UG::QCOL + 8 * ks,
+                             kd + (uint64_t)((pg * PAGE + ks * 2 * BS * 16) >> 4), idS, ks > 0 ? 1u : 0u);
+            }
+          }
         }
         umma::commit(&s_full[b]);
         if (j >= 1 && !issue_pv(j - 1)) ok = false;
@@ -291,30 +363,36 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       if (!ok) give_up();
       // every product issued so far is complete before TMEM can be freed
       umma::commit(all_done);
-      mbar_wait_bounded(all_done, 0);
+      umma::wait(all_done, 0);
     }
     __syncwarp();
   } else {
-    // ---- softmax / epilogue: thread r = row R0 + r = TMEM lane r
-    const int r = threadIdx.x;
+    // ---- softmax / epilogue: warps w and w + 4 share rows 32w .. 32w + 31
+    // (TMEM lanes); `half` 0 takes tokens 0..63 of every tile and O columns
+    // 0 .. D/2 - 1, half 1 the rest.  The halves exchange row maxima (and at
+    // the end row sums) through shared memory on the `xchg` barrier.
+    const int half = warp >> 2;
+    const int r = threadIdx.x & 127;
     const int64_t R = R0 + r;
     const bool in_tile = R < rows;      // a row of the sequence (else padding of the last tile)
     const bool on = in_tile && !bad;    // a row that sees keys
     const int t = in_tile ? (int)(R / G) : 0, g = in_tile ? (int)(R - (int64_t)t * G) : 0;
     const int end_r = on ? prefix + t + 1 : 0;
     const int beg_r = p.window > 0 ? end_r - p.window : 0;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-    // Q row -> TMEM columns QCOL .. QCOL + D/2 - 1 (element pairs)
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    constexpr int HK = KT / 2;   // tokens of a tile per half
+    constexpr int HD = D / 2;    // O columns per half
+    constexpr int QC = D / 4;    // Q columns (element pairs) per half
+    // Q row -> TMEM columns QCOL .. QCOL + D/2 - 1 (element pairs), QC per half
     {
-      uint32_t qv[32];
       const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
-          reinterpret_cast<const T*>(p.q) + (q0 + t) * p.q_tok_stride + (int64_t)(kvh * G + g) * p.q_head_stride);
+          reinterpret_cast<const T*>(p.q) + (q0 + t) * p.q_tok_stride + (int64_t)(kvh * G + g) * p.q_head_stride) +
+          half * QC;
+      uint32_t qv[32];
 #pragma unroll
-      for (int c = 0; c < D / 2; c += 32) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) qv[i] = on ? __ldg(qrow + c + i) : 0u;
-        umma::st32(lane_base + UG::QCOL + c, qv);
-      }
+      for (int i = 0; i < QC; ++i) qv[i] = on ? __ldg(qrow + i) : 0u;
+      if constexpr (QC == 32) umma::st32(lane_base + UG::QCOL + half * QC, qv);
+      else umma::st16(lane_base + UG::QCOL + half * QC, qv);
     }
     umma::wait_st();
     umma::fence_before();
@@ -324,9 +402,26 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     const float qk_scale = p.scale * kLog2e;
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
+    uint32_t xphase = 0;
+    // both halves' values of this row: write mine, hand over, read the other's
+    // (two buffers by phase parity: a warp a phase ahead cannot overwrite a
+    // value the other half has yet to read, since that phase needs its arrival)
+    auto exchange = [&](float mine) -> float {
+      float* buf = xbuf + (xphase & 1u) * 256;
+      buf[half * 128 + r] = mine;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(xchg);
+      const bool got = umma::wait(xchg, xphase & 1u);
+      ++xphase;
+      if (!got) {
+        ok = false;
+        return mine;
+      }
+      return buf[(half ^ 1) * 128 + r];
+    };
     for (int j = 0; j < ntiles; ++j) {
       const int b = j & 1, st = j % KST;
-      if (abort_now() || !mbar_wait_bounded(&s_full[b], (uint32_t)((j >> 1) & 1))) {
+      if (abort_now() || !umma::wait(&s_full[b], (uint32_t)((j >> 1) & 1))) {
         ok = false;
         break;
       }
@@ -334,46 +429,72 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       // (the stage's barrier orders the producer's page mask and the TMA-written
       // V before this thread reads or clears them; its phase cannot move on
       // before this tile's P is handed over)
-      if (!mbar_wait_bounded(&kv_full[st], (uint32_t)((j / KST) & 1))) {
+      if (!umma::wait(&kv_full[st], (uint32_t)((j / KST) & 1))) {
         ok = false;
         break;
       }
-      const int t0 = kv_beg + j * KT;
+      const int t0 = kv_beg + j * KT + half * HK;  // first token of my half
       const uint32_t pm = page_mask[st];
-      float x[KT];
+      float x[HK];
 #pragma unroll
-      for (int c = 0; c < KT; c += 32) {
+      for (int c = 0; c < HK; c += 32) {
         uint32_t v[32];
-        umma::ld32(lane_base + UG::SCOL + b * 128 + c, v);
-        umma::wait_ld();
+        umma::ld32(lane_base + UG::SCOL + b * 128 + half * HK + c, v);
 #pragma unroll
         for (int i = 0; i < 32; ++i) x[c + i] = __uint_as_float(v[i]);
       }
-      float mx = -INFINITY;
+      umma::wait_ld();
+      // A half tile every row of the warp sees whole (its pages loaded, inside
+      // every row's [start, end)) needs no per-token mask.
+      const uint32_t my_pages = HK >= BS ? ((1u << (HK / BS)) - 1u) << (half * HK / BS) : 0u;
+      const bool whole =
+          __all_sync(0xffffffffu, (pm & my_pages) == my_pages && t0 >= beg_r && t0 + HK <= end_r);
+      float mx;  // row max of my scaled scores (log2 units)
+      if (whole) {
+        float hi_raw = -INFINITY, lo_raw = INFINITY;
 #pragma unroll
-      for (int c = 0; c < KT; ++c) {
-        const int tok = t0 + c;
-        const bool vis = tok >= beg_r && tok < end_r && ((pm >> (c / BS)) & 1u);
-        x[c] = vis ? x[c] * qk_scale : -INFINITY;
-        mx = fmaxf(mx, x[c]);
+        for (int c = 0; c < HK; c += 2) {
+          hi_raw = fmaxf(hi_raw, fmaxf(x[c], x[c + 1]));
+          lo_raw = fminf(lo_raw, fminf(x[c], x[c + 1]));
+        }
+        mx = qk_scale >= 0.f ? hi_raw * qk_scale : lo_raw * qk_scale;
+      } else {
+        mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < HK; ++c) {
+          const int tok = t0 + c;
+          const bool vis = tok >= beg_r && tok < end_r && ((pm >> ((half * HK + c) / BS)) & 1u);
+          x[c] = vis ? x[c] * qk_scale : -INFINITY;
+          mx = fmaxf(mx, x[c]);
+        }
       }
-      // lazy max: rescale only when the max rises by more than 2^8
+      mx = fmaxf(mx, exchange(mx));
+      if (!ok) break;
+      // lazy max (the same in both halves): rescale only when it rises by more than 2^8
       float alpha = 1.f;
       if (mx > m_ref + 8.f) {
         alpha = m_ref == -INFINITY ? 0.f : fast_exp2(m_ref - mx);
         m_ref = mx;
       }
-      const float ref = m_ref == -INFINITY ? 0.f : m_ref;
+      const float neg_ref = m_ref == -INFINITY ? 0.f : -m_ref;
       float ps = 0.f;
+      if (whole) {
 #pragma unroll
-      for (int c = 0; c < KT; ++c) {
-        x[c] = fast_exp2(x[c] - ref);
-        ps += x[c];
+        for (int c = 0; c < HK; ++c) {
+          x[c] = fast_exp2(fmaf(x[c], qk_scale, neg_ref));
+          ps += x[c];
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < HK; ++c) {
+          x[c] = fast_exp2(x[c] + neg_ref);  // masked: exp2(-inf) = 0
+          ps += x[c];
+        }
       }
-      l = l * alpha + ps;
+      l = l * alpha + ps;  // this half's share of the row sum
       // O and the P buffer are free once P.V of the previous tile is done
       if (j >= 1) {
-        if (!mbar_wait_bounded(pv_done, (uint32_t)((j - 1) & 1))) {
+        if (!umma::wait(pv_done, (uint32_t)((j - 1) & 1))) {
           ok = false;
           break;
         }
@@ -381,22 +502,23 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       }
       if (__any_sync(0xffffffffu, alpha != 1.f) && j >= 1) {
 #pragma unroll
-        for (int c = 0; c < D; c += 32) {
+        for (int c = 0; c < HD; c += 32) {
           uint32_t v[32];
-          umma::ld32(lane_base + UG::OCOL + c, v);
+          umma::ld32(lane_base + UG::OCOL + half * HD + c, v);
           umma::wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-          umma::st32(lane_base + UG::OCOL + c, v);
+          umma::st32(lane_base + UG::OCOL + half * HD + c, v);
         }
       }
       // the last tile's partial page: V of tokens past the context end becomes 0
-      // (its slots may hold anything and 0 * NaN = NaN)
-      if (t0 + KT > kv_end && (kv_end - t0) % BS != 0) {
-        const int pg = (kv_end - t0) / BS, from = (kv_end - t0) % BS;
+      // (its slots may hold anything and 0 * NaN = NaN); half 0, thread d clears row d
+      const int tile0 = kv_beg + j * KT;
+      if (half == 0 && tile0 + KT > kv_end && (kv_end - tile0) % BS != 0) {
+        const int pg = (kv_end - tile0) / BS, from = (kv_end - tile0) % BS;
         if ((pm >> pg) & 1u) {
           uint8_t* vpage = ring + (size_t)st * UG::STAGE + PAGES * PAGE + pg * PAGE;
-          const int d = r;  // thread r clears row d of the page
+          const int d = r;
           if (d < D) {
             for (int tk = from; tk < BS; ++tk) {
               const int ch = tk / 8;
@@ -407,21 +529,26 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           fence_proxy_async();
         }
       }
-      // P over the S buffer: hi pairs in columns 0..63, lo pairs in 64..127
-#pragma unroll
-      for (int c = 0; c < KT; c += 64) {
+      // P over the S buffer: hi pairs of tokens 64h .. 64h + 63 in columns
+      // 32h .. 32h + 31, lo pairs 64 columns further
+      {
         uint32_t hi[32], lo[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           if constexpr (SPLIT) {
-            MmaOp<T>::pack_split(x[c + 2 * i], x[c + 2 * i + 1], hi[i], lo[i]);
+            // hi = the upper 16 bits of each fp32 (a bf16, truncated), lo =
+            // the exact remainder rounded to bf16: hi + lo carries ~16 bits of P
+            const uint32_t u0 = __float_as_uint(x[2 * i]), u1 = __float_as_uint(x[2 * i + 1]);
+            hi[i] = __byte_perm(u0, u1, 0x7632);
+            lo[i] = MmaOp<T>::pack(x[2 * i] - __uint_as_float(u0 & 0xFFFF0000u),
+                                   x[2 * i + 1] - __uint_as_float(u1 & 0xFFFF0000u));
           } else {
-            hi[i] = MmaOp<T>::pack(x[c + 2 * i], x[c + 2 * i + 1]);
+            hi[i] = MmaOp<T>::pack(x[2 * i], x[2 * i + 1]);
             lo[i] = 0u;
           }
         }
-        umma::st32(lane_base + UG::SCOL + b * 128 + c / 2, hi);
-        if constexpr (SPLIT) umma::st32(lane_base + UG::SCOL + b * 128 + 64 + c / 2, lo);
+        umma::st32(lane_base + UG::SCOL + b * 128 + half * 32, hi);
+        if constexpr (SPLIT) umma::st32(lane_base + UG::SCOL + b * 128 + 64 + half * 32, lo);
       }
       umma::wait_st();
       umma::fence_before();
@@ -431,18 +558,22 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     if (!ok && lane == 0) give_up();
     bool have = ok && ntiles > 0;
     if (have) {
-      have = mbar_wait_bounded(pv_done, (uint32_t)((ntiles - 1) & 1));
+      have = umma::wait(pv_done, (uint32_t)((ntiles - 1) & 1));
       if (!have && lane == 0) give_up();
       umma::fence_after();
     }
+    // both halves must take the last exchange (or time out on it) alike
+    const float l_all = l + exchange(l);
+    have = have && ok;
     // ---- epilogue: O / l (a row with no visible key, or after an abort, is 0)
-    const bool nonzero = have && l > 0.f;  // else explicit zeros (this CTA may never have written O)
-    const float inv = nonzero ? 1.f / l : 0.f;
-    T* orow = reinterpret_cast<T*>(p.out) + (q0 + t) * p.out_tok_stride + (int64_t)(kvh * G + g) * p.out_head_stride;
+    const bool nonzero = have && l_all > 0.f;  // else explicit zeros (this CTA may never have written O)
+    const float inv = nonzero ? 1.f / l_all : 0.f;
+    T* orow = reinterpret_cast<T*>(p.out) + (q0 + t) * p.out_tok_stride + (int64_t)(kvh * G + g) * p.out_head_stride +
+              half * HD;
 #pragma unroll
-    for (int c = 0; c < D; c += 32) {
+    for (int c = 0; c < HD; c += 32) {
       uint32_t v[32];
-      umma::ld32(lane_base + UG::OCOL + c, v);
+      umma::ld32(lane_base + UG::OCOL + half * HD + c, v);
       umma::wait_ld();
       if (R < rows) {
         uint32_t packed[16];
@@ -458,13 +589,28 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
 
   umma::fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     umma::fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
   }
 }
 
-template <typename T, int D, int BS>
+// K viewed as rows of one 8-dim chunk of one page of one head: [nb * H * D/8][BS * 8]
+// (needs the dense paged layout).
+static bool make_k_gather_map(const PrefillArgs& a, int D, int BS, CUtensorMap* map) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)BS * 8, (cuuint64_t)a.num_blocks * a.num_kv_heads * (D / 8)};
+  const cuuint64_t strides[1] = {(cuuint64_t)BS * 16};
+  const cuuint32_t box[2] = {(cuuint32_t)BS * 8, 1};
+  const cuuint32_t ones[2] = {1, 1};
+  return enc(map, a.q_type == ElemType::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+             const_cast<void*>(a.k_cache), dims, strides, box, ones, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+template <typename T, int D, int BS, bool GK>
 static cudaError_t launch_prefill_umma(const PrefillArgs& a, cudaStream_t stream) {
   using UG = UmmaGeom<D, BS>;
   DecodeParams dp;
@@ -483,7 +629,8 @@ static cudaError_t launch_prefill_umma(const PrefillArgs& a, cudaStream_t stream
   if (!make_tensor_maps(dp, std::is_same<T, __nv_bfloat16>::value ? ElemType::BF16 : ElemType::F16, D, BS, BS, BS * 2,
                         kTiles, &maps))
     return cudaErrorNotSupported;
-  auto kern = prefill_umma_kernel<T, D, BS>;
+  if (GK && !make_k_gather_map(a, D, BS, &maps.k)) return cudaErrorNotSupported;
+  auto kern = prefill_umma_kernel<T, D, BS, GK>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -497,7 +644,7 @@ static cudaError_t launch_prefill_umma(const PrefillArgs& a, cudaStream_t stream
   if (tiles <= 0) return cudaSuccess;
   if (tiles > 0x7fffffffll) return cudaErrorInvalidValue;
   kern<<<dim3((unsigned)tiles, (unsigned)a.num_seqs, (unsigned)a.num_kv_heads), kUmmaThreads, UG::SMEM, stream>>>(
-      a, maps.v);
+      a, maps);
   count_launch();
   return cudaGetLastError();
 }
@@ -515,14 +662,30 @@ static bool prefill_umma_supported(const PrefillArgs& a) {
 
 static cudaError_t launch_prefill_umma_any(const PrefillArgs& a, cudaStream_t stream) {
   const bool bf = a.q_type == ElemType::BF16;
+  const int64_t D = a.head_size, BS = a.block_size;
+  // the 4-row gathers need K rows uniformly strided: the dense paged layout
+  const bool dense = a.k_head_stride == D * BS && a.k_block_stride == (int64_t)a.num_kv_heads * D * BS &&
+                     a.num_blocks * a.num_kv_heads * (D / 8) < 0x7fffffffll;  // (row indices are 32-bit)
   if (a.head_size == 128) {
-    if (a.block_size == 32)
-      return bf ? launch_prefill_umma<__nv_bfloat16, 128, 32>(a, stream) : launch_prefill_umma<__half, 128, 32>(a, stream);
-    return bf ? launch_prefill_umma<__nv_bfloat16, 128, 16>(a, stream) : launch_prefill_umma<__half, 128, 16>(a, stream);
+    if (a.block_size == 32) {
+      if (dense)
+        return bf ? launch_prefill_umma<__nv_bfloat16, 128, 32, true>(a, stream)
+                  : launch_prefill_umma<__half, 128, 32, true>(a, stream);
+      return bf ? launch_prefill_umma<__nv_bfloat16, 128, 32, false>(a, stream)
+                : launch_prefill_umma<__half, 128, 32, false>(a, stream);
+    }
+    return bf ? launch_prefill_umma<__nv_bfloat16, 128, 16, false>(a, stream)
+              : launch_prefill_umma<__half, 128, 16, false>(a, stream);
   }
-  if (a.block_size == 32)
-    return bf ? launch_prefill_umma<__nv_bfloat16, 64, 32>(a, stream) : launch_prefill_umma<__half, 64, 32>(a, stream);
-  return bf ? launch_prefill_umma<__nv_bfloat16, 64, 16>(a, stream) : launch_prefill_umma<__half, 64, 16>(a, stream);
+  if (a.block_size == 32) {
+    if (dense)
+      return bf ? launch_prefill_umma<__nv_bfloat16, 64, 32, true>(a, stream)
+                : launch_prefill_umma<__half, 64, 32, true>(a, stream);
+    return bf ? launch_prefill_umma<__nv_bfloat16, 64, 32, false>(a, stream)
+              : launch_prefill_umma<__half, 64, 32, false>(a, stream);
+  }
+  return bf ? launch_prefill_umma<__nv_bfloat16, 64, 16, false>(a, stream)
+            : launch_prefill_umma<__half, 64, 16, false>(a, stream);
 }
 
 cudaError_t launch_paged_prefill(const PrefillArgs& a, cudaStream_t stream) {
