@@ -678,8 +678,11 @@ cudaError_t launch_paged_decode_cascade(const DecodeArgs& a, cudaStream_t stream
   if (!pages_aligned(a)) return cudaErrorMisalignedAddress;
   DecodeParams p = to_params(a);
   const bool tail = p.num_partitions > p.prefix_parts;
-  cudaError_t e = a.q_type == ElemType::BF16 ? launch_cascade_prefix_t<__nv_bfloat16>(p, a.head_size, stream, false)
-                                             : launch_cascade_prefix_t<__half>(p, a.head_size, stream, false);
+  // the prefix: the tcgen05 kernel where the cache suits it, else the mma.sync one
+  cudaError_t e = launch_cascade_prefix_umma(p, a, stream);
+  if (e == cudaErrorNotSupported)
+    e = a.q_type == ElemType::BF16 ? launch_cascade_prefix_t<__nv_bfloat16>(p, a.head_size, stream, false)
+                                   : launch_cascade_prefix_t<__half>(p, a.head_size, stream, false);
   if (e != cudaSuccess) return e;
   if (tail) {
     p.part_offset = p.prefix_parts;

@@ -120,6 +120,15 @@ struct PrefillArgs {
   ElemType q_type;   // float16 / bfloat16 (the caches' type too)
   int head_size;     // 64 or 128
   bool token_major;  // [nb, bs, H, D] / [slots, H, D] caches; else the paged layout
+  // Shared-prefix decode through the prefill kernel (the cascade form): rows
+  // are (sequence, head) pairs of q [num_seqs][H][D], the keys are prefix chunk
+  // blockIdx.y of sequence 0's table, and the results are split-K partials.
+  const uint32_t* context_lens;
+  int max_seq_len, prefix_len, prefix_part_size;
+  float* part_max;
+  float* part_sum;
+  float* part_out;
+  int64_t part_seq_stride, part_head_stride, part_out_seq_stride, part_out_head_stride, part_out_part_stride;
 };
 
 struct ReshapeArgs {

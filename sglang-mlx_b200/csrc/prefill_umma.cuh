@@ -144,7 +144,9 @@ struct UmmaGeom {
 // GK: K reaches shared memory as [D/8 chunks][128 tokens][8] through 4-row
 // gathers (a dense K cache, block size 32), so S is one N = 128 product per
 // k-step; else each K page is one bulk copy and S one N = BS chain per page.
-template <typename T, int D, int BS, bool GK>
+// CASCADE: the shared-prefix decode form (rows = (sequence, head) pairs, keys =
+// prefix chunk blockIdx.y, split-K partials out); else prefill / extend.
+template <typename T, int D, int BS, bool GK, bool CASCADE = false>
 __global__ void __launch_bounds__(kUmmaThreads, 1)
     prefill_umma_kernel(const PrefillArgs p, const __grid_constant__ TmaMaps maps) {
   using namespace mma_detail;
@@ -174,24 +176,38 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   const CUtensorMap* vmap = &maps.v;
   const CUtensorMap* kmap = &maps.k;
   static_assert(!GK || (BS == 32 && PAGES == 4), "the gathered K layout takes four 32-token pages");
-  const int64_t q0 = p.qo_indptr[seq];
-  const int64_t q1 = p.qo_indptr[seq + 1];
-  const int64_t kvl = p.kv_lens[seq];
-  const int64_t ql = q1 - q0;
-  const int64_t rows = ql * G;
+  // Prefill: this CTA's rows are (new token t, head g) of sequence `seq`, keys
+  // [kv_beg, kv_end) of its table.  Cascade: rows are (sequence, head) pairs
+  // of every sequence, keys prefix chunk `seq` (= blockIdx.y) of sequence 0's
+  // table.
+  int64_t q0 = 0, rows = 0;
+  int prefix = 0, kv_beg = 0, kv_end = 0;
+  bool bad = false;
   const int64_t R0 = (int64_t)(gridDim.x - 1 - blockIdx.x) * kUmmaRows;  // last tiles first
-  if (ql <= 0 || R0 >= rows) return;
-  const bool bad = q1 > p.num_tokens || ql > p.max_q_len || kvl < ql ||
-                   kvl > p.table_len * (int64_t)p.block_size || kvl > 0x7fffffffll - 256;
-  if (bad && threadIdx.x == 0 && blockIdx.x == gridDim.x - 1 && kvh == 0)
-    set_status(&g_decode_status, KVC_STATUS_INDEX_OOB);
-  if (q1 > p.num_tokens) return;
-  const int prefix = bad ? 0 : (int)(kvl - ql);
-  const int64_t R_last = (R0 + kUmmaRows < rows ? R0 + kUmmaRows : rows) - 1;
-  const int t_first = (int)(R0 / G), t_last = (int)(R_last / G);
-  const int kv_end = bad ? 0 : prefix + t_last + 1;
-  int kv_beg = p.window > 0 ? prefix + t_first + 1 - p.window : 0;
-  kv_beg = kv_beg > 0 ? kv_beg / KT * KT : 0;
+  if constexpr (CASCADE) {
+    rows = (int64_t)p.num_seqs * G;
+    if (R0 >= rows) return;
+    kv_beg = seq * p.prefix_part_size;
+    kv_end = kv_beg + p.prefix_part_size < p.prefix_len ? kv_beg + p.prefix_part_size : p.prefix_len;
+  } else {
+    q0 = p.qo_indptr[seq];
+    const int64_t q1 = p.qo_indptr[seq + 1];
+    const int64_t kvl = p.kv_lens[seq];
+    const int64_t ql = q1 - q0;
+    rows = ql * G;
+    if (ql <= 0 || R0 >= rows) return;
+    bad = q1 > p.num_tokens || ql > p.max_q_len || kvl < ql || kvl > p.table_len * (int64_t)p.block_size ||
+          kvl > 0x7fffffffll - 256;
+    if (bad && threadIdx.x == 0 && blockIdx.x == gridDim.x - 1 && kvh == 0)
+      set_status(&g_decode_status, KVC_STATUS_INDEX_OOB);
+    if (q1 > p.num_tokens) return;
+    prefix = bad ? 0 : (int)(kvl - ql);
+    const int64_t R_last = (R0 + kUmmaRows < rows ? R0 + kUmmaRows : rows) - 1;
+    const int t_first = (int)(R0 / G), t_last = (int)(R_last / G);
+    kv_end = bad ? 0 : prefix + t_last + 1;
+    kv_beg = p.window > 0 ? prefix + t_first + 1 - p.window : 0;
+    kv_beg = kv_beg > 0 ? kv_beg / KT * KT : 0;
+  }
   const int ntiles = kv_end > kv_beg ? (kv_end - kv_beg + KT - 1) / KT : 0;
 
   if (threadIdx.x == 0) {
@@ -232,7 +248,20 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   if (warp == kProducerWarp) {
     // ---- producer: 128-token tiles of whole pages
     const T* kbase = reinterpret_cast<const T*>(p.k_cache) + (int64_t)kvh * p.k_head_stride;
-    const uint32_t* table = p.block_tables + (int64_t)seq * p.table_stride;
+    const uint32_t* table = p.block_tables + (CASCADE ? (int64_t)0 : (int64_t)seq * p.table_stride);
+    if (CASCADE && kvh == 0) {
+      // every sequence of this tile must carry sequence 0's block ids over the
+      // chunk (the caller's promise; checked once per tile and chunk)
+      const int64_t R_last = (R0 + kUmmaRows < rows ? R0 + kUmmaRows : rows) - 1;
+      const int s0 = (int)(R0 / G), nseq = (int)(R_last / G) - s0 + 1;
+      const int b0 = kv_beg / BS, nb = (kv_end + BS - 1) / BS - b0;
+      bool diff = false;
+      for (int i = lane; i < nseq * nb; i += 32) {
+        const int sq = s0 + i / nb, bb = b0 + i % nb;
+        diff |= __ldg(p.block_tables + (int64_t)sq * p.table_stride + bb) != __ldg(p.block_tables + bb);
+      }
+      if (diff) set_status(&g_decode_status, KVC_STATUS_PREFIX_MISMATCH);
+    }
     auto load_id = [&](int j) -> uint32_t {
       uint32_t id = 0xffffffffu;
       const int tok = kv_beg + j * KT + lane * BS;
@@ -371,14 +400,32 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     // (TMEM lanes); `half` 0 takes tokens 0..63 of every tile and O columns
     // 0 .. D/2 - 1, half 1 the rest.  The halves exchange row maxima (and at
     // the end row sums) through shared memory on the `xchg` barrier.
+    // The warps' TMEM loads and stores are warp-collective: every decision
+    // ahead of one (a wait's outcome, the abort flag) is made for the whole warp.
+    auto uwait = [&](uint64_t* bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, umma::wait(bar, parity));
+    };
+    auto uabort = [&]() -> bool { return __any_sync(0xffffffffu, abort_now()); };
     const int half = warp >> 2;
     const int r = threadIdx.x & 127;
     const int64_t R = R0 + r;
-    const bool in_tile = R < rows;      // a row of the sequence (else padding of the last tile)
-    const bool on = in_tile && !bad;    // a row that sees keys
+    const bool in_tile = R < rows;      // a row (else padding of the last tile)
+    // t: the new token (prefill) or the sequence (cascade) of the row
     const int t = in_tile ? (int)(R / G) : 0, g = in_tile ? (int)(R - (int64_t)t * G) : 0;
-    const int end_r = on ? prefix + t + 1 : 0;
-    const int beg_r = p.window > 0 ? end_r - p.window : 0;
+    bool on;  // a row that sees keys
+    int end_r, beg_r;
+    if constexpr (CASCADE) {
+      // the row's sequence sees the chunk up to its own length; lengths the
+      // reference zeroes (0 or past max_seq_len) see nothing
+      const uint32_t ctx = in_tile ? __ldg(p.context_lens + t) : 0u;
+      on = in_tile && ctx != 0 && ctx <= (uint32_t)p.max_seq_len;
+      end_r = on ? ((int)ctx < kv_end ? (int)ctx : kv_end) : 0;
+      beg_r = 0;
+    } else {
+      on = in_tile && !bad;
+      end_r = on ? prefix + t + 1 : 0;
+      beg_r = p.window > 0 ? end_r - p.window : 0;
+    }
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     constexpr int HK = KT / 2;   // tokens of a tile per half
     constexpr int HD = D / 2;    // O columns per half
@@ -411,7 +458,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       buf[half * 128 + r] = mine;
       __syncwarp();
       if (lane == 0) mbar_arrive(xchg);
-      const bool got = umma::wait(xchg, xphase & 1u);
+      const bool got = uwait(xchg, xphase & 1u);
       ++xphase;
       if (!got) {
         ok = false;
@@ -421,7 +468,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     };
     for (int j = 0; j < ntiles; ++j) {
       const int b = j & 1, st = j % KST;
-      if (abort_now() || !umma::wait(&s_full[b], (uint32_t)((j >> 1) & 1))) {
+      if (uabort() || !uwait(&s_full[b], (uint32_t)((j >> 1) & 1))) {
         ok = false;
         break;
       }
@@ -429,7 +476,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       // (the stage's barrier orders the producer's page mask and the TMA-written
       // V before this thread reads or clears them; its phase cannot move on
       // before this tile's P is handed over)
-      if (!umma::wait(&kv_full[st], (uint32_t)((j / KST) & 1))) {
+      if (!uwait(&kv_full[st], (uint32_t)((j / KST) & 1))) {
         ok = false;
         break;
       }
@@ -494,7 +541,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       l = l * alpha + ps;  // this half's share of the row sum
       // O and the P buffer are free once P.V of the previous tile is done
       if (j >= 1) {
-        if (!umma::wait(pv_done, (uint32_t)((j - 1) & 1))) {
+        if (!uwait(pv_done, (uint32_t)((j - 1) & 1))) {
           ok = false;
           break;
         }
@@ -558,13 +605,41 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     if (!ok && lane == 0) give_up();
     bool have = ok && ntiles > 0;
     if (have) {
-      have = umma::wait(pv_done, (uint32_t)((ntiles - 1) & 1));
+      have = uwait(pv_done, (uint32_t)((ntiles - 1) & 1));
       if (!have && lane == 0) give_up();
       umma::fence_after();
     }
     // both halves must take the last exchange (or time out on it) alike
     const float l_all = l + exchange(l);
     have = have && ok;
+    if constexpr (CASCADE) {
+      // ---- partials of partition `seq` (the chunk): natural-log max, sum,
+      // unnormalised O (0 for a row without keys, whose max is -inf)
+      const bool keep = have && l_all > 0.f;
+      const int head = kvh * G + g;
+      float* po = p.part_out + (int64_t)t * p.part_out_seq_stride + (int64_t)head * p.part_out_head_stride +
+                  (int64_t)seq * p.part_out_part_stride + half * HD;
+#pragma unroll
+      for (int c = 0; c < HD; c += 32) {
+        uint32_t v[32];
+        // (tcgen05.ld is warp-collective: every lane loads, only rows store)
+        umma::ld32(lane_base + UG::OCOL + half * HD + c, v);
+        umma::wait_ld();
+        if (in_tile) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(po + c + i) =
+                keep ? make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]), __uint_as_float(v[i + 2]),
+                                   __uint_as_float(v[i + 3]))
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      if (in_tile && half == 0) {
+        const int64_t o = (int64_t)t * p.part_seq_stride + (int64_t)head * p.part_head_stride + seq;
+        p.part_max[o] = keep ? m_ref * kLn2 : -INFINITY;
+        p.part_sum[o] = keep ? l_all : 0.f;
+      }
+    } else {
     // ---- epilogue: O / l (a row with no visible key, or after an abort, is 0)
     const bool nonzero = have && l_all > 0.f;  // else explicit zeros (this CTA may never have written O)
     const float inv = nonzero ? 1.f / l_all : 0.f;
@@ -584,6 +659,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         for (int i = 0; i < 16; i += 4)
           *reinterpret_cast<uint4*>(orow + c + 2 * i) = make_uint4(packed[i], packed[i + 1], packed[i + 2], packed[i + 3]);
       }
+    }
     }
   }
 
@@ -686,6 +762,117 @@ static cudaError_t launch_prefill_umma_any(const PrefillArgs& a, cudaStream_t st
   }
   return bf ? launch_prefill_umma<__nv_bfloat16, 64, 16, false>(a, stream)
             : launch_prefill_umma<__half, 64, 16, false>(a, stream);
+}
+
+// ---- shared-prefix (cascade) decode through the tcgen05 kernel ----
+template <typename T, int D, int BS, bool GK>
+static cudaError_t launch_cascade_umma(const PrefillArgs& a, int prefix_parts, cudaStream_t stream) {
+  using UG = UmmaGeom<D, BS>;
+  DecodeParams dp;
+  memset(&dp, 0, sizeof(dp));
+  dp.k_cache = a.k_cache;
+  dp.v_cache = a.v_cache;
+  dp.num_blocks = a.num_blocks;
+  dp.num_kv_heads = a.num_kv_heads;
+  dp.k_head_stride = a.k_head_stride;
+  dp.k_block_stride = a.k_block_stride;
+  dp.v_head_stride = a.v_head_stride;
+  dp.v_block_stride = a.v_block_stride;
+  TmaMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  if (!make_tensor_maps(dp, std::is_same<T, __nv_bfloat16>::value ? ElemType::BF16 : ElemType::F16, D, BS, BS, BS * 2,
+                        kTiles, &maps))
+    return cudaErrorNotSupported;
+  if (GK && !make_k_gather_map(a, D, BS, &maps.k)) return cudaErrorNotSupported;
+  auto kern = prefill_umma_kernel<T, D, BS, GK, true>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, UG::SMEM);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  const int G = a.num_heads / a.num_kv_heads;
+  const int64_t tiles = ((int64_t)a.num_seqs * G + kUmmaRows - 1) / kUmmaRows;
+  kern<<<dim3((unsigned)tiles, (unsigned)prefix_parts, (unsigned)a.num_kv_heads), kUmmaThreads, UG::SMEM, stream>>>(a,
+                                                                                                                  maps);
+  count_launch();
+  return cudaGetLastError();
+}
+
+// The prefix of a shared-prefix decode on the tensor cores' own pipeline when
+// the cache suits the gathered-K tcgen05 kernel (dense paged layout, block size
+// 32, head size 64 / 128, partial buffers of 16-byte rows);
+// cudaErrorNotSupported otherwise (the caller then runs the mma.sync prefix
+// kernel).
+static cudaError_t launch_cascade_prefix_umma(const DecodeParams& p, const DecodeArgs& da, cudaStream_t stream) {
+  const int D = da.head_size, BS = da.block_size;
+  // Only the gathered-K form (block size 32, dense K): with per-page S chains
+  // (N = 16 for block size 16, 64 products per tile) the single-lane product
+  // issue sets the pace and config 4 measured 69.0 us against 65.9 us for the
+  // mma.sync prefix kernel.
+  if (BS != 32 || !(D == 64 || D == 128)) return cudaErrorNotSupported;
+  if (!(p.k_head_stride == (int64_t)D * BS && p.k_block_stride == (int64_t)p.num_kv_heads * D * BS))
+    return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(p.part_out) & 15u) || (p.part_out_seq_stride & 3) || (p.part_out_head_stride & 3) ||
+      (p.part_out_part_stride & 3) || (p.prefix_len % BS) || (p.prefix_part_size % BS))
+    return cudaErrorNotSupported;
+  const char* v = getenv("KVC_PREFILL_KERNEL");
+  if (v && (v[0] == 'm' || v[0] == 'M')) return cudaErrorNotSupported;
+  PrefillArgs a;
+  memset(&a, 0, sizeof(a));
+  a.q = p.q;
+  a.k_cache = p.k_cache;
+  a.v_cache = p.v_cache;
+  a.block_tables = p.block_tables;
+  a.num_seqs = p.num_seqs;
+  a.num_heads = p.num_heads;
+  a.num_kv_heads = p.num_kv_heads;
+  a.block_size = BS;
+  a.num_blocks = p.num_blocks;
+  a.table_stride = p.table_stride;
+  a.q_tok_stride = p.q_seq_stride;
+  a.q_head_stride = p.q_head_stride;
+  a.k_block_stride = p.k_block_stride;
+  a.k_head_stride = p.k_head_stride;
+  a.v_block_stride = p.v_block_stride;
+  a.v_head_stride = p.v_head_stride;
+  a.scale = p.scale;
+  a.q_type = da.q_type;
+  a.head_size = D;
+  a.context_lens = p.context_lens;
+  a.max_seq_len = p.max_seq_len;
+  a.prefix_len = p.prefix_len;
+  a.prefix_part_size = p.prefix_part_size;
+  a.part_max = p.part_max;
+  a.part_sum = p.part_sum;
+  a.part_out = p.part_out;
+  a.part_seq_stride = p.part_seq_stride;
+  a.part_head_stride = p.part_head_stride;
+  a.part_out_seq_stride = p.part_out_seq_stride;
+  a.part_out_head_stride = p.part_out_head_stride;
+  a.part_out_part_stride = p.part_out_part_stride;
+  const bool bf = a.q_type == ElemType::BF16;
+  const bool dense = a.k_head_stride == (int64_t)D * BS && a.k_block_stride == (int64_t)a.num_kv_heads * D * BS &&
+                     a.num_blocks * a.num_kv_heads * (D / 8) < 0x7fffffffll;
+  const int parts = p.prefix_parts;
+  if (D == 128) {
+    if (BS == 32)
+      return dense ? (bf ? launch_cascade_umma<__nv_bfloat16, 128, 32, true>(a, parts, stream)
+                         : launch_cascade_umma<__half, 128, 32, true>(a, parts, stream))
+                   : (bf ? launch_cascade_umma<__nv_bfloat16, 128, 32, false>(a, parts, stream)
+                         : launch_cascade_umma<__half, 128, 32, false>(a, parts, stream));
+    return bf ? launch_cascade_umma<__nv_bfloat16, 128, 16, false>(a, parts, stream)
+              : launch_cascade_umma<__half, 128, 16, false>(a, parts, stream);
+  }
+  if (BS == 32)
+    return dense ? (bf ? launch_cascade_umma<__nv_bfloat16, 64, 32, true>(a, parts, stream)
+                       : launch_cascade_umma<__half, 64, 32, true>(a, parts, stream))
+                 : (bf ? launch_cascade_umma<__nv_bfloat16, 64, 32, false>(a, parts, stream)
+                       : launch_cascade_umma<__half, 64, 32, false>(a, parts, stream));
+  return bf ? launch_cascade_umma<__nv_bfloat16, 64, 16, false>(a, parts, stream)
+            : launch_cascade_umma<__half, 64, 16, false>(a, parts, stream);
 }
 
 cudaError_t launch_paged_prefill(const PrefillArgs& a, cudaStream_t stream) {
