@@ -142,8 +142,9 @@ struct UmmaGeom {
 };
 
 // GK: K reaches shared memory as [D/8 chunks][128 tokens][8] through 4-row
-// gathers (a dense K cache, block size 32), so S is one N = 128 product per
-// k-step; else each K page is one bulk copy and S one N = BS chain per page.
+// gathers (a dense K cache; one gather per chunk and four pages), so S is one
+// N = 128 product per k-step; else each K page is one bulk copy and S one
+// N = BS chain per page.
 // CASCADE: the shared-prefix decode form (rows = (sequence, head) pairs, keys =
 // prefix chunk blockIdx.y, split-K partials out); else prefill / extend.
 template <typename T, int D, int BS, bool GK, bool CASCADE = false>
@@ -175,7 +176,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   const int G = p.num_heads / p.num_kv_heads;
   const CUtensorMap* vmap = &maps.v;
   const CUtensorMap* kmap = &maps.k;
-  static_assert(!GK || (BS == 32 && PAGES == 4), "the gathered K layout takes four 32-token pages");
+  static_assert(!GK || PAGES % 4 == 0, "the gathered K layout takes pages in fours");
   // Prefill: this CTA's rows are (new token t, head g) of sequence `seq`, keys
   // [kv_beg, kv_end) of its table.  Cascade: rows are (sequence, head) pairs
   // of every sequence, keys prefix chunk `seq` (= blockIdx.y) of sequence 0's
@@ -305,7 +306,10 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
               rb[i] = (int)(((int64_t)((mask >> i) & 1u ? ids[i] : any) * p.num_kv_heads + kvh) * (D / 8));
 #pragma unroll
             for (int c = 0; c < D / 8; ++c)
-              umma::tma_gather4(kst + c * KT * 16, kmap, 0, rb[0] + c, rb[1] + c, rb[2] + c, rb[3] + c, &kv_full[st]);
+#pragma unroll
+              for (int q = 0; q < PAGES; q += 4)  // pages q .. q + 3: tokens q*BS .. of the chunk row
+                umma::tma_gather4(kst + c * KT * 16 + q * BS * 16, kmap, 0, rb[q] + c, rb[q + 1] + c, rb[q + 2] + c,
+                                  rb[q + 3] + c, &kv_full[st]);
           } else {
             mbar_arrive_expect_tx(&kv_full[st], (uint32_t)__popc(mask) * 2u * (uint32_t)PAGE);
           }
@@ -525,17 +529,37 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       }
       const float neg_ref = m_ref == -INFINITY ? 0.f : -m_ref;
       float ps = 0.f;
+      // P pairs packed as soon as they are exponentiated (the integer / FMA
+      // work of the packing overlaps the special-function unit's exponentials):
+      // hi = the upper 16 bits of each fp32 (a bf16, truncated), lo = the exact
+      // remainder rounded to bf16, so hi + lo carries ~16 bits of P; f16 P is
+      // one rounding.  Pairs of tokens 64h + 2i, + 1 go to hi column 32h + i.
+      uint32_t hi[32], lo[32];
+      auto pack_pair = [&](int i, float p0, float p1) {
+        if constexpr (SPLIT) {
+          const uint32_t u0 = __float_as_uint(p0), u1 = __float_as_uint(p1);
+          hi[i] = __byte_perm(u0, u1, 0x7632);
+          lo[i] = MmaOp<T>::pack(p0 - __uint_as_float(u0 & 0xFFFF0000u), p1 - __uint_as_float(u1 & 0xFFFF0000u));
+        } else {
+          hi[i] = MmaOp<T>::pack(p0, p1);
+          lo[i] = 0u;
+        }
+      };
       if (whole) {
 #pragma unroll
-        for (int c = 0; c < HK; ++c) {
-          x[c] = fast_exp2(fmaf(x[c], qk_scale, neg_ref));
-          ps += x[c];
+        for (int i = 0; i < HK / 2; ++i) {
+          const float p0 = fast_exp2(fmaf(x[2 * i], qk_scale, neg_ref));
+          const float p1 = fast_exp2(fmaf(x[2 * i + 1], qk_scale, neg_ref));
+          ps += p0 + p1;
+          pack_pair(i, p0, p1);
         }
       } else {
 #pragma unroll
-        for (int c = 0; c < HK; ++c) {
-          x[c] = fast_exp2(x[c] + neg_ref);  // masked: exp2(-inf) = 0
-          ps += x[c];
+        for (int i = 0; i < HK / 2; ++i) {
+          const float p0 = fast_exp2(x[2 * i] + neg_ref);  // masked: exp2(-inf) = 0
+          const float p1 = fast_exp2(x[2 * i + 1] + neg_ref);
+          ps += p0 + p1;
+          pack_pair(i, p0, p1);
         }
       }
       l = l * alpha + ps;  // this half's share of the row sum
@@ -578,25 +602,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       }
       // P over the S buffer: hi pairs of tokens 64h .. 64h + 63 in columns
       // 32h .. 32h + 31, lo pairs 64 columns further
-      {
-        uint32_t hi[32], lo[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if constexpr (SPLIT) {
-            // hi = the upper 16 bits of each fp32 (a bf16, truncated), lo =
-            // the exact remainder rounded to bf16: hi + lo carries ~16 bits of P
-            const uint32_t u0 = __float_as_uint(x[2 * i]), u1 = __float_as_uint(x[2 * i + 1]);
-            hi[i] = __byte_perm(u0, u1, 0x7632);
-            lo[i] = MmaOp<T>::pack(x[2 * i] - __uint_as_float(u0 & 0xFFFF0000u),
-                                   x[2 * i + 1] - __uint_as_float(u1 & 0xFFFF0000u));
-          } else {
-            hi[i] = MmaOp<T>::pack(x[2 * i], x[2 * i + 1]);
-            lo[i] = 0u;
-          }
-        }
-        umma::st32(lane_base + UG::SCOL + b * 128 + half * 32, hi);
-        if constexpr (SPLIT) umma::st32(lane_base + UG::SCOL + b * 128 + 64 + half * 32, lo);
-      }
+      umma::st32(lane_base + UG::SCOL + b * 128 + half * 32, hi);
+      if constexpr (SPLIT) umma::st32(lane_base + UG::SCOL + b * 128 + 64 + half * 32, lo);
       umma::wait_st();
       umma::fence_before();
       __syncwarp();
@@ -750,6 +757,9 @@ static cudaError_t launch_prefill_umma_any(const PrefillArgs& a, cudaStream_t st
       return bf ? launch_prefill_umma<__nv_bfloat16, 128, 32, false>(a, stream)
                 : launch_prefill_umma<__half, 128, 32, false>(a, stream);
     }
+    if (dense)
+      return bf ? launch_prefill_umma<__nv_bfloat16, 128, 16, true>(a, stream)
+                : launch_prefill_umma<__half, 128, 16, true>(a, stream);
     return bf ? launch_prefill_umma<__nv_bfloat16, 128, 16, false>(a, stream)
               : launch_prefill_umma<__half, 128, 16, false>(a, stream);
   }
@@ -760,6 +770,9 @@ static cudaError_t launch_prefill_umma_any(const PrefillArgs& a, cudaStream_t st
     return bf ? launch_prefill_umma<__nv_bfloat16, 64, 32, false>(a, stream)
               : launch_prefill_umma<__half, 64, 32, false>(a, stream);
   }
+  if (dense)
+    return bf ? launch_prefill_umma<__nv_bfloat16, 64, 16, true>(a, stream)
+              : launch_prefill_umma<__half, 64, 16, true>(a, stream);
   return bf ? launch_prefill_umma<__nv_bfloat16, 64, 16, false>(a, stream)
             : launch_prefill_umma<__half, 64, 16, false>(a, stream);
 }
@@ -808,11 +821,11 @@ static cudaError_t launch_cascade_umma(const PrefillArgs& a, int prefix_parts, c
 // kernel).
 static cudaError_t launch_cascade_prefix_umma(const DecodeParams& p, const DecodeArgs& da, cudaStream_t stream) {
   const int D = da.head_size, BS = da.block_size;
-  // Only the gathered-K form (block size 32, dense K): with per-page S chains
-  // (N = 16 for block size 16, 64 products per tile) the single-lane product
-  // issue sets the pace and config 4 measured 69.0 us against 65.9 us for the
-  // mma.sync prefix kernel.
-  if (BS != 32 || !(D == 64 || D == 128)) return cudaErrorNotSupported;
+  // Only the gathered-K form (dense K): with per-page S chains (N = 16 for
+  // block size 16, 64 products per tile) the single-lane product issue set the
+  // pace and config 4 measured 69.0 us against 65.9 us for the mma.sync prefix
+  // kernel.
+  if (!(BS == 16 || BS == 32) || !(D == 64 || D == 128)) return cudaErrorNotSupported;
   if (!(p.k_head_stride == (int64_t)D * BS && p.k_block_stride == (int64_t)p.num_kv_heads * D * BS))
     return cudaErrorNotSupported;
   if ((reinterpret_cast<uintptr_t>(p.part_out) & 15u) || (p.part_out_seq_stride & 3) || (p.part_out_head_stride & 3) ||
@@ -857,22 +870,16 @@ static cudaError_t launch_cascade_prefix_umma(const DecodeParams& p, const Decod
   const bool dense = a.k_head_stride == (int64_t)D * BS && a.k_block_stride == (int64_t)a.num_kv_heads * D * BS &&
                      a.num_blocks * a.num_kv_heads * (D / 8) < 0x7fffffffll;
   const int parts = p.prefix_parts;
-  if (D == 128) {
-    if (BS == 32)
-      return dense ? (bf ? launch_cascade_umma<__nv_bfloat16, 128, 32, true>(a, parts, stream)
-                         : launch_cascade_umma<__half, 128, 32, true>(a, parts, stream))
-                   : (bf ? launch_cascade_umma<__nv_bfloat16, 128, 32, false>(a, parts, stream)
-                         : launch_cascade_umma<__half, 128, 32, false>(a, parts, stream));
-    return bf ? launch_cascade_umma<__nv_bfloat16, 128, 16, false>(a, parts, stream)
-              : launch_cascade_umma<__half, 128, 16, false>(a, parts, stream);
-  }
-  if (BS == 32)
-    return dense ? (bf ? launch_cascade_umma<__nv_bfloat16, 64, 32, true>(a, parts, stream)
-                       : launch_cascade_umma<__half, 64, 32, true>(a, parts, stream))
-                 : (bf ? launch_cascade_umma<__nv_bfloat16, 64, 32, false>(a, parts, stream)
-                       : launch_cascade_umma<__half, 64, 32, false>(a, parts, stream));
-  return bf ? launch_cascade_umma<__nv_bfloat16, 64, 16, false>(a, parts, stream)
-            : launch_cascade_umma<__half, 64, 16, false>(a, parts, stream);
+  if (!dense) return cudaErrorNotSupported;
+  if (D == 128)
+    return BS == 32 ? (bf ? launch_cascade_umma<__nv_bfloat16, 128, 32, true>(a, parts, stream)
+                          : launch_cascade_umma<__half, 128, 32, true>(a, parts, stream))
+                    : (bf ? launch_cascade_umma<__nv_bfloat16, 128, 16, true>(a, parts, stream)
+                          : launch_cascade_umma<__half, 128, 16, true>(a, parts, stream));
+  return BS == 32 ? (bf ? launch_cascade_umma<__nv_bfloat16, 64, 32, true>(a, parts, stream)
+                        : launch_cascade_umma<__half, 64, 32, true>(a, parts, stream))
+                  : (bf ? launch_cascade_umma<__nv_bfloat16, 64, 16, true>(a, parts, stream)
+                        : launch_cascade_umma<__half, 64, 16, true>(a, parts, stream));
 }
 
 cudaError_t launch_paged_prefill(const PrefillArgs& a, cudaStream_t stream) {

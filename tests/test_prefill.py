@@ -179,3 +179,20 @@ def test_pooled_cache_prefill_equals_gather_path(gpu, window):
         r = np.stack([kv_oracle.sdpa_masked(q[0, h], kf[h // 4], vf[h // 4], 128 ** -0.5, mask) for h in range(16)])
         assert_close(out.to_numpy()[0], r, ATOL_NS, RTOL_NS, f"chunk of {n} on {len(prefix)}")
         prefix = prefix + list(new)
+
+
+def test_non_dense_key_cache_pages(gpu):
+    """A key cache that is a view with a wider block stride (every page still
+    dense) takes the per-page path of the tcgen05 kernel (no row gathers)."""
+    c = prefill_case(7000, "bfloat16", 16, 4, 128, "paged", 32, [300, 0], [200, 77])
+    kc = c["kcd"].to_numpy()
+    nb, H = kc.shape[0], kc.shape[1]
+    wide = np.zeros((nb, H + 1) + kc.shape[2:], np.float32)
+    wide[:, :H] = kc
+    wd = DeviceArray.from_numpy(wide, dtype="bfloat16")
+    view = wd[:, :H]
+    out = mk.paged_prefill_attention(c["qd"], view, c["vcd"], DeviceArray.from_numpy(c["tables"]), c["indptr"],
+                                     DeviceArray.from_numpy(c["kvl"]), 4, c["scale"], 32).to_numpy()
+    assert_close(out, ref(c), ATOL_NS, RTOL_NS, "non-dense K")
+    assert gpu.get_status(clear=True) == 0
+
