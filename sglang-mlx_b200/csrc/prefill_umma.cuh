@@ -177,6 +177,9 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   const CUtensorMap* vmap = &maps.v;
   const CUtensorMap* kmap = &maps.k;
   static_assert(!GK || PAGES % 4 == 0, "the gathered K layout takes pages in fours");
+  // the shared-prefix form's tail partitions (a programmatic dependent that
+  // waits for this grid before exiting) may start beside it
+  grid_dependents_launch();
   // Prefill: this CTA's rows are (new token t, head g) of sequence `seq`, keys
   // [kv_beg, kv_end) of its table.  Cascade: rows are (sequence, head) pairs
   // of every sequence, keys prefix chunk `seq` (= blockIdx.y) of sequence 0's
