@@ -213,6 +213,17 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     kv_beg = kv_beg > 0 ? kv_beg / KT * KT : 0;
   }
   const int ntiles = kv_end > kv_beg ? (kv_end - kv_beg + KT - 1) / KT : 0;
+  // The producer starts its first block-id loads and the tensor-map descriptor
+  // fetches before the set-up below, so their latency overlaps it.
+  uint32_t first_id = 0xffffffffu;
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.v)) : "memory");
+      if (GK) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.k)) : "memory");
+    }
+    const uint32_t* t0row = p.block_tables + (CASCADE ? (int64_t)0 : (int64_t)seq * p.table_stride);
+    if (lane < PAGES && ntiles > 0 && kv_beg + lane * BS < kv_end) first_id = __ldg(t0row + (kv_beg + lane * BS) / BS);
+  }
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -230,9 +241,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     mbar_init(all_done, 1);
     mbar_fence_init();
   }
-  // stale ring contents are read as V of masked tokens (P = 0): start from zeros
-  for (int i = threadIdx.x; i < UG::RING / 16; i += kUmmaThreads)
-    reinterpret_cast<uint4*>(ring)[i] = make_uint4(0u, 0u, 0u, 0u);
+  // Stale V of pages a tile does not load meets P = 0 (0 * NaN = NaN): the V
+  // halves of the ring start from zeros.  (K of unloaded pages is only ever
+  // masked, or replaced by a loaded page's rows in the gathered form.)
+  constexpr int V16 = PAGES * PAGE / 16;  // 16-byte words of one stage's V pages
+  for (int i = threadIdx.x; i < KST * V16; i += kUmmaThreads)
+    reinterpret_cast<uint4*>(ring + (size_t)(i / V16) * UG::STAGE + PAGES * PAGE)[i % V16] = make_uint4(0u, 0u, 0u, 0u);
   fence_proxy_async();
   if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
@@ -272,7 +286,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       if (lane < PAGES && j < ntiles && tok < kv_end) id = __ldg(table + tok / BS);
       return id;
     };
-    uint32_t id = load_id(0);
+    uint32_t id = first_id;  // = load_id(0), issued before the set-up
     for (int j = 0; j < ntiles; ++j) {
       const int st = j % KST;
       bool ok = true;
