@@ -141,15 +141,84 @@ struct UmmaGeom {
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
+// Work item (the persistent grid walks them): a 128-row tile of one sequence
+// (prefill) or of all sequences (cascade), one key range, one KV head.
+// CTA c starts with item c; after that each CTA claims the next unclaimed item
+// from a device counter, so a CTA that drew short items takes more of them.
+// A launch uses one of kUmmaSchedSlots counter pairs (the host rotates them,
+// so launches in flight together on different streams use different pairs);
+// the last CTA of the launch to finish returns its pair to zero.
+struct UmmaSched {
+  unsigned next, done;
+};
+constexpr int kUmmaSchedSlots = 64;
+__device__ UmmaSched g_umma_sched[kUmmaSchedSlots];
+
+struct UmmaItem {
+  int64_t q0, rows, R0;
+  int y, kvh, prefix, kv_beg, kv_end, ntiles;
+  bool bad, skip, first_tile;
+};
+
+template <bool CASCADE>
+__device__ __forceinline__ UmmaItem umma_item(const PrefillArgs& p, int idx, int tiles_x, int ny) {
+  constexpr int KT = kUmmaTile;
+  UmmaItem it;
+  const int xi = idx % tiles_x;
+  it.y = (idx / tiles_x) % ny;
+  it.kvh = idx / (tiles_x * ny);
+  it.R0 = (int64_t)(tiles_x - 1 - xi) * kUmmaRows;  // within a sequence, the last (longest) tiles first
+  it.first_tile = xi == tiles_x - 1;
+  it.q0 = 0;
+  it.rows = 0;
+  it.prefix = 0;
+  it.kv_beg = 0;
+  it.kv_end = 0;
+  it.bad = false;
+  it.skip = true;
+  const int G = p.num_heads / p.num_kv_heads;
+  if constexpr (CASCADE) {
+    it.rows = (int64_t)p.num_seqs * G;
+    if (it.R0 >= it.rows) return it;
+    it.kv_beg = it.y * p.prefix_part_size;
+    it.kv_end = it.kv_beg + p.prefix_part_size < p.prefix_len ? it.kv_beg + p.prefix_part_size : p.prefix_len;
+  } else {
+    it.q0 = p.qo_indptr[it.y];
+    const int64_t q1 = p.qo_indptr[it.y + 1];
+    const int64_t kvl = p.kv_lens[it.y];
+    const int64_t ql = q1 - it.q0;
+    it.rows = ql * G;
+    if (ql <= 0 || it.R0 >= it.rows || q1 > p.num_tokens) {
+      // (q1 past num_tokens: no row of it may be written; flagged below)
+      it.bad = q1 > p.num_tokens && ql > 0;
+      return it;
+    }
+    it.bad = ql > p.max_q_len || kvl < ql || kvl > p.table_len * (int64_t)p.block_size || kvl > 0x7fffffffll - 256;
+    it.prefix = it.bad ? 0 : (int)(kvl - ql);
+    const int64_t R_last = (it.R0 + kUmmaRows < it.rows ? it.R0 + kUmmaRows : it.rows) - 1;
+    const int t_first = (int)(it.R0 / G), t_last = (int)(R_last / G);
+    it.kv_end = it.bad ? 0 : it.prefix + t_last + 1;
+    int kb = p.window > 0 ? it.prefix + t_first + 1 - p.window : 0;
+    it.kv_beg = kb > 0 ? kb / KT * KT : 0;
+  }
+  it.ntiles = it.kv_end > it.kv_beg ? (it.kv_end - it.kv_beg + KT - 1) / KT : 0;
+  it.skip = false;
+  return it;
+}
+
 // GK: K reaches shared memory as [D/8 chunks][128 tokens][8] through 4-row
 // gathers (a dense K cache; one gather per chunk and four pages), so S is one
 // N = 128 product per k-step; else each K page is one bulk copy and S one
 // N = BS chain per page.
 // CASCADE: the shared-prefix decode form (rows = (sequence, head) pairs, keys =
-// prefix chunk blockIdx.y, split-K partials out); else prefill / extend.
+// prefix chunk `y`, split-K partials out); else prefill / extend.  The grid is
+// persistent: CTA c takes work item c, then claims further ones (of the
+// tiles_x x ny x num_kv_heads items) until none is left, keeping TMEM, its
+// barriers and its ring across them (every barrier phase below counts this
+// CTA's tiles or items).
 template <typename T, int D, int BS, bool GK, bool CASCADE = false>
 __global__ void __launch_bounds__(kUmmaThreads, 1)
-    prefill_umma_kernel(const PrefillArgs p, const __grid_constant__ TmaMaps maps) {
+    prefill_umma_kernel(const PrefillArgs p, const __grid_constant__ TmaMaps maps, int tiles_x, int ny, int slot) {
   using namespace mma_detail;
   using UG = UmmaGeom<D, BS>;
   constexpr int PAGES = UG::PAGES, PAGE = UG::PAGE, KST = UG::KST, KT = kUmmaTile;
@@ -158,6 +227,11 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ int s_abort;
   __shared__ uint32_t s_tmem;
+  // the items the producer hands the MMA and softmax warps, two deep
+  __shared__ int s_item[2];
+  __shared__ __align__(8) uint64_t item_bars[4];
+  uint64_t* item_full = item_bars;       // the producer published slot i
+  uint64_t* item_empty = item_bars + 2;  // the MMA lane and the 8 softmax warps read slot i
   uint8_t* ring = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + UG::BAR_OFF);
   uint64_t* kv_full = bars;
@@ -172,57 +246,30 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   uint32_t* page_mask = reinterpret_cast<uint32_t*>(smem_raw + UG::MASK_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int seq = blockIdx.y, kvh = blockIdx.z;
   const int G = p.num_heads / p.num_kv_heads;
+  const int n_items = tiles_x * ny * p.num_kv_heads;
   const CUtensorMap* vmap = &maps.v;
   const CUtensorMap* kmap = &maps.k;
   static_assert(!GK || PAGES % 4 == 0, "the gathered K layout takes pages in fours");
   // the shared-prefix form's tail partitions (a programmatic dependent that
   // waits for this grid before exiting) may start beside it
   grid_dependents_launch();
-  // Prefill: this CTA's rows are (new token t, head g) of sequence `seq`, keys
-  // [kv_beg, kv_end) of its table.  Cascade: rows are (sequence, head) pairs
-  // of every sequence, keys prefix chunk `seq` (= blockIdx.y) of sequence 0's
-  // table.
-  int64_t q0 = 0, rows = 0;
-  int prefix = 0, kv_beg = 0, kv_end = 0;
-  bool bad = false;
-  const int64_t R0 = (int64_t)(gridDim.x - 1 - blockIdx.x) * kUmmaRows;  // last tiles first
-  if constexpr (CASCADE) {
-    rows = (int64_t)p.num_seqs * G;
-    if (R0 >= rows) return;
-    kv_beg = seq * p.prefix_part_size;
-    kv_end = kv_beg + p.prefix_part_size < p.prefix_len ? kv_beg + p.prefix_part_size : p.prefix_len;
-  } else {
-    q0 = p.qo_indptr[seq];
-    const int64_t q1 = p.qo_indptr[seq + 1];
-    const int64_t kvl = p.kv_lens[seq];
-    const int64_t ql = q1 - q0;
-    rows = ql * G;
-    if (ql <= 0 || R0 >= rows) return;
-    bad = q1 > p.num_tokens || ql > p.max_q_len || kvl < ql || kvl > p.table_len * (int64_t)p.block_size ||
-          kvl > 0x7fffffffll - 256;
-    if (bad && threadIdx.x == 0 && blockIdx.x == gridDim.x - 1 && kvh == 0)
-      set_status(&g_decode_status, KVC_STATUS_INDEX_OOB);
-    if (q1 > p.num_tokens) return;
-    prefix = bad ? 0 : (int)(kvl - ql);
-    const int64_t R_last = (R0 + kUmmaRows < rows ? R0 + kUmmaRows : rows) - 1;
-    const int t_first = (int)(R0 / G), t_last = (int)(R_last / G);
-    kv_end = bad ? 0 : prefix + t_last + 1;
-    kv_beg = p.window > 0 ? prefix + t_first + 1 - p.window : 0;
-    kv_beg = kv_beg > 0 ? kv_beg / KT * KT : 0;
-  }
-  const int ntiles = kv_end > kv_beg ? (kv_end - kv_beg + KT - 1) / KT : 0;
-  // The producer starts its first block-id loads and the tensor-map descriptor
-  // fetches before the set-up below, so their latency overlaps it.
+  // (fewer items than CTAs: each CTA has its one item and nothing is claimed)
+  const bool dynamic = n_items > (int)gridDim.x;
+  // The producer decodes its first item and starts that item's first block-id
+  // loads and the tensor-map descriptor fetches before the set-up below, so
+  // their latency overlaps it.
+  UmmaItem it0;
   uint32_t first_id = 0xffffffffu;
   if (warp == kProducerWarp) {
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.v)) : "memory");
       if (GK) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.k)) : "memory");
     }
-    const uint32_t* t0row = p.block_tables + (CASCADE ? (int64_t)0 : (int64_t)seq * p.table_stride);
-    if (lane < PAGES && ntiles > 0 && kv_beg + lane * BS < kv_end) first_id = __ldg(t0row + (kv_beg + lane * BS) / BS);
+    it0 = umma_item<CASCADE>(p, blockIdx.x, tiles_x, ny);
+    const uint32_t* t0row = p.block_tables + (CASCADE ? (int64_t)0 : (int64_t)it0.y * p.table_stride);
+    if (!it0.skip && lane < PAGES && it0.ntiles > 0 && it0.kv_beg + lane * BS < it0.kv_end)
+      first_id = __ldg(t0row + (it0.kv_beg + lane * BS) / BS);
   }
 
   if (threadIdx.x == 0) {
@@ -239,6 +286,10 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     mbar_init(q_ready, 8);
     mbar_init(xchg, 8);
     mbar_init(all_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], 9);
+    }
     mbar_fence_init();
   }
   // Stale V of pages a tile does not load meets P = 0 (0 * NaN = NaN): the V
@@ -264,152 +315,224 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   };
 
   if (warp == kProducerWarp) {
-    // ---- producer: 128-token tiles of whole pages
-    const T* kbase = reinterpret_cast<const T*>(p.k_cache) + (int64_t)kvh * p.k_head_stride;
-    const uint32_t* table = p.block_tables + (CASCADE ? (int64_t)0 : (int64_t)seq * p.table_stride);
-    if (CASCADE && kvh == 0) {
-      // every sequence of this tile must carry sequence 0's block ids over the
-      // chunk (the caller's promise; checked once per tile and chunk)
-      const int64_t R_last = (R0 + kUmmaRows < rows ? R0 + kUmmaRows : rows) - 1;
-      const int s0 = (int)(R0 / G), nseq = (int)(R_last / G) - s0 + 1;
-      const int b0 = kv_beg / BS, nb = (kv_end + BS - 1) / BS - b0;
-      bool diff = false;
-      for (int i = lane; i < nseq * nb; i += 32) {
-        const int sq = s0 + i / nb, bb = b0 + i % nb;
-        diff |= __ldg(p.block_tables + (int64_t)sq * p.table_stride + bb) != __ldg(p.block_tables + bb);
-      }
-      if (diff) set_status(&g_decode_status, KVC_STATUS_PREFIX_MISMATCH);
-    }
-    auto load_id = [&](int j) -> uint32_t {
-      uint32_t id = 0xffffffffu;
-      const int tok = kv_beg + j * KT + lane * BS;
-      if (lane < PAGES && j < ntiles && tok < kv_end) id = __ldg(table + tok / BS);
-      return id;
+    // ---- producer: claims items, hands each one with rows to the other warps,
+    // then loads its 128-token tiles of whole pages
+    int gt = 0;    // tiles issued by this CTA so far
+    int npub = 0;  // items handed over so far
+    bool stop = false;
+    // (lane 0) item idx into ring slot npub & 1, once both readers of the item
+    // two back have taken it
+    auto publish = [&](int idx) -> bool {
+      const int sl = npub & 1;
+      if (npub >= 2 && !umma::wait(&item_empty[sl], (uint32_t)(((npub >> 1) - 1) & 1))) return false;
+      *(volatile int*)&s_item[sl] = idx;
+      mbar_arrive(&item_full[sl]);  // (release: the index is seen by whoever waits on the slot)
+      ++npub;
+      return true;
     };
-    uint32_t id = first_id;  // = load_id(0), issued before the set-up
-    for (int j = 0; j < ntiles; ++j) {
-      const int st = j % KST;
-      bool ok = true;
-      if (j >= KST && lane == 0) ok = umma::wait(&kv_empty[st], (uint32_t)(((j / KST) - 1) & 1));
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) {
+    UmmaSched* sched = &g_umma_sched[slot];
+    for (int idx = blockIdx.x; idx < n_items && !stop;) {
+      const bool first = idx == (int)blockIdx.x;  // (claimed items are all past the grid)
+      const UmmaItem it = first ? it0 : umma_item<CASCADE>(p, idx, tiles_x, ny);
+      if (!CASCADE && it.bad && it.first_tile && it.kvh == 0 && lane == 0)
+        set_status(&g_decode_status, KVC_STATUS_INDEX_OOB);
+      // the next item is claimed once this one's loads are issued
+      auto claim = [&]() -> int {
+        unsigned nx = (unsigned)n_items;
+        if (dynamic && lane == 0) nx = gridDim.x + atomicAdd(&sched->next, 1u);
+        nx = __shfl_sync(0xffffffffu, nx, 0);
+        return nx < (unsigned)n_items ? (int)nx : n_items;
+      };
+      if (it.skip) {
+        idx = claim();
+        continue;
+      }
+      bool handed = true;
+      if (lane == 0) handed = publish(idx);
+      if (!__shfl_sync(0xffffffffu, handed, 0)) {
         if (lane == 0) give_up();
         break;
       }
       if (__shfl_sync(0xffffffffu, abort_now() ? 1 : 0, 0)) break;
-      const int t0 = kv_beg + j * KT;
-      const bool in_range = lane < PAGES && t0 + lane * BS < kv_end;
-      const bool valid = in_range && (int64_t)id < p.num_blocks;
-      if (in_range && !valid) set_status(&g_decode_status, KVC_STATUS_BLOCK_OOB);
-      const uint32_t mask = __ballot_sync(0xffffffffu, valid);
-      uint32_t ids[PAGES];
+      const int kvh = it.kvh, kv_beg = it.kv_beg, kv_end = it.kv_end, ntiles = it.ntiles;
+      const T* kbase = reinterpret_cast<const T*>(p.k_cache) + (int64_t)kvh * p.k_head_stride;
+      const uint32_t* table = p.block_tables + (CASCADE ? (int64_t)0 : (int64_t)it.y * p.table_stride);
+      if (CASCADE && kvh == 0) {
+        // every sequence of this tile must carry sequence 0's block ids over the
+        // chunk (the caller's promise; checked once per tile and chunk)
+        const int64_t R_last = (it.R0 + kUmmaRows < it.rows ? it.R0 + kUmmaRows : it.rows) - 1;
+        const int s0 = (int)(it.R0 / G), nseq = (int)(R_last / G) - s0 + 1;
+        const int b0 = kv_beg / BS, nb = (kv_end + BS - 1) / BS - b0;
+        bool diff = false;
+        for (int i = lane; i < nseq * nb; i += 32) {
+          const int sq = s0 + i / nb, bb = b0 + i % nb;
+          diff |= __ldg(p.block_tables + (int64_t)sq * p.table_stride + bb) != __ldg(p.block_tables + bb);
+        }
+        if (diff) set_status(&g_decode_status, KVC_STATUS_PREFIX_MISMATCH);
+      }
+      auto load_id = [&](int j) -> uint32_t {
+        uint32_t id = 0xffffffffu;
+        const int tok = kv_beg + j * KT + lane * BS;
+        if (lane < PAGES && j < ntiles && tok < kv_end) id = __ldg(table + tok / BS);
+        return id;
+      };
+      uint32_t id = first ? first_id : load_id(0);
+      for (int j = 0; j < ntiles; ++j) {
+        const int g = gt + j, st = g % KST;
+        bool ok = true;
+        if (g >= KST && lane == 0) ok = umma::wait(&kv_empty[st], (uint32_t)(((g / KST) - 1) & 1));
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+          if (lane == 0) give_up();
+          stop = true;
+          break;
+        }
+        if (__shfl_sync(0xffffffffu, abort_now() ? 1 : 0, 0)) {
+          stop = true;
+          break;
+        }
+        const int t0 = kv_beg + j * KT;
+        const bool in_range = lane < PAGES && t0 + lane * BS < kv_end;
+        const bool valid = in_range && (int64_t)id < p.num_blocks;
+        if (in_range && !valid) set_status(&g_decode_status, KVC_STATUS_BLOCK_OOB);
+        const uint32_t mask = __ballot_sync(0xffffffffu, valid);
+        uint32_t ids[PAGES];
 #pragma unroll
-      for (int i = 0; i < PAGES; ++i) ids[i] = __shfl_sync(0xffffffffu, id, i);
-      id = load_id(j + 1);  // next tile's ids, in flight while this one is issued
-      if (lane == 0) {
-        page_mask[st] = mask;
-        uint8_t* kst = ring + (size_t)st * UG::STAGE;
-        uint8_t* vst = kst + PAGES * PAGE;
-        // few and large requests (the copy engine serves them one by one):
-        // per page one tensor copy of V and one bulk copy of K, or with GK one
-        // 4-row gather per 8-dim chunk for the K of all four pages
-        if (mask) {
-          if constexpr (GK) {
-            mbar_arrive_expect_tx(&kv_full[st], (uint32_t)(PAGES + __popc(mask)) * (uint32_t)PAGE);
-            const uint32_t any = ids[__ffs(mask) - 1];  // pages without keys gather a loaded page's rows
-            int rb[PAGES];
+        for (int i = 0; i < PAGES; ++i) ids[i] = __shfl_sync(0xffffffffu, id, i);
+        id = load_id(j + 1);  // next tile's ids, in flight while this one is issued
+        if (lane == 0) {
+          page_mask[st] = mask;
+          uint8_t* kst = ring + (size_t)st * UG::STAGE;
+          uint8_t* vst = kst + PAGES * PAGE;
+          // few and large requests (the copy engine serves them one by one):
+          // per page one tensor copy of V and one bulk copy of K, or with GK one
+          // 4-row gather per 8-dim chunk for the K of four pages
+          if (mask) {
+            if constexpr (GK) {
+              mbar_arrive_expect_tx(&kv_full[st], (uint32_t)(PAGES + __popc(mask)) * (uint32_t)PAGE);
+              const uint32_t any = ids[__ffs(mask) - 1];  // pages without keys gather a loaded page's rows
+              int rb[PAGES];
 #pragma unroll
-            for (int i = 0; i < PAGES; ++i)
-              rb[i] = (int)(((int64_t)((mask >> i) & 1u ? ids[i] : any) * p.num_kv_heads + kvh) * (D / 8));
+              for (int i = 0; i < PAGES; ++i)
+                rb[i] = (int)(((int64_t)((mask >> i) & 1u ? ids[i] : any) * p.num_kv_heads + kvh) * (D / 8));
 #pragma unroll
-            for (int c = 0; c < D / 8; ++c)
+              for (int c = 0; c < D / 8; ++c)
 #pragma unroll
-              for (int q = 0; q < PAGES; q += 4)  // pages q .. q + 3: tokens q*BS .. of the chunk row
-                umma::tma_gather4(kst + c * KT * 16 + q * BS * 16, kmap, 0, rb[q] + c, rb[q + 1] + c, rb[q + 2] + c,
-                                  rb[q + 3] + c, &kv_full[st]);
-          } else {
-            mbar_arrive_expect_tx(&kv_full[st], (uint32_t)__popc(mask) * 2u * (uint32_t)PAGE);
-          }
-#pragma unroll
-          for (int i = 0; i < PAGES; ++i) {
-            if (mask & (1u << i)) {
-              if constexpr (!GK) bulk_g2s(kst + i * PAGE, kbase + (int64_t)ids[i] * p.k_block_stride, PAGE, &kv_full[st]);
-              tma_load_4d(vst + i * PAGE, vmap, 0, 0, kvh, (int)ids[i], &kv_full[st]);
+                for (int q = 0; q < PAGES; q += 4)  // pages q .. q + 3: tokens q*BS .. of the chunk row
+                  umma::tma_gather4(kst + c * KT * 16 + q * BS * 16, kmap, 0, rb[q] + c, rb[q + 1] + c, rb[q + 2] + c,
+                                    rb[q + 3] + c, &kv_full[st]);
+            } else {
+              mbar_arrive_expect_tx(&kv_full[st], (uint32_t)__popc(mask) * 2u * (uint32_t)PAGE);
             }
+#pragma unroll
+            for (int i = 0; i < PAGES; ++i) {
+              if (mask & (1u << i)) {
+                if constexpr (!GK)
+                  bulk_g2s(kst + i * PAGE, kbase + (int64_t)ids[i] * p.k_block_stride, PAGE, &kv_full[st]);
+                tma_load_4d(vst + i * PAGE, vmap, 0, 0, kvh, (int)ids[i], &kv_full[st]);
+              }
+            }
+          } else {
+            mbar_arrive(&kv_full[st]);
           }
-        } else {
-          mbar_arrive(&kv_full[st]);
         }
       }
+      gt += ntiles;
+      if (!stop) idx = claim();
     }
+    // the end marker (n_items) for the other warps
+    if (lane == 0 && !publish(n_items)) give_up();
+    __syncwarp();
   } else if (warp == kMmaWarp) {
-    // ---- MMA issue (one lane)
+    // ---- MMA issue (one lane), item after item
     if (lane == 0) {
       const uint32_t idS = umma::instr_desc(BF16, 128, GK ? KT : BS), idO = umma::instr_desc(BF16, 128, D);
-      bool o_init = false;
-      bool ok = umma::wait(q_ready, 0);
-      umma::fence_after();
       // Descriptors of stage 0, advanced by adding (byte offset >> 4) to the
       // start-address field (shared addresses stay below 256 KB: no carry).
       const uint32_t ring_addr = smem_u32(ring);
       const uint64_t k_desc0 = umma::smem_desc(ring_addr, (GK ? KT : BS) * 16, 128, umma::kLayoutNone);
       const uint64_t v_desc0 = BS == 32 ? umma::smem_desc(ring_addr + PAGES * PAGE, 16, 512, umma::kLayoutSw64)
                                         : umma::smem_desc(ring_addr + PAGES * PAGE, 16, 256, umma::kLayoutSw32);
-      auto issue_pv = [&](int i) -> bool {
-        const int b = i & 1, st = i % KST;
-        if (!umma::wait(&p_full[b], (uint32_t)((i >> 1) & 1))) return false;
-        umma::fence_after();
-        const uint64_t vd = v_desc0 + (uint64_t)((st * UG::STAGE) >> 4);
-        const int steps = (kv_end - (kv_beg + i * KT) + 15) / 16;  // 16-token k-steps with keys
-        const uint32_t pcol = tmem + UG::SCOL + b * 128;
-#pragma unroll
-        for (int ks = 0; ks < KT / 16; ++ks) {
-          if (ks < steps) {
-            // k-step ks: tokens 16ks.. = page (16ks)/BS, byte (16ks % BS) * 2 of its rows
-            const uint64_t d = vd + (uint64_t)((((16 * ks) / BS) * PAGE + ((16 * ks) % BS) * 2) >> 4);
-            umma::mma_ts(tmem + UG::OCOL, pcol + 8 * ks, d, idO, (o_init || ks > 0) ? 1u : 0u);
-            if (SPLIT) umma::mma_ts(tmem + UG::OCOL, pcol + 64 + 8 * ks, d, idO, 1u);
-          }
+      int gt = 0, nit = 0, nread = 0;  // tiles, items with keys, ring slots read of this CTA so far
+      bool ok = true;
+      for (;;) {
+        const int sl = nread & 1;
+        if (abort_now() || !umma::wait(&item_full[sl], (uint32_t)((nread >> 1) & 1))) {
+          ok = false;
+          break;
         }
-        o_init = true;
-        umma::commit(pv_done);
-        umma::commit(&kv_empty[st]);
-        return true;
-      };
-      for (int j = 0; j < ntiles && ok; ++j) {
-        const int st = j % KST, b = j & 1;
-        if (abort_now() || !umma::wait(&kv_full[st], (uint32_t)((j / KST) & 1))) {
+        const int idx = *(volatile int*)&s_item[sl];
+        mbar_arrive(&item_empty[sl]);
+        ++nread;
+        if (idx >= n_items) break;
+        const UmmaItem it = umma_item<CASCADE>(p, idx, tiles_x, ny);
+        if (it.skip || it.ntiles == 0) continue;  // (no Q is handed over for an item without keys)
+        if (abort_now() || !umma::wait(q_ready, (uint32_t)(nit & 1))) {
           ok = false;
           break;
         }
         umma::fence_after();
-        const int t0 = kv_beg + j * KT;
-        const int live = (kv_end - t0 + BS - 1) / BS;  // pages with keys
-        const uint64_t kd = k_desc0 + (uint64_t)((st * UG::STAGE) >> 4);
-        if constexpr (GK) {
-          // S = Q K^T as one N = 128 product per 16-dim k-step
+        ++nit;
+        const int kv_beg = it.kv_beg, kv_end = it.kv_end, ntiles = it.ntiles;
+        bool o_init = false;
+        // O += P_j V_j of tile j (this CTA's tile g)
+        auto issue_pv = [&](int j, int g) -> bool {
+          const int b = g & 1, st = g % KST;
+          if (!umma::wait(&p_full[b], (uint32_t)((g >> 1) & 1))) return false;
+          umma::fence_after();
+          const uint64_t vd = v_desc0 + (uint64_t)((st * UG::STAGE) >> 4);
+          const int steps = (kv_end - (kv_beg + j * KT) + 15) / 16;  // 16-token k-steps with keys
+          const uint32_t pcol = tmem + UG::SCOL + b * 128;
 #pragma unroll
-          for (int ks = 0; ks < D / 16; ++ks)
-            umma::mma_ts(tmem + UG::SCOL + b * 128, tmem + UG::QCOL + 8 * ks, kd + (uint64_t)((ks * 2 * KT * 16) >> 4),
-                         idS, ks > 0 ? 1u : 0u);
-          (void)live;
-        } else {
-          // S = Q K^T: per page a chain of D/16 products (N = BS); k-step outer
-          // so consecutive products go to different pages' accumulators
-#pragma unroll
-          for (int ks = 0; ks < D / 16; ++ks) {
-#pragma unroll
-            for (int pg = 0; pg < PAGES; ++pg) {
-              if (pg < live)
-                umma::mma_ts(tmem + UG::SCOL + b * 128 + pg * BS, tmem + UG::QCOL + 8 * ks,
-                             kd + (uint64_t)((pg * PAGE + ks * 2 * BS * 16) >> 4), idS, ks > 0 ? 1u : 0u);
+          for (int ks = 0; ks < KT / 16; ++ks) {
+            if (ks < steps) {
+              // k-step ks: tokens 16ks.. = page (16ks)/BS, byte (16ks % BS) * 2 of its rows
+              const uint64_t d = vd + (uint64_t)((((16 * ks) / BS) * PAGE + ((16 * ks) % BS) * 2) >> 4);
+              umma::mma_ts(tmem + UG::OCOL, pcol + 8 * ks, d, idO, (o_init || ks > 0) ? 1u : 0u);
+              if (SPLIT) umma::mma_ts(tmem + UG::OCOL, pcol + 64 + 8 * ks, d, idO, 1u);
             }
           }
+          o_init = true;
+          umma::commit(pv_done);
+          umma::commit(&kv_empty[st]);
+          return true;
+        };
+        for (int j = 0; j < ntiles && ok; ++j) {
+          const int g = gt + j, st = g % KST, b = g & 1;
+          if (abort_now() || !umma::wait(&kv_full[st], (uint32_t)((g / KST) & 1))) {
+            ok = false;
+            break;
+          }
+          umma::fence_after();
+          const int t0 = kv_beg + j * KT;
+          const int live = (kv_end - t0 + BS - 1) / BS;  // pages with keys
+          const uint64_t kd = k_desc0 + (uint64_t)((st * UG::STAGE) >> 4);
+          if constexpr (GK) {
+            // S = Q K^T as one N = 128 product per 16-dim k-step
+#pragma unroll
+            for (int ks = 0; ks < D / 16; ++ks)
+              umma::mma_ts(tmem + UG::SCOL + b * 128, tmem + UG::QCOL + 8 * ks,
+                           kd + (uint64_t)((ks * 2 * KT * 16) >> 4), idS, ks > 0 ? 1u : 0u);
+            (void)live;
+          } else {
+            // S = Q K^T: per page a chain of D/16 products (N = BS); k-step
+            // outer so consecutive products go to different pages' accumulators
+#pragma unroll
+            for (int ks = 0; ks < D / 16; ++ks) {
+#pragma unroll
+              for (int pg = 0; pg < PAGES; ++pg) {
+                if (pg < live)
+                  umma::mma_ts(tmem + UG::SCOL + b * 128 + pg * BS, tmem + UG::QCOL + 8 * ks,
+                               kd + (uint64_t)((pg * PAGE + ks * 2 * BS * 16) >> 4), idS, ks > 0 ? 1u : 0u);
+              }
+            }
+          }
+          umma::commit(&s_full[b]);
+          if (j >= 1 && !issue_pv(j - 1, g - 1)) ok = false;
         }
-        umma::commit(&s_full[b]);
-        if (j >= 1 && !issue_pv(j - 1)) ok = false;
+        if (ok && ntiles > 0 && !abort_now()) ok = issue_pv(ntiles - 1, gt + ntiles - 1);
+        gt += ntiles;
       }
-      if (ok && ntiles > 0 && !abort_now()) ok = issue_pv(ntiles - 1);
       if (!ok) give_up();
       // every product issued so far is complete before TMEM can be freed
       umma::commit(all_done);
@@ -429,46 +552,11 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     auto uabort = [&]() -> bool { return __any_sync(0xffffffffu, abort_now()); };
     const int half = warp >> 2;
     const int r = threadIdx.x & 127;
-    const int64_t R = R0 + r;
-    const bool in_tile = R < rows;      // a row (else padding of the last tile)
-    // t: the new token (prefill) or the sequence (cascade) of the row
-    const int t = in_tile ? (int)(R / G) : 0, g = in_tile ? (int)(R - (int64_t)t * G) : 0;
-    bool on;  // a row that sees keys
-    int end_r, beg_r;
-    if constexpr (CASCADE) {
-      // the row's sequence sees the chunk up to its own length; lengths the
-      // reference zeroes (0 or past max_seq_len) see nothing
-      const uint32_t ctx = in_tile ? __ldg(p.context_lens + t) : 0u;
-      on = in_tile && ctx != 0 && ctx <= (uint32_t)p.max_seq_len;
-      end_r = on ? ((int)ctx < kv_end ? (int)ctx : kv_end) : 0;
-      beg_r = 0;
-    } else {
-      on = in_tile && !bad;
-      end_r = on ? prefix + t + 1 : 0;
-      beg_r = p.window > 0 ? end_r - p.window : 0;
-    }
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     constexpr int HK = KT / 2;   // tokens of a tile per half
     constexpr int HD = D / 2;    // O columns per half
     constexpr int QC = D / 4;    // Q columns (element pairs) per half
-    // Q row -> TMEM columns QCOL .. QCOL + D/2 - 1 (element pairs), QC per half
-    {
-      const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
-          reinterpret_cast<const T*>(p.q) + (q0 + t) * p.q_tok_stride + (int64_t)(kvh * G + g) * p.q_head_stride) +
-          half * QC;
-      uint32_t qv[32];
-#pragma unroll
-      for (int i = 0; i < QC; ++i) qv[i] = on ? __ldg(qrow + i) : 0u;
-      if constexpr (QC == 32) umma::st32(lane_base + UG::QCOL + half * QC, qv);
-      else umma::st16(lane_base + UG::QCOL + half * QC, qv);
-    }
-    umma::wait_st();
-    umma::fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(q_ready);
-
     const float qk_scale = p.scale * kLog2e;
-    float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     uint32_t xphase = 0;
     // both halves' values of this row: write mine, hand over, read the other's
@@ -487,204 +575,264 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       }
       return buf[(half ^ 1) * 128 + r];
     };
-    for (int j = 0; j < ntiles; ++j) {
-      const int b = j & 1, st = j % KST;
-      if (uabort() || !uwait(&s_full[b], (uint32_t)((j >> 1) & 1))) {
+    int gt = 0, nread = 0;  // tiles and ring slots read of this CTA so far
+    while (ok) {
+      const int sl = nread & 1;
+      if (uabort() || !uwait(&item_full[sl], (uint32_t)((nread >> 1) & 1))) {
         ok = false;
         break;
       }
-      umma::fence_after();
-      // (the stage's barrier orders the producer's page mask and the TMA-written
-      // V before this thread reads or clears them; its phase cannot move on
-      // before this tile's P is handed over)
-      if (!uwait(&kv_full[st], (uint32_t)((j / KST) & 1))) {
-        ok = false;
-        break;
-      }
-      const int t0 = kv_beg + j * KT + half * HK;  // first token of my half
-      const uint32_t pm = page_mask[st];
-      float x[HK];
-#pragma unroll
-      for (int c = 0; c < HK; c += 32) {
-        uint32_t v[32];
-        umma::ld32(lane_base + UG::SCOL + b * 128 + half * HK + c, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) x[c + i] = __uint_as_float(v[i]);
-      }
-      umma::wait_ld();
-      // A half tile every row of the warp sees whole (its pages loaded, inside
-      // every row's [start, end)) needs no per-token mask.
-      const uint32_t my_pages = HK >= BS ? ((1u << (HK / BS)) - 1u) << (half * HK / BS) : 0u;
-      const bool whole =
-          __all_sync(0xffffffffu, (pm & my_pages) == my_pages && t0 >= beg_r && t0 + HK <= end_r);
-      float mx;  // row max of my scaled scores (log2 units)
-      if (whole) {
-        float hi_raw = -INFINITY, lo_raw = INFINITY;
-#pragma unroll
-        for (int c = 0; c < HK; c += 2) {
-          hi_raw = fmaxf(hi_raw, fmaxf(x[c], x[c + 1]));
-          lo_raw = fminf(lo_raw, fminf(x[c], x[c + 1]));
-        }
-        mx = qk_scale >= 0.f ? hi_raw * qk_scale : lo_raw * qk_scale;
+      const int idx = *(volatile int*)&s_item[sl];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[sl]);
+      ++nread;
+      if (idx >= n_items) break;
+      const UmmaItem it = umma_item<CASCADE>(p, idx, tiles_x, ny);
+      if (it.skip) continue;
+      const int kvh = it.kvh, kv_beg = it.kv_beg, kv_end = it.kv_end, ntiles = it.ntiles;
+      const int64_t R = it.R0 + r;
+      const bool in_tile = R < it.rows;  // a row (else padding of the last tile)
+      // t: the new token (prefill) or the sequence (cascade) of the row
+      const int t = in_tile ? (int)(R / G) : 0, g = in_tile ? (int)(R - (int64_t)t * G) : 0;
+      bool on;  // a row that sees keys
+      int end_r, beg_r;
+      if constexpr (CASCADE) {
+        // the row's sequence sees the chunk up to its own length; lengths the
+        // reference zeroes (0 or past max_seq_len) see nothing
+        const uint32_t ctx = in_tile ? __ldg(p.context_lens + t) : 0u;
+        on = in_tile && ctx != 0 && ctx <= (uint32_t)p.max_seq_len;
+        end_r = on ? ((int)ctx < kv_end ? (int)ctx : kv_end) : 0;
+        beg_r = 0;
       } else {
-        mx = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < HK; ++c) {
-          const int tok = t0 + c;
-          const bool vis = tok >= beg_r && tok < end_r && ((pm >> ((half * HK + c) / BS)) & 1u);
-          x[c] = vis ? x[c] * qk_scale : -INFINITY;
-          mx = fmaxf(mx, x[c]);
-        }
+        on = in_tile && !it.bad;
+        end_r = on ? it.prefix + t + 1 : 0;
+        beg_r = p.window > 0 ? end_r - p.window : 0;
       }
-      mx = fmaxf(mx, exchange(mx));
-      if (!ok) break;
-      // lazy max (the same in both halves): rescale only when it rises by more than 2^8
-      float alpha = 1.f;
-      if (mx > m_ref + 8.f) {
-        alpha = m_ref == -INFINITY ? 0.f : fast_exp2(m_ref - mx);
-        m_ref = mx;
-      }
-      const float neg_ref = m_ref == -INFINITY ? 0.f : -m_ref;
-      float ps = 0.f;
-      // P pairs packed as soon as they are exponentiated (the integer / FMA
-      // work of the packing overlaps the special-function unit's exponentials):
-      // hi = the upper 16 bits of each fp32 (a bf16, truncated), lo = the exact
-      // remainder rounded to bf16, so hi + lo carries ~16 bits of P; f16 P is
-      // one rounding.  Pairs of tokens 64h + 2i, + 1 go to hi column 32h + i.
-      uint32_t hi[32], lo[32];
-      auto pack_pair = [&](int i, float p0, float p1) {
-        if constexpr (SPLIT) {
-          const uint32_t u0 = __float_as_uint(p0), u1 = __float_as_uint(p1);
-          hi[i] = __byte_perm(u0, u1, 0x7632);
-          lo[i] = MmaOp<T>::pack(p0 - __uint_as_float(u0 & 0xFFFF0000u), p1 - __uint_as_float(u1 & 0xFFFF0000u));
-        } else {
-          hi[i] = MmaOp<T>::pack(p0, p1);
-          lo[i] = 0u;
-        }
-      };
-      if (whole) {
+      // Q row -> TMEM columns QCOL .. QCOL + D/2 - 1 (element pairs), QC per
+      // half.  (Every product of the previous item is complete: its last P.V
+      // was waited for before its epilogue.)
+      {
+        const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+            reinterpret_cast<const T*>(p.q) + (it.q0 + t) * p.q_tok_stride +
+            (int64_t)(kvh * G + g) * p.q_head_stride) + half * QC;
+        uint32_t qv[32];
 #pragma unroll
-        for (int i = 0; i < HK / 2; ++i) {
-          const float p0 = fast_exp2(fmaf(x[2 * i], qk_scale, neg_ref));
-          const float p1 = fast_exp2(fmaf(x[2 * i + 1], qk_scale, neg_ref));
-          ps += p0 + p1;
-          pack_pair(i, p0, p1);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < HK / 2; ++i) {
-          const float p0 = fast_exp2(x[2 * i] + neg_ref);  // masked: exp2(-inf) = 0
-          const float p1 = fast_exp2(x[2 * i + 1] + neg_ref);
-          ps += p0 + p1;
-          pack_pair(i, p0, p1);
-        }
+        for (int i = 0; i < QC; ++i) qv[i] = on ? __ldg(qrow + i) : 0u;
+        if constexpr (QC == 32) umma::st32(lane_base + UG::QCOL + half * QC, qv);
+        else umma::st16(lane_base + UG::QCOL + half * QC, qv);
       }
-      l = l * alpha + ps;  // this half's share of the row sum
-      // O and the P buffer are free once P.V of the previous tile is done
-      if (j >= 1) {
-        if (!uwait(pv_done, (uint32_t)((j - 1) & 1))) {
+      umma::wait_st();
+      umma::fence_before();
+      __syncwarp();
+      // (an item without keys hands over no Q: the MMA warp could otherwise see
+      // two phases of q_ready complete before it waits for the first)
+      if (lane == 0 && ntiles > 0) mbar_arrive(q_ready);
+
+      float m_ref = -INFINITY, l = 0.f;
+      for (int j = 0; j < ntiles; ++j) {
+        const int gg = gt + j, b = gg & 1, st = gg % KST;
+        if (uabort() || !uwait(&s_full[b], (uint32_t)((gg >> 1) & 1))) {
           ok = false;
           break;
         }
         umma::fence_after();
+        // (the stage's barrier orders the producer's page mask and the TMA-written
+        // V before this thread reads or clears them; its phase cannot move on
+        // before this tile's P is handed over)
+        if (!uwait(&kv_full[st], (uint32_t)((gg / KST) & 1))) {
+          ok = false;
+          break;
+        }
+        const int t0 = kv_beg + j * KT + half * HK;  // first token of my half
+        const uint32_t pm = page_mask[st];
+        float x[HK];
+#pragma unroll
+        for (int c = 0; c < HK; c += 32) {
+          uint32_t v[32];
+          umma::ld32(lane_base + UG::SCOL + b * 128 + half * HK + c, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[c + i] = __uint_as_float(v[i]);
+        }
+        umma::wait_ld();
+        // A half tile every row of the warp sees whole (its pages loaded, inside
+        // every row's [start, end)) needs no per-token mask.
+        const uint32_t my_pages = HK >= BS ? ((1u << (HK / BS)) - 1u) << (half * HK / BS) : 0u;
+        const bool whole =
+            __all_sync(0xffffffffu, (pm & my_pages) == my_pages && t0 >= beg_r && t0 + HK <= end_r);
+        float mx;  // row max of my scaled scores (log2 units)
+        if (whole) {
+          float hi_raw = -INFINITY, lo_raw = INFINITY;
+#pragma unroll
+          for (int c = 0; c < HK; c += 2) {
+            hi_raw = fmaxf(hi_raw, fmaxf(x[c], x[c + 1]));
+            lo_raw = fminf(lo_raw, fminf(x[c], x[c + 1]));
+          }
+          mx = qk_scale >= 0.f ? hi_raw * qk_scale : lo_raw * qk_scale;
+        } else {
+          mx = -INFINITY;
+#pragma unroll
+          for (int c = 0; c < HK; ++c) {
+            const int tok = t0 + c;
+            const bool vis = tok >= beg_r && tok < end_r && ((pm >> ((half * HK + c) / BS)) & 1u);
+            x[c] = vis ? x[c] * qk_scale : -INFINITY;
+            mx = fmaxf(mx, x[c]);
+          }
+        }
+        mx = fmaxf(mx, exchange(mx));
+        if (!ok) break;
+        // lazy max (the same in both halves): rescale only when it rises by more than 2^8
+        float alpha = 1.f;
+        if (mx > m_ref + 8.f) {
+          alpha = m_ref == -INFINITY ? 0.f : fast_exp2(m_ref - mx);
+          m_ref = mx;
+        }
+        const float neg_ref = m_ref == -INFINITY ? 0.f : -m_ref;
+        float ps = 0.f;
+        // P pairs packed as soon as they are exponentiated (the integer / FMA
+        // work of the packing overlaps the special-function unit's exponentials):
+        // hi = the upper 16 bits of each fp32 (a bf16, truncated), lo = the exact
+        // remainder rounded to bf16, so hi + lo carries ~16 bits of P; f16 P is
+        // one rounding.  Pairs of tokens 64h + 2i, + 1 go to hi column 32h + i.
+        uint32_t hi[32], lo[32];
+        auto pack_pair = [&](int i, float p0, float p1) {
+          if constexpr (SPLIT) {
+            const uint32_t u0 = __float_as_uint(p0), u1 = __float_as_uint(p1);
+            hi[i] = __byte_perm(u0, u1, 0x7632);
+            lo[i] = MmaOp<T>::pack(p0 - __uint_as_float(u0 & 0xFFFF0000u), p1 - __uint_as_float(u1 & 0xFFFF0000u));
+          } else {
+            hi[i] = MmaOp<T>::pack(p0, p1);
+            lo[i] = 0u;
+          }
+        };
+        if (whole) {
+#pragma unroll
+          for (int i = 0; i < HK / 2; ++i) {
+            const float p0 = fast_exp2(fmaf(x[2 * i], qk_scale, neg_ref));
+            const float p1 = fast_exp2(fmaf(x[2 * i + 1], qk_scale, neg_ref));
+            ps += p0 + p1;
+            pack_pair(i, p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < HK / 2; ++i) {
+            const float p0 = fast_exp2(x[2 * i] + neg_ref);  // masked: exp2(-inf) = 0
+            const float p1 = fast_exp2(x[2 * i + 1] + neg_ref);
+            ps += p0 + p1;
+            pack_pair(i, p0, p1);
+          }
+        }
+        l = l * alpha + ps;  // this half's share of the row sum
+        // O and the P buffer are free once P.V of the previous tile is done
+        if (j >= 1) {
+          if (!uwait(pv_done, (uint32_t)((gg - 1) & 1))) {
+            ok = false;
+            break;
+          }
+          umma::fence_after();
+        }
+        if (__any_sync(0xffffffffu, alpha != 1.f) && j >= 1) {
+#pragma unroll
+          for (int c = 0; c < HD; c += 32) {
+            uint32_t v[32];
+            umma::ld32(lane_base + UG::OCOL + half * HD + c, v);
+            umma::wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+            umma::st32(lane_base + UG::OCOL + half * HD + c, v);
+          }
+        }
+        // the last tile's partial page: V of tokens past the context end becomes 0
+        // (its slots may hold anything and 0 * NaN = NaN); half 0, thread d clears row d
+        const int tile0 = kv_beg + j * KT;
+        if (half == 0 && tile0 + KT > kv_end && (kv_end - tile0) % BS != 0) {
+          const int pg = (kv_end - tile0) / BS, from = (kv_end - tile0) % BS;
+          if ((pm >> pg) & 1u) {
+            uint8_t* vpage = ring + (size_t)st * UG::STAGE + PAGES * PAGE + pg * PAGE;
+            const int d = r;
+            if (d < D) {
+              for (int tk = from; tk < BS; ++tk) {
+                const int ch = tk / 8;
+                const int phys = BS == 32 ? (ch ^ ((d >> 1) & 3)) : (ch ^ ((d >> 2) & 1));
+                *reinterpret_cast<uint16_t*>(vpage + d * BS * 2 + phys * 16 + (tk % 8) * 2) = 0;
+              }
+            }
+            fence_proxy_async();
+          }
+        }
+        // P over the S buffer: hi pairs of tokens 64h .. 64h + 63 in columns
+        // 32h .. 32h + 31, lo pairs 64 columns further
+        umma::st32(lane_base + UG::SCOL + b * 128 + half * 32, hi);
+        if constexpr (SPLIT) umma::st32(lane_base + UG::SCOL + b * 128 + 64 + half * 32, lo);
+        umma::wait_st();
+        umma::fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[b]);
       }
-      if (__any_sync(0xffffffffu, alpha != 1.f) && j >= 1) {
+      bool have = ok && ntiles > 0;
+      if (have) {
+        have = uwait(pv_done, (uint32_t)((gt + ntiles - 1) & 1));
+        if (!have) ok = false;
+        umma::fence_after();
+      }
+      // both halves must take the last exchange (or time out on it) alike
+      const float l_all = l + exchange(l);
+      have = have && ok;
+      if constexpr (CASCADE) {
+        // ---- partials of partition y (the chunk): natural-log max, sum,
+        // unnormalised O (0 for a row without keys, whose max is -inf)
+        const bool keep = have && l_all > 0.f;
+        const int head = kvh * G + g;
+        float* po = p.part_out + (int64_t)t * p.part_out_seq_stride + (int64_t)head * p.part_out_head_stride +
+                    (int64_t)it.y * p.part_out_part_stride + half * HD;
+#pragma unroll
+        for (int c = 0; c < HD; c += 32) {
+          uint32_t v[32];
+          // (tcgen05.ld is warp-collective: every lane loads, only rows store)
+          umma::ld32(lane_base + UG::OCOL + half * HD + c, v);
+          umma::wait_ld();
+          if (in_tile) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(po + c + i) =
+                  keep ? make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]), __uint_as_float(v[i + 2]),
+                                     __uint_as_float(v[i + 3]))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+        if (in_tile && half == 0) {
+          const int64_t o = (int64_t)t * p.part_seq_stride + (int64_t)head * p.part_head_stride + it.y;
+          p.part_max[o] = keep ? m_ref * kLn2 : -INFINITY;
+          p.part_sum[o] = keep ? l_all : 0.f;
+        }
+      } else {
+        // ---- epilogue: O / l (a row with no visible key, or after an abort, is 0)
+        const bool nonzero = have && l_all > 0.f;  // else explicit zeros (O may hold another item's values)
+        const float inv = nonzero ? 1.f / l_all : 0.f;
+        T* orow = reinterpret_cast<T*>(p.out) + (it.q0 + t) * p.out_tok_stride +
+                  (int64_t)(kvh * G + g) * p.out_head_stride + half * HD;
 #pragma unroll
         for (int c = 0; c < HD; c += 32) {
           uint32_t v[32];
           umma::ld32(lane_base + UG::OCOL + half * HD + c, v);
           umma::wait_ld();
+          if (in_tile) {
+            uint32_t packed[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-          umma::st32(lane_base + UG::OCOL + half * HD + c, v);
-        }
-      }
-      // the last tile's partial page: V of tokens past the context end becomes 0
-      // (its slots may hold anything and 0 * NaN = NaN); half 0, thread d clears row d
-      const int tile0 = kv_beg + j * KT;
-      if (half == 0 && tile0 + KT > kv_end && (kv_end - tile0) % BS != 0) {
-        const int pg = (kv_end - tile0) / BS, from = (kv_end - tile0) % BS;
-        if ((pm >> pg) & 1u) {
-          uint8_t* vpage = ring + (size_t)st * UG::STAGE + PAGES * PAGE + pg * PAGE;
-          const int d = r;
-          if (d < D) {
-            for (int tk = from; tk < BS; ++tk) {
-              const int ch = tk / 8;
-              const int phys = BS == 32 ? (ch ^ ((d >> 1) & 3)) : (ch ^ ((d >> 2) & 1));
-              *reinterpret_cast<uint16_t*>(vpage + d * BS * 2 + phys * 16 + (tk % 8) * 2) = 0;
-            }
+            for (int i = 0; i < 16; ++i)
+              packed[i] =
+                  nonzero ? pack_out<T>(__uint_as_float(v[2 * i]) * inv, __uint_as_float(v[2 * i + 1]) * inv) : 0u;
+#pragma unroll
+            for (int i = 0; i < 16; i += 4)
+              *reinterpret_cast<uint4*>(orow + c + 2 * i) =
+                  make_uint4(packed[i], packed[i + 1], packed[i + 2], packed[i + 3]);
           }
-          fence_proxy_async();
         }
       }
-      // P over the S buffer: hi pairs of tokens 64h .. 64h + 63 in columns
-      // 32h .. 32h + 31, lo pairs 64 columns further
-      umma::st32(lane_base + UG::SCOL + b * 128 + half * 32, hi);
-      if constexpr (SPLIT) umma::st32(lane_base + UG::SCOL + b * 128 + 64 + half * 32, lo);
-      umma::wait_st();
+      // (the next item's Q store and its first P.V come after these O loads)
       umma::fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[b]);
+      gt += ntiles;
     }
     if (!ok && lane == 0) give_up();
-    bool have = ok && ntiles > 0;
-    if (have) {
-      have = uwait(pv_done, (uint32_t)((ntiles - 1) & 1));
-      if (!have && lane == 0) give_up();
-      umma::fence_after();
-    }
-    // both halves must take the last exchange (or time out on it) alike
-    const float l_all = l + exchange(l);
-    have = have && ok;
-    if constexpr (CASCADE) {
-      // ---- partials of partition `seq` (the chunk): natural-log max, sum,
-      // unnormalised O (0 for a row without keys, whose max is -inf)
-      const bool keep = have && l_all > 0.f;
-      const int head = kvh * G + g;
-      float* po = p.part_out + (int64_t)t * p.part_out_seq_stride + (int64_t)head * p.part_out_head_stride +
-                  (int64_t)seq * p.part_out_part_stride + half * HD;
-#pragma unroll
-      for (int c = 0; c < HD; c += 32) {
-        uint32_t v[32];
-        // (tcgen05.ld is warp-collective: every lane loads, only rows store)
-        umma::ld32(lane_base + UG::OCOL + half * HD + c, v);
-        umma::wait_ld();
-        if (in_tile) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<float4*>(po + c + i) =
-                keep ? make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]), __uint_as_float(v[i + 2]),
-                                   __uint_as_float(v[i + 3]))
-                     : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      }
-      if (in_tile && half == 0) {
-        const int64_t o = (int64_t)t * p.part_seq_stride + (int64_t)head * p.part_head_stride + seq;
-        p.part_max[o] = keep ? m_ref * kLn2 : -INFINITY;
-        p.part_sum[o] = keep ? l_all : 0.f;
-      }
-    } else {
-    // ---- epilogue: O / l (a row with no visible key, or after an abort, is 0)
-    const bool nonzero = have && l_all > 0.f;  // else explicit zeros (this CTA may never have written O)
-    const float inv = nonzero ? 1.f / l_all : 0.f;
-    T* orow = reinterpret_cast<T*>(p.out) + (q0 + t) * p.out_tok_stride + (int64_t)(kvh * G + g) * p.out_head_stride +
-              half * HD;
-#pragma unroll
-    for (int c = 0; c < HD; c += 32) {
-      uint32_t v[32];
-      umma::ld32(lane_base + UG::OCOL + half * HD + c, v);
-      umma::wait_ld();
-      if (R < rows) {
-        uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          packed[i] = nonzero ? pack_out<T>(__uint_as_float(v[2 * i]) * inv, __uint_as_float(v[2 * i + 1]) * inv) : 0u;
-#pragma unroll
-        for (int i = 0; i < 16; i += 4)
-          *reinterpret_cast<uint4*>(orow + c + 2 * i) = make_uint4(packed[i], packed[i + 1], packed[i + 2], packed[i + 3]);
-      }
-    }
-    }
   }
 
   umma::fence_before();
@@ -692,6 +840,14 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   if (warp == kMmaWarp) {
     umma::fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+  // this CTA claims no more items: the last CTA out returns the counters to zero
+  if (dynamic && threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&g_umma_sched[slot].done, 1u) == gridDim.x - 1) {
+      atomicExch(&g_umma_sched[slot].next, 0u);
+      atomicExch(&g_umma_sched[slot].done, 0u);
+    }
   }
 }
 
@@ -708,6 +864,23 @@ static bool make_k_gather_map(const PrefillArgs& a, int D, int BS, CUtensorMap* 
              const_cast<void*>(a.k_cache), dims, strides, box, ones, CU_TENSOR_MAP_INTERLEAVE_NONE,
              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
          CUDA_SUCCESS;
+}
+
+// The persistent grid: one CTA per SM (the ring and TMEM allow one), fewer
+// when there are fewer work items.
+static int umma_persistent_ctas(int dev, int64_t items) {
+  static int sms[64] = {0};
+  int n = dev >= 0 && dev < 64 ? sms[dev] : 0;
+  if (n <= 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    if (dev >= 0 && dev < 64) sms[dev] = n;
+  }
+  return (int)(items < n ? items : n);
+}
+
+static int umma_sched_slot() {
+  static std::atomic<unsigned> next{0};
+  return (int)(next.fetch_add(1u, std::memory_order_relaxed) % (unsigned)kUmmaSchedSlots);
 }
 
 template <typename T, int D, int BS, bool GK>
@@ -741,10 +914,11 @@ static cudaError_t launch_prefill_umma(const PrefillArgs& a, cudaStream_t stream
   }
   const int G = a.num_heads / a.num_kv_heads;
   const int64_t tiles = ((int64_t)a.max_q_len * G + kUmmaRows - 1) / kUmmaRows;
-  if (tiles <= 0) return cudaSuccess;
-  if (tiles > 0x7fffffffll) return cudaErrorInvalidValue;
-  kern<<<dim3((unsigned)tiles, (unsigned)a.num_seqs, (unsigned)a.num_kv_heads), kUmmaThreads, UG::SMEM, stream>>>(
-      a, maps);
+  if (tiles <= 0 || a.num_seqs <= 0) return cudaSuccess;
+  const int64_t items = tiles * a.num_seqs * a.num_kv_heads;
+  if (items > 0x7fffffffll - 1024) return cudaErrorInvalidValue;
+  const int ctas = umma_persistent_ctas(dev, items);
+  kern<<<ctas, kUmmaThreads, UG::SMEM, stream>>>(a, maps, (int)tiles, (int)a.num_seqs, umma_sched_slot());
   count_launch();
   return cudaGetLastError();
 }
@@ -825,8 +999,11 @@ static cudaError_t launch_cascade_umma(const PrefillArgs& a, int prefix_parts, c
   }
   const int G = a.num_heads / a.num_kv_heads;
   const int64_t tiles = ((int64_t)a.num_seqs * G + kUmmaRows - 1) / kUmmaRows;
-  kern<<<dim3((unsigned)tiles, (unsigned)prefix_parts, (unsigned)a.num_kv_heads), kUmmaThreads, UG::SMEM, stream>>>(a,
-                                                                                                                  maps);
+  const int64_t items = tiles * prefix_parts * a.num_kv_heads;
+  if (items <= 0) return cudaSuccess;
+  if (items > 0x7fffffffll - 1024) return cudaErrorInvalidValue;
+  const int ctas = umma_persistent_ctas(dev, items);
+  kern<<<ctas, kUmmaThreads, UG::SMEM, stream>>>(a, maps, (int)tiles, prefix_parts, umma_sched_slot());
   count_launch();
   return cudaGetLastError();
 }
