@@ -6,26 +6,33 @@
 // memory_pool.py:240-270), with the products on the tensor cores' own
 // pipeline instead of mma.sync:
 //
-//  * CTA = 128 query rows (new token, query head of the group) of one
-//    sequence and KV head; row r of the tile is TMEM lane r.
+//  * Work item = 128 query rows (new token, query head of the group) of one
+//    sequence and KV head (cascade form: 128 (sequence, head) rows and one
+//    prefix chunk); row r of the item is TMEM lane r.  The grid is
+//    persistent (one CTA per SM): CTA c takes item c, then claims further
+//    items from a device counter until none is left.
 //  * TMEM (512 columns): two S buffers of 128 fp32 columns (S = Q K^T of a
 //    128-token tile), O (D fp32 columns) and Q (D/2 columns of bf16/f16
 //    pairs).  P overwrites its own S buffer: hi parts in the first 64
 //    columns, lo parts (bf16 only) in the next 64.
-//  * Warp 4 (producer) streams 128-token tiles into a ring of KST stages:
-//    each K page as it is (its [D/8][bs][8] layout is the no-swizzle K-major
-//    operand layout: 8 tokens x 16 bytes per core matrix), each V page
-//    [D][bs] through a tensor map that writes it with the bs*2-byte swizzle,
-//    the K-major operand layout of P.V (tokens are its K).
-//  * Warp 5 (one lane) issues S_j = Q K_j^T (A = Q from TMEM, one chain of
-//    D/16 instructions per page, N = bs), then O += P_{j-1} V_{j-1} (A = P
-//    from TMEM, N = D, 16 tokens per instruction; bf16 P as hi + lo, two
-//    products), committing each to an mbarrier.
-//  * Warps 0-3 (one thread per row) read S_j, mask it (causal end, window
+//  * Warp 8 (producer) claims the items, hands each to the other warps, and
+//    streams its 128-token tiles into a ring of KST stages: K either as 4-row
+//    gathers of the dense cache (one [D/8][128][8] no-swizzle K-major operand
+//    per tile) or page by page as it is (its [D/8][bs][8] layout is that
+//    operand layout for N = bs), each V page [D][bs] through a tensor map
+//    that writes it with the bs*2-byte swizzle, the K-major operand layout of
+//    P.V (tokens are its K).
+//  * Warp 9 (one lane) issues S_j = Q K_j^T (A = Q from TMEM; N = 128 per
+//    16-dim k-step for gathered K, else a chain per page with N = bs), then
+//    O += P_{j-1} V_{j-1} (A = P from TMEM, N = D, 16 tokens per
+//    instruction; bf16 P as hi + lo, two products), committing each to an
+//    mbarrier.
+//  * Warps 0-7 (warps w and w + 4 share TMEM lanes 32w .. 32w + 31, one
+//    thread per row and half tile) read S_j, mask it (causal end, window
 //    start, context end), keep the running max lazily (O is rescaled only
 //    when a row's max rises by more than 2^8; until then P may exceed 1,
 //    exactly as the final O / l needs), write P, and at the end normalise
-//    O and store the row.
+//    O and store the row (cascade form: the split-K partials).
 // Every wait is bounded (KVC_STATUS_WAIT_TIMEOUT and an abort flag end every
 // loop); TMEM is freed only after a final commit shows every product done.
 #pragma once
