@@ -99,6 +99,14 @@ __device__ __forceinline__ void ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 32 lanes x 16 consecutive 32-bit columns
+__device__ __forceinline__ void ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void st16(uint32_t taddr, const uint32_t* r) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
@@ -364,19 +372,6 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       const int kvh = it.kvh, kv_beg = it.kv_beg, kv_end = it.kv_end, ntiles = it.ntiles;
       const T* kbase = reinterpret_cast<const T*>(p.k_cache) + (int64_t)kvh * p.k_head_stride;
       const uint32_t* table = p.block_tables + (CASCADE ? (int64_t)0 : (int64_t)it.y * p.table_stride);
-      if (CASCADE && kvh == 0) {
-        // every sequence of this tile must carry sequence 0's block ids over the
-        // chunk (the caller's promise; checked once per tile and chunk)
-        const int64_t R_last = (it.R0 + kUmmaRows < it.rows ? it.R0 + kUmmaRows : it.rows) - 1;
-        const int s0 = (int)(it.R0 / G), nseq = (int)(R_last / G) - s0 + 1;
-        const int b0 = kv_beg / BS, nb = (kv_end + BS - 1) / BS - b0;
-        bool diff = false;
-        for (int i = lane; i < nseq * nb; i += 32) {
-          const int sq = s0 + i / nb, bb = b0 + i % nb;
-          diff |= __ldg(p.block_tables + (int64_t)sq * p.table_stride + bb) != __ldg(p.block_tables + bb);
-        }
-        if (diff) set_status(&g_decode_status, KVC_STATUS_PREFIX_MISMATCH);
-      }
       auto load_id = [&](int j) -> uint32_t {
         uint32_t id = 0xffffffffu;
         const int tok = kv_beg + j * KT + lane * BS;
@@ -443,6 +438,20 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
             mbar_arrive(&kv_full[st]);
           }
         }
+      }
+      if (CASCADE && kvh == 0) {
+        // every sequence of this tile must carry sequence 0's block ids over the
+        // chunk (the caller's promise; checked once per tile and chunk, after
+        // the item's copies are issued: it only sets a status bit)
+        const int64_t R_last = (it.R0 + kUmmaRows < it.rows ? it.R0 + kUmmaRows : it.rows) - 1;
+        const int s0 = (int)(it.R0 / G), nseq = (int)(R_last / G) - s0 + 1;
+        const int b0 = kv_beg / BS, nb = (kv_end + BS - 1) / BS - b0;
+        bool diff = false;
+        for (int i = lane; i < nseq * nb; i += 32) {
+          const int sq = s0 + i / nb, bb = b0 + i % nb;
+          diff |= __ldg(p.block_tables + (int64_t)sq * p.table_stride + bb) != __ldg(p.block_tables + bb);
+        }
+        if (diff) set_status(&g_decode_status, KVC_STATUS_PREFIX_MISMATCH);
       }
       gt += ntiles;
       if (!stop) idx = claim();
@@ -563,6 +572,9 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     constexpr int HK = KT / 2;   // tokens of a tile per half
     constexpr int HD = D / 2;    // O columns per half
     constexpr int QC = D / 4;    // Q columns (element pairs) per half
+    // O columns per rescale step (P's 64 registers are live there; the cascade
+    // forms spill at 32)
+    constexpr int RC = CASCADE ? 16 : 32;
     const float qk_scale = p.scale * kLog2e;
     bool ok = true;
     uint32_t xphase = 0;
@@ -739,13 +751,15 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         }
         if (__any_sync(0xffffffffu, alpha != 1.f) && j >= 1) {
 #pragma unroll
-          for (int c = 0; c < HD; c += 32) {
-            uint32_t v[32];
-            umma::ld32(lane_base + UG::OCOL + half * HD + c, v);
+          for (int c = 0; c < HD; c += RC) {
+            uint32_t v[RC];
+            if constexpr (RC == 16) umma::ld16(lane_base + UG::OCOL + half * HD + c, v);
+            else umma::ld32(lane_base + UG::OCOL + half * HD + c, v);
             umma::wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-            umma::st32(lane_base + UG::OCOL + half * HD + c, v);
+            for (int i = 0; i < RC; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+            if constexpr (RC == 16) umma::st16(lane_base + UG::OCOL + half * HD + c, v);
+            else umma::st32(lane_base + UG::OCOL + half * HD + c, v);
           }
         }
         // the last tile's partial page: V of tokens past the context end becomes 0
