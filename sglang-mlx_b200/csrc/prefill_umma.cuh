@@ -160,13 +160,16 @@ struct UmmaGeom {
 // (prefill) or of all sequences (cascade), one key range, one KV head.
 // CTA c starts with item c; after that each CTA claims the next unclaimed item
 // from a device counter, so a CTA that drew short items takes more of them.
-// A launch uses one of kUmmaSchedSlots counter pairs (the host rotates them,
-// so launches in flight together on different streams use different pairs);
-// the last CTA of the launch to finish returns its pair to zero.
+// A launch uses one of kUmmaSchedSlots counter pairs and the last CTA of the
+// launch to finish returns its pair to zero.  The host hands the pairs out in
+// turn: launches recorded into a CUDA graph (replayed for as long as the graph
+// lives) from the last kUmmaSchedCaptured pairs, the others from the rest, so
+// two launches running at the same time share a pair only if one stream
+// trails another by thousands of launches of this kernel.
 struct UmmaSched {
   unsigned next, done;
 };
-constexpr int kUmmaSchedSlots = 64;
+constexpr int kUmmaSchedSlots = 4096, kUmmaSchedCaptured = 1024;
 __device__ UmmaSched g_umma_sched[kUmmaSchedSlots];
 
 struct UmmaItem {
@@ -899,9 +902,17 @@ static int umma_persistent_ctas(int dev, int64_t items) {
   return (int)(items < n ? items : n);
 }
 
-static int umma_sched_slot() {
-  static std::atomic<unsigned> next{0};
-  return (int)(next.fetch_add(1u, std::memory_order_relaxed) % (unsigned)kUmmaSchedSlots);
+static int umma_sched_slot(cudaStream_t stream) {
+  static std::atomic<unsigned> next{0}, next_captured{0};
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) {
+    (void)cudaGetLastError();  // (the launch on this stream reports any real fault)
+    cs = cudaStreamCaptureStatusNone;
+  }
+  if (cs == cudaStreamCaptureStatusActive)
+    return kUmmaSchedSlots - kUmmaSchedCaptured +
+           (int)(next_captured.fetch_add(1u, std::memory_order_relaxed) % (unsigned)kUmmaSchedCaptured);
+  return (int)(next.fetch_add(1u, std::memory_order_relaxed) % (unsigned)(kUmmaSchedSlots - kUmmaSchedCaptured));
 }
 
 template <typename T, int D, int BS, bool GK>
@@ -939,7 +950,8 @@ static cudaError_t launch_prefill_umma(const PrefillArgs& a, cudaStream_t stream
   const int64_t items = tiles * a.num_seqs * a.num_kv_heads;
   if (items > 0x7fffffffll - 1024) return cudaErrorInvalidValue;
   const int ctas = umma_persistent_ctas(dev, items);
-  kern<<<ctas, kUmmaThreads, UG::SMEM, stream>>>(a, maps, (int)tiles, (int)a.num_seqs, umma_sched_slot());
+  const int slot = umma_sched_slot(stream);  // (runtime queries stay outside the launch statement)
+  kern<<<ctas, kUmmaThreads, UG::SMEM, stream>>>(a, maps, (int)tiles, (int)a.num_seqs, slot);
   count_launch();
   return cudaGetLastError();
 }
@@ -1024,7 +1036,8 @@ static cudaError_t launch_cascade_umma(const PrefillArgs& a, int prefix_parts, c
   if (items <= 0) return cudaSuccess;
   if (items > 0x7fffffffll - 1024) return cudaErrorInvalidValue;
   const int ctas = umma_persistent_ctas(dev, items);
-  kern<<<ctas, kUmmaThreads, UG::SMEM, stream>>>(a, maps, (int)tiles, prefix_parts, umma_sched_slot());
+  const int slot = umma_sched_slot(stream);
+  kern<<<ctas, kUmmaThreads, UG::SMEM, stream>>>(a, maps, (int)tiles, prefix_parts, slot);
   count_launch();
   return cudaGetLastError();
 }
