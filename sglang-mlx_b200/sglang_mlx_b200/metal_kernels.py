@@ -242,11 +242,12 @@ def cascade_partitions(num_seqs: int, num_heads: int, num_kv_heads: int, max_seq
                        block_size: int = 16, sm_count: int = 148) -> tuple[int, int]:
     """(prefix_partition_size, partition_size) for paged_attention_cascade.
 
-    The prefix kernel's grid is (64-row tiles of the B*G query rows) x (prefix
-    chunks) x (kv heads); chunks are sized for at most two CTAs per SM (one
-    wave, which leaves the tail partitions room to run beside it).  The
-    tokens after the prefix form one partition when there are at most 1024 of
-    them, else 1024-token partitions."""
+    Prefix chunks are sized so that (64-row tiles of the B*G query rows) x
+    (chunks) x (kv heads) is at most two per SM: one wave of the mma.sync
+    prefix kernel, and at most one 128-row work item per SM for the tcgen05
+    prefix kernel, which leaves the tail partitions room to run beside it.
+    The tokens after the prefix form one partition when there are at most
+    1024 of them, else 1024-token partitions."""
     unit = 32 * block_size // math.gcd(32, block_size)
     tiles = -(-num_seqs * (num_heads // num_kv_heads) // 64)
     chunks = max(1, 2 * sm_count // max(1, tiles * num_kv_heads))

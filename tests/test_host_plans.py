@@ -1,0 +1,29 @@
+"""Host-side planning helpers of the Python shim (no GPU)."""
+import math
+
+from sglang_mlx_b200 import metal_kernels as mk
+
+
+def test_cascade_partitions_config4():
+    # 64 sequences, 64 / 8 heads, a 2048-token shared prefix and 256 tail tokens, block size 16:
+    # 8 tiles of 64 rows x 8 kv heads -> 4 prefix chunks of 512 (one wave), one 256-token tail partition
+    assert mk.cascade_partitions(64, 64, 8, 2304, 2048, 16) == (512, 256)
+
+
+def test_cascade_partitions_units_and_bounds():
+    for bs in (8, 16, 32):
+        unit = 32 * bs // math.gcd(32, bs)
+        for B, Hq, Hkv, prefix, tail in [(1, 8, 8, 100, 0), (3, 28, 4, 4096, 5000), (512, 32, 8, 64, 17),
+                                         (7, 16, 1, 33, 1024), (7, 16, 1, 33, 1025)]:
+            pp, pt = mk.cascade_partitions(B, Hq, Hkv, prefix + tail, prefix, bs)
+            assert pp % unit == 0 and pp >= unit and pp >= -(-prefix // max(1, 2 * 148))
+            assert pt % unit == 0 and pt >= unit
+            if tail > 1024:
+                assert pt == 1024
+            else:
+                assert pt >= tail
+            tiles = -(-B * (Hq // Hkv) // 64)
+            chunks = -(-prefix // pp)
+            # one wave of the prefix kernel (unless one chunk per kv head and tile already exceeds it)
+            assert chunks * tiles * Hkv <= max(2 * 148, tiles * Hkv)
+
