@@ -1044,7 +1044,8 @@ static cudaError_t launch_cascade_umma(const PrefillArgs& a, int prefix_parts, c
 
 // The prefix of a shared-prefix decode on the tensor cores' own pipeline when
 // the cache suits the gathered-K tcgen05 kernel (dense paged layout, block size
-// 32, head size 64 / 128, partial buffers of 16-byte rows);
+// 16 or 32, head size 64 / 128, prefix and chunks in whole blocks, partial
+// buffers of 16-byte rows);
 // cudaErrorNotSupported otherwise (the caller then runs the mma.sync prefix
 // kernel).
 static cudaError_t launch_cascade_prefix_umma(const DecodeParams& p, const DecodeArgs& da, cudaStream_t stream) {
