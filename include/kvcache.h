@@ -275,11 +275,17 @@ int kvc_swap_blocks(const kvc_dltensor* src, kvc_dltensor* dst, const kvc_dltens
  * V [num_blocks, H, D, bs]; a value is stored as encode(x / scale) and reads
  * back as decode(code) * scale, with one scale for K and one for V.
  * fp8_format 0 = E4M3 as float8.metal defines it (all-ones exponent kept for
- * Inf/NaN, largest finite 240), 1 = E5M2.  Encoding rounds to nearest even,
- * saturates to +-Inf past the largest finite value and underflows gradually
- * (the behaviour float8.metal:65-68 states; its code sends exponents past the
- * last finite one down the subnormal branch and drops a subnormal's carry into
- * the smallest normal, which this encoder does not). */
+ * Inf/NaN, largest finite 240), 1 = E5M2.  Encoding is bit-exact with the
+ * reference's encoder code (float8.metal:69-118): round to nearest even in the
+ * normal range (a carry past the last finite exponent gives +-Inf), gradual
+ * underflow rounded half up, values past the last finite exponent sent down
+ * the subnormal branch (E4M3: 256 <= |x| < 2^14 keep the low bits of that
+ * shift; 300 encodes as 0) and a subnormal's carry into the smallest normal
+ * dropped.  Where that code's shift count is negative (undefined in C++ and
+ * MSL: E4M3 |x| >= 2^14, E5M2 |x| >= 2^16) the code is +-Inf.
+ * fp8_format 2 = E4M3-sat and 3 = E5M2-sat encode with the behaviour the
+ * reference's comment states instead (float8.metal:65-68): +-Inf past the
+ * largest finite value and the carry kept; they decode like 0 and 1. */
 
 /* reshape_and_cache into one-byte caches; key/value f32/f16/bf16, head_size a
  * multiple of 16, slot < 0 skips the token. */
@@ -332,6 +338,9 @@ int kvc_device_synchronize(void);
 int kvc_event_create(void** event);
 int kvc_event_destroy(void* event);
 int kvc_event_record(void* event, void* stream);
+/* Work queued on `stream` after this call waits for `event`'s recorded work
+ * (overlapping host copies on one stream with compute on another). */
+int kvc_stream_wait_event(void* stream, void* event);
 int kvc_event_synchronize(void* event);
 int kvc_event_elapsed_ms(void* start, void* end, float* ms);
 /* Writes `bytes` of garbage over a device buffer to evict it from L2. */

@@ -115,12 +115,24 @@ def pool_fetch(k_buffer, v_buffer, indices):
 # ---------------------------------------------------------------------------
 # FP8 codecs — float8.metal:13-125 (used by convert_fp8.metal:13-80)
 # ---------------------------------------------------------------------------
+FP8_FORMATS = ("e4m3", "e5m2", "e4m3-sat", "e5m2-sat")
+
+
+def _fp8_layout(fmt: str):
+    """(exponent bits, mantissa bits, bias, saturating) of an FP8 format name."""
+    if fmt not in FP8_FORMATS:
+        raise ValueError(f"unknown FP8 format {fmt!r}")
+    eb, mb, bias = (4, 3, 7) if fmt.startswith("e4m3") else (5, 2, 15)
+    return eb, mb, bias, fmt.endswith("-sat")
+
+
 def fp8_to_float(v, fmt: str = "e4m3"):
-    """Decodes uint8 codes (float8.metal:13-63).  Both formats keep the
+    """Decodes uint8 codes (float8.metal:14-63).  Both formats keep the
     all-ones exponent for Inf (mantissa 0) and NaN, IEEE style: E4M3's largest
-    finite value is 240 here, not OCP E4M3FN's 448."""
+    finite value is 240 here, not OCP E4M3FN's 448.  The "-sat" formats decode
+    the same way."""
+    eb, mb, bias, _ = _fp8_layout(fmt)
     v = np.asarray(v, dtype=np.uint8).astype(np.int64)
-    eb, mb, bias = (4, 3, 7) if fmt == "e4m3" else (5, 2, 15)
     s = v >> 7
     e = (v >> mb) & ((1 << eb) - 1)
     m = v & ((1 << mb) - 1)
@@ -133,15 +145,24 @@ def fp8_to_float(v, fmt: str = "e4m3"):
 
 
 def float_to_fp8(f, fmt: str = "e4m3"):
-    """Encodes float32 values with the behaviour float8.metal:65-68 states:
-    round to nearest even in the normal range, saturation to Inf above the
-    last finite exponent, NaN kept, gradual underflow (the shifted mantissa
-    rounded half up, as :110-117 does).  Two departures from the code of
-    :69-118, both outside its stated behaviour: values whose exponent is past
-    the last finite one go down its subnormal branch there (garbage codes)
-    and are saturated to Inf here; a subnormal that rounds up to the smallest
-    normal keeps the carry here (the code masks it away and returns zero)."""
-    eb, mb, bias = (4, 3, 7) if fmt == "e4m3" else (5, 2, 15)
+    """Encodes float32 values as float8.metal:69-118 (detail::fp32_to_fp8)
+    does, step for step:
+      * NaN keeps its sign with mantissa 1, +-Inf the all-ones exponent (:75-79);
+      * biased FP8 exponent in [1, last finite]: round to nearest even, a
+        mantissa carry past the last finite exponent gives +-Inf (:85-103);
+      * below 2^(1 - bias - mantissa bits): +-0 (:106-107);
+      * otherwise the subnormal branch (:110-116): the mantissa with its
+        implicit 1 shifted right by (1 - e) + (23 - mantissa bits), rounded half
+        up, of which only the mantissa bits are kept.  So a subnormal that rounds
+        up to the smallest normal becomes +-0, and values past the last finite
+        exponent (E4M3: 256 <= |x| < 2^14) get the low bits of that shift ("300
+        encodes as 0").
+    Past that (E4M3 |x| >= 2^14, E5M2 |x| >= 2^16) the reference's shift count is
+    negative, undefined in C++ and MSL; there the result is +-Inf.
+    The "-sat" formats keep the encoder's stated behaviour (:65-68) instead:
+    +-Inf for every value past the last finite exponent, and a subnormal that
+    rounds up keeps its carry into the smallest normal."""
+    eb, mb, bias, sat = _fp8_layout(fmt)
     bits = np.ascontiguousarray(np.asarray(f, dtype=np.float32)).view(np.uint32).astype(np.int64)
     s = bits >> 31
     a = bits & 0x7FFFFFFF
@@ -160,10 +181,16 @@ def float_to_fp8(f, fmt: str = "e4m3"):
     ef_n = np.where(carry, ef + 1, ef)
     mant = np.where(carry, 0, mant)
     normal = np.where(ef_n > exp_max, (s << 7) | top, (s << 7) | (ef_n << mb) | (mant & ((1 << mb) - 1)))
-    rshift = np.clip((1 - ef) + (23 - mb), 1, 62)
-    rounded = ((0x800000 | m) + (np.int64(1) << (rshift - 1))) >> rshift
-    sub = np.where((ef < 1 - mb) | (rounded == 0), s << 7, (s << 7) | rounded)  # rounded <= 1 << mb
-    out = np.where(ef > exp_max, (s << 7) | top, np.where(ef >= 1, normal, sub))
+    rshift = (1 - ef) + (23 - mb)
+    rounded = ((0x800000 | m) + (np.int64(1) << np.clip(rshift - 1, 0, 62))) >> np.clip(rshift, 0, 62)
+    if sat:
+        branch = (s << 7) | rounded  # rounded <= 1 << mb: the carry lands in the exponent field
+        past = ef > exp_max
+    else:
+        branch = (s << 7) | (rounded & ((1 << mb) - 1))
+        past = rshift < 1
+    sub = np.where(ef < 1 - mb, s << 7, np.where(past, (s << 7) | top, branch))
+    out = np.where((ef >= 1) & (ef <= exp_max), normal, sub)
     nan_inf = a >= 0x7F800000
     out = np.where(nan_inf, (s << 7) | top | (a != 0x7F800000), out)
     return out.astype(np.uint8)

@@ -384,14 +384,26 @@ cudaError_t launch_gather_kv(const GatherArgs& a, cudaStream_t stream) {
 
 // ---------------------------------------------------------------------------
 // FP8 (one-byte) KV cache: quantising append and the elementwise codec.
-// Encoding follows the behaviour float8.metal:65-68 states: round to nearest
-// even in the normal range, +-Inf past the last finite exponent (E4M3: 240,
-// its all-ones exponent is kept for Inf/NaN), NaN kept, gradual underflow
-// with the shifted mantissa rounded half up (float8.metal:110-117).  Values
-// are quantised as code = encode(x / scale) and read back as decode(code) *
-// scale (convert_fp8.metal:28-36).
+// Values are quantised as code = encode(x / scale) and read back as
+// decode(code) * scale (convert_fp8.metal:28-36).
+//
+// encode_fp8<.., SAT = false> gives the code float8.metal:69-118
+// (detail::fp32_to_fp8) computes, step for step: NaN / Inf codes (:75-79);
+// round to nearest even in the normal range with a carry past the last finite
+// exponent going to +-Inf (:85-103); +-0 below the smallest subnormal
+// (:106-107); otherwise the subnormal branch (:110-116): the mantissa with its
+// implicit 1 shifted right by (1 - e) + (23 - MB), rounded half up, keeping
+// only the MB mantissa bits.  That branch also takes the values past the last
+// finite exponent (E4M3 256 <= |x| < 2^14) and drops a subnormal's carry into
+// the smallest normal, as the reference's code does.  Where the reference's
+// shift count turns negative (E4M3 |x| >= 2^14, E5M2 |x| >= 2^16; undefined
+// behaviour there) the code is +-Inf.
+// SAT = true (formats "e4m3-sat" / "e5m2-sat") follows the behaviour the
+// reference's comment states instead (:65-68): +-Inf for every value past the
+// last finite exponent, and a subnormal that rounds up carries into the
+// smallest normal.
 // ---------------------------------------------------------------------------
-template <int EB, int MB, int BIAS>
+template <int EB, int MB, int BIAS, bool SAT>
 __device__ __forceinline__ uint8_t encode_fp8(float f) {
   const uint32_t bits = __float_as_uint(f);
   const uint32_t s = (bits >> 31) << 7;
@@ -401,8 +413,7 @@ __device__ __forceinline__ uint8_t encode_fp8(float f) {
   const int exp_max = (1 << EB) - 2;
   const int ef = (int)((a >> 23) & 0xFFu) - 127 + BIAS;
   const uint32_t m = a & 0x7FFFFFu;
-  if (ef > exp_max) return (uint8_t)(s | top);
-  if (ef >= 1) {
+  if (ef >= 1 && ef <= exp_max) {
     constexpr int SH = 23 - MB;
     uint32_t mant = m >> SH;
     const uint32_t rnd = (m >> (SH - 1)) & 1u;
@@ -417,8 +428,9 @@ __device__ __forceinline__ uint8_t encode_fp8(float f) {
   }
   if (ef < 1 - MB) return (uint8_t)s;
   const int rshift = (1 - ef) + (23 - MB);
-  const uint32_t rounded = ((0x800000u | m) + (1u << (rshift - 1))) >> rshift;  // <= 1 << MB: carry kept
-  return (uint8_t)(s | rounded);
+  if (SAT ? ef > exp_max : rshift < 1) return (uint8_t)(s | top);
+  const uint32_t rounded = ((0x800000u | m) + (1u << (rshift - 1))) >> rshift;
+  return (uint8_t)(s | (SAT ? rounded : (rounded & ((1u << MB) - 1u))));  // SAT: rounded <= 1 << MB
 }
 
 template <int EB, int MB, int BIAS>
@@ -431,14 +443,15 @@ __device__ __forceinline__ float decode_fp8(uint32_t c) {
   return (c & 0x80u) ? -v : v;
 }
 
+// FMT: 0 E4M3, 1 E5M2 (the reference's encoder), 2 E4M3-sat, 3 E5M2-sat.
 template <int FMT>
 __device__ __forceinline__ uint8_t fp8_encode(float f) {
-  if constexpr (FMT == 0) return encode_fp8<4, 3, 7>(f);
-  else return encode_fp8<5, 2, 15>(f);
+  if constexpr (FMT == 0 || FMT == 2) return encode_fp8<4, 3, 7, FMT == 2>(f);
+  else return encode_fp8<5, 2, 15, FMT == 3>(f);
 }
 template <int FMT>
 __device__ __forceinline__ float fp8_decode(uint32_t c) {
-  if constexpr (FMT == 0) return decode_fp8<4, 3, 7>(c);
+  if constexpr (FMT == 0 || FMT == 2) return decode_fp8<4, 3, 7>(c);
   else return decode_fp8<5, 2, 15>(c);
 }
 
@@ -482,8 +495,12 @@ static cudaError_t launch_fp8_append_t(const ReshapeArgs& a, cudaStream_t stream
   const int64_t total = a.num_tokens * a.num_heads * (a.head_size / 16);
   if (total == 0) return cudaSuccess;
   const unsigned grid = (unsigned)((total + 255) / 256);
-  if (a.fp8_format == 1) reshape_and_cache_fp8_kernel<KV_T, 1><<<grid, 256, 0, stream>>>(a);
-  else reshape_and_cache_fp8_kernel<KV_T, 0><<<grid, 256, 0, stream>>>(a);
+  switch (a.fp8_format) {
+    case 1: reshape_and_cache_fp8_kernel<KV_T, 1><<<grid, 256, 0, stream>>>(a); break;
+    case 2: reshape_and_cache_fp8_kernel<KV_T, 2><<<grid, 256, 0, stream>>>(a); break;
+    case 3: reshape_and_cache_fp8_kernel<KV_T, 3><<<grid, 256, 0, stream>>>(a); break;
+    default: reshape_and_cache_fp8_kernel<KV_T, 0><<<grid, 256, 0, stream>>>(a); break;
+  }
   count_launch();
   return cudaGetLastError();
 }
@@ -516,12 +533,14 @@ static cudaError_t launch_convert_t(const void* src, void* dst, float scale, int
   if (n == 0) return cudaSuccess;
   const int64_t want = (n + 255) / 256;
   const unsigned grid = (unsigned)(want < 65535 * 8 ? want : 65535 * 8);
-  if (fmt == 1)
-    convert_fp8_kernel<SRC, DST, 1><<<grid, 256, 0, stream>>>(static_cast<const SRC*>(src), static_cast<DST*>(dst),
-                                                              scale, n);
-  else
-    convert_fp8_kernel<SRC, DST, 0><<<grid, 256, 0, stream>>>(static_cast<const SRC*>(src), static_cast<DST*>(dst),
-                                                              scale, n);
+  const SRC* s = static_cast<const SRC*>(src);
+  DST* d = static_cast<DST*>(dst);
+  switch (fmt) {
+    case 1: convert_fp8_kernel<SRC, DST, 1><<<grid, 256, 0, stream>>>(s, d, scale, n); break;
+    case 2: convert_fp8_kernel<SRC, DST, 2><<<grid, 256, 0, stream>>>(s, d, scale, n); break;
+    case 3: convert_fp8_kernel<SRC, DST, 3><<<grid, 256, 0, stream>>>(s, d, scale, n); break;
+    default: convert_fp8_kernel<SRC, DST, 0><<<grid, 256, 0, stream>>>(s, d, scale, n); break;
+  }
   count_launch();
   return cudaGetLastError();
 }

@@ -1303,7 +1303,7 @@ static cudaError_t launch_mma_fp8(const DecodeParams& p, int block_size, cudaStr
 template <typename T>
 static cudaError_t launch_mma_t(const DecodeParams& p, const DecodeArgs& a, cudaStream_t stream) {
   if (a.cache_type == ElemType::U8) {
-    const bool e5m2 = a.fp8_format == 1;
+    const bool e5m2 = a.fp8_format == 1 || a.fp8_format == 3;  // the -sat formats decode alike
     if (a.head_size == 128)
       return e5m2 ? launch_mma_fp8<T, 128, kFp8E5M2>(p, a.block_size, stream)
                   : launch_mma_fp8<T, 128, kFp8E4M3>(p, a.block_size, stream);

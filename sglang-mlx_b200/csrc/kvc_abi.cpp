@@ -978,7 +978,8 @@ int kvc_gather_kv(kvc_dltensor* k_out, kvc_dltensor* v_out, const kvc_dltensor* 
 static int check_fp8_args(float k_scale, float v_scale, int fp8_format) {
   if (!(k_scale > 0.f) || !(v_scale > 0.f) || !std::isfinite(k_scale) || !std::isfinite(v_scale))
     return fail(KVC_EINVAL, "k_scale and v_scale must be positive and finite");
-  if (fp8_format != 0 && fp8_format != 1) return fail(KVC_EINVAL, "fp8_format must be 0 (e4m3) or 1 (e5m2)");
+  if (fp8_format < 0 || fp8_format > 3)
+    return fail(KVC_EINVAL, "fp8_format must be 0 (e4m3), 1 (e5m2), 2 (e4m3-sat) or 3 (e5m2-sat)");
   return KVC_OK;
 }
 
@@ -1187,6 +1188,11 @@ int kvc_event_destroy(void* event) {
 int kvc_event_record(void* event, void* stream) {
   cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(event), static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaEventRecord");
+}
+
+int kvc_stream_wait_event(void* stream, void* event) {
+  cudaError_t e = cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), static_cast<cudaEvent_t>(event), 0);
+  return e == cudaSuccess ? KVC_OK : cuda_fail(e, "cudaStreamWaitEvent");
 }
 
 int kvc_event_synchronize(void* event) {

@@ -93,7 +93,7 @@ struct DecodeArgs {
   bool flash;                                 // token-major caches ([nb, bs, H, D] / [slots, H, D])
   int prefix_len, prefix_parts, prefix_part_size;  // shared-prefix decode (0 = off)
   float k_scale, v_scale;                     // one-byte (FP8) caches: value = code * scale
-  int fp8_format;                             // 0 = E4M3, 1 = E5M2
+  int fp8_format;                             // 0 E4M3, 1 E5M2, 2 E4M3-sat, 3 E5M2-sat
   int64_t table_stride;                       // elements
   int partition_size;                         // tokens per partition (split-K)
   int num_partitions;                         // 1 = single pass
@@ -144,7 +144,7 @@ struct ReshapeArgs {
   int64_t key_tok_stride, key_head_stride;      // elements
   int64_t value_tok_stride, value_head_stride;  // elements
   float k_scale, v_scale;                       // one-byte caches: code = encode(x / scale)
-  int fp8_format;                               // 0 = E4M3, 1 = E5M2
+  int fp8_format;                               // 0 E4M3, 1 E5M2, 2 E4M3-sat, 3 E5M2-sat
   int64_t kc_block_stride, kc_head_stride;      // vLLM: [nb, H, D/x, bs, x]; flash: [nb, bs, H, D]
   int64_t vc_block_stride, vc_head_stride;
   int64_t kc_tok_stride, vc_tok_stride;         // flash layout only

@@ -414,7 +414,19 @@ def _mapping(block_mapping):
     return np.ascontiguousarray(np.asarray(block_mapping, dtype=np.int64))
 
 
-_FP8 = {"e4m3": 0, "e5m2": 1}
+# FP8 formats.  "e4m3" / "e5m2" encode exactly as the reference's float8.metal
+# code does (values past E4M3's last finite exponent go down its subnormal
+# branch, a subnormal's carry into the smallest normal is dropped; +-Inf where
+# that code's shift is undefined).  "e4m3-sat" / "e5m2-sat" encode with the
+# behaviour that file's comment states instead: +-Inf past the largest finite
+# value and the carry kept.  Decoding is the same for both.
+_FP8 = {"e4m3": 0, "e5m2": 1, "e4m3-sat": 2, "e5m2-sat": 3}
+
+
+def _fp8_format(name: str) -> int:
+    if name not in _FP8:
+        raise ValueError(f"fp8_format must be one of {sorted(_FP8)}")
+    return _FP8[name]
 
 
 def reshape_and_cache_fp8(key, value, key_cache, value_cache, slot_mapping, k_scale: float = 1.0,
@@ -425,7 +437,7 @@ def reshape_and_cache_fp8(key, value, key_cache, value_cache, slot_mapping, k_sc
     ptrs = [as_dltensor(_dev(a), n) for a, n in ((key, "key"), (value, "value"), (key_cache, "key_cache"),
                                                  (value_cache, "value_cache"), (slot_mapping, "slot_mapping"))]
     _lib.check(_L.kvc_reshape_and_cache_fp8(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ptrs[4][0],
-                                            float(k_scale), float(v_scale), _FP8[fp8_format], _stream(stream)))
+                                            float(k_scale), float(v_scale), _fp8_format(fp8_format), _stream(stream)))
     return [key_cache, value_cache]
 
 
@@ -454,7 +466,7 @@ def paged_attention_fp8(query, key_cache, value_cache, block_tables, context_len
     rc = _L.kvc_paged_attention_fp8(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ptrs[4][0], ptrs[5][0],
                                     ptrs[6][0], ptrs[7][0], ptrs[8][0], int(num_kv_heads), float(scale),
                                     int(block_size), int(max_seq_len), ptrs[9][0], float(k_scale), float(v_scale),
-                                    _FP8[fp8_format], int(partition_size), _stream(stream))
+                                    _fp8_format(fp8_format), int(partition_size), _stream(stream))
     _lib.check(rc)
     return out
 
@@ -465,7 +477,7 @@ def convert_fp8(dst, src, scale: float = 1.0, fp8_format: str = "e4m3", *, strea
     decode(code) * scale, rescale codes, or scale floats).  Returns dst."""
     d, dk = as_dltensor(_dev(dst), "dst")
     s, sk = as_dltensor(_dev(src), "src")
-    _lib.check(_L.kvc_convert_fp8(d, s, float(scale), _FP8[fp8_format], _stream(stream)))
+    _lib.check(_L.kvc_convert_fp8(d, s, float(scale), _fp8_format(fp8_format), _stream(stream)))
     del dk, sk
     return dst
 

@@ -1,7 +1,7 @@
 """Generates tests/golden/golden.npz from the reference implementation itself.
 
 Run in a container where the reference checkout is present:
-    python tests/golden/make_golden.py [--reference PATH]
+    python tests/golden/make_golden.py --reference PATH   (or SGLANG_MLX_REFERENCE=PATH)
 
 What it runs (all reference code, unmodified, imported from the checkout):
   * `ref_reshape_and_cache` and `ref_paged_attention`, the NumPy oracles of
@@ -116,9 +116,12 @@ def run_pool_case(mp, out: dict) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("SGLANG_MLX_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("SGLANG_MLX_REFERENCE"),
+                    help="path of the sglang-mlx checkout (or set SGLANG_MLX_REFERENCE)")
     ap.add_argument("--out", default=os.path.join(HERE, "golden.npz"))
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference PATH or set SGLANG_MLX_REFERENCE to the sglang-mlx checkout")
     kt, mp = load_reference(args.reference)
     out: dict = {}
     print("reference kernel oracles:", flush=True)

@@ -1,10 +1,14 @@
-"""GPU tests of the one-byte (FP8) KV cache: the quantising append and the
+"""GPU tests of the one-byte (FP8) KV cache: the codec bit-exact against the
+reference's own float8.metal functions (vectors and an exhaustive 2^32 sweep
+digest from tests/golden/make_fp8_golden.py), the quantising append and the
 elementwise codec bit-exact against oracle/kv_oracle.py's restatement of
 float8.metal / convert_fp8.metal, and the decode against the float64 decode
 of the dequantised caches, over formats, query dtypes, head sizes, block
 sizes, group sizes, split-K, ALiBi and the edge rules."""
 
+import hashlib
 import math
+import os
 
 import numpy as np
 import pytest
@@ -59,7 +63,7 @@ def ref_decode(c, kc, vc, alibi=None, max_seq_len=None):
                                          c["v_scale"], c["fmt"], alibi)
 
 
-@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2", "e4m3-sat", "e5m2-sat"])
 @pytest.mark.parametrize("kv_dtype", ["float32", "float16", "bfloat16"])
 def test_append_is_bit_exact(gpu, fmt, kv_dtype):
     c = fp8_case(6000, "bfloat16", 3, 8, 2, 128, 16, [5, 77, 300], fmt)
@@ -171,3 +175,68 @@ def test_config2_shape(gpu):
     ref = kv_oracle.paged_attention_fp8(c["q"][pick], kc, vc, c["block_tables"][pick], c["context_lens"][pick], 8,
                                         c["scale"], 16, c["max_seq_len"], c["k_scale"], c["v_scale"], "e4m3")
     assert_close(out[pick], ref, ATOL_NS, RTOL_NS, "oracle subset")
+
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "fp8_ref.npz")
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_codec_matches_reference_vectors(gpu, fmt):
+    """The device codec against the reference's float8.metal functions run on
+    the host: encode of every bfloat16 pattern, every float16 value and 2^17
+    seeded float32 patterns (kvc_convert_fp8 with scale 1), decode of all 256
+    codes; the "-sat" format against the oracle's restatement of it."""
+    import make_fp8_golden as g
+
+    ref = np.load(GOLDEN)
+    x = g.enc_inputs()
+    assert hashlib.sha256(x.tobytes()).hexdigest() == str(ref["enc_inputs_sha256"])
+    f = x.view(np.float32)
+    src = DeviceArray.from_numpy(f)
+    for name, want in ((fmt, ref[f"enc_{fmt}"]), (fmt + "-sat", kv_oracle.float_to_fp8(f, fmt + "-sat"))):
+        codes = DeviceArray.zeros(f.shape, "uint8")
+        mk.convert_fp8(codes, src, 1.0, name)
+        got = codes.to_numpy()
+        nan_in = np.isnan(f)
+        # NaN inputs: a NaN code either way (the division by the scale may drop a NaN's sign)
+        top = 0x78 if fmt == "e4m3" else 0x7C
+        assert ((got[nan_in] & top) == top).all() and ((got[nan_in] & ~np.uint8(0x80 | top)) != 0).all()
+        np.testing.assert_array_equal(got[~nan_in], want[~nan_in], err_msg=name)
+    dec = DeviceArray.empty((256,), "float32")
+    mk.convert_fp8(dec, DeviceArray.from_numpy(np.arange(256, dtype=np.uint8)), 1.0, fmt)
+    got = dec.to_numpy()
+    want = ref[f"dec_{fmt}"].view(np.float32)
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    np.testing.assert_array_equal(got[~np.isnan(got)], want[~np.isnan(want)])
+    assert gpu.get_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_encoder_exhaustive_sweep(gpu, fmt):
+    """The device encoder on every float32 bit pattern 0 .. 2^32 - 1, hashed in
+    order: equal to the SHA-256 of the reference encoder's codes (+-Inf where
+    that code's shift is undefined).  NaN inputs are checked to give NaN codes
+    and then hashed as the reference codes them (sign | all-ones | 1)."""
+    torch = pytest.importorskip("torch")
+    ref = np.load(GOLDEN)
+    dev = torch.device("cuda", 0)
+    top = 0x78 if fmt == "e4m3" else 0x7C
+    n = 1 << 26
+    h = hashlib.sha256()
+    codes = DeviceArray.zeros((n,), "uint8")
+    codes_t = torch.from_dlpack(codes)
+    starts = list(range(0, 1 << 31, n)) + list(range(-(1 << 31), 0, n))  # bit patterns 0 .. 2^32 - 1 in order
+    for start in starts:
+        bits = torch.arange(start, start + n, dtype=torch.int32, device=dev)
+        x = bits.view(torch.float32)
+        mk.convert_fp8(codes, x, 1.0, fmt)
+        c = codes_t.to(torch.int32)
+        nan_in = torch.isnan(x)
+        bad = nan_in & (((c & top) != top) | ((c & ~(0x80 | top)) == 0))
+        assert not bool(bad.any()), f"non-NaN code for a NaN input near pattern {start & 0xFFFFFFFF:#x}"
+        want_nan = ((bits >> 31) & 1) * 0x80 | top | 1
+        c = torch.where(nan_in, want_nan, c)
+        h.update(c.to(torch.uint8).cpu().numpy().tobytes())
+    torch.cuda.synchronize()
+    assert h.hexdigest() == str(ref[f"sweep_sha256_{fmt}"])
+    assert gpu.get_status(clear=True) == 0

@@ -2,11 +2,16 @@
 made by tests/golden/make_golden.py from the reference's NumPy oracles and its
 MHATokenPool).  No GPU."""
 
+import hashlib
+import os
+
 import numpy as np
 import pytest
 
 import cases
 from oracle import c_oracle, kv_oracle
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 REF_CASES = {
     "ref_setup": cases.ref_setup_data,
@@ -191,7 +196,9 @@ def test_fp8_codec_restatement():
     """float8.metal's codecs restated in kv_oracle: checked against torch's OCP
     formats where the formats coincide (every E5M2 code; E4M3 codes below the
     all-ones exponent, which the reference keeps for Inf/NaN) and on known
-    answers of the reference's IEEE-style E4M3 (max finite 240, Inf above)."""
+    answers of the reference's IEEE-style E4M3 (max finite 240) and of its
+    encoder's code path (values past 240 through the subnormal branch, a
+    subnormal's carry dropped), beside the "-sat" formats' stated behaviour."""
     import torch
 
     codes = np.arange(256, dtype=np.uint8)
@@ -205,19 +212,53 @@ def test_fp8_codec_restatement():
     assert np.isposinf(d4[0x78]) and np.isneginf(d4[0xF8]) and np.isnan(d4[0x79])
     for fmt, dec in (("e4m3", d4), ("e5m2", d5)):  # every finite code survives encode(decode(c))
         fin = np.isfinite(dec)
-        assert np.array_equal(kv_oracle.float_to_fp8(dec[fin], fmt), codes[fin])
+        for f in (fmt, fmt + "-sat"):
+            assert np.array_equal(kv_oracle.float_to_fp8(dec[fin], f), codes[fin])
     rng = np.random.default_rng(0)
     x = (rng.standard_normal(50000) * 20).astype(np.float32)
     x = x[(np.abs(x) > 2.0 ** -5) & (np.abs(x) < 240)]  # normal range: round to nearest even, as torch
-    assert np.array_equal(kv_oracle.float_to_fp8(x, "e4m3"),
-                          torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy())
+    for f in ("e4m3", "e4m3-sat"):
+        assert np.array_equal(kv_oracle.float_to_fp8(x, f),
+                              torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy())
     enc = lambda v, f="e4m3": int(kv_oracle.float_to_fp8(np.array([v], np.float32), f)[0])
     assert enc(1.0) == 0x38 and enc(240.0) == 0x77 and enc(-240.0) == 0xF7
-    assert enc(300.0) == 0x78 and enc(np.inf) == 0x78 and enc(np.nan) == 0x79  # saturates to Inf / keeps NaN
+    assert enc(np.inf) == 0x78 and enc(np.nan) == 0x79 and enc(-np.nan) == 0xF9
     assert enc(2.0 ** -9) == 0x01 and enc(-0.0) == 0x80 and enc(2.0 ** -11) == 0x00
-    assert enc(2.0 ** -6 * (1 - 2.0 ** -10)) == 0x08  # subnormal rounding up into the smallest normal
-    assert enc(1e6) == 0x78 and enc(-1e6) == 0xF8 and enc(250.0) == 0x78  # past 240: +-Inf
-    assert enc(57344.0, "e5m2") == 0x7B and enc(65536.0, "e5m2") == 0x7C
+    assert enc(250.0) == 0x78  # rounds past 240 in the normal path: +-Inf in every format
+    # the reference's encoder code: 300 goes down the subnormal branch and keeps its low bits (0)
+    assert enc(300.0) == 0x00 and enc(300.0, "e4m3-sat") == 0x78
+    # a subnormal rounding up to the smallest normal: carry dropped (+0) / kept (0x08)
+    assert enc(2.0 ** -6 * (1 - 2.0 ** -10)) == 0x00 and enc(2.0 ** -6 * (1 - 2.0 ** -10), "e4m3-sat") == 0x08
+    # past the reference's defined range (negative shift count): +-Inf in every format
+    assert enc(1e6) == 0x78 and enc(-1e6) == 0xF8 and enc(1e6, "e4m3-sat") == 0x78
+    assert enc(57344.0, "e5m2") == 0x7B and enc(65536.0, "e5m2") == 0x7C and enc(65536.0, "e5m2-sat") == 0x7C
+
+
+def test_fp8_codec_matches_reference_vectors():
+    """kv_oracle's FP8 codec against the reference's own float8.metal functions,
+    compiled as host C++ (tests/golden/make_fp8_golden.py): the decode of all
+    256 codes, and the encode of every bfloat16 pattern, every float16 value
+    and 2^17 seeded float32 patterns, bit for bit in both formats.  The "-sat"
+    formats differ from the reference only on values past the last finite
+    exponent and on subnormals that round up to the smallest normal."""
+    import make_fp8_golden as g
+
+    ref = np.load(os.path.join(ROOT, "tests", "golden", "fp8_ref.npz"))
+    x = g.enc_inputs()
+    assert hashlib.sha256(x.tobytes()).hexdigest() == str(ref["enc_inputs_sha256"])
+    f = x.view(np.float32)
+    codes = np.arange(256, dtype=np.uint8)
+    for fmt, finite_max, smallest_normal in (("e4m3", 240.0, 2.0 ** -6), ("e5m2", 57344.0, 2.0 ** -14)):
+        got = kv_oracle.fp8_to_float(codes, fmt)
+        want = ref[f"dec_{fmt}"].view(np.float32)
+        assert np.array_equal(np.isnan(got), np.isnan(want))
+        assert np.array_equal(got[~np.isnan(got)].view(np.uint32), want[~np.isnan(want)].view(np.uint32))
+        np.testing.assert_array_equal(kv_oracle.float_to_fp8(f, fmt), ref[f"enc_{fmt}"])
+        sat = kv_oracle.float_to_fp8(f, fmt + "-sat")
+        differ = sat != ref[f"enc_{fmt}"]
+        a = np.abs(f[differ])
+        assert ((a > finite_max) | (a < smallest_normal)).all()
+        assert differ.any()
 
 
 # ---- prefill / extend attention oracle --------------------------------------------
