@@ -90,6 +90,7 @@ SIGNATURES: dict[str, tuple] = {
     "kvc_event_create": (_i, [ctypes.POINTER(_p)]),
     "kvc_event_destroy": (_i, [_p]),
     "kvc_event_record": (_i, [_p, _p]),
+    "kvc_stream_wait_event": (_i, [_p, _p]),
     "kvc_event_synchronize": (_i, [_p]),
     "kvc_event_elapsed_ms": (_i, [_p, _p, ctypes.POINTER(_f)]),
     "kvc_l2_flush": (_i, [_p, _sz, _p]),

@@ -367,6 +367,10 @@ class Stream:
     def synchronize(self) -> None:
         _lib.check(_lib_ref.kvc_stream_synchronize(ctypes.c_void_p(self.handle)))
 
+    def wait(self, event: "Event") -> None:
+        """Work queued on this stream from now on waits for `event`."""
+        _lib.check(_lib_ref.kvc_stream_wait_event(ctypes.c_void_p(self.handle), ctypes.c_void_p(event.handle)))
+
 
 class Graph:
     """A captured sequence of libkvcache work, replayed with one launch.
