@@ -6,7 +6,8 @@ bf16, 32 layers each with its own paged pool, batch 256, 32 q / 8 kv heads,
 head_dim 128, block_size 16, context lengths uniform in [512, 4096] (seeded),
 K/V ~ N(0, 1).  One step = for every layer, append one new token per sequence
 through reshape_and_cache, then the decode over context + 1 tokens.  A step
-emits 256 tokens (one per sequence).
+emits 256 tokens (one per sequence).  On one GPU the same JSON line also
+carries configs 3, 4 and 5 (`other_configs`), each timed the same way.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|4|5]
     python bench.py --impl reference ...     # CPU reference arm
@@ -24,6 +25,8 @@ Multi-GPU (torchrun, one process per GPU): the KV pool is sharded by KV head
 GPUs); block tables and lengths are replicated; no collective runs in the data
 path.  Total work is fixed, so scaling is strong.  Timing: CUDA events on the
 launching stream, barrier + synchronize around the timed region, max over ranks.
+After timing, every rank checks a sample of its own outputs against the CPU
+oracle (float64 gather + SDPA) and the run fails if any rank is off.
 
 Inputs are synthetic (seeded N(0,1)); torch fills the device caches
 (plumbing); every timed kernel is libkvcache's.
@@ -57,14 +60,12 @@ CONTEXT_DESC = {
     5: "lognormal(median 1500, sigma 1.0) clipped to [16, 32768] (seeded)",
 }
 
-# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one decode launch, from the ncu captures
-# summarised in profiles/ (config 2: captured at batch 64 and scaled by KV bytes to the full launch).
-TRAFFIC_PER_LAUNCH = {
-    2: (2.289e9 + 0.016e9, "profiles/paged_decode_mma_bs16_small.md (batch-64 capture scaled to batch 256)"),
-    3: (537.1e6 + 9.8e6, "profiles/paged_decode_mma_bs32_config3.md (partition kernel; reduce adds 8.6e6)"),
-}
+# ncu-measured DRAM traffic per decode launch (the profiles/ summaries name the commands)
+TRAFFIC_FILE = os.path.join(ROOT, "profiles", "dram_traffic_per_launch.json")
 
 L2_FLUSH_BYTES = 512 << 20  # > 4x the 126 MB L2
+
+ATOL, RTOL = 2e-3, 1e-2  # north-star tolerance of bf16 attention outputs
 
 
 def load_peaks():
@@ -74,6 +75,27 @@ def load_peaks():
             d = json.load(f)
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def load_traffic(config: int, kernel_key: str):
+    """(bytes per launch, description) of an ncu capture of this workload's decode, or None."""
+    try:
+        with open(TRAFFIC_FILE) as f:
+            d = json.load(f)
+    except (OSError, ValueError):
+        return None
+    e = d.get(f"config{config}/{kernel_key}")
+    if not e:
+        return None
+    return float(e["bytes_per_launch"]), e["how"]
+
+
+def host_threads() -> int:
+    """Host threads for the CPU legs: every core this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 def decode_bytes(tables, lens_after, hq, hkv, d, bs, shared: bool, s=2, s_kv=None):
@@ -100,7 +122,7 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.path = os.path.join("/tmp", f"kvc_clocks_{os.getpid()}.csv")
+        self.path = os.path.join("/tmp", f"kvc_clocks_{os.getpid()}_{index}.csv")
 
     def start(self):
         try:
@@ -152,49 +174,86 @@ def lscpu_model():
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline (oracle port: C + OpenMP, float64 gather + SDPA)
+# CPU legs: the reference's serving dataflow (gather the sequence's K/V token
+# rows out of the pool, then scaled-dot-product attention) restated on the host
 # ---------------------------------------------------------------------------
-def compact_sample(tables, lens_after, bs, n_seq):
-    """Block ids of the first n_seq sequences and tables renumbered onto them."""
-    nblk = [(-(-int(lens_after[b]) // bs)) for b in range(n_seq)]
-    blocks = np.concatenate([tables[b, :n] for b, n in zip(range(n_seq), nblk)]).astype(np.int64)
-    t2 = np.zeros((n_seq, max(nblk)), np.uint32)
-    o = 0
-    for i, n in enumerate(nblk):
-        t2[i, :n] = np.arange(o, o + n)
-        o += n
-    return blocks, t2
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    u = bits.astype(np.uint32)
+    np.left_shift(u, np.uint32(16), out=u)  # in place: a Python-int shift is far slower here
+    return u.view(np.float32)
 
 
-def time_oracle(q_bits, kc_bits, vc_bits, t2, lens, hkv, d, bs, budget_s=10.0, reps_min=1):
+def numpy_gather_sdpa(q_bits, kc_bits, vc_bits, tables, lens, hkv, scale, bs, threads):
+    """fp32 gather + SDPA of a batch, the dataflow of the reference's
+    gather-then-mx.fast.scaled_dot_product_attention path
+    (bench_paged_vs_gather.py:83-103; PooledKVCache.update_and_fetch + SDPA):
+    per sequence, its blocks' K/V token rows are gathered out of the paged
+    cache into token-major fp32 arrays, then softmax(q K^T * scale) V with the
+    GQA broadcast, as batched BLAS matmuls.  Sequences are spread over
+    `threads` worker threads (NumPy releases the GIL in the copies and BLAS
+    calls, which run single-threaded each)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from threadpoolctl import threadpool_limits
+
+    B, Hq, D = q_bits.shape
+    G = Hq // hkv
+    qf = bf16_bits_to_f32(q_bits)
+    out = np.empty((B, Hq, D), np.float32)
+
+    def rows(b0, b1):
+        for b in range(b0, b1):
+            C = int(lens[b])
+            nb = -(-C // bs)
+            blk = tables[b, :nb]
+            K = bf16_bits_to_f32(kc_bits[blk]).transpose(1, 0, 3, 2, 4).reshape(hkv, nb * bs, D)[:, :C]
+            V = bf16_bits_to_f32(vc_bits[blk]).transpose(1, 0, 3, 2).reshape(hkv, nb * bs, D)[:, :C]
+            s = np.matmul(qf[b].reshape(hkv, G, D), K.transpose(0, 2, 1))
+            s *= np.float32(scale)
+            s -= s.max(axis=-1, keepdims=True)
+            np.exp(s, out=s)
+            l_ = s.sum(axis=-1, keepdims=True)
+            out[b] = (np.matmul(s, V) / l_).reshape(Hq, D)
+
+    cuts = np.linspace(0, B, num=min(B, 4 * threads) + 1).astype(int)
+    with threadpool_limits(1), ThreadPoolExecutor(max_workers=threads) as ex:
+        list(ex.map(lambda i: rows(cuts[i], cuts[i + 1]), range(len(cuts) - 1)))
+    return out
+
+
+def c_float64_gather_sdpa(q_bits, kc_bits, vc_bits, tables, lens, hkv, scale, bs, threads):
+    """The C oracle (float64 gather + SDPA, OpenMP over sequences)."""
     from oracle import c_oracle
 
-    threads = c_oracle.num_threads()
-    reps, t0 = 0, time.perf_counter()
-    while True:
-        c_oracle.paged_attention(q_bits, "bfloat16", kc_bits, vc_bits, "bfloat16", t2, lens.astype(np.uint32), hkv,
-                                 1.0 / math.sqrt(d), int(t2.shape[1] * bs), threads=threads)
-        reps += 1
-        el = time.perf_counter() - t0
-        if (el > budget_s and reps >= reps_min) or reps >= 2000:
-            break
-    return el / reps, threads
+    return c_oracle.paged_attention(q_bits, "bfloat16", kc_bits, vc_bits, "bfloat16", tables,
+                                    np.asarray(lens).astype(np.uint32), hkv, scale, int(tables.shape[1] * bs),
+                                    threads=threads)
 
 
-def workload(args):
-    w = cases.baseline_workload(args.config, batch=args.batch or None)
+def mlx_probe():
+    """The reference's own CPU path needs MLX (mx.fast.scaled_dot_product_attention)."""
+    try:
+        import mlx.core  # noqa: F401
+        return "importable"
+    except Exception as e:  # noqa: BLE001
+        return f"not importable ({type(e).__name__})"
+
+
+def workload(args, config=None):
+    config = config or args.config
+    w = cases.baseline_workload(config, batch=args.batch or None)
     cfg = dict(w["cfg"])
-    if args.layers:
+    if args.layers and config == args.config:
         cfg["layers"] = args.layers
-    if args.layers or args.batch or args.kv_heads:
+    if (args.layers or args.batch or args.kv_heads) and config == args.config:
         cfg["name"] += f" (reduced: {cfg['layers']} layers, batch {cfg['batch']}, kv heads {args.kv_heads or cfg['hkv']})"
     return w, cfg
 
 
-def config_json(cfg, args, world, extra=None):
+def config_json(cfg, config, world, extra=None):
     d = {"workload": cfg["name"], "global_batch": cfg["batch"], "layers": cfg["layers"],
          "heads": f"{cfg['hq']}q/{cfg['hkv']}kv", "head_dim": cfg["d"], "block_size": cfg["bs"],
-         "context": CONTEXT_DESC[args.config], "parallelism": f"kv-head-shard{world}"}
+         "context": CONTEXT_DESC[config], "parallelism": f"kv-head-shard{world}"}
     if cfg.get("prefill_chunks"):
         d["prefill"] = f"{cfg['prefill_chunks']} chunks x {cfg['chunk']} tokens appended per step"
     if extra:
@@ -202,43 +261,75 @@ def config_json(cfg, args, world, extra=None):
     return d
 
 
+def random_bf16_bits(rng, shape, chunk=1 << 24):
+    """N(0, 1) values as bf16 bits, generated in chunks."""
+    out = np.empty(int(np.prod(shape)), np.uint16)
+    for o in range(0, out.size, chunk):
+        n = min(chunk, out.size - o)
+        out[o:o + n] = rng.standard_normal(n, dtype=np.float32).view(np.uint32) >> 16
+    return out.reshape(shape)
+
+
+def cpu_legs(cfg, w, threads, reps=1):
+    """Times both host legs over one full layer of the workload (all sequences):
+    (fp32 NumPy/BLAS seconds, float64 C seconds), means over `reps`."""
+    lens_after = w["lens"] + 1
+    bs, d, hkv, hq, B = cfg["bs"], cfg["d"], cfg["hkv"], cfg["hq"], cfg["batch"]
+    tables = np.ascontiguousarray(w["tables"])
+    rng = np.random.default_rng(99)
+    kc = random_bf16_bits(rng, (w["num_blocks"], hkv, d // 8, bs, 8))
+    vc = random_bf16_bits(rng, (w["num_blocks"], hkv, d, bs))
+    q = random_bf16_bits(rng, (B, hq, d))
+    scale = 1.0 / math.sqrt(d)
+    t_np, t_c = [], []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        numpy_gather_sdpa(q, kc, vc, tables, lens_after, hkv, scale, bs, threads)
+        t1 = time.perf_counter()
+        c_float64_gather_sdpa(q, kc, vc, tables, lens_after, hkv, scale, bs, threads)
+        t2 = time.perf_counter()
+        t_np.append(t1 - t0)
+        t_c.append(t2 - t1)
+    return float(np.mean(t_np)), float(np.mean(t_c))
+
+
+def cpu_baseline_entry(cfg, w, threads, reps):
+    """The faster of the two host legs as the baseline (tokens/s), the other beside it."""
+    L, B = cfg["layers"], cfg["batch"]
+    t_np, t_c = cpu_legs(cfg, w, threads, reps)
+    legs = {"numpy_fp32_blas": B / (t_np * L), "c_float64_openmp": B / (t_c * L)}
+    best = max(legs, key=legs.get)
+    what = {"numpy_fp32_blas": "fp32 NumPy/BLAS gather + SDPA", "c_float64_openmp": "float64 C gather + SDPA (OpenMP)"}
+    return {"value": legs[best], "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"all {B} sequences x 1 of {L} layers per rep ({reps} reps), scaled x{L}; the faster of two "
+                      f"restatements of the reference's gather-then-SDPA dataflow: {what[best]} "
+                      f"(legs: {', '.join(f'{k} {v:.3g}' for k, v in legs.items())} tokens/s); {lscpu_model()}",
+            "leg": best, "legs_tokens_per_s": legs}
+
+
 # ---------------------------------------------------------------------------
 # reference arm
 # ---------------------------------------------------------------------------
 def run_reference(args, rank, world):
-    """The reference's own CPU path is MLX (gather + mx.fast.scaled_dot_product_attention),
-    not installed here; the oracle port (same dataflow, float64, all host cores) runs
-    instead on a bounded sample of the same workload, scaled to the full step."""
+    """The reference's own CPU path is MLX's gather + mx.fast.scaled_dot_product_attention;
+    MLX is not installed on these hosts (probed: `mlx` below), so its dataflow is
+    restated twice, an fp32 NumPy/BLAS gather + SDPA and the float64 C port, both
+    on every host thread, each step one full layer of the workload (all
+    sequences) scaled to the step's layers; `value` is the faster leg."""
     if rank != 0:
         return
     w, cfg = workload(args)
-    lens_after = w["lens"] + 1
-    bs, d, hkv, hq = cfg["bs"], cfg["d"], cfg["hkv"], cfg["hq"]
-    n_seq = min(8, cfg["batch"])
-    blocks, t2 = compact_sample(w["tables"], lens_after, bs, n_seq)
-    rng = np.random.default_rng(99)
-
-    def rand_bits(shape):
-        return (rng.standard_normal(shape, dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
-
-    kc = rand_bits((len(blocks), hkv, d // 8, bs, 8))
-    vc = rand_bits((len(blocks), hkv, d, bs))
-    q = rand_bits((n_seq, hq, d))
-    scale_factor = (cfg["batch"] / n_seq) * cfg["layers"]
-    times, threads = [], 1
-    for i in range(args.warmup + args.steps):
-        el, threads = time_oracle(q, kc, vc, t2, lens_after[:n_seq], hkv, d, bs, budget_s=0.0)
-        if i >= args.warmup:
-            times.append(el)
-    step_s = float(np.mean(times)) * scale_factor
-    toks = cfg["batch"] / step_s
-    sample = (f"{n_seq} of {cfg['batch']} sequences x 1 of {cfg['layers']} layers per step, scaled x"
-              f"{scale_factor:g}; C oracle port (float64 gather+SDPA), {threads} threads, {lscpu_model()}")
+    B = cfg["batch"]
+    threads = host_threads()
+    if args.warmup:
+        cpu_legs(cfg, w, threads, 1)
+    entry = cpu_baseline_entry(cfg, w, threads, max(1, args.steps))
+    toks = entry["value"]
+    step_s = B / toks
     line = {"metric": METRIC, "value": toks, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
-            "config": config_json(cfg, args, world),
-            "cpu_baseline": {"value": toks, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "warmup": min(args.warmup, 1), "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
+            "config": config_json(cfg, args.config, world), "cpu_baseline": entry, "mlx": mlx_probe(),
             "e2e": {"value": toks, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -246,7 +337,50 @@ def run_reference(args, rank, world):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
-def run_ours(args, rank, world, local_rank):
+def check_outputs(torch, q_t, kc_t, vc_t, out, tables, lens_after, hkv, D, bs, mode, fmt=None):
+    """A sample of this rank's sequences (first, middle, last) of one layer
+    against the CPU oracle: float64 gather + SDPA over the rank's own caches.
+    Returns (ok, max |err|, rows checked)."""
+    from oracle import c_oracle, kv_oracle
+
+    B = len(lens_after)
+    rows = sorted({0, B // 2, B - 1})
+    dev = kc_t.device
+    got = out.to_numpy()[rows]
+    nb = [(-(-int(lens_after[b]) // bs)) for b in rows]
+    ids = np.concatenate([tables[b, :n] for b, n in zip(rows, nb)]).astype(np.int64)
+    t2 = np.zeros((len(rows), max(nb)), np.uint32)
+    o = 0
+    for i, n in enumerate(nb):
+        t2[i, :n] = np.arange(o, o + n)
+        o += n
+    idx = torch.from_numpy(ids).to(dev)
+    kg, vg = kc_t.index_select(0, idx), vc_t.index_select(0, idx)
+    qr = q_t.index_select(0, torch.tensor(rows, device=dev))
+    scale = 1.0 / math.sqrt(D)
+
+    def bits(t):
+        return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+    if mode == "fp8":
+        kq = kv_oracle.dequantize(kg.cpu().numpy(), 0.05, fmt)
+        vq = kv_oracle.dequantize(vg.cpu().numpy(), 0.05, fmt)
+        ref = kv_oracle.paged_attention_v1(bf16_bits_to_f32(bits(qr)), kq, vq, t2, lens_after[rows], hkv, scale, bs,
+                                           int(t2.shape[1] * bs))
+    else:
+        kb, vb = bits(kg), bits(vg)
+        if mode == "pool":  # token rows [n, H, D] = paged pages of one token
+            kb = kb.reshape(kb.shape[0], hkv, D // 8, 1, 8)
+            vb = vb.reshape(vb.shape[0], hkv, D, 1)
+        ref = c_oracle.paged_attention(bits(qr), "bfloat16", kb, vb, "bfloat16", t2, lens_after[rows], hkv, scale,
+                                       int(t2.shape[1] * bs))
+    ok, err, _ = kv_oracle.allclose_report(got, ref, ATOL, RTOL)
+    return bool(ok and np.isfinite(got).all()), float(err), len(rows)
+
+
+def measure_decode(args, config, rank, world, local_rank, top=True):
+    """Times `config` on this rank's share; returns the JSON line (rank 0) or None.
+    top=False (the other configs of a one-GPU run): no e2e, no CPU baseline."""
     import torch
 
     from sglang_mlx_b200 import _lib, sharding
@@ -254,13 +388,10 @@ def run_ours(args, rank, world, local_rank):
     from sglang_mlx_b200.device_array import DeviceArray, Event, Graph, HostBuffer, Stream
 
     dev = local_rank
-    _lib.set_device(dev)
-    torch.cuda.set_device(dev)
     tdev = torch.device("cuda", dev)
-
-    w, cfg = workload(args)
+    w, cfg = workload(args, config)
     L, B_all, HQ, HKV, D, BS = cfg["layers"], cfg["batch"], cfg["hq"], cfg["hkv"], cfg["d"], cfg["bs"]
-    if args.kv_heads:  # profiling: one rank's share of a head-sharded run, on one GPU
+    if args.kv_heads and top:  # profiling: one rank's share of a head-sharded run, on one GPU
         HQ, HKV = HQ * args.kv_heads // HKV, args.kv_heads
         cfg["hq"], cfg["hkv"] = HQ, HKV
     plan = sharding.plan(HQ, HKV, world, rank, w["lens"] + 1)
@@ -280,11 +411,11 @@ def run_ours(args, rank, world, local_rank):
         pre = np.concatenate([pre[c * chunk:(c + 1) * chunk] for c in mine]) if mine else pre[:0]
     slots = np.concatenate([pre, w["decode_slots"][plan.seqs]]).astype(np.int32)
     T_new = len(slots)
-    shared = args.config == 4
-    pool = args.layout == "pool"
-    fp8 = args.kv_dtype.startswith("fp8")
+    shared = config == 4
+    pool = args.layout == "pool" and top
+    fp8 = args.kv_dtype.startswith("fp8") and top
     fmt = args.kv_dtype[4:] if fp8 else None
-    if fp8 and (pool or args.decode == "cascade"):
+    if fp8 and (pool or args.decode in ("cascade", "planned")):
         raise SystemExit("--kv-dtype fp8 runs on the paged layout with the single-pass / split-K decode")
     if pool:
         # MHATokenPool layout: block b's tokens are slots b*BS+1 .. b*BS+BS (slot 0 is
@@ -305,10 +436,11 @@ def run_ours(args, rank, world, local_rank):
             v = torch.randn((num_blocks * BS + 1, hkv, D), generator=g, device=tdev, dtype=tdt)
         elif fp8:
             # finite codes only (exponent field below all-ones), random sign
-            top = 0x78 if fmt == "e4m3" else 0x7C
-            k = (torch.randint(0, top, (num_blocks, hkv, D // 16, BS, 16), generator=g, device=tdev, dtype=torch.int32)
+            top_code = 0x78 if fmt == "e4m3" else 0x7C
+            k = (torch.randint(0, top_code, (num_blocks, hkv, D // 16, BS, 16), generator=g, device=tdev,
+                               dtype=torch.int32)
                  | (torch.randint(0, 2, (1,), generator=g, device=tdev, dtype=torch.int32) << 7)).to(torch.uint8)
-            v = (torch.randint(0, top, (num_blocks, hkv, D, BS), generator=g, device=tdev, dtype=torch.int32)
+            v = (torch.randint(0, top_code, (num_blocks, hkv, D, BS), generator=g, device=tdev, dtype=torch.int32)
                  | (torch.randint(0, 2, (1,), generator=g, device=tdev, dtype=torch.int32) << 7)).to(torch.uint8)
         else:
             k = torch.randn((num_blocks, hkv, D // 8, BS, 8), generator=g, device=tdev, dtype=tdt)
@@ -335,9 +467,9 @@ def run_ours(args, rank, world, local_rank):
     psize = cfg["partition"] or mk.choose_decode(B, hkv, max_seq_len, 16 if pool else BS)
     if args.decode == "v1":
         psize = 0
-    elif args.decode == "v2":
+    elif args.decode in ("v2", "planned"):
         psize = args.partition or psize or 512
-    if args.partition and psize:
+    if args.partition and psize and top:
         psize = args.partition
     # config 4 is a radix-cache hit: every table starts with the same prefix, which
     # the serving stack knows, so the default decode is the shared-prefix (cascade) one
@@ -345,40 +477,49 @@ def run_ours(args, rank, world, local_rank):
     if cascade:
         prefix = cfg["prefix"]
         pp, pt = mk.cascade_partitions(B, hq, hkv, max_seq_len, prefix, BS)
-        pp, pt = args.partition_prefix or pp, args.partition or pt
+        if top:
+            pp, pt = args.partition_prefix or pp, args.partition or pt
         cws = mk.cascade_workspace(B, hq, D, max_seq_len, prefix, pp, pt, dev)
         psize = 0
     split = psize > 0
+    planned = split and args.decode == "planned" and not pool
     ws = mk.splitk_workspace(B, hq, D, max_seq_len, psize, dev) if split else None
+    dplan = mk.DecodePlan(B, hkv, max_seq_len, psize, dev) if planned else None
     torch.cuda.synchronize()
     st = Stream()  # all work of the step runs on this stream (graph-capturable)
 
-    def append(i):
+    def append(i, stream=st):
         if fp8:
-            return mk.reshape_and_cache_fp8(kn[i], vn[i], kc[i], vc[i], slots_d, 0.05, 0.05, fmt, stream=st)
+            return mk.reshape_and_cache_fp8(kn[i], vn[i], kc[i], vc[i], slots_d, 0.05, 0.05, fmt, stream=stream)
         if pool:
-            return mk.reshape_and_cache_flash(kn[i], vn[i], kc[i], vc[i], slots_d, stream=st)
-        return mk.reshape_and_cache(kn[i], vn[i], kc[i], vc[i], slots_d, stream=st)
+            return mk.reshape_and_cache_flash(kn[i], vn[i], kc[i], vc[i], slots_d, stream=stream)
+        return mk.reshape_and_cache(kn[i], vn[i], kc[i], vc[i], slots_d, stream=stream)
 
-    def decode(i):
+    def make_plan(stream=st):
+        # one work list per step (every layer has the same lengths)
+        if planned:
+            mk.make_decode_plan(lens_d, hkv, max_seq_len, psize, plan=dplan, stream=stream)
+
+    def decode(i, stream=st):
         if fp8:
             return mk.paged_attention_fp8(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, BS, max_seq_len,
                                           k_scale=0.05, v_scale=0.05, fp8_format=fmt, partition_size=psize,
-                                          workspace=ws, out=out[i], stream=st)
+                                          workspace=ws, out=out[i], stream=stream)
         if cascade:
             return mk.paged_attention_cascade(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, BS, max_seq_len, prefix,
                                               prefix_partition_size=pp, partition_size=pt, workspace=cws, out=out[i],
-                                              stream=st)
+                                              stream=stream)
         if pool:
             return mk.paged_attention_flash(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, 1, max_seq_len,
-                                            partition_size=psize, workspace=ws, out=out[i], stream=st)
+                                            partition_size=psize, workspace=ws, out=out[i], stream=stream)
         if split:
             return mk.paged_attention_v2(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, BS, max_seq_len,
-                                         partition_size=psize, workspace=ws, out=out[i], stream=st)
+                                         partition_size=psize, workspace=ws, out=out[i], stream=stream, plan=dplan)
         return mk.paged_attention_v1(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, BS, max_seq_len, out=out[i],
-                                     stream=st)
+                                     stream=stream)
 
     def step(ev=None):
+        make_plan()
         for i in range(L):
             append(i)
             if ev is not None:
@@ -392,7 +533,7 @@ def run_ours(args, rank, world, local_rank):
             flush.fill_zero(stream=st)
 
     dist = None
-    if world > 1:
+    if world > 1 and top:
         import torch.distributed as dist
 
     def barrier():
@@ -447,9 +588,13 @@ def run_ours(args, rank, world, local_rank):
     barrier()
 
     # ---- e2e through the public API with pinned host buffers ----
+    # Every step copies its inputs (q, the new K/V rows, lengths, slots) from pinned
+    # host memory and its outputs back.  Copies run on two side streams (host ->
+    # device, device -> host), ordered with events, so layer i + 1's inputs land
+    # while layer i computes and layer i's output leaves while layer i + 1 does.
     e2e_ms = float("nan")
     h2d = d2h = 0
-    if not args.no_e2e:
+    if not args.no_e2e and top:
         h_q = [HostBuffer((B, hq, D), "bfloat16") for _ in range(L)]
         h_k = [HostBuffer((T_new, hkv, D), "bfloat16") for _ in range(L)]
         h_v = [HostBuffer((T_new, hkv, D), "bfloat16") for _ in range(L)]
@@ -457,62 +602,98 @@ def run_ours(args, rank, world, local_rank):
         rng = np.random.default_rng(5 + rank)
         for i in range(L):
             for hb in (h_q[i], h_k[i], h_v[i]):
-                hb.array[...] = rng.integers(0x3c00, 0x4000, size=hb.shape, dtype=np.uint16)
+                hb.array[...] = random_bf16_bits(rng, hb.shape)
         h_lens = HostBuffer((B,), "int32")
         h_lens.array[...] = lens_after
         h_slots = HostBuffer((T_new,), "int32")
         h_slots.array[...] = slots
+        up, down = Stream(), Stream()
+        ev_in = [Event() for _ in range(L)]    # layer i's inputs are on the device
+        ev_dec = [Event() for _ in range(L)]   # layer i's decode is done (inputs free, output ready)
+        ev_out = [Event() for _ in range(L)]   # layer i's output is on the host (output buffer free)
+        ev_meta = Event()
 
-        def e2e_step():
-            lens_d.copy_from_host(h_lens, stream=st)
-            slots_d.copy_from_host(h_slots, stream=st)
+        def e2e_step(first):
+            if not first:
+                up.wait(ev_dec[L - 1])  # the previous step's last decode has read lengths and slots
+            lens_d.copy_from_host(h_lens, stream=up)
+            slots_d.copy_from_host(h_slots, stream=up)
+            ev_meta.record(up)
             for i in range(L):
-                q[i].copy_from_host(h_q[i], stream=st)
-                kn[i].copy_from_host(h_k[i], stream=st)
-                vn[i].copy_from_host(h_v[i], stream=st)
+                if not first:
+                    up.wait(ev_dec[i])
+                q[i].copy_from_host(h_q[i], stream=up)
+                kn[i].copy_from_host(h_k[i], stream=up)
+                vn[i].copy_from_host(h_v[i], stream=up)
+                ev_in[i].record(up)
+            st.wait(ev_meta)
+            make_plan()
+            for i in range(L):
+                st.wait(ev_in[i])
+                if not first:
+                    st.wait(ev_out[i])
                 append(i)
                 decode(i)
-                out[i].copy_to_host(h_o[i], stream=st)
+                ev_dec[i].record(st)
+                down.wait(ev_dec[i])
+                out[i].copy_to_host(h_o[i], stream=down)
+                ev_out[i].record(down)
 
-        for _ in range(max(1, args.warmup)):
+        for s in range(max(2, args.warmup)):
             l2_flush()
-            e2e_step()
+            e2e_step(first=(s == 0))
         st.synchronize()
+        down.synchronize()
         barrier()
-        eev = [[Event(), Event()] for _ in range(args.steps)]
+        t0, t1 = Event(), Event()
+        t0.record(st)
+        up.wait(t0)
         for s in range(args.steps):
-            l2_flush()
-            eev[s][0].record(st)
-            e2e_step()
-            eev[s][1].record(st)
+            e2e_step(first=False)
+        st.wait(ev_out[L - 1])
+        t1.record(st)
         st.synchronize()
-        e2e_ms = sum(a.elapsed_ms(b) for a, b in eev)
+        e2e_ms = t0.elapsed_ms(t1)
         h2d = B * 4 + T_new * 4 + L * (B * hq * D * 2 + 2 * T_new * hkv * D * 2)
         d2h = L * B * hq * D * 2
 
-    # ---- reduce over ranks (max time; bytes summed) ----
+    # ---- every rank checks a sample of its outputs (the last layer) against the oracle ----
+    mode = "fp8" if fp8 else ("pool" if pool else "paged")
+    ok, err, nrows = check_outputs(torch, q_t[L - 1], kc_t[L - 1], vc_t[L - 1], out[L - 1], tables, lens_after, hkv,
+                                   D, tab_bs, mode, fmt)
+    status = _lib.get_status(dev, clear=True)
+    ok = ok and status == 0
+
+    # ---- reduce over ranks (max time; bytes summed; worst check) ----
     step_ms = total_ms / args.steps
     e2e_step_ms = e2e_ms / args.steps
     mean_dec_ms = float(np.mean(dec_ms))
     alg, logical = decode_bytes(tables, lens_after, hq, hkv, D, tab_bs, shared, s_kv=1 if fp8 else 2)
     sums = np.array([float(alg), float(logical), float(h2d), float(d2h)])
     if dist is not None:
-        t = torch.tensor([step_ms, e2e_step_ms, mean_dec_ms], dtype=torch.float64)
+        t = torch.tensor([step_ms, e2e_step_ms, mean_dec_ms, 0.0 if ok else 1.0, err], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        step_ms, e2e_step_ms, _ = [float(x) for x in t]
-        st = torch.tensor(sums, dtype=torch.float64)
-        dist.all_reduce(st, op=dist.ReduceOp.SUM)
-        sums = st.numpy()
+        step_ms, e2e_step_ms, _, bad, err = [float(x) for x in t]
+        ok = bad == 0.0
+        tt = torch.tensor(np.concatenate([sums, [float(nrows)]]), dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.SUM)
+        sums, nrows = tt.numpy()[:4], int(tt.numpy()[4])
+    del kc_t, vc_t, kc, vc, q_t, kn_t, vn_t
     if rank != 0:
-        return
+        if not ok:
+            raise SystemExit(f"rank {rank}: outputs differ from the CPU oracle or kernel status flags are set")
+        return None
     alg_all, logical_all, h2d_all, d2h_all = sums
     peak, peak_kind = load_peaks()
-    traffic = (TRAFFIC_PER_LAUNCH.get(args.config)
-               if (world == 1 and not pool and not cascade and not fp8 and not (args.layers or args.batch or args.kv_heads))
-               else None)
+    kernel_key = ("cascade" if cascade else "pool" if pool else f"fp8-{fmt}" if fp8 else
+                  f"planned{psize}" if planned else f"splitk{psize}" if split else "v1")
+    traffic = (load_traffic(config, kernel_key)
+               if (world == 1 and not (args.layers or args.batch or args.kv_heads)) else None)
     achieved = alg / (mean_dec_ms * 1e-3) / 1e9
     toks = B_all / (step_ms * 1e-3)
     kernel = f"split-K v2, {psize}-token partitions" if split else "paged_attention_v1"
+    if planned:
+        kernel = f"planned split-K, {psize}-token partitions longest first, merge fused"
     if pool:
         kernel = "token-pool decode (paged_attention_flash, slot lists" + (
             f", {psize}-token partitions)" if split else ", single pass)")
@@ -523,6 +704,8 @@ def run_ours(args, rank, world, local_rank):
     extra = {"kernel": kernel, "launch": "one CUDA graph per step (decode timing from an eager pass)" if graph is not None else "eager",
              "l2": ("flushed between steps (unique KV fits in L2)" if flush is not None else
                     f"inputs larger than L2 (KV per layer {logical_all / 1e9:.2f} GB); no flush")}
+    if pool:
+        extra["layout"] = "MHATokenPool buffers [slots, kv_heads, head_dim], slot-list tables"
     line = {
         "metric": METRIC,
         "value": toks,
@@ -536,40 +719,73 @@ def run_ours(args, rank, world, local_rank):
         "vs_baseline": None,
         "dtype": f"{args.kv_dtype} cache, f16 products" if fp8 else "bf16",
         "data": "synthetic",
-        "config": config_json(cfg, args, world, extra),
+        "config": config_json(cfg, config, world, extra),
         "kv_gbs": L * alg_all / (step_ms * 1e-3) / 1e9,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic[0] if traffic else None,
                      "traffic_source": traffic[1] if traffic else None,
                      "peak_kind": peak_kind, "kernel": f"paged decode ({kernel}), per layer launch",
                      "algorithmic_bytes_per_launch": alg, "mean_launch_ms": mean_dec_ms},
-        "e2e": None if args.no_e2e else {"value": B_all / (e2e_step_ms * 1e-3), "unit": "tokens/s",
-                                         "h2d_bytes_per_step": int(h2d_all), "d2h_bytes_per_step": int(d2h_all)},
+        "e2e": None if (args.no_e2e or not top) else {
+            "value": B_all / (e2e_step_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d_all),
+            "d2h_bytes_per_step": int(d2h_all),
+            "how": "public API per layer (append + decode) with pinned host inputs/outputs copied every step on "
+                   "two side streams overlapping the compute"},
         "gpu_launches": int(launches),
         "clocks": clocks,
+        "output_check": {"ok": bool(ok), "ranks": world, "rows_checked": int(nrows), "max_abs_err": err,
+                         "against": "CPU oracle (float64 gather + SDPA) on each rank's own caches, last layer; "
+                                    "kernel status word clear",
+                         "tolerance": f"{ATOL:g} abs + {RTOL:g} rel"},
     }
     if shared:
         line["effective_kv_gbs"] = L * logical_all / (step_ms * 1e-3) / 1e9
         line["roofline"]["note"] = "achieved counts each shared prefix block once (unique bytes)"
     if len(w["prefill_slots"]):
         line["prefill_tokens_per_s"] = len(w["prefill_slots"]) / (step_ms * 1e-3)
-    if pool:
-        extra["layout"] = "MHATokenPool buffers [slots, kv_heads, head_dim], slot-list tables"
-    if not args.no_cpu_baseline and world == 1 and not pool:
-        n_seq = min(8, B)
-        blocks, t2 = compact_sample(tables, lens_after, BS, n_seq)
+    if not ok:
+        print(json.dumps(line), flush=True)
+        raise SystemExit("outputs differ from the CPU oracle or kernel status flags are set (output_check)")
+    return line
 
-        def bits(t):
-            return t.view(torch.int16).cpu().numpy().view(np.uint16)
 
-        idx = torch.from_numpy(blocks).to(tdev)
-        kb, vb, qb = bits(kc_t[0].index_select(0, idx)), bits(vc_t[0].index_select(0, idx)), bits(q_t[0][:n_seq])
-        t_sample, threads = time_oracle(qb, kb, vb, t2, lens_after[:n_seq], hkv, D, BS)
-        scale_factor = (B / n_seq) * L
-        cpu_step = t_sample * scale_factor
-        line["cpu_baseline"] = {"value": B / cpu_step, "unit": "tokens/s", "cores": threads, "kind": "port",
-                                "sample": f"{n_seq} of {B} sequences x 1 of {L} layers, scaled x{scale_factor:g}; "
-                                          f"C oracle (float64 gather+SDPA, OpenMP), {lscpu_model()}"}
+def add_cpu_baseline(line, args, config):
+    """The host legs (cpu_baseline_entry) over one full layer of the workload, twice."""
+    w, cfg = workload(args, config)
+    line["cpu_baseline"] = cpu_baseline_entry(cfg, w, host_threads(), 2)
+
+
+OTHER_KEYS = ("value", "unit", "ms_per_step", "kv_gbs", "effective_kv_gbs", "prefill_tokens_per_s", "roofline",
+              "gpu_launches", "clocks", "output_check")
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+
+    from sglang_mlx_b200 import _lib
+
+    _lib.set_device(local_rank)
+    torch.cuda.set_device(local_rank)
+    line = measure_decode(args, args.config, rank, world, local_rank, top=True)
+    plain = (world == 1 and args.config == 2 and args.layout == "paged" and args.kv_dtype == "bf16"
+             and args.decode == "auto" and not (args.layers or args.batch or args.kv_heads or args.partition))
+    if rank != 0:
+        return
+    if plain and not args.no_other_configs:
+        torch.cuda.empty_cache()
+        others = {}
+        for c in (3, 4, 5):
+            sub = argparse.Namespace(**vars(args))
+            sub.config, sub.steps, sub.warmup = c, max(args.steps, 20), max(args.warmup, 3)
+            lc = measure_decode(sub, c, 0, 1, local_rank, top=False)
+            entry = {k: lc[k] for k in OTHER_KEYS if k in lc}
+            entry["config"] = lc["config"]
+            entry["steps"] = sub.steps
+            others[str(c)] = entry
+            torch.cuda.empty_cache()
+        line["other_configs"] = others
+    if not args.no_cpu_baseline and world == 1 and args.layout == "paged" and args.kv_dtype == "bf16":
+        add_cpu_baseline(line, args, args.config)
     print(json.dumps(line), flush=True)
 
 
@@ -791,6 +1007,7 @@ def load_tensor_peak():
     return 1590.0, "fallback"
 
 
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -800,13 +1017,15 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=sorted(cases.BASELINE))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
+    ap.add_argument("--no-other-configs", action="store_true",
+                    help="one-GPU default run: skip the nested measurements of configs 3, 4 and 5")
     ap.add_argument("--kv-dtype", default="bf16", choices=["bf16", "fp8-e4m3", "fp8-e5m2"],
                     help="cache element type: bf16 (default) or one-byte FP8 codes (half the KV bytes)")
     ap.add_argument("--layout", default="paged", choices=["paged", "pool"],
                     help="cache layout: the vLLM paged layout (default) or the MHATokenPool token pool")
-    ap.add_argument("--decode", default="auto", choices=["auto", "v1", "v2", "cascade"],
+    ap.add_argument("--decode", default="auto", choices=["auto", "v1", "v2", "planned", "cascade"],
                     help="decode form: the shim's choice (default; shared-prefix cascade for config 4), single pass, "
-                         "split-K, or cascade")
+                         "split-K, planned split-K (work list longest first, merge fused), or cascade")
     ap.add_argument("--partition", type=int, default=0, help="split-K partition size (tokens) when split")
     ap.add_argument("--partition-prefix", type=int, default=0,
                     help="cascade: shared-prefix chunk size (tokens); default from cascade_partitions")

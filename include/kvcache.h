@@ -68,6 +68,7 @@ typedef struct {
 #define KVC_STATUS_WAIT_TIMEOUT 0x4u /* a bounded pipeline wait gave up */
 #define KVC_STATUS_INDEX_OOB 0x8u   /* a gather/copy index beyond its buffer was skipped */
 #define KVC_STATUS_PREFIX_MISMATCH 0x10u /* a sequence's table did not start with the shared prefix blocks */
+#define KVC_STATUS_PLAN_MISMATCH 0x20u /* a decode plan was made for other launch parameters (nothing written) */
 
 /* ---- errors / info --------------------------------------------------------- */
 /* Thread-local message of the last failing call ("" if none). */
@@ -112,6 +113,42 @@ int kvc_paged_attention_v2(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltens
                            const kvc_dltensor* block_tables, const kvc_dltensor* context_lens,
                            int num_kv_heads, float scale, int block_size, int max_seq_len,
                            const kvc_dltensor* alibi_slopes, int partition_size, void* stream);
+
+/* Planned split-K decode: the same result as kvc_paged_attention_v2, for
+ * batches too small to fill the GPU with one CTA per (sequence, KV head) (a
+ * KV-head shard of a multi-GPU run, long contexts).  No reference counterpart
+ * (split-K is deferred in sglang-mlx, README.md:11-20).
+ *
+ * kvc_decode_plan reads the context lengths on the device and writes a work
+ * list into `plan`: every (sequence, partition) item, longest first, so the
+ * GPU starts the long partitions first and ends the launch on short ones, plus
+ * one arrival counter per (sequence, KV head).  Every layer of a decode step
+ * has the same lengths, so one plan per step serves all of them.
+ * kvc_paged_attention_planned then runs one CTA per (item, KV head); when a
+ * sequence has up to 32 partitions the CTA that finishes its last partition
+ * merges the partials into `out` (no separate reduce kernel) and resets the
+ * counter; a sequence of one partition writes `out` directly.
+ *   plan          int32/uint32 [>= kvc_decode_plan_size(...)] on the device,
+ *                 written by kvc_decode_plan (nothing to initialise)
+ *   workspace     exp_sums / max_logits / tmp_out of kvc_paged_attention_v2
+ *   partition_size  a multiple of 32 and of block_size, at most 8192; the
+ *                 same value (and num_seqs, num_kv_heads, max_seq_len) in both
+ *                 calls: a decode given a plan made for other values writes
+ *                 nothing and sets KVC_STATUS_PLAN_MISMATCH
+ * Calls that share a plan or a workspace must not overlap on the GPU.  f32
+ * queries and caches, head sizes other than 64/128 and groups above 16 query
+ * heads run as kvc_paged_attention_v2 (the plan is then unused).
+ * kvc_decode_plan_size returns the plan's element count, or -1 for arguments
+ * a plan cannot cover (over 65535 sequences or partitions per sequence). */
+int64_t kvc_decode_plan_size(int num_seqs, int num_kv_heads, int max_seq_len, int partition_size);
+int kvc_decode_plan(kvc_dltensor* plan, const kvc_dltensor* context_lens, int num_kv_heads, int max_seq_len,
+                    int partition_size, void* stream);
+int kvc_paged_attention_planned(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltensor* max_logits,
+                                kvc_dltensor* tmp_out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                                const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                                const kvc_dltensor* context_lens, int num_kv_heads, float scale, int block_size,
+                                int max_seq_len, const kvc_dltensor* alibi_slopes, int partition_size,
+                                kvc_dltensor* plan, void* stream);
 
 /* Paged decode over token-major caches: the reshape_and_cache_flash layout
  * [num_blocks, block_size, num_kv_heads, head_size], or the MHATokenPool
@@ -201,7 +238,10 @@ int kvc_paged_prefill(kvc_dltensor* out, const kvc_dltensor* query, const kvc_dl
  *     (head_size + 2) * 4 bytes <= KVC_NOALLOC_SCRATCH_BYTES; larger calls
  *     return KVC_EINVAL without launching anything.
  *   - The first call on a device looks up the array's device address (with that
- *     device current); make that first call before any stream capture.
+ *     device current); make that first call before any stream capture (a first
+ *     call made while `stream` is capturing returns KVC_EINVAL and launches
+ *     nothing).  The address is remembered per device and CUDA context, so the
+ *     first call after cudaDeviceReset looks it up again, with the same rule.
  *   - All calls on a device share the one array and it keeps the previous
  *     call's contents (nothing in it needs to start at zero).  Calls that overlap
  *     on the GPU — on different streams, or from different threads — race on it:

@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(256) row_copy_kernel(RowCopyParams p) {
 }
 
 static int sm_count() {
-  static int count[64] = {0};
+  static std::atomic<int> count[64];  // per device, written once (any racing writer stores the same value)
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return 148;

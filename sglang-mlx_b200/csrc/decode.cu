@@ -57,6 +57,14 @@ struct DecodeParams {
   int64_t part_seq_stride, part_head_stride;
   int64_t part_out_seq_stride, part_out_head_stride, part_out_part_stride;
   float scale;
+  // Planned split-K: CTA i of a 1-D grid runs work item i / num_kv_heads of the
+  // plan (kvc_decode_plan) for KV head i % num_kv_heads; a sequence split in
+  // several partitions has its partials merged by the CTA that finishes last
+  // (plan_counters) when fused_merge is set, else by the reduce kernel.
+  const uint32_t* plan_header;
+  const uint32_t* plan_items;
+  uint32_t* plan_counters;
+  int fused_merge;
 };
 
 // Programmatic dependent launch: the partition kernels let the split-K reduce be
@@ -108,12 +116,82 @@ __device__ __forceinline__ void write_zero_heads(const DecodeParams& p, int seq,
   }
 }
 
+// ---------------------------------------------------------------------------
+// Planned split-K (kvc_decode_plan + kvc_paged_attention_planned).
+// ---------------------------------------------------------------------------
+
+// The work item of this CTA: false when the CTA has none (past the plan's item
+// count, or a plan written for other launch parameters, which is flagged).
+__device__ __forceinline__ bool planned_item(const DecodeParams& p, int* kvh, int* seq, int* part) {
+  const uint32_t* h = p.plan_header;
+  if (h[0] != kPlanMagic || h[1] != (uint32_t)p.num_seqs || h[2] != (uint32_t)p.num_kv_heads ||
+      h[3] != (uint32_t)p.max_seq_len || h[4] != (uint32_t)p.partition_size) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) set_status(&g_decode_status, KVC_STATUS_PLAN_MISMATCH);
+    return false;
+  }
+  const uint32_t item_idx = blockIdx.x / (uint32_t)p.num_kv_heads;
+  if (item_idx >= h[5]) return false;
+  const uint32_t item = p.plan_items[item_idx];
+  *kvh = (int)(blockIdx.x - item_idx * (uint32_t)p.num_kv_heads);
+  *seq = (int)(item & 0xFFFFu);
+  *part = (int)(item >> 16);
+  return true;
+}
+
+// Partitions of a sequence of `ctx` tokens (valid ctx only).
+__device__ __forceinline__ int planned_parts(const DecodeParams& p, uint32_t ctx) {
+  return (int)((ctx + (uint32_t)p.partition_size - 1) / (uint32_t)p.partition_size);
+}
+
+// Called by every thread of the CTA after it wrote its partition's partials:
+// counts the arrival, and the CTA that completes the sequence's set merges
+// the `nparts` (<= 32) partials of heads h0 .. h0 + G - 1 into the output and
+// resets the counter.  `scratch` holds at least G * 32 + G floats (shared).
+template <typename T>
+__device__ __forceinline__ void planned_arrive_and_merge(const DecodeParams& p, int seq, int kvh, int h0, int G,
+                                                         int D, int nparts, float* scratch) {
+  __shared__ uint32_t s_last;
+  __threadfence();  // this thread's partials are visible before the arrival below
+  __syncthreads();
+  uint32_t* counter = p.plan_counters + (int64_t)seq * p.num_kv_heads + kvh;
+  if (threadIdx.x == 0) s_last = atomicAdd(counter, 1u) == (uint32_t)(nparts - 1) ? 1u : 0u;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // weights e^{m_k - M} of every partition, and 1 / (L + 1e-6), per head
+  float* w = scratch;                 // [G][32]
+  float* inv = scratch + G * 32;      // [G]
+  for (int g = threadIdx.x; g < G; g += blockDim.x) {
+    const int64_t o = (int64_t)seq * p.part_seq_stride + (int64_t)(h0 + g) * p.part_head_stride;
+    float M = -INFINITY;
+    for (int k = 0; k < nparts; ++k) M = fmaxf(M, __ldcg(p.part_max + o + k));
+    float L = 0.f;
+    for (int k = 0; k < nparts; ++k) {
+      const float mk = __ldcg(p.part_max + o + k);
+      const float wt = (M == -INFINITY || mk == -INFINITY) ? 0.f : expf(mk - M);
+      w[g * 32 + k] = wt;
+      L += wt * __ldcg(p.part_sum + o + k);
+    }
+    inv[g] = 1.f / (L + 1e-6f);  // paged_attention_kernels.metal:144
+  }
+  __syncthreads();
+  T* out = reinterpret_cast<T*>(p.out);
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int g = i / D, d = i - g * D;
+    const float* po = p.part_out + (int64_t)seq * p.part_out_seq_stride + (int64_t)(h0 + g) * p.part_out_head_stride + d;
+    float a = 0.f;
+    for (int k = 0; k < nparts; ++k) a += w[g * 32 + k] * __ldcg(po + (int64_t)k * p.part_out_part_stride);
+    out[(int64_t)seq * p.out_seq_stride + (int64_t)(h0 + g) * p.out_head_stride + d] = from_float<T>(a * inv[g]);
+  }
+  if (threadIdx.x == 0) *counter = 0u;  // ready for the next call with this plan
+}
+
 // Writes one merged (max, sum, acc) triple: the final output in single-pass
 // mode, the partition's partials in split mode.
 template <typename T>
 __device__ __forceinline__ void emit(const DecodeParams& p, int seq, int head, int part, int d, float m, float l,
-                                     float acc, bool first_d) {
-  if (p.num_partitions == 1) {
+                                     float acc, bool first_d, bool direct) {
+  if (direct) {
     T* out = reinterpret_cast<T*>(p.out);
     // paged_attention_kernels.metal:144 — inv_sum = 1 / (sum + 1e-6)
     const float inv = 1.f / (l + 1e-6f);
@@ -301,7 +379,7 @@ __global__ void __launch_bounds__(kGenericWarps * 32) paged_decode_generic_kerne
         A += wt * red_o[w][g][d];
       }
     }
-    emit<Q_T>(p, seq, h0 + g, part, d, M, L, A, d == 0);
+    emit<Q_T>(p, seq, h0 + g, part, d, M, L, A, d == 0, p.num_partitions == 1);
   }
 }
 
@@ -580,6 +658,12 @@ static DecodeParams to_params(const DecodeArgs& a) {
   p.part_out_head_stride = a.part_out_head_stride;
   p.part_out_part_stride = a.part_out_part_stride;
   p.scale = a.scale;
+  p.plan_header = a.plan;
+  p.plan_items = a.plan ? a.plan + kPlanHeader : nullptr;
+  p.plan_counters = a.plan ? a.plan + kPlanHeader + plan_max_items(a.num_seqs, a.max_seq_len, a.partition_size)
+                           : nullptr;
+  // the CTA that completes a sequence merges its partials when they are few
+  p.fused_merge = a.plan && a.num_partitions <= 32 ? 1 : 0;
   return p;
 }
 
@@ -594,6 +678,13 @@ static bool pages_aligned(const DecodeArgs& a) {
 cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   if (a.num_seqs > 65535) return cudaErrorInvalidValue;
   DecodeParams p = to_params(a);
+  if (a.plan && (!mma_supported(a) ||
+                 plan_max_items(a.num_seqs, a.max_seq_len, a.partition_size) * a.num_kv_heads > 0x7FFFFFFF)) {
+    // the plan only orders the work: without the tensor-core kernel it runs as plain split-K
+    p.plan_header = p.plan_items = nullptr;
+    p.plan_counters = nullptr;
+    p.fused_merge = 0;
+  }
   const int D = a.head_size;
   cudaError_t e = cudaErrorInvalidValue;
   // Loads are 16-byte vectors: page bases must be 16-byte aligned.
@@ -616,7 +707,7 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   } else if (a.q_type == ElemType::BF16 && a.cache_type == ElemType::BF16) {
     e = launch_generic_d<__nv_bfloat16, __nv_bfloat16>(p, D, stream);
   }
-  if (e != cudaSuccess || a.num_partitions == 1) return e;
+  if (e != cudaSuccess || a.num_partitions == 1 || p.fused_merge) return e;
   if (a.q_type == ElemType::F32) return launch_reduce<float>(p, D, stream);
   if (a.q_type == ElemType::F16) return launch_reduce<__half>(p, D, stream);
   return launch_reduce<__nv_bfloat16>(p, D, stream);
@@ -635,7 +726,7 @@ static cudaError_t launch_cascade_prefix(const DecodeParams& p, cudaStream_t str
   constexpr int STAGES = BS <= 16 ? 6 : 4;
   using CG = CascadeGeom<D, BS, STAGES, GT>;
   auto kern = cascade_prefix_kernel<T, D, BS, STAGES, GT>;
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // per device; setting the attribute twice is harmless
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
@@ -698,6 +789,118 @@ cudaError_t launch_paged_decode_cascade(const DecodeArgs& a, cudaStream_t stream
 }
 
 // ---------------------------------------------------------------------------
+// Decode plan (kvc_decode_plan): the work items of a split-K decode, longest
+// first.  A sequence of C tokens (1 <= C <= max_seq_len) has n = ceil(C / P)
+// partitions: n - 1 full ones of P tokens and a last one of C - (n - 1) P;
+// a sequence whose length gives zeros (0, or past max_seq_len) gets one
+// item of size 0 that writes them.  Items are ordered by size, descending (a
+// counting sort over sizes 0..P), so the thread-block scheduler, which starts
+// CTAs in index order as slots free up, hands out the long partitions first
+// and fills the tail of the launch with the short ones (longest-processing-
+// time-first list scheduling).  One CTA of 1024 threads; the size histogram
+// (P + 1 counters) lives in shared memory.
+// ---------------------------------------------------------------------------
+constexpr int kPlanThreads = 1024;
+
+__device__ __forceinline__ void plan_classify(uint32_t C, int max_seq_len, int P, uint32_t* full, uint32_t* last) {
+  if (C == 0 || C > (uint32_t)max_seq_len) {  // one item of size 0: writes the zeros
+    *full = 0;
+    *last = 0;
+    return;
+  }
+  const uint32_t n = (C + (uint32_t)P - 1) / (uint32_t)P;
+  *full = n - 1;
+  *last = C - (n - 1) * (uint32_t)P;  // 1 .. P
+}
+
+__global__ void __launch_bounds__(kPlanThreads) decode_plan_kernel(const uint32_t* __restrict__ lens, int num_seqs,
+                                                                   int num_kv_heads, int max_seq_len, int P,
+                                                                   uint32_t* __restrict__ plan, int64_t max_items) {
+  extern __shared__ uint32_t cursor[];  // [P + 1]: items of each size, then the next free position for that size
+  __shared__ uint32_t warp_tot[kPlanThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i <= P; i += kPlanThreads) cursor[i] = 0u;
+  __syncthreads();
+  for (int b = tid; b < num_seqs; b += kPlanThreads) {
+    uint32_t full, last;
+    plan_classify(lens[b], max_seq_len, P, &full, &last);
+    if (full) atomicAdd(&cursor[P], full);
+    atomicAdd(&cursor[last], 1u);
+  }
+  __syncthreads();
+  // exclusive scan in descending size order: thread t owns sizes P - t*K .. P - t*K - K + 1
+  const int K = (P + 1 + kPlanThreads - 1) / kPlanThreads;
+  uint32_t local = 0;
+  for (int j = 0; j < K; ++j) {
+    const int sz = P - (tid * K + j);
+    if (sz >= 0) local += cursor[sz];
+  }
+  uint32_t incl = local;
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += v;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t v = warp_tot[lane];
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t u = __shfl_up_sync(0xffffffffu, v, off);
+      if (lane >= off) v += u;
+    }
+    warp_tot[lane] = v;  // inclusive over warps
+  }
+  __syncthreads();
+  uint32_t base = (warp ? warp_tot[warp - 1] : 0u) + incl - local;
+  const uint32_t total = warp_tot[kPlanThreads / 32 - 1];
+  for (int j = 0; j < K; ++j) {
+    const int sz = P - (tid * K + j);
+    if (sz >= 0) {
+      const uint32_t c = cursor[sz];
+      cursor[sz] = base;
+      base += c;
+    }
+  }
+  __syncthreads();
+  uint32_t* items = plan + kPlanHeader;
+  for (int b = tid; b < num_seqs; b += kPlanThreads) {
+    uint32_t full, last;
+    plan_classify(lens[b], max_seq_len, P, &full, &last);
+    if (full) {
+      const uint32_t o = atomicAdd(&cursor[P], full);
+      for (uint32_t k = 0; k < full; ++k) items[o + k] = (k << 16) | (uint32_t)b;
+    }
+    items[atomicAdd(&cursor[last], 1u)] = (full << 16) | (uint32_t)b;
+  }
+  uint32_t* counters = items + max_items;
+  const int64_t nc = (int64_t)num_seqs * num_kv_heads;
+  for (int64_t i = tid; i < nc; i += kPlanThreads) counters[i] = 0u;
+  if (tid == 0) {
+    plan[0] = kPlanMagic;
+    plan[1] = (uint32_t)num_seqs;
+    plan[2] = (uint32_t)num_kv_heads;
+    plan[3] = (uint32_t)max_seq_len;
+    plan[4] = (uint32_t)P;
+    plan[5] = total;
+    plan[6] = 0u;
+    plan[7] = 0u;
+  }
+}
+
+cudaError_t launch_decode_plan(const uint32_t* context_lens, int num_seqs, int num_kv_heads, int max_seq_len,
+                               int partition_size, uint32_t* plan, cudaStream_t stream) {
+  if (num_seqs <= 0 || num_seqs > 65535 || partition_size <= 0 || partition_size > kPlanMaxPartition ||
+      max_seq_len <= 0 || (max_seq_len + partition_size - 1) / partition_size > 65535)
+    return cudaErrorInvalidValue;
+  const size_t smem = (size_t)(partition_size + 1) * sizeof(uint32_t);
+  decode_plan_kernel<<<1, kPlanThreads, smem, stream>>>(context_lens, num_seqs, num_kv_heads, max_seq_len,
+                                                        partition_size, plan,
+                                                        plan_max_items(num_seqs, max_seq_len, partition_size));
+  count_launch();
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
 // Scratch of kvc_paged_attention_v2_noalloc: the split-K partials
 // [tmp_out | max_logits | exp_sums] of one call, in a static array so callers
 // that cannot allocate device memory still get the split-K decode.  Every GPU
@@ -707,12 +910,38 @@ cudaError_t launch_paged_decode_cascade(const DecodeArgs& a, cudaStream_t stream
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) float g_noalloc_scratch[KVC_NOALLOC_SCRATCH_BYTES / sizeof(float)];
 
+// The current CUDA context (driver entry point looked up through the runtime,
+// so the library needs no link against libcuda); nullptr if unavailable.
+static void* current_cuda_context() {
+  typedef CUresult (*CtxGetCurrent)(CUcontext*);
+  static CtxGetCurrent fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrent>(f);
+  });
+  CUcontext c = nullptr;
+  if (fn) fn(&c);
+  return c;
+}
+
 // Host code must not use g_noalloc_scratch as an address (it names the host
-// shadow).  The device address is looked up once per device, with that device
-// current, and cached.
-static float* noalloc_scratch_address(cudaError_t* err) {
+// shadow).  The device address is looked up with cudaGetSymbolAddress, with
+// the device current, and cached per device together with the CUDA context it
+// belongs to: after cudaDeviceReset (a new context) it is looked up again.
+// The lookup may load the module, which must not happen inside a stream
+// capture: a first call that finds `stream` capturing gets
+// cudaErrorStreamCaptureUnsupported back and nothing is launched.
+static float* noalloc_scratch_address(cudaStream_t stream, cudaError_t* err) {
+  struct Entry {
+    void* ctx;
+    float* addr;
+  };
   static std::mutex mu;
-  static float* addr[64] = {nullptr};
+  static Entry cache[64] = {};
   int dev = 0;
   *err = cudaGetDevice(&dev);
   if (*err != cudaSuccess) return nullptr;
@@ -720,14 +949,20 @@ static float* noalloc_scratch_address(cudaError_t* err) {
     *err = cudaErrorInvalidDevice;
     return nullptr;
   }
+  void* ctx = current_cuda_context();
   std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
-    void* p = nullptr;
-    *err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (*err != cudaSuccess) return nullptr;
-    addr[dev] = static_cast<float*>(p);
+  if (cache[dev].addr != nullptr && cache[dev].ctx == ctx) return cache[dev].addr;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone) {
+    *err = cudaErrorStreamCaptureUnsupported;
+    return nullptr;
   }
-  return addr[dev];
+  void* p = nullptr;
+  *err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (*err != cudaSuccess) return nullptr;
+  cache[dev].ctx = current_cuda_context();
+  cache[dev].addr = static_cast<float*>(p);
+  return cache[dev].addr;
 }
 
 cudaError_t launch_paged_decode_noalloc(DecodeArgs a, cudaStream_t stream) {
@@ -735,7 +970,7 @@ cudaError_t launch_paged_decode_noalloc(DecodeArgs a, cudaStream_t stream) {
   const int64_t floats = rows * (a.head_size + 2);
   if (floats * (int64_t)sizeof(float) > (int64_t)KVC_NOALLOC_SCRATCH_BYTES) return cudaErrorInvalidValue;
   cudaError_t err = cudaSuccess;
-  float* base = noalloc_scratch_address(&err);
+  float* base = noalloc_scratch_address(stream, &err);
   if (base == nullptr) return err;
   // tmp_out first (16-byte rows for the reduce's vector loads), then the two
   // [B, Hq, P] arrays.

@@ -692,18 +692,20 @@ __global__ void __launch_bounds__(NW * 32)
   constexpr int NT = D / 8;     // n-tiles of P.V
   extern __shared__ __align__(128) uint8_t smem[];
 
-  const int kvh = blockIdx.x, seq = blockIdx.y, part = blockIdx.z + p.part_offset;
+  int kvh = blockIdx.x, seq = blockIdx.y, part = blockIdx.z + p.part_offset;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, q4 = lane & 3;
   const int G = p.num_heads / p.num_kv_heads;
-  const int h0 = kvh * G;
 
   grid_dependents_launch();
+  if (p.plan_items && !planned_item(p, &kvh, &seq, &part)) return;  // planned: CTA -> work item of the plan
+  const int h0 = kvh * G;
   const uint32_t ctx = p.context_lens[seq];
   int begin = 0, end = 0;
   bool zero_out = false;
   if (!partition_range(p, seq, part, ctx, &begin, &end, &zero_out)) {
-    if (zero_out) write_zero_heads<T>(p, seq, h0, G, D);
+    // planned: the item of a sequence with zero output (length 0 or past max_seq_len) writes it
+    if (zero_out || p.plan_items) write_zero_heads<T>(p, seq, h0, G, D);
     if (p.wait_prior_at_end) grid_dependency_wait();
     return;
   }
@@ -1036,6 +1038,10 @@ __global__ void __launch_bounds__(NW * 32)
     }
   }
   __syncthreads();
+  // planned split-K with the merge fused: a sequence of one partition writes its
+  // output directly, the others write partials and the last CTA merges them
+  const int nparts = p.plan_items ? planned_parts(p, ctx) : p.num_partitions;
+  const bool direct = p.num_partitions == 1 || (p.plan_items && p.fused_merge && nparts == 1);
   for (int i = threadIdx.x; i < G * D; i += NW * 32) {
     const int g = i / D, d = i - g * D;
     float M = -INFINITY;
@@ -1052,8 +1058,10 @@ __global__ void __launch_bounds__(NW * 32)
       }
     }
     // partial maxima are exchanged in natural-log units (as the generic kernel)
-    emit<T>(p, seq, h0 + g, part, d, M * kLn2, L, A, d == 0);
+    emit<T>(p, seq, h0 + g, part, d, M * kLn2, L, A, d == 0, direct);
   }
+  if (p.plan_items && p.fused_merge && !direct)
+    planned_arrive_and_merge<T>(p, seq, kvh, h0, G, D, nparts, reinterpret_cast<float*>(smem));
   if (p.wait_prior_at_end) grid_dependency_wait();
 }
 
@@ -1206,7 +1214,7 @@ static cudaError_t launch_mma_nw(const DecodeParams& p, cudaStream_t stream) {
     const ElemType et = std::is_same<T, __nv_bfloat16>::value ? ElemType::BF16 : ElemType::F16;
     if (!make_tensor_maps(p, et, D, BS, Geo::VBS, Geo::VSWZ, MODE, &maps)) return cudaErrorNotSupported;
   }
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // per device; setting the attribute twice is harmless
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
@@ -1215,6 +1223,8 @@ static cudaError_t launch_mma_nw(const DecodeParams& p, cudaStream_t stream) {
     configured[dev] = true;
   }
   dim3 grid((unsigned)p.num_kv_heads, (unsigned)p.num_seqs, (unsigned)(p.num_partitions - p.part_offset));
+  if (p.plan_items)  // planned: one CTA per (work item, KV head), items longest first
+    grid = dim3((unsigned)(plan_max_items(p.num_seqs, p.max_seq_len, p.partition_size) * p.num_kv_heads));
   if (p.wait_prior_at_end) {
     // shared-prefix order: a programmatic dependent of the prefix kernel that
     // runs beside it and waits for it before exiting

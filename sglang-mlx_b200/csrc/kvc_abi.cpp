@@ -488,6 +488,91 @@ int kvc_paged_attention_v2(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltens
   return KVC_OK;
 }
 
+// ---- planned split-K (work list longest first, merge fused into the last partition) ----
+
+static int check_plan_args(int num_seqs, int num_kv_heads, int max_seq_len, int partition_size) {
+  if (num_seqs < 0 || num_seqs > 65535) return fail(KVC_EINVAL, "a decode plan covers at most 65535 sequences");
+  if (num_kv_heads <= 0) return fail(KVC_EINVAL, "num_kv_heads must be positive");
+  if (max_seq_len <= 0) return fail(KVC_EINVAL, "max_seq_len must be positive");
+  if (partition_size <= 0 || partition_size % 32 != 0 || partition_size > kPlanMaxPartition)
+    return fail(KVC_EINVAL, "partition_size of a decode plan must be a positive multiple of 32, at most " +
+                                std::to_string(kPlanMaxPartition));
+  if ((max_seq_len + partition_size - 1) / partition_size > 65535)
+    return fail(KVC_EINVAL, "a decode plan holds at most 65535 partitions per sequence");
+  return KVC_OK;
+}
+
+// The plan tensor: 1-D int32/uint32, contiguous, on `device` (or any CUDA device
+// when *device < 0), at least kvc_decode_plan_size elements.
+static int parse_plan(kvc_dltensor* plan, int num_seqs, int num_kv_heads, int max_seq_len, int partition_size,
+                      int* device, uint32_t** data) {
+  View pl;
+  if (!parse(plan, "plan", &pl)) return KVC_EINVAL;
+  if (int rc = check_index_type(pl, "plan", false)) return rc;
+  if (pl.ndim != 1 || pl.stride(0) != 1) return fail(KVC_EINVAL, "plan must be a contiguous 1-D array");
+  const int64_t need = plan_elems(num_seqs, num_kv_heads, max_seq_len, partition_size);
+  if (pl.shape[0] < need)
+    return fail(KVC_EINVAL, "plan holds " + std::to_string(pl.shape[0]) + " elements; this decode needs " +
+                                std::to_string(need) + " (kvc_decode_plan_size)");
+  int dev = -1;
+  if (int rc = check_all_cuda({&pl}, &dev)) return rc;
+  if (*device >= 0 && dev != *device) return fail(KVC_EINVAL, "all tensors must live on the same CUDA device");
+  *device = dev;
+  *data = reinterpret_cast<uint32_t*>(pl.data);
+  return KVC_OK;
+}
+
+int64_t kvc_decode_plan_size(int num_seqs, int num_kv_heads, int max_seq_len, int partition_size) {
+  if (check_plan_args(num_seqs, num_kv_heads, max_seq_len, partition_size) != KVC_OK) return -1;
+  return plan_elems(num_seqs, num_kv_heads, max_seq_len, partition_size);
+}
+
+int kvc_decode_plan(kvc_dltensor* plan, const kvc_dltensor* context_lens, int num_kv_heads, int max_seq_len,
+                    int partition_size, void* stream) {
+  View cl;
+  if (!parse(context_lens, "context_lens", &cl)) return KVC_EINVAL;
+  if (cl.ndim != 1 || cl.stride(0) != 1) return fail(KVC_EINVAL, "context_lens must be a contiguous 1-D array");
+  if (int rc = check_index_type(cl, "context_lens", false)) return rc;
+  if (cl.shape[0] > 65535) return fail(KVC_EINVAL, "a decode plan covers at most 65535 sequences");
+  const int num_seqs = (int)cl.shape[0];
+  if (int rc = check_plan_args(num_seqs, num_kv_heads, max_seq_len, partition_size)) return rc;
+  int device = -1;
+  if (int rc = check_all_cuda({&cl}, &device)) return rc;
+  uint32_t* data = nullptr;
+  if (int rc = parse_plan(plan, num_seqs, num_kv_heads, max_seq_len, partition_size, &device, &data)) return rc;
+  if (num_seqs == 0) return KVC_OK;
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_decode_plan(reinterpret_cast<const uint32_t*>(cl.data), num_seqs, num_kv_heads, max_seq_len,
+                                     partition_size, data, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "decode_plan launch");
+  return KVC_OK;
+}
+
+int kvc_paged_attention_planned(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltensor* max_logits,
+                                kvc_dltensor* tmp_out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                                const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                                const kvc_dltensor* context_lens, int num_kv_heads, float scale, int block_size,
+                                int max_seq_len, const kvc_dltensor* alibi_slopes, int partition_size,
+                                kvc_dltensor* plan, void* stream) {
+  DecodeArgs a;
+  int device = -1;
+  if (int rc = prepare_decode(out, query, key_cache, value_cache, block_tables, context_lens, num_kv_heads, scale,
+                              block_size, max_seq_len, alibi_slopes, &a, &device))
+    return rc;
+  if (int rc = attach_splitk_workspace(exp_sums, max_logits, tmp_out, partition_size, block_size, max_seq_len,
+                                       device, &a))
+    return rc;
+  if (int rc = check_plan_args(a.num_seqs, num_kv_heads, max_seq_len, partition_size)) return rc;
+  if (int rc = parse_plan(plan, a.num_seqs, num_kv_heads, max_seq_len, partition_size, &device, &a.plan)) return rc;
+  if (a.num_seqs == 0) return KVC_OK;
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_paged_decode(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "paged_attention_planned launch");
+  return KVC_OK;
+}
+
 int kvc_paged_attention_flash(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltensor* max_logits,
                               kvc_dltensor* tmp_out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
                               const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
@@ -692,6 +777,10 @@ int kvc_paged_attention_v2_noalloc(kvc_dltensor* out, const kvc_dltensor* query,
   DeviceGuard g(device);
   if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
   cudaError_t e = launch_paged_decode_noalloc(a, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorStreamCaptureUnsupported)
+    return fail(KVC_EINVAL, "paged_attention_v2_noalloc: the first call on a device (and the first after "
+                            "cudaDeviceReset) looks up the static scratch and must run outside stream capture; "
+                            "call it once eagerly before capturing");
   if (e != cudaSuccess) return cuda_fail(e, "paged_attention_v2_noalloc launch");
   return KVC_OK;
 }

@@ -100,7 +100,26 @@ struct DecodeArgs {
   int64_t part_seq_stride, part_head_stride;  // elements of part_max / part_sum
   int64_t part_out_seq_stride, part_out_head_stride, part_out_part_stride;
   float scale;
+  // Planned split-K (kvc_paged_attention_planned): the work list of
+  // kvc_decode_plan (header, items, arrival counters), or nullptr.
+  uint32_t* plan;
 };
+
+// Planned split-K decode: layout of the plan buffer (uint32 elements).
+//   [0, kPlanHeader)                 header (kPlanMagic, num_seqs, num_kv_heads,
+//                                    max_seq_len, partition_size, item count, 0, 0)
+//   [kPlanHeader, + max_items)       work items, longest first: (partition << 16) | sequence
+//   [.., + num_seqs * num_kv_heads)  per-(sequence, KV head) arrival counters, zero between calls
+constexpr int kPlanHeader = 8;
+constexpr uint32_t kPlanMagic = 0x4E4C5044u;  // "DPLN"
+constexpr int kPlanMaxPartition = 8192;       // the planner's size histogram lives in shared memory
+inline int64_t plan_max_items(int64_t num_seqs, int max_seq_len, int partition_size) {
+  const int64_t parts = ((int64_t)max_seq_len + partition_size - 1) / partition_size;
+  return num_seqs * (parts > 1 ? parts : 1);
+}
+inline int64_t plan_elems(int64_t num_seqs, int num_kv_heads, int max_seq_len, int partition_size) {
+  return kPlanHeader + plan_max_items(num_seqs, max_seq_len, partition_size) + num_seqs * num_kv_heads;
+}
 
 // Paged prefill / extend attention (prefill.cuh).  Strides in elements.
 struct PrefillArgs {
@@ -170,6 +189,9 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream);
 // Split-K decode with its partials in the library's static scratch array
 // (kvc_paged_attention_v2_noalloc).  `a` carries no workspace pointers.
 cudaError_t launch_paged_decode_noalloc(DecodeArgs a, cudaStream_t stream);
+// Writes the work list of a planned split-K decode (one CTA).
+cudaError_t launch_decode_plan(const uint32_t* context_lens, int num_seqs, int num_kv_heads, int max_seq_len,
+                               int partition_size, uint32_t* plan, cudaStream_t stream);
 // Shared-prefix decode: tail partitions, the cascade prefix kernel, the reduce.
 cudaError_t launch_paged_decode_cascade(const DecodeArgs& a, cudaStream_t stream);
 // Paged prefill / extend attention (prefill.cuh); enqueues one kernel.

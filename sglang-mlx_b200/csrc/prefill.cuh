@@ -309,7 +309,7 @@ static cudaError_t launch_prefill(const PrefillParams& p, cudaStream_t stream) {
   constexpr int STAGES = 4;
   using PG = PrefillGeom<D, BS, STAGES, MODE>;
   auto kern = prefill_kernel<T, D, BS, STAGES, MODE>;
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // per device; setting the attribute twice is harmless
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {

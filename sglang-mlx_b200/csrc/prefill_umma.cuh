@@ -893,8 +893,8 @@ static bool make_k_gather_map(const PrefillArgs& a, int D, int BS, CUtensorMap* 
 // The persistent grid: one CTA per SM (the ring and TMEM allow one), fewer
 // when there are fewer work items.
 static int umma_persistent_ctas(int dev, int64_t items) {
-  static int sms[64] = {0};
-  int n = dev >= 0 && dev < 64 ? sms[dev] : 0;
+  static std::atomic<int> sms[64];  // per device, written once (any racing writer stores the same value)
+  int n = dev >= 0 && dev < 64 ? sms[dev].load() : 0;
   if (n <= 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
     if (dev >= 0 && dev < 64) sms[dev] = n;
@@ -936,7 +936,7 @@ static cudaError_t launch_prefill_umma(const PrefillArgs& a, cudaStream_t stream
     return cudaErrorNotSupported;
   if (GK && !make_k_gather_map(a, D, BS, &maps.k)) return cudaErrorNotSupported;
   auto kern = prefill_umma_kernel<T, D, BS, GK>;
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // per device; setting the attribute twice is harmless
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
@@ -1022,7 +1022,7 @@ static cudaError_t launch_cascade_umma(const PrefillArgs& a, int prefix_parts, c
     return cudaErrorNotSupported;
   if (GK && !make_k_gather_map(a, D, BS, &maps.k)) return cudaErrorNotSupported;
   auto kern = prefill_umma_kernel<T, D, BS, GK, true>;
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // per device; setting the attribute twice is harmless
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {

@@ -32,6 +32,7 @@ STATUS_BLOCK_OOB = 0x2
 STATUS_WAIT_TIMEOUT = 0x4
 STATUS_INDEX_OOB = 0x8
 STATUS_PREFIX_MISMATCH = 0x10
+STATUS_PLAN_MISMATCH = 0x20
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int
@@ -49,6 +50,12 @@ SIGNATURES: dict[str, tuple] = {
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _i, _p],
     ),
     "kvc_paged_attention_v2_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _i, _p]),
+    "kvc_decode_plan_size": (ctypes.c_int64, [_i, _i, _i, _i]),
+    "kvc_decode_plan": (_i, [_p, _p, _i, _i, _i, _p]),
+    "kvc_paged_attention_planned": (
+        _i,
+        [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _i, _p, _p],
+    ),
     "kvc_paged_attention_cascade": (
         _i,
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _i, _i, _i, _p],

@@ -120,13 +120,20 @@ def paged_attention_v2(
     workspace=None,
     out=None,
     stream=None,
+    plan=None,
 ):
     """Split-K decode: partitions of `partition_size` tokens, each producing
     (max, sum, unnormalised output) partials, merged by a log-sum-exp reduce.
-    Same arguments and result as paged_attention_v1."""
+    Same arguments and result as paged_attention_v1.
+
+    plan: a DecodePlan of make_decode_plan (same lengths, num_kv_heads,
+    max_seq_len and partition_size): the partitions then run longest first and
+    the last partition of a sequence merges its partials (no reduce kernel)."""
     query, key_cache, value_cache = _dev(query), _dev(key_cache), _dev(value_cache)
     block_tables, context_lens, alibi_slopes = _dev(block_tables), _dev(context_lens), _dev(alibi_slopes)
     shape, _, _, _, dev = describe(query)
+    if plan is not None and int(plan.partition_size) != int(partition_size):
+        raise ValueError(f"the plan was made for partition_size {plan.partition_size}, not {partition_size}")
     if out is None:
         out = _out_like_query(query)
     if workspace is None:
@@ -136,12 +143,60 @@ def paged_attention_v2(
                                            (query, "query"), (key_cache, "key_cache"), (value_cache, "value_cache"),
                                            (block_tables, "block_tables"), (context_lens, "context_lens"),
                                            (alibi_slopes, "alibi_slopes"))]
-    rc = _L.kvc_paged_attention_v2(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ptrs[4][0], ptrs[5][0],
-                                   ptrs[6][0], ptrs[7][0], ptrs[8][0], int(num_kv_heads), float(scale),
-                                   int(block_size), int(max_seq_len), ptrs[9][0], int(partition_size),
-                                   _stream(stream))
+    if plan is not None:
+        pl = as_dltensor(plan.array, "plan")
+        rc = _L.kvc_paged_attention_planned(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ptrs[4][0], ptrs[5][0],
+                                            ptrs[6][0], ptrs[7][0], ptrs[8][0], int(num_kv_heads), float(scale),
+                                            int(block_size), int(max_seq_len), ptrs[9][0], int(partition_size),
+                                            pl[0], _stream(stream))
+    else:
+        rc = _L.kvc_paged_attention_v2(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ptrs[4][0], ptrs[5][0],
+                                       ptrs[6][0], ptrs[7][0], ptrs[8][0], int(num_kv_heads), float(scale),
+                                       int(block_size), int(max_seq_len), ptrs[9][0], int(partition_size),
+                                       _stream(stream))
     _lib.check(rc)
     return out
+
+
+def decode_plan_size(num_seqs: int, num_kv_heads: int, max_seq_len: int, partition_size: int) -> int:
+    """int32 elements of a decode plan (kvc_decode_plan_size)."""
+    n = int(_L.kvc_decode_plan_size(int(num_seqs), int(num_kv_heads), int(max_seq_len), int(partition_size)))
+    if n < 0:
+        raise ValueError(_lib.last_error() or "no decode plan covers these arguments")
+    return n
+
+
+class DecodePlan:
+    """The work list of a planned split-K decode (kvc_decode_plan): device
+    memory written on the GPU from the context lengths, reused by every layer
+    of a decode step (rewrite it with make_decode_plan(..., plan=p) when the
+    lengths change)."""
+
+    def __init__(self, num_seqs: int, num_kv_heads: int, max_seq_len: int, partition_size: int,
+                 device: int | None = None):
+        self.num_seqs, self.num_kv_heads = int(num_seqs), int(num_kv_heads)
+        self.max_seq_len, self.partition_size = int(max_seq_len), int(partition_size)
+        self.array = DeviceArray.empty((decode_plan_size(num_seqs, num_kv_heads, max_seq_len, partition_size),),
+                                       dtypes.int32, device)
+
+
+def make_decode_plan(context_lens, num_kv_heads: int, max_seq_len: int, partition_size: int, *, plan=None,
+                     stream=None) -> DecodePlan:
+    """Writes (into `plan`, or a new DecodePlan) the work list of a split-K
+    decode over `context_lens`: every (sequence, partition) item ordered
+    longest first, and zeroed per-(sequence, KV head) arrival counters."""
+    context_lens = _dev(context_lens)
+    shape, _, _, _, dev = describe(context_lens)
+    if plan is None:
+        plan = DecodePlan(shape[0], num_kv_heads, max_seq_len, partition_size, dev)
+    elif (plan.num_seqs, plan.num_kv_heads, plan.max_seq_len, plan.partition_size) != (
+            int(shape[0]), int(num_kv_heads), int(max_seq_len), int(partition_size)):
+        raise ValueError("plan was sized for other num_seqs / num_kv_heads / max_seq_len / partition_size")
+    cl = as_dltensor(context_lens, "context_lens")
+    pl = as_dltensor(plan.array, "plan")
+    _lib.check(_L.kvc_decode_plan(pl[0], cl[0], int(num_kv_heads), int(max_seq_len), int(partition_size),
+                                  _stream(stream)))
+    return plan
 
 
 def paged_attention_flash(

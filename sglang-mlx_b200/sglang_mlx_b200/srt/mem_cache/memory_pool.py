@@ -31,9 +31,11 @@ _L = _lib.lib
 
 
 class TokenPoolAllocator:
-    """Manages allocation of token slots in the KV pool.
+    """Free list of the pool's token slots, handed out last-in first-out.
 
-    Slot 0 is reserved as padding and never allocated.
+    Slot 0 is the padding slot that block tables point at for unused
+    positions; it is never handed out, so a fresh pool gives n, n-1, ..., 1
+    for alloc(n).
     """
 
     def __init__(self, pool_size: int):
@@ -78,11 +80,12 @@ def _index_array(indices, device: int) -> DeviceArray:
 
 
 class MHATokenPool:
-    """Pre-allocated KV cache buffers for all layers.
+    """The K and V device buffers of every layer, allocated once up front.
 
-    Buffer layout per layer: ``(pool_size + 1, n_kv_heads, head_dim)``; slot 0
-    is padding.  Token-first layout; store/fetch convert to/from the
-    ``(1, n_kv_heads, S, head_dim)`` attention format.
+    Each layer holds one ``(pool_size + 1, n_kv_heads, head_dim)`` buffer for K
+    and one for V, a token's row per slot (slot 0 stays padding).  Attention
+    code sees ``(1, n_kv_heads, S, head_dim)`` arrays: store takes that shape
+    and fetch returns it; the decode reads the slots in place.
     """
 
     def __init__(self, pool_size: int, num_layers: int, n_kv_heads: int, head_dim: int,

@@ -267,3 +267,29 @@ def test_prefill_refuses_unsupported_types():
     assert rc == _lib.KVC_EUNSUPPORTED and "paged_prefill supports float16/bfloat16" in _lib.last_error()
     rc = call_prefill(q=(10, 8, 96), kc=(20, 4, 12, 16, 8), vc=(20, 4, 96, 16))
     assert rc == _lib.KVC_EUNSUPPORTED
+
+
+def test_decode_plan_size_and_rejections():
+    L = _lib.lib
+    assert L.kvc_decode_plan_size(256, 1, 4112, 2048) == 8 + 256 * 3 + 256
+    assert L.kvc_decode_plan_size(4, 2, 100, 512) == 8 + 4 * 1 + 8
+    assert L.kvc_decode_plan_size(4, 2, 100, 48) == -1      # not a multiple of 32
+    assert L.kvc_decode_plan_size(4, 2, 100, 16384) == -1   # larger than the planner's histogram
+    assert L.kvc_decode_plan_size(70000, 2, 100, 512) == -1
+    with pytest.raises(ValueError):
+        metal_kernels.decode_plan_size(4, 2, 100, 48)
+    rc = L.kvc_decode_plan(fake((100,), "int32"), fake((4,), "int32"), 2, 100, 48, None)
+    expect(rc, "partition_size of a decode plan")
+    rc = L.kvc_decode_plan(fake((10,), "int32"), fake((4,), "int32"), 2, 100, 512, None)
+    expect(rc, "plan holds 10 elements")
+    rc = L.kvc_decode_plan(fake((100,), "float32"), fake((4,), "int32"), 2, 100, 512, None)
+    expect(rc, "plan must be int32")
+
+
+def test_planned_decode_rejects_small_plan():
+    q = (2, 8, 64)
+    rc = _lib.lib.kvc_paged_attention_planned(
+        fake(q), fake((2, 8, 2), "float32"), fake((2, 8, 2), "float32"), fake((2, 8, 2, 64), "float32"), fake(q),
+        fake((20, 4, 8, 16, 8)), fake((20, 4, 64, 16)), fake((2, 4), "int32"), fake((2,), "int32"), 4, 0.1, 16, 64,
+        None, 32, fake((5,), "int32"), None)
+    expect(rc, "plan holds 5 elements")

@@ -1,0 +1,234 @@
+"""GPU tests of the planned split-K decode (kvc_decode_plan +
+kvc_paged_attention_planned): the work list the plan kernel writes (every
+(sequence, partition) item exactly once, sizes non-increasing, counters zero),
+and the decode against the float64 oracle and the plain split-K decode, over
+dtypes, head and block sizes, group sizes, ALiBi, the zero-output edge rules,
+many partitions (the separate-reduce form), a plan reused by many layers,
+CUDA-graph capture and a mismatched plan."""
+
+import math
+
+import numpy as np
+import pytest
+
+import cases
+from helpers import ATOL_NS, RTOL_NS, assert_close, fill_cache, oracle_fill, upload_case
+from oracle import kv_oracle
+from sglang_mlx_b200 import _lib
+from sglang_mlx_b200 import metal_kernels as mk
+from sglang_mlx_b200.device_array import DeviceArray, Graph, Stream
+
+pytestmark = pytest.mark.gpu
+
+
+def expected_items(lens, max_seq_len, P):
+    """(sequence, partition, size) of every item the plan must hold."""
+    items = []
+    for b, C in enumerate(int(x) for x in lens):
+        if C == 0 or C > max_seq_len:
+            items.append((b, 0, 0))
+            continue
+        n = -(-C // P)
+        items += [(b, k, P) for k in range(n - 1)]
+        items.append((b, n - 1, C - (n - 1) * P))
+    return items
+
+
+@pytest.mark.parametrize("P,lens", [
+    (512, [1, 512, 513, 4097, 0, 9000, 1500, 2048]),
+    (2048, list(np.random.default_rng(3).integers(0, 6000, size=300))),
+    (32, [31, 32, 33, 64, 1000]),
+])
+def test_plan_holds_every_item_longest_first(gpu, P, lens):
+    lens = np.asarray(lens, np.int32)
+    max_seq_len = 8192
+    hkv = 3
+    plan = mk.make_decode_plan(DeviceArray.from_numpy(lens), hkv, max_seq_len, P)
+    raw = plan.array.to_numpy().view(np.uint32)
+    want = expected_items(lens, max_seq_len, P)
+    assert raw[0] == 0x4E4C5044 and list(raw[1:5]) == [len(lens), hkv, max_seq_len, P]
+    n = int(raw[5])
+    assert n == len(want)
+    items = raw[8:8 + n]
+    got = [(int(i & 0xFFFF), int(i >> 16)) for i in items]
+    assert sorted(got) == sorted((b, k) for b, k, _ in want)
+    size = {(b, k): s for b, k, s in want}
+    sizes = [size[x] for x in got]
+    assert all(a >= b for a, b in zip(sizes, sizes[1:])), "items must be ordered longest first"
+    max_items = mk.decode_plan_size(len(lens), hkv, max_seq_len, P) - 8 - len(lens) * hkv
+    counters = raw[8 + max_items:8 + max_items + len(lens) * hkv]
+    assert not counters.any()
+
+
+def _run(c, d, P, alibi=None, plan=None, max_seq_len=None):
+    msl = max_seq_len or c["max_seq_len"]
+    if plan is None:
+        plan = mk.make_decode_plan(d["context_lens"], c["num_kv_heads"], msl, P)
+    return mk.paged_attention_v2(d["q"], d["k_cache"], d["v_cache"], d["block_tables"], d["context_lens"],
+                                 c["num_kv_heads"], c["scale"], c["block_size"], msl, alibi, partition_size=P,
+                                 plan=plan).to_numpy()
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("bs", [8, 16, 32])
+def test_planned_matches_oracle(gpu, dtype, D, bs):
+    lens = [1, 37, 300, 1025, 2048, 2049, 5000, 640]
+    c = cases.paged_batch(7000 + D + bs, dtype, len(lens), 8, 2, D, bs, lens)
+    d = upload_case(c)
+    fill_cache(d)
+    kc, vc = oracle_fill(c, dtype)
+    ref = kv_oracle.paged_attention_v1(c["q"], kc, vc, c["block_tables"], c["context_lens"], 2, c["scale"], bs,
+                                       c["max_seq_len"])
+    for P in (256, 1024):
+        out = _run(c, d, P)
+        assert_close(out, ref, ATOL_NS, RTOL_NS, f"planned P={P}")
+    assert gpu.get_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(4, 1), (16, 2), (28, 4), (64, 8), (32, 2)])
+def test_planned_group_sizes_and_v2_agreement(gpu, Hq, Hkv):
+    rng = np.random.default_rng(Hq)
+    lens = rng.integers(1, 3000, size=40)
+    c = cases.paged_batch(7100 + Hq, "bfloat16", len(lens), Hq, Hkv, 128, 16, lens)
+    d = upload_case(c)
+    fill_cache(d)
+    kc, vc = oracle_fill(c, "bfloat16")
+    out = _run(c, d, 512)
+    v2 = mk.paged_attention_v2(d["q"], d["k_cache"], d["v_cache"], d["block_tables"], d["context_lens"], Hkv,
+                               c["scale"], 16, c["max_seq_len"], partition_size=512).to_numpy()
+    assert_close(out, v2, ATOL_NS, RTOL_NS, "planned vs v2")
+    pick = [0, len(lens) // 2, len(lens) - 1]
+    ref = kv_oracle.paged_attention_v1(c["q"][pick], kc, vc, c["block_tables"][pick], c["context_lens"][pick], Hkv,
+                                       c["scale"], 16, c["max_seq_len"])
+    assert_close(out[pick], ref, ATOL_NS, RTOL_NS, "planned vs oracle")
+    assert gpu.get_status(clear=True) == 0
+
+
+def test_planned_alibi_and_zero_rules(gpu):
+    lens = [0, 100, 700, 2000, 1500]
+    c = cases.paged_batch(7200, "float16", len(lens), 8, 2, 128, 16, lens)
+    d = upload_case(c)
+    fill_cache(d)
+    kc, vc = oracle_fill(c, "float16")
+    slopes = np.linspace(-0.5, 0.25, 8).astype(np.float32)
+    out = _run(c, d, 512, alibi=DeviceArray.from_numpy(slopes))
+    ref = kv_oracle.paged_attention_v1(c["q"], kc, vc, c["block_tables"], c["context_lens"], 2, c["scale"], 16,
+                                       c["max_seq_len"], slopes)
+    assert_close(out, ref, ATOL_NS, RTOL_NS, "alibi")
+    assert not out[0].any()
+    # lengths past max_seq_len give zeros (paged_attention_kernels.metal:45-50)
+    out = _run(c, d, 512, max_seq_len=1024)
+    assert not out[0].any() and not out[3].any() and not out[4].any()
+    ref = kv_oracle.paged_attention_v1(c["q"], kc, vc, c["block_tables"], c["context_lens"], 2, c["scale"], 16, 1024)
+    assert_close(out, ref, ATOL_NS, RTOL_NS, "max_seq_len")
+    assert gpu.get_status(clear=True) == 0
+
+
+def test_many_partitions_use_the_reduce_kernel(gpu):
+    """Over 32 partitions per sequence the partials go through the reduce kernel."""
+    lens = [40000, 5, 17000]
+    c = cases.paged_batch(7300, "bfloat16", len(lens), 8, 1, 64, 32, lens)
+    d = upload_case(c)
+    fill_cache(d)
+    kc, vc = oracle_fill(c, "bfloat16")
+    out = _run(c, d, 512)
+    ref = kv_oracle.paged_attention_v1(c["q"], kc, vc, c["block_tables"], c["context_lens"], 1, c["scale"], 32,
+                                       c["max_seq_len"])
+    assert_close(out, ref, ATOL_NS, RTOL_NS, "80 partitions")
+    assert gpu.get_status(clear=True) == 0
+
+
+def test_plan_reused_by_layers_and_graph_capture(gpu):
+    """One plan serves many decodes (the counters return to zero), also when the
+    plan and the decodes are replayed as one CUDA graph."""
+    lens = list(np.random.default_rng(9).integers(100, 4000, size=64))
+    c = cases.paged_batch(7400, "bfloat16", len(lens), 4, 1, 128, 16, lens)
+    d = upload_case(c)
+    fill_cache(d)
+    kc, vc = oracle_fill(c, "bfloat16")
+    ref = kv_oracle.paged_attention_v1(c["q"], kc, vc, c["block_tables"], c["context_lens"], 1, c["scale"], 16,
+                                       c["max_seq_len"])
+    plan = mk.make_decode_plan(d["context_lens"], 1, c["max_seq_len"], 1024)
+    ws = mk.splitk_workspace(len(lens), 4, 128, c["max_seq_len"], 1024)
+    outs = [DeviceArray.empty((len(lens), 4, 128), "bfloat16") for _ in range(4)]
+    st = Stream()
+
+    def step():
+        mk.make_decode_plan(d["context_lens"], 1, c["max_seq_len"], 1024, plan=plan, stream=st)
+        for o in outs:
+            mk.paged_attention_v2(d["q"], d["k_cache"], d["v_cache"], d["block_tables"], d["context_lens"], 1,
+                                  c["scale"], 16, c["max_seq_len"], partition_size=1024, workspace=ws, out=o,
+                                  stream=st, plan=plan)
+
+    step()
+    st.synchronize()
+    for o in outs:
+        assert_close(o.to_numpy(), ref, ATOL_NS, RTOL_NS, "eager layer")
+        o.fill_zero()
+    _lib.synchronize()
+    g = Graph.capture(st, step)
+    for _ in range(3):
+        g.replay(st)
+    st.synchronize()
+    for o in outs:
+        assert_close(o.to_numpy(), ref, ATOL_NS, RTOL_NS, "graph replay")
+    assert gpu.get_status(clear=True) == 0
+
+
+def test_mismatched_plan_writes_nothing_and_flags(gpu):
+    lens = [300, 900]
+    c = cases.paged_batch(7500, "bfloat16", 2, 8, 2, 128, 16, lens)
+    d = upload_case(c)
+    fill_cache(d)
+    # a plan for another max_seq_len: large enough to pass the size check, so the kernel must catch it
+    big = mk.make_decode_plan(d["context_lens"], 2, 2 * c["max_seq_len"], 256)
+    out = DeviceArray.from_numpy(np.full((2, 8, 128), 3.0, np.float32), dtype="bfloat16")
+    mk.paged_attention_v2(d["q"], d["k_cache"], d["v_cache"], d["block_tables"], d["context_lens"], 2, c["scale"], 16,
+                          c["max_seq_len"], partition_size=256, out=out, plan=big)
+    assert (out.to_numpy() == 3.0).all()
+    assert gpu.get_status(clear=True) & _lib.STATUS_PLAN_MISMATCH
+
+
+def test_config2_eight_way_share(gpu):
+    """The share of one rank of an 8-GPU run of BASELINE config 2 (one KV head,
+    256 sequences of U[512, 4096] tokens) with 2048-token partitions, against
+    the plain split-K decode, plus a sample against the CPU oracle."""
+    torch = pytest.importorskip("torch")
+    from oracle import c_oracle
+
+    w = cases.baseline_workload(2)
+    lens = (w["lens"] + 1).astype(np.int32)
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    kc = torch.randn((w["num_blocks"], 1, 16, 16, 8), generator=g, device=dev, dtype=torch.bfloat16)
+    vc = torch.randn((w["num_blocks"], 1, 128, 16), generator=g, device=dev, dtype=torch.bfloat16)
+    q = torch.randn((256, 4, 128), generator=g, device=dev, dtype=torch.bfloat16)
+    tables = DeviceArray.from_numpy(w["tables"])
+    lens_d = DeviceArray.from_numpy(lens)
+    scale = 1.0 / math.sqrt(128)
+    plan = mk.make_decode_plan(lens_d, 1, w["max_seq_len"], 2048)
+    out = mk.paged_attention_v2(q, kc, vc, tables, lens_d, 1, scale, 16, w["max_seq_len"], partition_size=2048,
+                                plan=plan).to_numpy()
+    v2 = mk.paged_attention_v2(q, kc, vc, tables, lens_d, 1, scale, 16, w["max_seq_len"],
+                               partition_size=2048).to_numpy()
+    assert_close(out, v2, ATOL_NS, RTOL_NS, "planned vs v2")
+    rows = [0, 100, 255]
+    nb = [(-(-int(lens[b]) // 16)) for b in rows]
+    ids = np.concatenate([w["tables"][b, :n] for b, n in zip(rows, nb)]).astype(np.int64)
+    t2 = np.zeros((3, max(nb)), np.uint32)
+    o = 0
+    for i, n in enumerate(nb):
+        t2[i, :n] = np.arange(o, o + n)
+        o += n
+    idx = torch.from_numpy(ids).to(dev)
+
+    def bits(t):
+        return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+    ref = c_oracle.paged_attention(bits(q[torch.tensor(rows, device=dev)]), "bfloat16", bits(kc.index_select(0, idx)),
+                                   bits(vc.index_select(0, idx)), "bfloat16", t2, lens[rows], 1, scale,
+                                   int(t2.shape[1] * 16))
+    assert_close(out[rows], ref, ATOL_NS, RTOL_NS, "planned vs oracle")
+    assert gpu.get_status(clear=True) == 0
