@@ -412,14 +412,17 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
     slots = np.concatenate([pre, w["decode_slots"][plan.seqs]]).astype(np.int32)
     T_new = len(slots)
     shared = config == 4
-    pool = args.layout == "pool" and top
+    pool = args.layout in ("pool", "pool-pages") and top
+    pool_pages = args.layout == "pool-pages" and top  # the pool read through page tables (page_size = block size)
     fp8 = args.kv_dtype.startswith("fp8") and top
     fmt = args.kv_dtype[4:] if fp8 else None
     if fp8 and (pool or args.decode in ("cascade", "planned")):
         raise SystemExit("--kv-dtype fp8 runs on the paged layout with the single-pass / split-K decode")
+    page_tables = tables
     if pool:
         # MHATokenPool layout: block b's tokens are slots b*BS+1 .. b*BS+BS (slot 0 is
-        # the pool's padding slot); the block tables become per-token slot lists
+        # the pool's padding slot), i.e. block b is page b of a page-granular pool; the
+        # slot-list form of the tables lists every token's slot
         t = np.arange(tables.shape[1] * BS)
         blk = tables[:, t // BS].astype(np.int64)
         tables = np.ascontiguousarray(np.where(blk >= 0, blk * BS + t % BS + 1, 0).astype(np.int32))
@@ -456,19 +459,31 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
     kn = [DeviceArray.from_dlpack(kn_t[i]) for i in range(L)]
     vn = [DeviceArray.from_dlpack(vn_t[i]) for i in range(L)]
     out = [DeviceArray.empty((B, hq, D), "bfloat16", dev) for _ in range(L)]
-    tables_d = DeviceArray.from_numpy(tables, device=dev)
+    tables_d = DeviceArray.from_numpy(page_tables if pool_pages else tables, device=dev)
+    if pool_pages:  # page view of each layer's pool buffers: [num_blocks, BS, kv heads, D] from slot 1
+        kview = [a[1:].reshape(num_blocks, BS, hkv, D) for a in kc]
+        vview = [a[1:].reshape(num_blocks, BS, hkv, D) for a in vc]
     lens_d = DeviceArray.from_numpy(lens_after.astype(np.int32), device=dev)
     slots_d = DeviceArray.from_numpy(slots, device=dev)
     flush = DeviceArray.empty((L2_FLUSH_BYTES,), "int32", dev) if cfg.get("l2_flush") else None
     scale = 1.0 / math.sqrt(D)
 
-    # decode form: config 3 fixes 512-token partitions; otherwise the shim's heuristic
-    # (the token-pool kernel runs 16-token groups, two CTAs per SM)
-    psize = cfg["partition"] or mk.choose_decode(B, hkv, max_seq_len, 16 if pool else BS)
+    # decode form.  auto: config 3 runs BASELINE's 512-token split-K; the paged bf16
+    # caches otherwise run the planned split-K (work list longest first, one plan per
+    # step) with the shim's partition choice; the token pool and FP8 caches, which
+    # have no planned entry point, the shim's single-pass / split-K heuristic (the
+    # token-pool kernel runs 16-token groups, two CTAs per SM)
+    heuristic = mk.choose_decode(B, hkv, max_seq_len, 16 if pool else BS)
+    planned_p = mk.choose_planned_partition(B, hkv, max_seq_len, BS, lens_after)
+    auto_planned = args.decode == "auto" and not (cfg["partition"] or pool or fp8)
     if args.decode == "v1":
         psize = 0
-    elif args.decode in ("v2", "planned"):
-        psize = args.partition or psize or 512
+    elif args.decode == "v2":
+        psize = args.partition or cfg["partition"] or heuristic or 512
+    elif args.decode == "planned" or auto_planned:
+        psize = args.partition or planned_p
+    else:
+        psize = cfg["partition"] or heuristic
     if args.partition and psize and top:
         psize = args.partition
     # config 4 is a radix-cache hit: every table starts with the same prefix, which
@@ -482,7 +497,7 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
         cws = mk.cascade_workspace(B, hq, D, max_seq_len, prefix, pp, pt, dev)
         psize = 0
     split = psize > 0
-    planned = split and args.decode == "planned" and not pool
+    planned = split and (args.decode == "planned" or auto_planned) and not pool
     ws = mk.splitk_workspace(B, hq, D, max_seq_len, psize, dev) if split else None
     dplan = mk.DecodePlan(B, hkv, max_seq_len, psize, dev) if planned else None
     torch.cuda.synchronize()
@@ -509,6 +524,9 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
             return mk.paged_attention_cascade(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, BS, max_seq_len, prefix,
                                               prefix_partition_size=pp, partition_size=pt, workspace=cws, out=out[i],
                                               stream=stream)
+        if pool_pages:
+            return mk.paged_attention_flash(q[i], kview[i], vview[i], tables_d, lens_d, hkv, scale, BS, max_seq_len,
+                                            partition_size=psize, workspace=ws, out=out[i], stream=stream)
         if pool:
             return mk.paged_attention_flash(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, 1, max_seq_len,
                                             partition_size=psize, workspace=ws, out=out[i], stream=stream)
@@ -668,7 +686,8 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
     step_ms = total_ms / args.steps
     e2e_step_ms = e2e_ms / args.steps
     mean_dec_ms = float(np.mean(dec_ms))
-    alg, logical = decode_bytes(tables, lens_after, hq, hkv, D, tab_bs, shared, s_kv=1 if fp8 else 2)
+    alg, logical = decode_bytes(page_tables if pool_pages else tables, lens_after, hq, hkv, D,
+                                BS if pool_pages else tab_bs, shared, s_kv=1 if fp8 else 2)
     sums = np.array([float(alg), float(logical), float(h2d), float(d2h)])
     if dist is not None:
         t = torch.tensor([step_ms, e2e_step_ms, mean_dec_ms, 0.0 if ok else 1.0, err], dtype=torch.float64)
@@ -685,7 +704,7 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
         return None
     alg_all, logical_all, h2d_all, d2h_all = sums
     peak, peak_kind = load_peaks()
-    kernel_key = ("cascade" if cascade else "pool" if pool else f"fp8-{fmt}" if fp8 else
+    kernel_key = ("cascade" if cascade else "pool-pages" if pool_pages else "pool" if pool else f"fp8-{fmt}" if fp8 else
                   f"planned{psize}" if planned else f"splitk{psize}" if split else "v1")
     traffic = (load_traffic(config, kernel_key)
                if (world == 1 and not (args.layers or args.batch or args.kv_heads)) else None)
@@ -695,7 +714,8 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
     if planned:
         kernel = f"planned split-K, {psize}-token partitions longest first, merge fused"
     if pool:
-        kernel = "token-pool decode (paged_attention_flash, slot lists" + (
+        kernel = "token-pool decode (paged_attention_flash, " + (
+            f"{BS}-token page tables, tensor copies" if pool_pages else "slot lists") + (
             f", {psize}-token partitions)" if split else ", single pass)")
     if fp8:
         kernel = f"FP8 ({fmt}) cache decode, " + (f"{psize}-token partitions" if split else "single pass")
@@ -705,7 +725,8 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
              "l2": ("flushed between steps (unique KV fits in L2)" if flush is not None else
                     f"inputs larger than L2 (KV per layer {logical_all / 1e9:.2f} GB); no flush")}
     if pool:
-        extra["layout"] = "MHATokenPool buffers [slots, kv_heads, head_dim], slot-list tables"
+        extra["layout"] = ("MHATokenPool buffers [slots, kv_heads, head_dim], " +
+                           (f"page tables ({BS}-slot pages)" if pool_pages else "slot-list tables"))
     line = {
         "metric": METRIC,
         "value": toks,
@@ -1021,8 +1042,9 @@ def main():
                     help="one-GPU default run: skip the nested measurements of configs 3, 4 and 5")
     ap.add_argument("--kv-dtype", default="bf16", choices=["bf16", "fp8-e4m3", "fp8-e5m2"],
                     help="cache element type: bf16 (default) or one-byte FP8 codes (half the KV bytes)")
-    ap.add_argument("--layout", default="paged", choices=["paged", "pool"],
-                    help="cache layout: the vLLM paged layout (default) or the MHATokenPool token pool")
+    ap.add_argument("--layout", default="paged", choices=["paged", "pool", "pool-pages"],
+                    help="cache layout: the vLLM paged layout (default), the MHATokenPool token pool read through "
+                         "slot lists, or the same pool read through page tables (a page-granular allocator)")
     ap.add_argument("--decode", default="auto", choices=["auto", "v1", "v2", "planned", "cascade"],
                     help="decode form: the shim's choice (default; shared-prefix cascade for config 4), single pass, "
                          "split-K, planned split-K (work list longest first, merge fused), or cascade")

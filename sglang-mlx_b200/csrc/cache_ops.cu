@@ -15,6 +15,12 @@
 
 namespace kvc {
 
+// Programmatic dependent launch: the appends let the decode that follows them
+// on the stream get its CTAs resident while they run (the decode waits, with
+// griddepcontrol.wait, for their completion before it reads anything).
+__device__ __forceinline__ void let_dependents_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+
 __device__ unsigned int g_cache_ops_status = 0;
 
 // ---------------------------------------------------------------------------
@@ -51,6 +57,7 @@ __global__ void __launch_bounds__(kAppendThreads) reshape_and_cache_kernel(Resha
   constexpr int X = 16 / sizeof(CACHE_T);
   constexpr int VPAD = sizeof(CACHE_T) == 2 ? 2 : 1;  // odd word stride for the V tile
   extern __shared__ __align__(16) unsigned char smem_raw[];
+  let_dependents_launch();
   __shared__ int64_t s_blk[kTokTile];
   __shared__ int s_off[kTokTile];
 
@@ -172,6 +179,7 @@ struct RowCopyParams {
 
 template <typename VEC>
 __global__ void __launch_bounds__(256) row_copy_kernel(RowCopyParams p) {
+  let_dependents_launch();
   const int which = blockIdx.y;
   const int vec_per_row = p.row_bytes / (int)sizeof(VEC);
   const int64_t rows = p.n_rows_tok * p.num_heads;
@@ -460,6 +468,7 @@ __device__ __forceinline__ float fp8_decode(uint32_t c) {
 // the chunk of K (one 16-byte store) and of V (16 bytes at a stride of bs).
 template <typename KV_T, int FMT>
 __global__ void __launch_bounds__(256) reshape_and_cache_fp8_kernel(ReshapeArgs a) {
+  let_dependents_launch();
   const int chunks = a.head_size / 16;
   const int64_t total = a.num_tokens * a.num_heads * chunks;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;

@@ -53,6 +53,8 @@ struct DecodeParams {
   int prefix_len, prefix_parts, prefix_part_size, part_offset;
   float k_scale, v_scale;  // one-byte caches: dequantisation scales (value = code * scale)
   int wait_prior_at_end;   // partition kernel: griddepcontrol.wait before exiting (shared-prefix launch order)
+  int wait_prior_at_start; // partition kernel launched as a programmatic dependent of the kernel before it
+                           // (an append): griddepcontrol.wait before its first global read
   int64_t table_stride;
   int64_t part_seq_stride, part_head_stride;
   int64_t part_out_seq_stride, part_out_head_stride, part_out_part_stride;
@@ -143,21 +145,12 @@ __device__ __forceinline__ int planned_parts(const DecodeParams& p, uint32_t ctx
   return (int)((ctx + (uint32_t)p.partition_size - 1) / (uint32_t)p.partition_size);
 }
 
-// Called by every thread of the CTA after it wrote its partition's partials:
-// counts the arrival, and the CTA that completes the sequence's set merges
-// the `nparts` (<= 32) partials of heads h0 .. h0 + G - 1 into the output and
-// resets the counter.  `scratch` holds at least G * 32 + G floats (shared).
+// Merges the `nparts` (<= 32) partials of heads h0 .. h0 + G - 1 of `seq` into
+// the output.  Every thread of the CTA calls it; the partials must be visible to
+// the CTA, and `scratch` (at least G * 32 + G floats of shared memory) free.
 template <typename T>
-__device__ __forceinline__ void planned_arrive_and_merge(const DecodeParams& p, int seq, int kvh, int h0, int G,
-                                                         int D, int nparts, float* scratch) {
-  __shared__ uint32_t s_last;
-  __threadfence();  // this thread's partials are visible before the arrival below
-  __syncthreads();
-  uint32_t* counter = p.plan_counters + (int64_t)seq * p.num_kv_heads + kvh;
-  if (threadIdx.x == 0) s_last = atomicAdd(counter, 1u) == (uint32_t)(nparts - 1) ? 1u : 0u;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
+__device__ __forceinline__ void merge_head_partials(const DecodeParams& p, int seq, int h0, int G, int D, int nparts,
+                                                    float* scratch) {
   // weights e^{m_k - M} of every partition, and 1 / (L + 1e-6), per head
   float* w = scratch;                 // [G][32]
   float* inv = scratch + G * 32;      // [G]
@@ -183,6 +176,23 @@ __device__ __forceinline__ void planned_arrive_and_merge(const DecodeParams& p, 
     for (int k = 0; k < nparts; ++k) a += w[g * 32 + k] * __ldcg(po + (int64_t)k * p.part_out_part_stride);
     out[(int64_t)seq * p.out_seq_stride + (int64_t)(h0 + g) * p.out_head_stride + d] = from_float<T>(a * inv[g]);
   }
+}
+
+// Called by every thread of the CTA after it wrote its partition's partials:
+// counts the arrival, and the CTA that completes the sequence's set merges
+// the `nparts` (<= 32) partials into the output and resets the counter.
+template <typename T>
+__device__ __forceinline__ void planned_arrive_and_merge(const DecodeParams& p, int seq, int kvh, int h0, int G,
+                                                         int D, int nparts, float* scratch) {
+  __shared__ uint32_t s_last;
+  __threadfence();  // this thread's partials are visible before the arrival below
+  __syncthreads();
+  uint32_t* counter = p.plan_counters + (int64_t)seq * p.num_kv_heads + kvh;
+  if (threadIdx.x == 0) s_last = atomicAdd(counter, 1u) == (uint32_t)(nparts - 1) ? 1u : 0u;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  merge_head_partials<T>(p, seq, h0, G, D, nparts, scratch);
   if (threadIdx.x == 0) *counter = 0u;  // ready for the next call with this plan
 }
 
@@ -649,6 +659,7 @@ static DecodeParams to_params(const DecodeArgs& a) {
   p.prefix_part_size = a.prefix_part_size;
   p.part_offset = 0;
   p.wait_prior_at_end = 0;
+  p.wait_prior_at_start = 0;
   p.k_scale = a.cache_type == ElemType::U8 ? a.k_scale : 1.f;
   p.v_scale = a.cache_type == ElemType::U8 ? a.v_scale : 1.f;
   p.table_stride = a.table_stride;

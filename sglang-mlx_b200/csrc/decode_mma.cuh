@@ -141,6 +141,14 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
 __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -230,7 +238,15 @@ constexpr float kLn2 = 0.6931471805599453f;
 //  kFp8E4M3 / kFp8E5M2  one-byte caches in the paged layout (K pages
 //             [D/16][bs][16], V pages [D][bs] bytes), 1-D bulk copies of whole
 //             pages; mma_group_fp8 converts codes to f16 in registers.
-constexpr int kBulk = 0, kTiles = 1, kSwizzledV = 2, kFlash = 3, kFp8E4M3 = 4, kFp8E5M2 = 5, kFlashBulk = 6;
+//  kFlashTma  token-major caches whose blocks hold a multiple of 16 tokens in
+//             consecutive rows ([nb, bs, H, D] with dense blocks, or a token pool
+//             handing out whole pages): a group's GT rows of one head are one
+//             tiled tensor copy per 64 dims, landing as GT rows of 128 bytes with
+//             the 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r & 7)),
+//             K and V both read with ldmatrix (V transposed).  One copy per
+//             (group, head, 64 dims) instead of a 16-byte cp.async per lane and row.
+constexpr int kBulk = 0, kTiles = 1, kSwizzledV = 2, kFlash = 3, kFp8E4M3 = 4, kFp8E5M2 = 5, kFlashBulk = 6,
+              kFlashTma = 7;
 
 template <int D, int BS, int NW, int STAGES, int GT_ = 32, int MODE = kBulk>
 struct MmaGeom {
@@ -238,7 +254,8 @@ struct MmaGeom {
   static constexpr bool FLASH = MODE == kFlash || MODE == kFlashBulk;  // token-major K/V rows
   static constexpr bool CP_ASYNC = MODE == kFlash;        // stage completion: 32 cp.async arrivals
   static constexpr bool FP8 = MODE == kFp8E4M3 || MODE == kFp8E5M2;  // one-byte caches
-  static constexpr int VBS = FLASH ? 1 : (MODE == kTiles ? (GT < BS ? GT : BS) : BS);  // tokens per box
+  static constexpr bool TROWS = MODE == kFlashTma;        // token rows by tensor copies, swizzled 128-byte halves
+  static constexpr int VBS = FLASH ? 1 : (TROWS ? GT : (MODE == kTiles ? (GT < BS ? GT : BS) : BS));  // tokens per box
   static constexpr int NBOX = GT / VBS;                   // boxes per group (K and V each)
   static constexpr uint32_t FULL_MASK = NBOX >= 32 ? 0xffffffffu : (1u << (NBOX & 31)) - 1u;  // every box loaded
   static_assert(GT % 16 == 0 && GT % VBS == 0, "a group is whole boxes and whole 16-token k-steps");
@@ -247,7 +264,7 @@ struct MmaGeom {
   static constexpr int BOX = FLASH ? ROWB + 16 : D * VBS * (FP8 ? 1 : 2);  // bytes (stride) of one K (or V) box
   static constexpr int VSWZ = MODE == kSwizzledV ? 128 : (MODE == kTiles && VBS * 2 >= 32 ? VBS * 2 : 0);
   static constexpr int STAGE = NBOX * 2 * BOX;            // K boxes then V boxes
-  static constexpr int ALIGN = (MODE == kTiles || MODE == kSwizzledV) ? 1024 : 0;  // ring alignment (swizzle atoms)
+  static constexpr int ALIGN = (MODE == kTiles || MODE == kSwizzledV || TROWS) ? 1024 : 0;  // ring alignment (swizzle atoms)
   static constexpr int RING = NW * STAGES * STAGE;
   static constexpr int BAR_OFF = ALIGN + RING;            // NW*STAGES mbarriers
   static constexpr int MASK_OFF = BAR_OFF + NW * STAGES * 8;
@@ -333,7 +350,10 @@ __device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa
 #pragma unroll
     for (int ks = 0; ks < KS; ks += 2) {
       const int chunk = 2 * ks + (lane >> 3);
-      const uint32_t addr = kst + bx * BOX + (chunk * VBS + off) * 16;
+      // kFlashTma: 64-dim halves of GT swizzled 128-byte rows
+      const uint32_t addr = Geo::TROWS ? kst + (uint32_t)((chunk >> 3) * (GT * 128) + tok * 128 +
+                                                         (((chunk & 7) ^ (tok & 7)) << 4))
+                                       : kst + bx * BOX + (chunk * VBS + off) * 16;
       uint32_t b0, b1, b2, b3;
       ldmatrix_x4(addr, b0, b1, b2, b3);
       MmaOp<T>::run(sacc[j], qa[ks], b0, b1);
@@ -442,6 +462,13 @@ __device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa
         // 16-byte dim chunk nt + mi/2; transposed on load
         const uint32_t row = (uint32_t)(vtok + (lane & 7));
         ldmatrix_x4_trans(vst + row * BOX + (uint32_t)(nt + (mi >> 1)) * 16, b0, b1, b2, b3);
+        (void)voffb;
+      } else if constexpr (Geo::TROWS) {
+        // the same rows as 64-dim halves of swizzled 128-byte rows
+        const uint32_t row = (uint32_t)(vtok + (lane & 7));
+        const uint32_t ch = (uint32_t)(nt + (mi >> 1));
+        ldmatrix_x4_trans(vst + (ch >> 3) * (uint32_t)(GT * 128) + row * 128u + (((ch & 7u) ^ (row & 7u)) << 4), b0, b1,
+                          b2, b3);
         (void)voffb;
       } else {
         ldmatrix_x4(vst + vbx * BOX + voffb, b0, b1, b2, b3);
@@ -698,6 +725,7 @@ __global__ void __launch_bounds__(NW * 32)
   const int G = p.num_heads / p.num_kv_heads;
 
   grid_dependents_launch();
+  if (p.wait_prior_at_start) grid_dependency_wait();  // the append before us has written the new tokens
   if (p.plan_items && !planned_item(p, &kvh, &seq, &part)) return;  // planned: CTA -> work item of the plan
   const int h0 = kvh * G;
   const uint32_t ctx = p.context_lens[seq];
@@ -789,7 +817,8 @@ __global__ void __launch_bounds__(NW * 32)
   const uint32_t* table = p.block_tables + (int64_t)seq * p.table_stride;
   const int ngroups = (end - begin + GT - 1) / GT;
   const int n_mine = warp < ngroups ? (ngroups - warp + NW - 1) / NW : 0;
-  const int page_end = (end + BS - 1) / BS;  // first page past the context
+  const int rbs = Geo::TROWS ? p.block_size : BS;  // kFlashTma: the block size is read at run time
+  const int page_end = (end + rbs - 1) / rbs;  // first page past the context
 
   // Lane i < NBOX fetches the block id of box i of group `k` of this warp.
   // Token-major caches: lane i < GT fetches the block id of token i of the
@@ -799,7 +828,7 @@ __global__ void __launch_bounds__(NW * 32)
     uint32_t b = 0xffffffffu;
     if constexpr (!Geo::FLASH) {
       if (lane < NBOX && k < n_mine) {
-        const int pg = (begin + (warp + k * NW) * GT + lane * VBS) / BS;
+        const int pg = (begin + (warp + k * NW) * GT + lane * VBS) / rbs;
         if (pg < page_end) b = __ldg(table + pg);
       }
     }
@@ -906,7 +935,7 @@ __global__ void __launch_bounds__(NW * 32)
         uint32_t mask = 0, bytes = 0;
 #pragma unroll
         for (int i = 0; i < NBOX; ++i) {
-          if ((t0 + i * VBS) / BS < page_end) {
+          if ((t0 + i * VBS) / rbs < page_end) {
             if ((int64_t)ids[i] < p.num_blocks) {
               mask |= 1u << i;
               bytes += 2 * BOX;
@@ -922,7 +951,17 @@ __global__ void __launch_bounds__(NW * 32)
 #pragma unroll
           for (int i = 0; i < NBOX; ++i) {
             if (mask & (1u << i)) {
-              if constexpr (MODE == kTiles) {
+              if constexpr (Geo::TROWS) {
+                // GT consecutive rows of block ids[i] (the group never crosses a block:
+                // the block size is a multiple of 16 and groups start 16-aligned)
+                const int row = (int)ids[i] * rbs + (t0 - (t0 / rbs) * rbs);
+                constexpr int HALF = GT * 128;
+#pragma unroll
+                for (int h = 0; h < D / 64; ++h) {
+                  tma_load_3d(st + i * BOX + h * HALF, &tm.k, 64 * h, kvh, row, &bars[s]);
+                  tma_load_3d(st + (NBOX + i) * BOX + h * HALF, &tm.v, 64 * h, kvh, row, &bars[s]);
+                }
+              } else if constexpr (MODE == kTiles) {
                 // token offset of the box inside its page: 0 or a multiple of 16
                 // (16 tokens * 2 bytes = 32 B, so the innermost V coordinate is
                 // 16-byte aligned as tiled copies require)
@@ -1142,8 +1181,12 @@ static bool make_tensor_maps(const DecodeParams& p, ElemType et, int D, int BS, 
   key.ks[1] = p.k_block_stride;
   key.vs[0] = p.v_head_stride;
   key.vs[1] = p.v_block_stride;
+  if (mode == kFlashTma) {  // token rows: the row stride and the run-time block size define the maps
+    key.ks[1] = p.k_tok_stride;
+    key.vs[1] = p.v_tok_stride;
+  }
   key.d = D;
-  key.bs = BS;
+  key.bs = mode == kFlashTma ? p.block_size : BS;
   key.vbs = VBS;
   key.swz = swz;
   key.dt = (int)et;
@@ -1164,6 +1207,27 @@ static bool make_tensor_maps(const DecodeParams& p, ElemType et, int D, int BS, 
   TmaMaps m;
   memset(&m, 0, sizeof(m));
   cuuint32_t ones[5] = {1, 1, 1, 1, 1};
+  if (mode == kFlashTma) {
+    // [rows = num_blocks * bs][H][D] token rows (dense blocks), boxes of 64 dims x 1 head x VBS rows
+    const cuuint64_t rows = (cuuint64_t)p.num_blocks * (cuuint64_t)p.block_size;
+    cuuint64_t dim[3] = {(cuuint64_t)D, (cuuint64_t)p.num_kv_heads, rows};
+    cuuint64_t kstr[2] = {(cuuint64_t)p.k_head_stride * es, (cuuint64_t)p.k_tok_stride * es};
+    cuuint64_t vstr[2] = {(cuuint64_t)p.v_head_stride * es, (cuuint64_t)p.v_tok_stride * es};
+    cuuint32_t box[3] = {64, 1, (cuuint32_t)VBS};
+    if (enc(&m.k, dt, 3, const_cast<void*>(p.k_cache), dim, kstr, box, ones, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+            CUDA_SUCCESS ||
+        enc(&m.v, dt, 3, const_cast<void*>(p.v_cache), dim, vstr, box, ones, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+            CUDA_SUCCESS)
+      return false;
+    keys[next] = key;
+    maps[next] = m;
+    next = (next + 1) % 32;
+    if (used < 32) ++used;
+    *out = m;
+    return true;
+  }
   if (mode == kSwizzledV) {
     const cuuint64_t rows = (cuuint64_t)D * BS / 64;  // 128-byte rows per page
     cuuint64_t vdim[4] = {64, rows, (cuuint64_t)p.num_kv_heads, (cuuint64_t)p.num_blocks};
@@ -1210,7 +1274,7 @@ static cudaError_t launch_mma_nw(const DecodeParams& p, cudaStream_t stream) {
   auto kern = paged_decode_mma_kernel<T, D, BS, NW, STAGES, GT, MODE>;
   TmaMaps maps;
   memset(&maps, 0, sizeof(maps));
-  if (MODE == kTiles || MODE == kSwizzledV) {
+  if (MODE == kTiles || MODE == kSwizzledV || MODE == kFlashTma) {
     const ElemType et = std::is_same<T, __nv_bfloat16>::value ? ElemType::BF16 : ElemType::F16;
     if (!make_tensor_maps(p, et, D, BS, Geo::VBS, Geo::VSWZ, MODE, &maps)) return cudaErrorNotSupported;
   }
@@ -1242,9 +1306,24 @@ static cudaError_t launch_mma_nw(const DecodeParams& p, cudaStream_t stream) {
     count_launch();
     return e != cudaSuccess ? e : cudaGetLastError();
   }
-  kern<<<grid, NW * 32, Geo::SMEM, stream>>>(p, maps);
+  // a programmatic dependent of the kernel before it on the stream: its CTAs
+  // become resident while that kernel (typically the append) finishes, and wait
+  // for it before reading anything (wait_prior_at_start)
+  DecodeParams pp = p;
+  pp.wait_prior_at_start = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(NW * 32);
+  cfg.dynamicSmemBytes = Geo::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, pp, maps);
   count_launch();
-  return cudaGetLastError();
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 // Variant id = warps * 1000 + stages * 100 + group tokens, + 100000 for tiled
@@ -1324,10 +1403,20 @@ static cudaError_t launch_mma_t(const DecodeParams& p, const DecodeArgs& a, cuda
     // token-major caches: 16-token groups, 4 warps x 3 stages (108 KB for
     // D = 128, two CTAs per SM); the block size is read at run time.
     // KVC_FLASH_COPY=bulk selects per-row bulk copies (tuning runs).
+    // KVC_FLASH_COPY=cpasync keeps the per-lane row copies where tensor copies apply (tuning runs).
     const char* fc = getenv("KVC_FLASH_COPY");
     if (fc && fc[0] == 'b') {
       if (a.head_size == 128) return launch_mma_nw<T, 128, 16, 4, 3, 16, kFlashBulk>(p, stream);
       return launch_mma_nw<T, 64, 16, 4, 3, 16, kFlashBulk>(p, stream);
+    }
+    // blocks of 16k consecutive token rows: a tensor copy per (16-token group, head, 64 dims)
+    const bool rows_ok = a.block_size % 16 == 0 && a.k_block_stride == (int64_t)a.block_size * a.k_tok_stride &&
+                         a.v_block_stride == (int64_t)a.block_size * a.v_tok_stride &&
+                         a.num_blocks * (int64_t)a.block_size < (int64_t)1 << 31 && !(fc && fc[0] == 'c');
+    if (rows_ok) {
+      cudaError_t e = a.head_size == 128 ? launch_mma_nw<T, 128, 16, 4, 3, 16, kFlashTma>(p, stream)
+                                         : launch_mma_nw<T, 64, 16, 4, 3, 16, kFlashTma>(p, stream);
+      if (e != cudaErrorNotSupported) return e;
     }
     if (a.head_size == 128) return launch_mma_nw<T, 128, 16, 4, 3, 16, kFlash>(p, stream);
     return launch_mma_nw<T, 64, 16, 4, 3, 16, kFlash>(p, stream);

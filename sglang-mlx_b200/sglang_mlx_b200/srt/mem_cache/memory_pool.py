@@ -36,36 +36,120 @@ class TokenPoolAllocator:
     Slot 0 is the padding slot that block tables point at for unused
     positions; it is never handed out, so a fresh pool gives n, n-1, ..., 1
     for alloc(n).
+
+    page_size > 1 (the reference's radix cache is page-size-1 only,
+    radix_cache.py:11, cache_init_params.py:16) hands out whole pages: page p
+    holds slots p * page_size + 1 .. (p + 1) * page_size, so a request's slots
+    fill its pages in order and a decode can read them page by page
+    (MHATokenPool.decode_pages) instead of slot by slot.  alloc(n) takes
+    ceil(n / page_size) free pages and returns their first n slots;
+    alloc_extend(last_slot, n) continues inside last_slot's page before taking
+    new ones; a page returns to the free list once every slot handed out from
+    it has been freed.
     """
 
-    def __init__(self, pool_size: int):
+    def __init__(self, pool_size: int, page_size: int = 1):
         if pool_size <= 0:
             raise ValueError(f"pool_size must be positive, got {pool_size}")
+        if page_size <= 0 or pool_size % page_size:
+            raise ValueError(f"pool_size ({pool_size}) must be a positive multiple of page_size ({page_size})")
         self._pool_size = pool_size
-        # Slots 1..pool_size are allocatable; kept as a stack (memory_pool.py:38).
-        self._free_slots: list[int] = list(range(pool_size, 0, -1))
+        self.page_size = page_size
+        if page_size == 1:
+            # Slots 1..pool_size are allocatable; kept as a stack (memory_pool.py:38).
+            self._free_slots: list[int] = list(range(pool_size, 0, -1))
+        else:
+            self._num_pages = pool_size // page_size
+            self._free_pages: list[int] = list(range(self._num_pages - 1, -1, -1))
+            self._used = [0] * self._num_pages  # slots handed out per page
+
+    def _page_slots(self, page: int) -> range:
+        return range(page * self.page_size + 1, (page + 1) * self.page_size + 1)
+
+    def _take_pages(self, n_pages: int) -> list[int]:
+        if n_pages > len(self._free_pages):
+            raise MemoryError(f"Cannot allocate {n_pages} pages: only {len(self._free_pages)} available")
+        pages = self._free_pages[-n_pages:][::-1]
+        del self._free_pages[-n_pages:]
+        return pages
 
     def alloc(self, n: int) -> list[int]:
-        """Pops the last *n* free slots; MemoryError if fewer are free."""
+        """Pops the last *n* free slots; MemoryError if fewer are free.  With
+        pages: the first n slots of ceil(n / page_size) free pages."""
         if n <= 0:
             return []
-        if n > len(self._free_slots):
-            raise MemoryError(f"Cannot allocate {n} slots: only {len(self._free_slots)} available")
-        allocated = self._free_slots[-n:]
-        del self._free_slots[-n:]
-        return allocated
+        if self.page_size == 1:
+            if n > len(self._free_slots):
+                raise MemoryError(f"Cannot allocate {n} slots: only {len(self._free_slots)} available")
+            allocated = self._free_slots[-n:]
+            del self._free_slots[-n:]
+            return allocated
+        pages = self._take_pages(-(-n // self.page_size))
+        out = []
+        for pg in pages:
+            take = min(self.page_size, n - len(out))
+            out.extend(self._page_slots(pg)[:take])
+            self._used[pg] = take
+        return out
+
+    def alloc_extend(self, last_slot: int, n: int) -> list[int]:
+        """n more slots for a request whose last slot is `last_slot`: the rest of
+        its page first (pages), then new pages.  Page size 1: alloc(n)."""
+        if self.page_size == 1 or n <= 0:
+            return self.alloc(n)
+        page = (int(last_slot) - 1) // self.page_size
+        room = (page + 1) * self.page_size - int(last_slot)
+        take = min(room, n)
+        if take and not 0 <= page < self._num_pages:
+            raise ValueError(f"slot {last_slot} is not in the pool")
+        out = list(range(int(last_slot) + 1, int(last_slot) + 1 + take))
+        if take:
+            self._used[page] += take
+        if n > take:
+            out += self.alloc(n - take)
+        return out
 
     def free(self, indices: list[int]) -> None:
-        """Returns *indices* to the free list."""
-        self._free_slots.extend(indices)
+        """Returns *indices* to the free list (pages: a page once all its handed-out slots are back)."""
+        if self.page_size == 1:
+            self._free_slots.extend(indices)
+            return
+        for i in indices:
+            pg = (int(i) - 1) // self.page_size
+            self._used[pg] -= 1
+            if self._used[pg] == 0:
+                self._free_pages.append(pg)
 
     @property
     def available_size(self) -> int:
-        return len(self._free_slots)
+        if self.page_size == 1:
+            return len(self._free_slots)
+        return len(self._free_pages) * self.page_size
 
     def clear(self) -> None:
         """Resets all slots to free."""
-        self._free_slots = list(range(self._pool_size, 0, -1))
+        if self.page_size == 1:
+            self._free_slots = list(range(self._pool_size, 0, -1))
+        else:
+            self._free_pages = list(range(self._num_pages - 1, -1, -1))
+            self._used = [0] * self._num_pages
+
+
+def slots_to_pages(slots, page_size: int):
+    """The page table of a slot list that fills pages in order (TokenPoolAllocator
+    with page_size > 1), or None when the slots are not page-aligned: slot i of
+    the list must be page_i * page_size + 1 + i % page_size."""
+    s = np.asarray(slots, dtype=np.int64)
+    if page_size <= 1 or s.size == 0:
+        return None
+    pos = np.arange(s.size)
+    pages = (s - 1) // page_size
+    if np.any((s - 1) % page_size != pos % page_size):
+        return None
+    head = pages[::page_size]
+    if np.any(pages != np.repeat(head, page_size)[: s.size]):
+        return None
+    return head.astype(np.int32)
 
 
 def _index_array(indices, device: int) -> DeviceArray:
@@ -89,8 +173,11 @@ class MHATokenPool:
     """
 
     def __init__(self, pool_size: int, num_layers: int, n_kv_heads: int, head_dim: int,
-                 dtype=dtypes.float16, device: int | None = None):
+                 dtype=dtypes.float16, device: int | None = None, page_size: int = 1):
+        if page_size <= 0 or pool_size % page_size:
+            raise ValueError(f"pool_size ({pool_size}) must be a positive multiple of page_size ({page_size})")
         self.pool_size = pool_size
+        self.page_size = page_size
         self.num_layers = num_layers
         self.n_kv_heads = n_kv_heads
         self.head_dim = head_dim
@@ -177,6 +264,38 @@ class MHATokenPool:
                                         partition_size=partition_size, out=out, stream=stream)
 
 
+    def page_view(self, layer_idx: int):
+        """K and V of `layer_idx` as [pool_size / page_size, page_size, n_kv_heads,
+        head_dim] pages (the reshape_and_cache_flash layout), page p being slots
+        p * page_size + 1 .. (p + 1) * page_size: a view from slot 1, no copy."""
+        ps = self.page_size
+        if ps <= 1:
+            raise ValueError("page_view needs a pool made with page_size > 1")
+        shape = (self.pool_size // ps, ps, self.n_kv_heads, self.head_dim)
+        return (self.k_buffer[layer_idx][1:].reshape(*shape), self.v_buffer[layer_idx][1:].reshape(*shape))
+
+    def decode_pages(self, layer_idx: int, queries, page_tables, context_lens, scale: float | None = None, *,
+                     max_seq_len: int | None = None, alibi_slopes=None, partition_size: int | None = None,
+                     out=None, stream=None):
+        """decode() over page tables: sequence b's token t is slot
+        page_tables[b, t // page_size] * page_size + 1 + t % page_size (slots from
+        TokenPoolAllocator(page_size=...)).  Pages of 16k tokens are read with
+        one tensor copy per 16 tokens and head."""
+        from ... import metal_kernels as mk
+
+        ps = self.page_size
+        tshape = describe(page_tables)[0] if not isinstance(page_tables, (list, np.ndarray)) \
+            else np.asarray(page_tables).shape
+        if max_seq_len is None:
+            max_seq_len = max(1, int(tshape[1]) * ps)
+        if scale is None:
+            scale = self.head_dim ** -0.5
+        kv, vv = self.page_view(layer_idx)
+        return mk.paged_attention_flash(queries, kv, vv, page_tables, context_lens, self.n_kv_heads, scale, ps,
+                                        max_seq_len, alibi_slopes, partition_size=partition_size, out=out,
+                                        stream=stream)
+
+
 class PooledKVCache:
     """Adapter that makes the shared KV pool look like a per-request KV cache.
 
@@ -253,16 +372,25 @@ class PooledKVCache:
 
         kbuf, vbuf = self._pool.k_buffer[self._layer_idx], self._pool.v_buffer[self._layer_idx]
         if N == 1 and not window_size:
+            # slots that fill whole pages in order (a page-granular allocator) are read page by page
+            ps = getattr(self._pool, "page_size", 1)
+            pages = slots_to_pages(slots[0], ps)
+            bs, msl = 1, T
+            if pages is not None:
+                kbuf, vbuf = self._pool.page_view(self._layer_idx)
+                tables = DeviceArray.from_numpy(pages[None, :], device=qdev)
+                bs, msl = ps, len(pages) * ps
             ws = (None, None, None)
-            psize = mk.choose_decode(1, self._pool.n_kv_heads, T, 16)
+            psize = mk.choose_decode(1, self._pool.n_kv_heads, msl, 16)
             if psize:
-                ws = mk.splitk_workspace(1, qshape[1], qshape[3], T, psize, qdev)
+                psize = -(-psize // bs) * bs
+                ws = mk.splitk_workspace(1, qshape[1], qshape[3], msl, psize, qdev)
             ptrs = [as_dltensor(a, n) for a, n in ((out, "out"), (ws[0], "exp_sums"), (ws[1], "max_logits"),
                                                    (ws[2], "tmp_out"), (kbuf, "k"), (vbuf, "v"), (tables, "tables"),
                                                    (lens, "lens"))]
             _lib.check(_L.kvc_paged_attention_flash(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0],
                                                     ctypes.pointer(qt), ptrs[4][0], ptrs[5][0], ptrs[6][0],
-                                                    ptrs[7][0], self._pool.n_kv_heads, float(scale), 1, T, None,
+                                                    ptrs[7][0], self._pool.n_kv_heads, float(scale), bs, msl, None,
                                                     int(psize), _stream(stream)))
         else:
             indptr = DeviceArray.from_numpy(np.array([0, N], dtype=np.int32), device=qdev)

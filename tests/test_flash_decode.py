@@ -140,10 +140,10 @@ def test_matches_paged_layout_at_scale(gpu):
 
 # ---- the pool API ----------------------------------------------------------------
 
-def _pool_batch(seed, dtype, hq, hkv, d, prompt_lens, pool_size=6000):
+def _pool_batch(seed, dtype, hq, hkv, d, prompt_lens, pool_size=6000, page_size=1):
     rng = np.random.default_rng(seed)
-    pool = MHATokenPool(pool_size, 2, hkv, d, dtype)
-    alloc = TokenPoolAllocator(pool_size)
+    pool = MHATokenPool(pool_size, 2, hkv, d, dtype, page_size=page_size)
+    alloc = TokenPoolAllocator(pool_size, page_size=page_size)
     slots, keys = [], []
     for n in prompt_lens:
         idx = alloc.alloc(int(n))
@@ -202,3 +202,96 @@ def test_pooled_cache_update_and_attend_equals_gather_path(gpu):
         caches[0].update_and_attend(DeviceArray.from_numpy(np.zeros((1, 16, 2, 128), np.float32), dtype=dtype),
                                     DeviceArray.from_numpy(np.zeros((1, 4, 3, 128), np.float32), dtype=dtype),
                                     DeviceArray.from_numpy(np.zeros((1, 4, 3, 128), np.float32), dtype=dtype))
+
+
+# ---- blocks of consecutive token rows: tensor copies (kFlashTma) ---------------------
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("bs", [16, 32, 64])
+def test_tensor_copy_rows_match_row_copies(gpu, dtype, D, bs, monkeypatch):
+    """Block sizes that are multiples of 16 read each 16-token group of a head with
+    tensor copies; KVC_FLASH_COPY=cpasync forces the per-lane 16-byte row copies.
+    Both agree with the oracle, single pass and split-K."""
+    fc = flash_case(5000 + D + bs, dtype, 4, 8, 2, D, bs, [1, 16, 333, 2000])
+    d = upload_flash(fc)
+    ref = oracle_flash(fc)
+    for psize in (0, 256):
+        tma = run_flash(fc, d, partition_size=psize)
+        monkeypatch.setenv("KVC_FLASH_COPY", "cpasync")
+        rows = run_flash(fc, d, partition_size=psize)
+        monkeypatch.delenv("KVC_FLASH_COPY")
+        assert_close(tma, ref, ATOL_NS, RTOL_NS, f"tensor copies bs{bs} P={psize}")
+        assert_close(rows, ref, ATOL_NS, RTOL_NS, f"row copies bs{bs} P={psize}")
+    assert gpu.get_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+def test_paged_pool_decode_pages_matches_slot_lists(gpu, dtype):
+    """A pool whose allocator hands out 16-token pages: requests allocated in
+    turns (alloc, then alloc_extend token by token) hold interleaved pages;
+    decode_pages over the page tables equals decode over the slot lists and the
+    oracle."""
+    ps = 16
+    rng = np.random.default_rng(5100)
+    pool = MHATokenPool(4096, 2, 4, 128, dtype, page_size=ps)
+    alloc = TokenPoolAllocator(4096, page_size=ps)
+    lens = [5, 40, 300, 17]
+    slots = [alloc.alloc(1) for _ in lens]
+    for step in range(1, max(lens)):
+        for b, n in enumerate(lens):
+            if step < n:
+                slots[b] += alloc.alloc_extend(slots[b][-1], 1)
+    keys = []
+    for b, n in enumerate(lens):
+        kv = [kv_oracle.round_to(rng.standard_normal((1, 4, n, 128)).astype(np.float32), dtype) for _ in range(2)]
+        pool.store(1, slots[b], DeviceArray.from_numpy(kv[0], dtype=dtype), DeviceArray.from_numpy(kv[1], dtype=dtype))
+        keys.append(kv)
+    from sglang_mlx_b200.srt.mem_cache.memory_pool import slots_to_pages
+
+    T = max(lens)
+    st = np.zeros((len(lens), T), np.int32)
+    pt = np.zeros((len(lens), -(-T // ps)), np.int32)
+    for b, idx in enumerate(slots):
+        st[b, :len(idx)] = idx
+        pages = slots_to_pages(idx, ps)
+        assert pages is not None
+        pt[b, :len(pages)] = pages
+    q = kv_oracle.round_to(rng.standard_normal((len(lens), 16, 128)).astype(np.float32), dtype)
+    qd = DeviceArray.from_numpy(q, dtype=dtype)
+    by_pages = pool.decode_pages(1, qd, pt, np.array(lens, np.int32)).to_numpy()
+    by_slots = pool.decode(1, qd, st, np.array(lens, np.int32)).to_numpy()
+    ref = np.zeros((len(lens), 16, 128))
+    for b in range(len(lens)):
+        k = keys[b][0][0].transpose(1, 0, 2)
+        v = keys[b][1][0].transpose(1, 0, 2)
+        for h in range(4):
+            ref[b, 4 * h:4 * h + 4] = kv_oracle.attend(q[b, 4 * h:4 * h + 4], k[:, h], v[:, h], 128 ** -0.5)
+    assert_close(by_pages, ref, ATOL_NS, RTOL_NS, "decode_pages")
+    assert_close(by_slots, ref, ATOL_NS, RTOL_NS, "decode (slot lists)")
+    assert gpu.get_status(clear=True) == 0
+
+
+def test_paged_pool_update_and_attend_equals_gather_path(gpu):
+    """update_and_attend on a page-granular pool reads the request's pages (its
+    slots fill them in order) and matches update_and_fetch + the oracle."""
+    dtype = "bfloat16"
+    pool, alloc, slots, keys, rng = _pool_batch(5200, dtype, 16, 4, 128, [700], pool_size=4096, page_size=32)
+    prefix = list(slots[0])
+    for step in range(3):
+        new = alloc.alloc_extend(prefix[-1], 1)
+        caches = [PooledKVCache(pool, 0), PooledKVCache(pool, 1)]
+        q = kv_oracle.round_to(rng.standard_normal((1, 16, 1, 128)).astype(np.float32), dtype)
+        kn = kv_oracle.round_to(rng.standard_normal((1, 4, 1, 128)).astype(np.float32), dtype)
+        vn = kv_oracle.round_to(rng.standard_normal((1, 4, 1, 128)).astype(np.float32), dtype)
+        caches[0].set_indices(prefix, new)
+        caches[1].set_indices(prefix, new)
+        out = caches[0].update_and_attend(DeviceArray.from_numpy(q, dtype=dtype), DeviceArray.from_numpy(kn, dtype=dtype),
+                                          DeviceArray.from_numpy(vn, dtype=dtype))
+        kf, vf = caches[1].update_and_fetch(DeviceArray.from_numpy(kn, dtype=dtype),
+                                            DeviceArray.from_numpy(vn, dtype=dtype))
+        kf, vf = kf.to_numpy()[0], vf.to_numpy()[0]
+        ref = np.stack([kv_oracle.attend(q[0, 4 * h:4 * h + 4, 0], kf[h], vf[h], 128 ** -0.5) for h in range(4)])
+        assert_close(out.to_numpy()[0, :, 0], ref.reshape(16, 128), ATOL_NS, RTOL_NS, f"step {step}")
+        prefix = prefix + new
+    assert gpu.get_status(clear=True) == 0

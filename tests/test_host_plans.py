@@ -1,6 +1,8 @@
 """Host-side planning helpers of the Python shim (no GPU)."""
 import math
 
+import cases
+
 from sglang_mlx_b200 import metal_kernels as mk
 
 
@@ -27,3 +29,19 @@ def test_cascade_partitions_units_and_bounds():
             # one wave of the prefix kernel (unless one chunk per kv head and tile already exceeds it)
             assert chunks * tiles * Hkv <= max(2 * 148, tiles * Hkv)
 
+
+
+def test_planned_partition_choice():
+    """choose_planned_partition: the largest of 4096/2048/1024/512 tokens whose
+    items fill 1.25x the resident CTA slots (296 for 16-token blocks)."""
+    from sglang_mlx_b200 import metal_kernels as mk
+
+    lens = cases.baseline_workload(2)["lens"] + 1
+    assert mk.choose_planned_partition(256, 1, 4112, 16, lens) == 2048   # one rank of an 8-GPU run
+    assert mk.choose_planned_partition(256, 2, 4112, 16, lens) == 4096
+    assert mk.choose_planned_partition(256, 8, 4112, 16, lens) == 4096
+    assert mk.choose_planned_partition(4, 1, 300, 16, [100, 200, 300, 50]) == 512   # too few items for any size
+    assert mk.choose_planned_partition(1, 8, 131072, 32) == 512   # one 128k sequence (taken as 64k): 1024 gives 512 items < 555
+    for bs in (8, 16, 32):
+        p = mk.choose_planned_partition(64, 8, 8192, bs)
+        assert p % 32 == 0 and p % bs == 0

@@ -260,3 +260,58 @@ class TestPooledKVCache:
             ko, _ = c.update_and_fetch(knd, vnd)
             assert ko.shape == (1, 2, 5, 4)
             np.testing.assert_array_equal(ko.to_numpy()[:, :, :4], k_in)
+
+
+
+class TestPagedAllocator:
+    """page_size > 1: whole pages, page p = slots p*ps+1 .. (p+1)*ps."""
+
+    def test_alloc_takes_whole_pages_in_order(self):
+        a = TokenPoolAllocator(16, page_size=4)
+        assert a.alloc(5) == [1, 2, 3, 4, 5]
+        assert a.available_size == 8
+        assert a.alloc(2) == [9, 10]
+
+    def test_alloc_extend_fills_the_page_first(self):
+        a = TokenPoolAllocator(16, page_size=4)
+        s = a.alloc(3)
+        other = a.alloc(1)
+        assert other == [5]
+        s += a.alloc_extend(s[-1], 3)
+        assert s == [1, 2, 3, 4, 9, 10]
+        assert a.alloc_extend(other[-1], 2) == [6, 7]
+
+    def test_pages_return_when_every_slot_is_freed(self):
+        a = TokenPoolAllocator(8, page_size=4)
+        s = a.alloc(6)
+        a.free(s[:3])
+        assert a.available_size == 0
+        a.free(s[3:4])
+        assert a.available_size == 4
+        a.free(s[4:])
+        assert a.available_size == 8
+        assert len(set(a.alloc(8))) == 8
+
+    def test_overflow_and_bad_sizes(self):
+        a = TokenPoolAllocator(8, page_size=4)
+        a.alloc(5)
+        with pytest.raises(MemoryError):
+            a.alloc(1)
+        with pytest.raises(ValueError):
+            TokenPoolAllocator(10, page_size=4)
+        a.clear()
+        assert a.available_size == 8
+
+    def test_page_size_one_is_the_reference_allocator(self):
+        a, b = TokenPoolAllocator(10), TokenPoolAllocator(10, page_size=1)
+        assert a.alloc(3) == b.alloc(3) == [3, 2, 1]
+        assert b.alloc_extend(1, 2) == a.alloc(2)
+
+    def test_slots_to_pages(self):
+        from sglang_mlx_b200.srt.mem_cache.memory_pool import slots_to_pages
+
+        assert list(slots_to_pages([1, 2, 3, 4, 9, 10], 4)) == [0, 2]
+        assert slots_to_pages([1, 2, 4], 4) is None
+        assert slots_to_pages([2, 3], 4) is None
+        assert slots_to_pages([5, 6, 7, 8, 1], 4).tolist() == [1, 0]
+        assert slots_to_pages([3, 2, 1], 1) is None

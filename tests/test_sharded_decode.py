@@ -4,8 +4,9 @@ Every rank's share of BASELINE configs 2 and 5 at full size (one layer) is
 cut out exactly as a rank of `bench.py --gpus N` holds it: its KV heads of the
 pool (a dense copy), its query heads, and for config 5 at N = 8 (4 KV heads on
 8 ranks) its token-balanced half of the sequences (sharding.plan).  Each share
-is decoded on one GPU, one rank after another, with the form the shim picks
-for that share (metal_kernels.choose_decode: split-K at these small shares).
+is decoded on one GPU, one rank after another, with the form the shim's
+default decode runs for that share (metal_kernels.paged_attention: the planned
+split-K, partition size from choose_planned_partition on the share's lengths).
 The shares assembled by sharding.assemble must equal the unsharded decode
 within the north-star tolerance, and a sample of sequences of every rank is
 checked against the CPU oracle (float64 gather + SDPA)."""
@@ -81,7 +82,7 @@ def test_sharded_decode_matches_unsharded(gpu, full_config, world):
         q = fc["q"].index_select(0, seqs)[:, q0:q1].contiguous()
         tables = np.ascontiguousarray(w["tables"][p.seqs])
         lens = fc["lens"][p.seqs]
-        psize = mk.choose_decode(len(lens), p.num_kv_heads, w["max_seq_len"], BS)
+        psize = mk.choose_planned_partition(len(lens), p.num_kv_heads, w["max_seq_len"], BS, lens)
         out = mk.paged_attention(q, kc, vc, tables, lens, p.num_kv_heads, fc["scale"], BS,
                                  w["max_seq_len"]).to_numpy()
         assert np.isfinite(out).all()
