@@ -725,7 +725,6 @@ __global__ void __launch_bounds__(NW * 32)
   const int G = p.num_heads / p.num_kv_heads;
 
   grid_dependents_launch();
-  if (p.wait_prior_at_start) grid_dependency_wait();  // the append before us has written the new tokens
   if (p.plan_items && !planned_item(p, &kvh, &seq, &part)) return;  // planned: CTA -> work item of the plan
   const int h0 = kvh * G;
   const uint32_t ctx = p.context_lens[seq];
@@ -733,6 +732,8 @@ __global__ void __launch_bounds__(NW * 32)
   bool zero_out = false;
   if (!partition_range(p, seq, part, ctx, &begin, &end, &zero_out)) {
     // planned: the item of a sequence with zero output (length 0 or past max_seq_len) writes it
+    // (after the kernel before us, which may write the same output buffer, has finished)
+    if (p.wait_prior_at_start) grid_dependency_wait();
     if (zero_out || p.plan_items) write_zero_heads<T>(p, seq, h0, G, D);
     if (p.wait_prior_at_end) grid_dependency_wait();
     return;
@@ -985,6 +986,15 @@ __global__ void __launch_bounds__(NW * 32)
       }
     }
   };
+
+  // Launched as a programmatic dependent (wait_prior_at_start): what is read
+  // above (the plan's header and items, lengths, block tables, queries) is
+  // written by none of this library's kernels that let their dependents start
+  // early (the appends write cache rows; the decode and prefill kernels write
+  // outputs, partials and plan counters), so it was final before the kernel
+  // before us started.  The cache, the partials and the counters are touched
+  // only from here on, after that kernel has finished.
+  if (p.wait_prior_at_start) grid_dependency_wait();
 
   // ---- prologue: fill the ring
   uint32_t ids_next[IDV];  // token-major caches: the chunk after the current one

@@ -148,6 +148,7 @@ struct PrefillArgs {
   float* part_sum;
   float* part_out;
   int64_t part_seq_stride, part_head_stride, part_out_seq_stride, part_out_head_stride, part_out_part_stride;
+  int single_issue;  // tcgen05 kernel: the producer's lane 0 issues every copy of a tile (tuning; default: spread)
 };
 
 struct ReshapeArgs {

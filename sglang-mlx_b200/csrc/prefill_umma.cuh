@@ -405,7 +405,49 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
 #pragma unroll
         for (int i = 0; i < PAGES; ++i) ids[i] = __shfl_sync(0xffffffffu, id, i);
         id = load_id(j + 1);  // next tile's ids, in flight while this one is issued
-        if (lane == 0) {
+        if (!p.single_issue) {
+          // the tile's copies spread over the warp: lane 0 posts the byte count
+          // first; then with GK lane c < D/8 issues the 4-row gathers of K chunk
+          // c and lane 16 + i the V copy of page i, without GK lane i the K and V
+          // copies of page i
+          uint8_t* kst = ring + (size_t)st * UG::STAGE;
+          uint8_t* vst = kst + PAGES * PAGE;
+          if (lane == 0) {
+            page_mask[st] = mask;
+            if (mask)
+              mbar_arrive_expect_tx(&kv_full[st], (uint32_t)((GK ? PAGES : 0) + (GK ? 1 : 2) * __popc(mask)) *
+                                                      (uint32_t)PAGE);
+            else
+              mbar_arrive(&kv_full[st]);
+          }
+          __syncwarp();
+          if (mask) {
+            if constexpr (GK) {
+              static_assert(D / 8 <= 16 && PAGES <= 16, "lanes of the spread issue");
+              const uint32_t any = ids[__ffs(mask) - 1];  // pages without keys gather a loaded page's rows
+              if (lane < D / 8) {
+                int rb[PAGES];
+#pragma unroll
+                for (int i = 0; i < PAGES; ++i)
+                  rb[i] = (int)(((int64_t)((mask >> i) & 1u ? ids[i] : any) * p.num_kv_heads + kvh) * (D / 8));
+                const int c = lane;
+#pragma unroll
+                for (int q = 0; q < PAGES; q += 4)
+                  umma::tma_gather4(kst + c * KT * 16 + q * BS * 16, kmap, 0, rb[q] + c, rb[q + 1] + c, rb[q + 2] + c,
+                                    rb[q + 3] + c, &kv_full[st]);
+              } else if (lane >= 16 && lane - 16 < PAGES && ((mask >> (lane - 16)) & 1u)) {
+                const int i = lane - 16;
+                tma_load_4d(vst + i * PAGE, vmap, 0, 0, kvh, (int)ids[i], &kv_full[st]);
+              }
+            } else {
+              if (lane < PAGES && ((mask >> lane) & 1u)) {
+                const int i = lane;
+                bulk_g2s(kst + i * PAGE, kbase + (int64_t)ids[i] * p.k_block_stride, PAGE, &kv_full[st]);
+                tma_load_4d(vst + i * PAGE, vmap, 0, 0, kvh, (int)ids[i], &kv_full[st]);
+              }
+            }
+          }
+        } else if (lane == 0) {
           page_mask[st] = mask;
           uint8_t* kst = ring + (size_t)st * UG::STAGE;
           uint8_t* vst = kst + PAGES * PAGE;
@@ -890,6 +932,12 @@ static bool make_k_gather_map(const PrefillArgs& a, int D, int BS, CUtensorMap* 
          CUDA_SUCCESS;
 }
 
+// KVC_PREFILL_ISSUE=single: the producer's lane 0 issues every copy (tuning runs).
+static int umma_single_issue() {
+  const char* v = getenv("KVC_PREFILL_ISSUE");
+  return v && v[0] == 's' ? 1 : 0;
+}
+
 // The persistent grid: one CTA per SM (the ring and TMEM allow one), fewer
 // when there are fewer work items.
 static int umma_persistent_ctas(int dev, int64_t items) {
@@ -951,7 +999,9 @@ static cudaError_t launch_prefill_umma(const PrefillArgs& a, cudaStream_t stream
   if (items > 0x7fffffffll - 1024) return cudaErrorInvalidValue;
   const int ctas = umma_persistent_ctas(dev, items);
   const int slot = umma_sched_slot(stream);  // (runtime queries stay outside the launch statement)
-  kern<<<ctas, kUmmaThreads, UG::SMEM, stream>>>(a, maps, (int)tiles, (int)a.num_seqs, slot);
+  PrefillArgs aa = a;
+  aa.single_issue = umma_single_issue();
+  kern<<<ctas, kUmmaThreads, UG::SMEM, stream>>>(aa, maps, (int)tiles, (int)a.num_seqs, slot);
   count_launch();
   return cudaGetLastError();
 }
@@ -1037,7 +1087,9 @@ static cudaError_t launch_cascade_umma(const PrefillArgs& a, int prefix_parts, c
   if (items > 0x7fffffffll - 1024) return cudaErrorInvalidValue;
   const int ctas = umma_persistent_ctas(dev, items);
   const int slot = umma_sched_slot(stream);
-  kern<<<ctas, kUmmaThreads, UG::SMEM, stream>>>(a, maps, (int)tiles, prefix_parts, slot);
+  PrefillArgs aa = a;
+  aa.single_issue = umma_single_issue();
+  kern<<<ctas, kUmmaThreads, UG::SMEM, stream>>>(aa, maps, (int)tiles, prefix_parts, slot);
   count_launch();
   return cudaGetLastError();
 }
