@@ -416,8 +416,8 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
     pool_pages = args.layout == "pool-pages" and top  # the pool read through page tables (page_size = block size)
     fp8 = args.kv_dtype.startswith("fp8") and top
     fmt = args.kv_dtype[4:] if fp8 else None
-    if fp8 and (pool or args.decode in ("cascade", "planned")):
-        raise SystemExit("--kv-dtype fp8 runs on the paged layout with the single-pass / split-K decode")
+    if fp8 and (pool or args.decode == "cascade"):
+        raise SystemExit("--kv-dtype fp8 runs on the paged layout with the single-pass / split-K / planned decode")
     page_tables = tables
     if pool:
         # MHATokenPool layout: block b's tokens are slots b*BS+1 .. b*BS+BS (slot 0 is
@@ -475,7 +475,7 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
     # token-pool kernel runs 16-token groups, two CTAs per SM)
     heuristic = mk.choose_decode(B, hkv, max_seq_len, 16 if pool else BS)
     planned_p = mk.choose_planned_partition(B, hkv, max_seq_len, BS, lens_after)
-    auto_planned = args.decode == "auto" and not (cfg["partition"] or pool or fp8)
+    auto_planned = args.decode == "auto" and not (cfg["partition"] or pool)
     if args.decode == "v1":
         psize = 0
     elif args.decode == "v2":
@@ -488,7 +488,7 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
         psize = args.partition
     # config 4 is a radix-cache hit: every table starts with the same prefix, which
     # the serving stack knows, so the default decode is the shared-prefix (cascade) one
-    cascade = (args.decode == "cascade" or (args.decode == "auto" and shared)) and not pool
+    cascade = (args.decode == "cascade" or (args.decode == "auto" and shared)) and not pool and not fp8
     if cascade:
         prefix = cfg["prefix"]
         pp, pt = mk.cascade_partitions(B, hq, hkv, max_seq_len, prefix, BS)
@@ -519,7 +519,7 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
         if fp8:
             return mk.paged_attention_fp8(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, BS, max_seq_len,
                                           k_scale=0.05, v_scale=0.05, fp8_format=fmt, partition_size=psize,
-                                          workspace=ws, out=out[i], stream=stream)
+                                          workspace=ws, out=out[i], stream=stream, plan=dplan)
         if cascade:
             return mk.paged_attention_cascade(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, BS, max_seq_len, prefix,
                                               prefix_partition_size=pp, partition_size=pt, workspace=cws, out=out[i],
@@ -718,7 +718,9 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
             f"{BS}-token page tables, tensor copies" if pool_pages else "slot lists") + (
             f", {psize}-token partitions)" if split else ", single pass)")
     if fp8:
-        kernel = f"FP8 ({fmt}) cache decode, " + (f"{psize}-token partitions" if split else "single pass")
+        kernel = f"FP8 ({fmt}) cache decode, " + (
+            f"planned split-K, {psize}-token partitions longest first" if planned else
+            f"{psize}-token partitions" if split else "single pass")
     if cascade:
         kernel = f"shared-prefix cascade ({prefix}-token prefix in {pp}-token chunks, tail partitions of {pt})"
     extra = {"kernel": kernel, "launch": "one CUDA graph per step (decode timing from an eager pass)" if graph is not None else "eager",

@@ -347,6 +347,17 @@ int kvc_paged_attention_fp8(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dlten
                             int max_seq_len, const kvc_dltensor* alibi_slopes, float k_scale, float v_scale,
                             int fp8_format, int partition_size, void* stream);
 
+/* kvc_paged_attention_fp8 as a planned split-K decode: the work list of
+ * kvc_decode_plan (made for the same lengths, num_kv_heads, max_seq_len and
+ * partition_size), longest items first, merge fused into the last partition of
+ * each sequence; see kvc_paged_attention_planned.  No reference counterpart. */
+int kvc_paged_attention_fp8_planned(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltensor* max_logits,
+                                    kvc_dltensor* tmp_out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                                    const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                                    const kvc_dltensor* context_lens, int num_kv_heads, float scale, int block_size,
+                                    int max_seq_len, const kvc_dltensor* alibi_slopes, float k_scale, float v_scale,
+                                    int fp8_format, int partition_size, kvc_dltensor* plan, void* stream);
+
 /* convert_fp8_kernel (convert_fp8.metal:13-80) on dense arrays of one shape:
  * float -> uint8 quantises (encode(x / scale)), uint8 -> float dequantises
  * (decode(code) * scale), uint8 -> uint8 rescales, float -> float scales. */

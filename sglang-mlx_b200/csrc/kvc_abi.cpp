@@ -1125,6 +1125,38 @@ int kvc_paged_attention_fp8(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dlten
   return KVC_OK;
 }
 
+int kvc_paged_attention_fp8_planned(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltensor* max_logits,
+                                    kvc_dltensor* tmp_out, const kvc_dltensor* query, const kvc_dltensor* key_cache,
+                                    const kvc_dltensor* value_cache, const kvc_dltensor* block_tables,
+                                    const kvc_dltensor* context_lens, int num_kv_heads, float scale, int block_size,
+                                    int max_seq_len, const kvc_dltensor* alibi_slopes, float k_scale, float v_scale,
+                                    int fp8_format, int partition_size, kvc_dltensor* plan, void* stream) {
+  if (int rc = check_fp8_args(k_scale, v_scale, fp8_format)) return rc;
+  DecodeArgs a;
+  int device = -1;
+  if (int rc = prepare_decode(out, query, key_cache, value_cache, block_tables, context_lens, num_kv_heads, scale,
+                              block_size, max_seq_len, alibi_slopes, &a, &device, true))
+    return rc;
+  const int G = a.num_heads / a.num_kv_heads;
+  if (!(a.head_size == 64 || a.head_size == 128) || G > 16)
+    return fail(KVC_EUNSUPPORTED, "paged_attention_fp8 supports head_size 64 or 128 and up to 16 query heads per "
+                                  "KV head");
+  if (int rc = attach_splitk_workspace(exp_sums, max_logits, tmp_out, partition_size, block_size, max_seq_len,
+                                       device, &a))
+    return rc;
+  if (int rc = check_plan_args(a.num_seqs, num_kv_heads, max_seq_len, partition_size)) return rc;
+  if (int rc = parse_plan(plan, a.num_seqs, num_kv_heads, max_seq_len, partition_size, &device, &a.plan)) return rc;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  a.fp8_format = fp8_format;
+  if (a.num_seqs == 0) return KVC_OK;
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_paged_decode(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "paged_attention_fp8_planned launch");
+  return KVC_OK;
+}
+
 int kvc_convert_fp8(kvc_dltensor* dst, const kvc_dltensor* src, float scale, int fp8_format, void* stream) {
   if (int rc = check_fp8_args(scale, 1.f, fp8_format)) return rc;
   View d, s;

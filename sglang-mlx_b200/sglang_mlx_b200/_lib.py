@@ -74,6 +74,10 @@ SIGNATURES: dict[str, tuple] = {
         _i,
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _f, _f, _i, _i, _p],
     ),
+    "kvc_paged_attention_fp8_planned": (
+        _i,
+        [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _f, _f, _i, _i, _p, _p],
+    ),
     "kvc_convert_fp8": (_i, [_p, _p, _f, _i, _p]),
     "kvc_swap_blocks": (_i, [_p, _p, _p, _p]),
     "kvc_get_max_shared_memory_per_block_device_attribute": (

@@ -533,10 +533,15 @@ def reshape_and_cache_fp8(key, value, key_cache, value_cache, slot_mapping, k_sc
 def paged_attention_fp8(query, key_cache, value_cache, block_tables, context_lens, num_kv_heads: int, scale: float,
                         block_size: int, max_seq_len: int, alibi_slopes=None, *, k_scale: float = 1.0,
                         v_scale: float = 1.0, fp8_format: str = "e4m3", partition_size: int | None = None,
-                        workspace=None, out=None, stream=None):
+                        workspace=None, out=None, stream=None, plan=None):
     """paged_attention_v1 over one-byte caches written by reshape_and_cache_fp8
     (values decode(code) * scale).  partition_size None lets choose_decode pick
-    (0 = single pass)."""
+    (0 = single pass); with a DecodePlan (make_decode_plan) the planned split-K
+    runs with the plan's partition size."""
+    if plan is not None:
+        if partition_size not in (None, plan.partition_size):
+            raise ValueError(f"the plan was made for partition_size {plan.partition_size}, not {partition_size}")
+        partition_size = plan.partition_size
     query, key_cache, value_cache = _dev(query), _dev(key_cache), _dev(value_cache)
     block_tables, context_lens, alibi_slopes = _dev(block_tables), _dev(context_lens), _dev(alibi_slopes)
     shape, _, _, _, dev = describe(query)
@@ -552,10 +557,19 @@ def paged_attention_fp8(query, key_cache, value_cache, block_tables, context_len
                                            (ws[2], "tmp_out"), (query, "query"), (key_cache, "key_cache"),
                                            (value_cache, "value_cache"), (block_tables, "block_tables"),
                                            (context_lens, "context_lens"), (alibi_slopes, "alibi_slopes"))]
-    rc = _L.kvc_paged_attention_fp8(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ptrs[4][0], ptrs[5][0],
-                                    ptrs[6][0], ptrs[7][0], ptrs[8][0], int(num_kv_heads), float(scale),
-                                    int(block_size), int(max_seq_len), ptrs[9][0], float(k_scale), float(v_scale),
-                                    _fp8_format(fp8_format), int(partition_size), _stream(stream))
+    if plan is not None:
+        pl = as_dltensor(plan.array, "plan")
+        rc = _L.kvc_paged_attention_fp8_planned(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ptrs[4][0],
+                                                ptrs[5][0], ptrs[6][0], ptrs[7][0], ptrs[8][0], int(num_kv_heads),
+                                                float(scale), int(block_size), int(max_seq_len), ptrs[9][0],
+                                                float(k_scale), float(v_scale), _fp8_format(fp8_format),
+                                                int(partition_size), pl[0], _stream(stream))
+    else:
+        rc = _L.kvc_paged_attention_fp8(ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ptrs[4][0], ptrs[5][0],
+                                        ptrs[6][0], ptrs[7][0], ptrs[8][0], int(num_kv_heads), float(scale),
+                                        int(block_size), int(max_seq_len), ptrs[9][0], float(k_scale),
+                                        float(v_scale), _fp8_format(fp8_format), int(partition_size),
+                                        _stream(stream))
     _lib.check(rc)
     return out
 

@@ -240,3 +240,22 @@ def test_encoder_exhaustive_sweep(gpu, fmt):
     torch.cuda.synchronize()
     assert h.hexdigest() == str(ref[f"sweep_sha256_{fmt}"])
     assert gpu.get_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_planned_fp8_decode(gpu, fmt):
+    """The planned split-K over one-byte caches (kvc_paged_attention_fp8_planned)
+    equals the float64 decode of the dequantised caches, with zero-length and
+    over-long sequences in the batch."""
+    lens = [0, 1, 100, 700, 2500, 3100, 40]
+    c = fp8_case(6700, "bfloat16", len(lens), 8, 2, 128, 16, lens, fmt)
+    d = upload(c)
+    kc, vc = oracle_caches(c)
+    for P, msl in ((512, None), (1024, 3072)):
+        plan = mk.make_decode_plan(d["lens"], 2, msl or c["max_seq_len"], P)
+        out = mk.paged_attention_fp8(d["q"], d["kc"], d["vc"], d["tables"], d["lens"], 2, c["scale"], 16,
+                                     msl or c["max_seq_len"], k_scale=c["k_scale"], v_scale=c["v_scale"],
+                                     fp8_format=fmt, plan=plan).to_numpy()
+        assert_close(out, ref_decode(c, kc, vc, max_seq_len=msl), ATOL_NS, RTOL_NS, f"planned fp8 P={P}")
+        assert not out[0].any()
+    assert gpu.get_status(clear=True) == 0
