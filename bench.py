@@ -928,6 +928,11 @@ def run_prefill(args, rank, world, local_rank):
     st.synchronize()
     launches = _lib.launch_count() - launches0  # prefill kernels (the L2 flush memsets are not counted)
     clocks = sampler.stop()
+    # the timed launches' results: status word, and the last layer against the oracle
+    status = _lib.get_status(clear=True)
+    ok, err, nrows = check_prefill(torch, keep[3 * (L - 1) + 2], keep[3 * (L - 1)], keep[3 * (L - 1) + 1],
+                                   out[L - 1], tables, indptr, kvl, hkv, D, BS, pool)
+    ok = ok and status == 0
     lay_ms = [evs[s][i][0].elapsed_ms(evs[s][i][1]) for s in range(args.steps) for i in range(L)]
     step_ms = float(np.sum(lay_ms)) / args.steps
     mean_ms = float(np.mean(lay_ms))
@@ -963,9 +968,10 @@ def run_prefill(args, rank, world, local_rank):
     flops = prefill_flops(prefixes, qlens, hq, D)
     sums = np.array([flops, float(T), float(h2d), float(d2h)])
     if dist is not None:
-        t = torch.tensor([step_ms, e2e_ms, mean_ms], dtype=torch.float64)
+        t = torch.tensor([step_ms, e2e_ms, mean_ms, 0.0 if ok else 1.0, err], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        step_ms, e2e_ms, mean_ms = [float(x) for x in t]
+        step_ms, e2e_ms, mean_ms = [float(x) for x in t[:3]]
+        ok, err = bool(t[3] == 0.0), float(t[4])  # every rank's sample passed; the largest error
         tt = torch.tensor(sums, dtype=torch.float64)
         dist.all_reduce(tt, op=dist.ReduceOp.SUM)
         sums = tt.numpy()
@@ -1002,7 +1008,14 @@ def run_prefill(args, rank, world, local_rank):
                                          "h2d_bytes_per_step": int(h2d_all), "d2h_bytes_per_step": int(d2h_all)},
         "gpu_launches": int(launches),
         "clocks": clocks,
+        "output_check": {"ok": bool(ok), "ranks": world, "rows_checked": int(nrows), "max_abs_err": err,
+                         "against": "CPU oracle (float64 gather + masked SDPA) on the last 8 new tokens of 3 "
+                                    "sequences of the last layer; kernel status word clear",
+                         "tolerance": f"{ATOL:g} abs + {RTOL:g} rel"},
     }
+    if not ok:
+        print(json.dumps(line), flush=True)
+        raise SystemExit("prefill outputs differ from the CPU oracle or kernel status flags are set (output_check)")
     if not args.no_cpu_baseline and world == 1:
         from oracle import kv_oracle
         from threadpoolctl import threadpool_limits
@@ -1020,6 +1033,42 @@ def run_prefill(args, rank, world, local_rank):
                                 "sample": f"{n_s} of {B} sequences x 1 of {L} layers (float64 gather + masked SDPA, "
                                           f"NumPy, 1 thread), {lscpu_model()}"}
     print(json.dumps(line), flush=True)
+
+
+def check_prefill(torch, q_t, kc_t, vc_t, out, tables, indptr, kvl, hkv, D, bs, pool, n_last=8):
+    """The last n_last new tokens of a sample of this rank's sequences (first,
+    middle, last) of one layer against the CPU oracle (float64 gather + masked
+    SDPA over the rank's own caches).  Returns (ok, max |err|, rows checked)."""
+    from oracle import kv_oracle
+
+    B = len(kvl)
+    seqs = sorted({0, B // 2, B - 1})
+    dev = kc_t.device
+    got, qs, ind, ids, t2, lens = [], [], [0], [], [], []
+    o = 0
+    for b in seqs:
+        q1 = int(indptr[b + 1])
+        q0 = max(int(indptr[b]), q1 - n_last)
+        got.append(out.to_numpy()[q0:q1])
+        qs.append(q_t[q0:q1].float().cpu().numpy())
+        ind.append(ind[-1] + q1 - q0)
+        n = int(kvl[b]) if pool else -(-int(kvl[b]) // bs)  # slots, or pages
+        ids.append(tables[b, :n].astype(np.int64))
+        t2.append(np.arange(o, o + n))
+        lens.append(int(kvl[b]))
+        o += n
+    width = max(len(t) for t in t2)
+    tab = np.zeros((len(seqs), width), np.int64)
+    for i, t in enumerate(t2):
+        tab[i, :len(t)] = t
+    idx = torch.from_numpy(np.concatenate(ids)).to(dev)
+    kg = kc_t.index_select(0, idx).float().cpu().numpy()
+    vg = vc_t.index_select(0, idx).float().cpu().numpy()
+    ref = kv_oracle.paged_prefill(np.concatenate(qs), kg, vg, tab, np.asarray(ind), np.asarray(lens), hkv,
+                                  1.0 / math.sqrt(D))
+    got = np.concatenate(got)
+    ok, err, _ = kv_oracle.allclose_report(got, ref, ATOL, RTOL)
+    return bool(ok and np.isfinite(got).all()), float(err), int(got.shape[0])
 
 
 def load_tensor_peak():

@@ -490,6 +490,7 @@ __global__ void __launch_bounds__(kReduceWarps * 32) splitk_reduce_kernel(Decode
 #include "cascade.cuh"
 #include "prefill.cuh"
 #include "prefill_umma.cuh"
+#include "prefill_umma_pair.cuh"
 
 namespace kvc {
 

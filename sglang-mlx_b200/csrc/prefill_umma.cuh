@@ -725,13 +725,23 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
             __all_sync(0xffffffffu, (pm & my_pages) == my_pages && t0 >= beg_r && t0 + HK <= end_r);
         float mx;  // row max of my scaled scores (log2 units)
         if (whole) {
-          float hi_raw = -INFINITY, lo_raw = INFINITY;
+          // the largest raw score, or the smallest for a negative scale
+          float h0 = -INFINITY, h1 = -INFINITY;
+          if (qk_scale >= 0.f) {
 #pragma unroll
-          for (int c = 0; c < HK; c += 2) {
-            hi_raw = fmaxf(hi_raw, fmaxf(x[c], x[c + 1]));
-            lo_raw = fminf(lo_raw, fminf(x[c], x[c + 1]));
+            for (int c = 0; c < HK; c += 2) {
+              h0 = fmaxf(h0, x[c]);
+              h1 = fmaxf(h1, x[c + 1]);
+            }
+            mx = fmaxf(h0, h1) * qk_scale;
+          } else {
+#pragma unroll
+            for (int c = 0; c < HK; c += 2) {
+              h0 = fmaxf(h0, -x[c]);
+              h1 = fmaxf(h1, -x[c + 1]);
+            }
+            mx = -fmaxf(h0, h1) * qk_scale;
           }
-          mx = qk_scale >= 0.f ? hi_raw * qk_scale : lo_raw * qk_scale;
         } else {
           mx = -INFINITY;
 #pragma unroll
@@ -751,41 +761,42 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           m_ref = mx;
         }
         const float neg_ref = m_ref == -INFINITY ? 0.f : -m_ref;
-        float ps = 0.f;
         // P pairs packed as soon as they are exponentiated (the integer / FMA
         // work of the packing overlaps the special-function unit's exponentials):
         // hi = the upper 16 bits of each fp32 (a bf16, truncated), lo = the exact
         // remainder rounded to bf16, so hi + lo carries ~16 bits of P; f16 P is
         // one rounding.  Pairs of tokens 64h + 2i, + 1 go to hi column 32h + i.
+        // The exponent, the row sum and the remainder run as f32x2 pairs.
+        float2 ps = make_float2(0.f, 0.f);
         uint32_t hi[32], lo[32];
-        auto pack_pair = [&](int i, float p0, float p1) {
+        auto pack_pair = [&](int i, float2 pp) {
+          ps = add_x2(ps, pp);
           if constexpr (SPLIT) {
-            const uint32_t u0 = __float_as_uint(p0), u1 = __float_as_uint(p1);
+            const uint32_t u0 = __float_as_uint(pp.x), u1 = __float_as_uint(pp.y);
             hi[i] = __byte_perm(u0, u1, 0x7632);
-            lo[i] = MmaOp<T>::pack(p0 - __uint_as_float(u0 & 0xFFFF0000u), p1 - __uint_as_float(u1 & 0xFFFF0000u));
+            const float2 r = sub_x2(pp, make_float2(__uint_as_float(u0 & 0xFFFF0000u), __uint_as_float(u1 & 0xFFFF0000u)));
+            lo[i] = MmaOp<T>::pack(r.x, r.y);
           } else {
-            hi[i] = MmaOp<T>::pack(p0, p1);
+            hi[i] = MmaOp<T>::pack(pp.x, pp.y);
             lo[i] = 0u;
           }
         };
         if (whole) {
+          const float2 sc = make_float2(qk_scale, qk_scale), nr = make_float2(neg_ref, neg_ref);
 #pragma unroll
           for (int i = 0; i < HK / 2; ++i) {
-            const float p0 = fast_exp2(fmaf(x[2 * i], qk_scale, neg_ref));
-            const float p1 = fast_exp2(fmaf(x[2 * i + 1], qk_scale, neg_ref));
-            ps += p0 + p1;
-            pack_pair(i, p0, p1);
+            const float2 e = fma_x2(make_float2(x[2 * i], x[2 * i + 1]), sc, nr);
+            pack_pair(i, make_float2(fast_exp2(e.x), fast_exp2(e.y)));
           }
         } else {
+          const float2 nr = make_float2(neg_ref, neg_ref);
 #pragma unroll
           for (int i = 0; i < HK / 2; ++i) {
-            const float p0 = fast_exp2(x[2 * i] + neg_ref);  // masked: exp2(-inf) = 0
-            const float p1 = fast_exp2(x[2 * i + 1] + neg_ref);
-            ps += p0 + p1;
-            pack_pair(i, p0, p1);
+            const float2 e = add_x2(make_float2(x[2 * i], x[2 * i + 1]), nr);  // masked: exp2(-inf) = 0
+            pack_pair(i, make_float2(fast_exp2(e.x), fast_exp2(e.y)));
           }
         }
-        l = l * alpha + ps;  // this half's share of the row sum
+        l = l * alpha + (ps.x + ps.y);  // this half's share of the row sum
         // O and the P buffer are free once P.V of the previous tile is done
         if (j >= 1) {
           if (!uwait(pv_done, (uint32_t)((gg - 1) & 1))) {
@@ -963,6 +974,11 @@ static int umma_sched_slot(cudaStream_t stream) {
   return (int)(next.fetch_add(1u, std::memory_order_relaxed) % (unsigned)(kUmmaSchedSlots - kUmmaSchedCaptured));
 }
 
+// the two-tile form of the gathered-K kernel (prefill_umma_pair.cuh)
+static bool pair_enabled();
+template <typename T, int D, int BS, bool CASCADE>
+static cudaError_t launch_pair(const PrefillArgs& a, const TmaMaps& maps, int64_t tiles, int ny, cudaStream_t stream);
+
 template <typename T, int D, int BS, bool GK>
 static cudaError_t launch_prefill_umma(const PrefillArgs& a, cudaStream_t stream) {
   using UG = UmmaGeom<D, BS>;
@@ -983,6 +999,15 @@ static cudaError_t launch_prefill_umma(const PrefillArgs& a, cudaStream_t stream
                         kTiles, &maps))
     return cudaErrorNotSupported;
   if (GK && !make_k_gather_map(a, D, BS, &maps.k)) return cudaErrorNotSupported;
+  if constexpr (GK) {
+    if (pair_enabled()) {
+      const int G2 = a.num_heads / a.num_kv_heads;
+      const int64_t tiles2 = ((int64_t)a.max_q_len * G2 + kUmmaRows - 1) / kUmmaRows;
+      if (tiles2 <= 0 || a.num_seqs <= 0) return cudaSuccess;
+      const cudaError_t e = launch_pair<T, D, BS, false>(a, maps, tiles2, (int)a.num_seqs, stream);
+      if (e != cudaErrorNotSupported) return e;
+    }
+  }
   auto kern = prefill_umma_kernel<T, D, BS, GK>;
   static std::atomic<bool> configured[64];  // per device; setting the attribute twice is harmless
   int dev = 0;
@@ -1071,6 +1096,14 @@ static cudaError_t launch_cascade_umma(const PrefillArgs& a, int prefix_parts, c
                         kTiles, &maps))
     return cudaErrorNotSupported;
   if (GK && !make_k_gather_map(a, D, BS, &maps.k)) return cudaErrorNotSupported;
+  if constexpr (GK) {
+    if (pair_enabled()) {
+      const int G2 = a.num_heads / a.num_kv_heads;
+      const cudaError_t e = launch_pair<T, D, BS, true>(
+          a, maps, ((int64_t)a.num_seqs * G2 + kUmmaRows - 1) / kUmmaRows, prefix_parts, stream);
+      if (e != cudaErrorNotSupported) return e;
+    }
+  }
   auto kern = prefill_umma_kernel<T, D, BS, GK, true>;
   static std::atomic<bool> configured[64];  // per device; setting the attribute twice is harmless
   int dev = 0;

@@ -198,3 +198,25 @@ def test_replays_as_cuda_graph(gpu):
         st.synchronize()
         np.testing.assert_array_equal(o.to_numpy(), eager)
     assert_close(eager, ref_of(c), ATOL_NS, RTOL_NS, "graph")
+
+
+@pytest.mark.parametrize("num_seqs,bs", [(40, 16), (16, 32), (100, 16)])
+def test_two_tile_and_one_tile_prefix_forms(gpu, monkeypatch, num_seqs, bs):
+    """The shared prefix on the gathered-K tcgen05 kernel runs items of two
+    128-row tiles of (sequence, head) rows: 40 x 8 rows = 3 tiles (the second
+    pair's tile B empty), 16 x 8 = 1 tile, 100 x 8 = 7 tiles; with sequences
+    shorter than the prefix.  The result matches the oracle and the one-tile
+    kernel (KVC_PREFILL_PAIR=0); KVC_PREFILL_PAIR=1 forces the two-tile kernel
+    (unset, it runs only when its items fill the SMs)."""
+    lens = [1024 + 13 * i if i % 5 else 300 + i for i in range(num_seqs)]
+    c = cascade_case(5800 + num_seqs + bs, "bfloat16", num_seqs, 64, 8, 128, bs, 1024, lens)
+    d = upload_case(c)
+    fill_cache(d)
+    r = ref_of(c)
+    monkeypatch.setenv("KVC_PREFILL_PAIR", "1")
+    two = run_cascade(d, c)
+    assert_close(two, r, ATOL_NS, RTOL_NS, "two-tile prefix")
+    monkeypatch.setenv("KVC_PREFILL_PAIR", "0")
+    one = run_cascade(d, c)
+    assert_close(one, r, ATOL_NS, RTOL_NS, "one-tile prefix")
+    assert gpu.get_status(clear=True) == 0

@@ -196,3 +196,60 @@ def test_non_dense_key_cache_pages(gpu):
     assert_close(out, ref(c), ATOL_NS, RTOL_NS, "non-dense K")
     assert gpu.get_status(clear=True) == 0
 
+
+
+@pytest.fixture
+def one_tile_form(monkeypatch):
+    """Forces the two-tile tcgen05 kernel for the test (KVC_PREFILL_PAIR=1, read
+    at every launch; unset, it runs only when its items fill the SMs) and
+    returns a runner of a callable on the one-tile kernel (KVC_PREFILL_PAIR=0)."""
+    monkeypatch.setenv("KVC_PREFILL_PAIR", "1")
+
+    def call(fn):
+        monkeypatch.setenv("KVC_PREFILL_PAIR", "0")
+        try:
+            return fn()
+        finally:
+            monkeypatch.setenv("KVC_PREFILL_PAIR", "1")
+    return call
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+@pytest.mark.parametrize("D,bs", [(64, 16), (128, 16), (64, 32), (128, 32)])
+def test_two_tile_and_one_tile_forms(gpu, one_tile_form, dtype, D, bs):
+    """The gathered-K tcgen05 kernel runs items of two 128-row tiles: rows of
+    tile B past the sequence (B empty), odd tile counts (3 and 5 tiles of G x
+    new tokens), a one-row tile and a whole pair all match the oracle and the
+    one-tile kernel."""
+    # G = 4: 96 new tokens = 3 tiles, 160 = 5 tiles, 32 = 1 tile, 64 = 2 tiles, 1 token = 4 rows
+    c = prefill_case(7100 + D + bs, dtype, 16, 4, D, "paged", bs, [0, 500, 33, 128, 7], [96, 160, 32, 64, 1])
+    r = ref(c)
+    two = run(c)
+    assert_close(two, r, ATOL_NS, RTOL_NS, f"two-tile {dtype} D{D} bs{bs}")
+    one = one_tile_form(lambda: run(c))
+    assert_close(one, r, ATOL_NS, RTOL_NS, f"one-tile {dtype} D{D} bs{bs}")
+    assert gpu.get_status(clear=True) == 0
+
+
+def test_many_short_sequences_per_cta(gpu, one_tile_form):
+    """600 sequences of 1 to 40 new tokens (each one item whose tile B is
+    empty; 4800 items over the persistent grid, so every CTA claims many of
+    them back to back) on prefixes of 0 to 700 tokens."""
+    rng = np.random.default_rng(7200)
+    B = 600
+    prefixes = [int(x) for x in rng.integers(0, 700, B)]
+    qlens = [int(x) for x in rng.integers(1, 41, B)]
+    c = prefill_case(7200, "bfloat16", 32, 8, 128, "paged", 16, prefixes, qlens)
+    assert_close(run(c), ref(c), ATOL_NS, RTOL_NS, "600 short sequences")
+    assert gpu.get_status(clear=True) == 0
+
+
+def test_two_tile_windows_and_long_rows(gpu, one_tile_form):
+    """Sliding windows narrower than a pair's row span (tile B's rows start past
+    keys tile A needs) and a 2000-token chunk, against the one-tile kernel."""
+    c = prefill_case(7300, "bfloat16", 28, 4, 128, "paged", 32, [1000, 0, 64], [2000, 300, 900])
+    for window in (None, 100, 700):
+        r = ref(c, window=window)
+        assert_close(run(c, window=window), r, ATOL_NS, RTOL_NS, f"two-tile window {window}")
+        assert_close(one_tile_form(lambda: run(c, window=window)), r, ATOL_NS, RTOL_NS, f"one-tile window {window}")
+    assert gpu.get_status(clear=True) == 0
