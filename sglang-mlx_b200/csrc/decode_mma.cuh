@@ -149,6 +149,17 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// Four rows (row0..row3 of a 2-D tensor map whose box is one row high) land
+// one after another at `dst`.
+__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, int col, int row0, int row1, int row2,
+                                            int row3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(col), "r"(row0), "r"(row1), "r"(row2), "r"(row3)
+      : "memory");
+}
+
 __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -272,8 +283,15 @@ constexpr float kLn2 = 0.6931471805599453f;
 //             the 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r & 7)),
 //             K and V both read with ldmatrix (V transposed).  One copy per
 //             (group, head, 64 dims) instead of a 16-byte cp.async per lane and row.
+//  kFlashGather  token-major caches whose rows are dense ([slots, H, D] of the
+//             token pool's slot lists, or [nb, bs, H, D] with any bs): the same
+//             shared layout as kFlashTma, each token's row fetched where its own
+//             slot is by 4-row tensor gathers (tile::gather4, 64 dims per
+//             request): 16 requests per 16-token group and head at D = 128.
+//             The stage mask has a bit per token; a token past the context or
+//             with a bad slot gathers a valid token's row and is masked.
 constexpr int kBulk = 0, kTiles = 1, kSwizzledV = 2, kFlash = 3, kFp8E4M3 = 4, kFp8E5M2 = 5, kFlashBulk = 6,
-              kFlashTma = 7;
+              kFlashTma = 7, kFlashGather = 8;
 
 template <int D, int BS, int NW, int STAGES, int GT_ = 32, int MODE = kBulk>
 struct MmaGeom {
@@ -281,10 +299,14 @@ struct MmaGeom {
   static constexpr bool FLASH = MODE == kFlash || MODE == kFlashBulk;  // token-major K/V rows
   static constexpr bool CP_ASYNC = MODE == kFlash;        // stage completion: 32 cp.async arrivals
   static constexpr bool FP8 = MODE == kFp8E4M3 || MODE == kFp8E5M2;  // one-byte caches
-  static constexpr bool TROWS = MODE == kFlashTma;        // token rows by tensor copies, swizzled 128-byte halves
+  static constexpr bool GATHER = MODE == kFlashGather;   // token rows by 4-row tensor gathers
+  static constexpr bool TROWS = MODE == kFlashTma || GATHER;  // token rows as swizzled 128-byte halves
+  static constexpr bool TOKIDS = FLASH || GATHER;         // a block id per token (the id chunks)
   static constexpr int VBS = FLASH ? 1 : (TROWS ? GT : (MODE == kTiles ? (GT < BS ? GT : BS) : BS));  // tokens per box
   static constexpr int NBOX = GT / VBS;                   // boxes per group (K and V each)
-  static constexpr uint32_t FULL_MASK = NBOX >= 32 ? 0xffffffffu : (1u << (NBOX & 31)) - 1u;  // every box loaded
+  static constexpr int MBS = GATHER ? 1 : VBS;            // tokens per stage-mask bit
+  static constexpr int NMB = GT / MBS;                    // mask bits per group
+  static constexpr uint32_t FULL_MASK = NMB >= 32 ? 0xffffffffu : (1u << (NMB & 31)) - 1u;  // everything loaded
   static_assert(GT % 16 == 0 && GT % VBS == 0, "a group is whole boxes and whole 16-token k-steps");
   static_assert(!FLASH || GT == 16 || GT == 32, "token-major groups are 16 or 32 tokens (one mask bit per token)");
   static constexpr int ROWB = D * 2;                      // bytes of one token row (kFlash)
@@ -300,8 +322,9 @@ struct MmaGeom {
   // token), filled a chunk ahead of the copies that use them
   static constexpr int IDC = 8;
   static constexpr int IDS_OFF = (MASK_OFF + NW * STAGES * 4 + 15) / 16 * 16;
-  static constexpr int SMEM = IDS_OFF + (FLASH ? NW * 2 * IDC * GT * 4 : 0);
-  static_assert(!FLASH || (STAGES <= IDC && (IDC * GT) % 32 == 0), "id chunks cover the ring");
+  static constexpr int SMEM = IDS_OFF + (TOKIDS ? NW * 2 * IDC * GT * 4 : 0);
+  static_assert(!TOKIDS || (STAGES <= IDC && (IDC * GT) % 32 == 0), "id chunks cover the ring");
+  static_assert(!GATHER || GT == 16, "a gathered group is 16 tokens (4 requests of 4 rows per 64 dims)");
   static_assert(COMBINE <= RING, "combine buffer must fit in the ring");
 };
 
@@ -403,7 +426,7 @@ __device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa
         x_hi += slope_hi * pos;
       }
       if (tail) {
-        const bool ok = (tok0 + t < end) && ((pmask >> (t / VBS)) & 1u);
+        const bool ok = (tok0 + t < end) && ((pmask >> (t / Geo::MBS)) & 1u);
         x_lo = (ok && tok0 + t < end_lo && tok0 + t >= beg_lo) ? x_lo : -INFINITY;
         x_hi = (ok && tok0 + t < end_hi && tok0 + t >= beg_hi) ? x_hi : -INFINITY;
       }
@@ -471,10 +494,10 @@ __device__ __forceinline__ void mma_group(GroupState<D>& gs, const uint32_t (&qa
     bool ok_lo0 = true, ok_lo1 = true, ok_hi0 = true, ok_hi1 = true;
     if (tail) {
       const int tl = 16 * kk + 2 * q4;
-      ok_lo0 = (t_lo < end) && ((pmask >> (tl / VBS)) & 1u);
-      ok_lo1 = (t_lo + 1 < end) && ((pmask >> ((tl + 1) / VBS)) & 1u);
-      ok_hi0 = (t_lo + 8 < end) && ((pmask >> ((tl + 8) / VBS)) & 1u);
-      ok_hi1 = (t_lo + 9 < end) && ((pmask >> ((tl + 9) / VBS)) & 1u);
+      ok_lo0 = (t_lo < end) && ((pmask >> (tl / Geo::MBS)) & 1u);
+      ok_lo1 = (t_lo + 1 < end) && ((pmask >> ((tl + 1) / Geo::MBS)) & 1u);
+      ok_hi0 = (t_lo + 8 < end) && ((pmask >> ((tl + 8) / Geo::MBS)) & 1u);
+      ok_hi1 = (t_lo + 9 < end) && ((pmask >> ((tl + 9) / Geo::MBS)) & 1u);
     }
 #pragma unroll
     for (int nt = 0; nt < NT; nt += 2) {
@@ -854,7 +877,7 @@ __global__ void __launch_bounds__(NW * 32)
   // Token-major caches use the id chunks instead (load_ids / store_ids).
   auto load_block = [&](int k) -> uint32_t {
     uint32_t b = 0xffffffffu;
-    if constexpr (!Geo::FLASH) {
+    if constexpr (!Geo::TOKIDS) {
       if (lane < NBOX && k < n_mine) {
         const int pg = (begin + (warp + k * NW) * GT + lane * VBS) / rbs;
         if (pg < page_end) b = __ldg(table + pg);
@@ -954,6 +977,38 @@ __global__ void __launch_bounds__(NW * 32)
         }
       }
       cp_async_arrive(&bars[s]);
+    } else if constexpr (Geo::GATHER) {
+      // kFlashGather: token i's row is (block * bs + offset) * H + kvh of the
+      // 2-D [rows][D] maps; lane 0 posts the bytes of the whole group (every
+      // row is gathered: a token past the context or with a bad slot takes the
+      // first valid token's row), then lane (kv, half, quad) < 2 * D / 64 * 4
+      // gathers rows 4q .. 4q + 3 of K or V, 64 dims of them, to quad q of that
+      // half (the 128-byte swizzle places them as the shared layout expects)
+      const uint32_t* cid = ids + ((k / IDC) & 1) * IDC * GT + (k % IDC) * GT;
+      const int t0 = begin + (warp + k * NW) * GT;
+      const int tt = t0 + lane;
+      const bool in_ctx = lane < GT && tt < end;
+      const uint32_t b = cid[lane < GT ? lane : 0];
+      const bool ok = in_ctx && (int64_t)b < p.num_blocks;
+      if (in_ctx && !ok) set_status(&g_decode_status, KVC_STATUS_BLOCK_OOB);
+      const uint32_t mask = __ballot_sync(0xffffffffu, ok);
+      int row = ok ? (int)(((tok_blocks ? (int64_t)b : (int64_t)b * tbs + tt % tbs) * p.num_kv_heads + kvh)) : 0;
+      row = __shfl_sync(0xffffffffu, row, ok ? lane : (mask ? __ffs(mask) - 1 : 0));
+      if (lane == 0) {
+        masks[s] = mask;
+        if (mask) mbar_arrive_expect_tx(&bars[s], 2u * (uint32_t)BOX);
+        else mbar_arrive(&bars[s]);
+      }
+      __syncwarp();
+      if (mask) {
+        constexpr int Q = GT / 4, HALVES = D / 64;
+        const int q = lane % Q, h = (lane / Q) % HALVES, kv = lane / (Q * HALVES);
+        const int r0 = __shfl_sync(0xffffffffu, row, 4 * q), r1 = __shfl_sync(0xffffffffu, row, 4 * q + 1);
+        const int r2 = __shfl_sync(0xffffffffu, row, 4 * q + 2), r3 = __shfl_sync(0xffffffffu, row, 4 * q + 3);
+        if (lane < 2 * HALVES * Q)
+          tma_gather4(ring + (size_t)s * Geo::STAGE + kv * BOX + h * (GT * 128) + q * 4 * 128, kv ? &tm.v : &tm.k,
+                      64 * h, r0, r1, r2, r3, &bars[s]);
+      }
     } else {
       uint32_t ids[NBOX];
 #pragma unroll
@@ -1025,7 +1080,7 @@ __global__ void __launch_bounds__(NW * 32)
 
   // ---- prologue: fill the ring
   uint32_t ids_next[IDV];  // token-major caches: the chunk after the current one
-  if constexpr (Geo::FLASH) {
+  if constexpr (Geo::TOKIDS) {
     uint32_t first[IDV];
     load_ids(0, first);
     load_ids(1, ids_next);
@@ -1042,7 +1097,7 @@ __global__ void __launch_bounds__(NW * 32)
 
   for (int k = 0; k < n_mine; ++k) {
     const int s = k % STAGES;
-    if constexpr (Geo::FLASH) {
+    if constexpr (Geo::TOKIDS) {
       // chunk c + 1 (loaded a chunk ago) replaces chunk c - 1, whose last
       // group was issued STAGES groups before this one; chunk c + 2 is loaded
       if (k % IDC == 0 && k + STAGES < n_mine) {
@@ -1218,12 +1273,12 @@ static bool make_tensor_maps(const DecodeParams& p, ElemType et, int D, int BS, 
   key.ks[1] = p.k_block_stride;
   key.vs[0] = p.v_head_stride;
   key.vs[1] = p.v_block_stride;
-  if (mode == kFlashTma) {  // token rows: the row stride and the run-time block size define the maps
+  if (mode == kFlashTma || mode == kFlashGather) {  // token rows: the row stride and the run-time block size
     key.ks[1] = p.k_tok_stride;
     key.vs[1] = p.v_tok_stride;
   }
   key.d = D;
-  key.bs = mode == kFlashTma ? p.block_size : BS;
+  key.bs = (mode == kFlashTma || mode == kFlashGather) ? p.block_size : BS;
   key.vbs = VBS;
   key.swz = swz;
   key.dt = (int)et;
@@ -1255,6 +1310,27 @@ static bool make_tensor_maps(const DecodeParams& p, ElemType et, int D, int BS, 
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
             CUDA_SUCCESS ||
         enc(&m.v, dt, 3, const_cast<void*>(p.v_cache), dim, vstr, box, ones, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+            CUDA_SUCCESS)
+      return false;
+    keys[next] = key;
+    maps[next] = m;
+    next = (next + 1) % 32;
+    if (used < 32) ++used;
+    *out = m;
+    return true;
+  }
+  if (mode == kFlashGather) {
+    // [rows = num_blocks * bs * H][D]: dense token rows of every head, boxes of
+    // 64 dims x 1 row (the 4-row gathers), landing with the 128-byte swizzle
+    const cuuint64_t rows = (cuuint64_t)p.num_blocks * (cuuint64_t)p.block_size * (cuuint64_t)p.num_kv_heads;
+    cuuint64_t dim[2] = {(cuuint64_t)D, rows};
+    cuuint64_t str[1] = {(cuuint64_t)D * es};
+    cuuint32_t box[2] = {64, 1};
+    if (enc(&m.k, dt, 2, const_cast<void*>(p.k_cache), dim, str, box, ones, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+            CUDA_SUCCESS ||
+        enc(&m.v, dt, 2, const_cast<void*>(p.v_cache), dim, str, box, ones, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
             CUDA_SUCCESS)
       return false;
@@ -1311,7 +1387,7 @@ static cudaError_t launch_mma_nw(const DecodeParams& p, cudaStream_t stream) {
   auto kern = paged_decode_mma_kernel<T, D, BS, NW, STAGES, GT, MODE>;
   TmaMaps maps;
   memset(&maps, 0, sizeof(maps));
-  if (MODE == kTiles || MODE == kSwizzledV || MODE == kFlashTma) {
+  if (MODE == kTiles || MODE == kSwizzledV || MODE == kFlashTma || MODE == kFlashGather) {
     const ElemType et = std::is_same<T, __nv_bfloat16>::value ? ElemType::BF16 : ElemType::F16;
     if (!make_tensor_maps(p, et, D, BS, Geo::VBS, Geo::VSWZ, MODE, &maps)) return cudaErrorNotSupported;
   }
@@ -1441,6 +1517,7 @@ static cudaError_t launch_mma_t(const DecodeParams& p, const DecodeArgs& a, cuda
     // D = 128, two CTAs per SM); the block size is read at run time.
     // KVC_FLASH_COPY=bulk selects per-row bulk copies (tuning runs).
     // KVC_FLASH_COPY=cpasync keeps the per-lane row copies where tensor copies apply (tuning runs).
+    // KVC_FLASH_COPY=gather reads dense rows in any order by tensor gathers (below).
     const char* fc = getenv("KVC_FLASH_COPY");
     if (fc && fc[0] == 'b') {
       if (a.head_size == 128) return launch_mma_nw<T, 128, 16, 4, 3, 16, kFlashBulk>(p, stream);
@@ -1453,6 +1530,22 @@ static cudaError_t launch_mma_t(const DecodeParams& p, const DecodeArgs& a, cuda
     if (rows_ok) {
       cudaError_t e = a.head_size == 128 ? launch_mma_nw<T, 128, 16, 4, 3, 16, kFlashTma>(p, stream)
                                          : launch_mma_nw<T, 64, 16, 4, 3, 16, kFlashTma>(p, stream);
+      if (e != cudaErrorNotSupported) return e;
+    }
+    // KVC_FLASH_COPY=gather: dense token rows in any order (the pool's slot
+    // lists) by 4-row tensor gathers.  Not the default: on config 2's slot-list
+    // pool they measured 0.661 of the copy peak against 0.708 for the per-lane
+    // row copies (16 gather requests per 16-token group and head, against 4
+    // tensor copies for blocks of consecutive rows).
+    // (block size 1, the pool's [slots, H, D]: a block is one row and carries no token stride)
+    const int64_t D = a.head_size, H = a.num_kv_heads, rbs = a.block_size;
+    const int64_t ktok = rbs == 1 ? H * D : a.k_tok_stride, vtok = rbs == 1 ? H * D : a.v_tok_stride;
+    const bool dense = a.k_head_stride == D && ktok == H * D && a.k_block_stride == rbs * H * D &&
+                       a.v_head_stride == D && vtok == H * D && a.v_block_stride == rbs * H * D &&
+                       a.num_blocks * rbs * H < (int64_t)1 << 31 && fc && fc[0] == 'g';
+    if (dense) {
+      cudaError_t e = a.head_size == 128 ? launch_mma_nw<T, 128, 16, 4, 3, 16, kFlashGather>(p, stream)
+                                         : launch_mma_nw<T, 64, 16, 4, 3, 16, kFlashGather>(p, stream);
       if (e != cudaErrorNotSupported) return e;
     }
     if (a.head_size == 128) return launch_mma_nw<T, 128, 16, 4, 3, 16, kFlash>(p, stream);

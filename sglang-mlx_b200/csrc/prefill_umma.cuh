@@ -120,17 +120,8 @@ __device__ __forceinline__ void st32(uint32_t taddr, const uint32_t (&r)[32]) {
   st16(taddr + 16, r + 16);
 }
 
-// Four rows (row0..row3 of a 2-D tensor map whose box is one row high) land
-// one after another at `dst`: a gather of the same chunk of four pages.
-__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, int col, int row0, int row1, int row2,
-                                            int row3, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
-      "%5, %6, %7}], [%2];" ::"r"(mma_detail::smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(mma_detail::smem_u32(bar)), "r"(col), "r"(row0), "r"(row1), "r"(row2),
-      "r"(row3)
-      : "memory");
-}
+// (the 4-row gather of the same chunk of four pages: mma_detail::tma_gather4)
+using mma_detail::tma_gather4;
 
 }  // namespace umma
 

@@ -226,6 +226,85 @@ def test_tensor_copy_rows_match_row_copies(gpu, dtype, D, bs, monkeypatch):
     assert gpu.get_status(clear=True) == 0
 
 
+# ---- dense token rows in any order (slot lists): 4-row tensor gathers (kFlashGather) --------
+
+def scatter_slots(fc, seed):
+    """A token-pool case (block size 1) with its slots moved to a random
+    permutation of the pool (slot 0, the padding slot, stays): neighbouring
+    tokens of a sequence land anywhere."""
+    rng = np.random.default_rng(seed)
+    n = fc["shape"][0]
+    perm = np.concatenate([[0], 1 + rng.permutation(n - 1)]).astype(np.int64)
+    fc = dict(fc)
+    fc["slots"] = perm[fc["slots"].astype(np.int64)].astype(np.int32)
+    fc["tables"] = perm[fc["tables"].astype(np.int64)].astype(np.int32)
+    return fc
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("bs", [1, 8])
+def test_gathered_rows_match_row_copies(gpu, dtype, D, bs, monkeypatch):
+    """KVC_FLASH_COPY=gather reads each token's K and V rows of slot lists
+    (block size 1) and of 8-token blocks by 4-row tensor gathers; the default
+    is the per-lane 16-byte row copies.  Lengths end inside a 4-row quad and
+    inside a 16-token group; both forms agree with the oracle, single pass and
+    split-K."""
+    fc = flash_case(5100 + D + bs, dtype, 5, 8, 2, D, bs, [1, 3, 17, 334, 2001])
+    if bs == 1:
+        fc = scatter_slots(fc, 5100 + D)
+    d = upload_flash(fc)
+    ref = oracle_flash(fc)
+    for psize in (0, 256):
+        monkeypatch.setenv("KVC_FLASH_COPY", "gather")
+        gat = run_flash(fc, d, partition_size=psize)
+        monkeypatch.delenv("KVC_FLASH_COPY")
+        rows = run_flash(fc, d, partition_size=psize)
+        assert_close(gat, ref, ATOL_NS, RTOL_NS, f"gathers bs{bs} P={psize}")
+        assert_close(rows, ref, ATOL_NS, RTOL_NS, f"row copies bs{bs} P={psize}")
+    assert gpu.get_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("copy", ["gather", "cpasync"])
+def test_gathered_rows_bad_slots_inside_a_group(gpu, copy, monkeypatch):
+    """Out-of-range slots in the middle of a 16-token group (and one as its first
+    token) are flagged and masked; the other tokens of the group still count:
+    the result equals the oracle over the same table with those tokens dropped
+    (tensor gathers and row copies alike)."""
+    fc = scatter_slots(flash_case(5200, "bfloat16", 2, 8, 2, 128, 1, [48, 48]), 5200)
+    d = upload_flash(fc)
+    t = fc["tables"].copy()
+    bad = [(0, 16), (0, 21), (1, 5)]
+    for b, i in bad:
+        t[b, i] = 10_000_000
+    d["tables"] = DeviceArray.from_numpy(t)
+    gpu.get_status(clear=True)
+    monkeypatch.setenv("KVC_FLASH_COPY", copy)
+    out = run_flash(fc, d)
+    monkeypatch.delenv("KVC_FLASH_COPY")
+    assert gpu.get_status(clear=True) & _lib.STATUS_BLOCK_OOB
+    # the oracle without those tokens: their keys get a score of -inf
+    c = fc["c"]
+    fk = np.zeros(fc["shape"], np.float32)
+    fv = np.zeros(fc["shape"], np.float32)
+    kv_oracle.reshape_and_cache_flash(kv_oracle.round_to(c["k"], c["dtype"]), kv_oracle.round_to(c["v"], c["dtype"]),
+                                      fk, fv, fc["slots"])
+    q = kv_oracle.round_to(c["q"], c["dtype"]).astype(np.float64)
+    ref = np.zeros_like(q)
+    G = 8 // 2
+    for b in range(2):
+        n = int(c["context_lens"][b])
+        keep = [i for i in range(n) if (b, i) not in bad]
+        slots = fc["tables"][b, keep]
+        for h in range(8):
+            k = fk[slots, h // G].astype(np.float64)
+            v = fv[slots, h // G].astype(np.float64)
+            sc = k @ q[b, h] * c["scale"]
+            w = np.exp(sc - sc.max())
+            ref[b, h] = w @ v / w.sum()
+    assert_close(out, ref, ATOL_NS, RTOL_NS, "bad slots masked")
+
+
 @pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
 def test_paged_pool_decode_pages_matches_slot_lists(gpu, dtype):
     """A pool whose allocator hands out 16-token pages: requests allocated in
