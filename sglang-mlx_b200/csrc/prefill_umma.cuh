@@ -671,8 +671,19 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
             reinterpret_cast<const T*>(p.q) + (it.q0 + t) * p.q_tok_stride +
             (int64_t)(kvh * G + g) * p.q_head_stride) + half * QC;
         uint32_t qv[32];
+        if (on && (reinterpret_cast<uintptr_t>(qrow) & 15u) == 0) {  // 16-byte loads where the row allows
 #pragma unroll
-        for (int i = 0; i < QC; ++i) qv[i] = on ? __ldg(qrow + i) : 0u;
+          for (int i = 0; i < QC; i += 4) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(qrow + i));
+            qv[i] = v.x;
+            qv[i + 1] = v.y;
+            qv[i + 2] = v.z;
+            qv[i + 3] = v.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < QC; ++i) qv[i] = on ? __ldg(qrow + i) : 0u;
+        }
         if constexpr (QC == 32) umma::st32(lane_base + UG::QCOL + half * QC, qv);
         else umma::st16(lane_base + UG::QCOL + half * QC, qv);
       }
