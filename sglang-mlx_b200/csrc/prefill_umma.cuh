@@ -356,6 +356,18 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         idx = claim();
         continue;
       }
+      // the item's query rows toward L2: the softmax warps load them only after
+      // finishing the item before this one
+      if (!it.bad && it.ntiles > 0) {
+        const int64_t nrows = it.rows - it.R0 < kUmmaRows ? it.rows - it.R0 : kUmmaRows;
+        for (int r = lane; r < nrows; r += 32) {
+          const int64_t R = it.R0 + r, t = R / G;
+          const char* a = reinterpret_cast<const char*>(reinterpret_cast<const T*>(p.q) + (it.q0 + t) * p.q_tok_stride +
+                                                        (int64_t)(it.kvh * G + (int)(R - t * G)) * p.q_head_stride);
+#pragma unroll
+          for (int b = 0; b < D * 2; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(a + b));
+        }
+      }
       bool handed = true;
       if (lane == 0) handed = publish(idx);
       if (!__shfl_sync(0xffffffffu, handed, 0)) {
