@@ -532,7 +532,25 @@ __global__ void __launch_bounds__(kReduceHeadsPerCta * 32) splitk_reduce_few_ker
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.x * kReduceHeadsPerCta + warp, seq = blockIdx.y;
   if (head >= p.num_heads) return;
+  // Every load is issued before any of them is used (one memory latency, not a
+  // chain): the length, lane i's partial max and sum (i < num_partitions <= 32)
+  // and this lane's columns of the first PRE partials.  Entries past the
+  // sequence's own partitions may be stale; they are selected away below before
+  // any arithmetic touches them.
+  constexpr int PRE = 8;
+  const int NP = p.num_partitions;
   const uint32_t ctx = p.context_lens[seq];
+  const float* pm = p.part_max + (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride;
+  const float* pl = p.part_sum + (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride;
+  const float* po = p.part_out + (int64_t)seq * p.part_out_seq_stride + (int64_t)head * p.part_out_head_stride;
+  const float m_raw = lane < NP ? pm[lane] : -INFINITY;
+  const float l_raw = lane < NP ? pl[lane] : 0.f;
+  const bool col = VEC && lane < head_size / 4;  // VEC: this lane's first 4 columns (4 * lane ..)
+  float4 x[PRE];
+#pragma unroll
+  for (int i = 0; i < PRE; ++i)
+    x[i] = (col && i < NP) ? reinterpret_cast<const float4*>(po + (int64_t)i * p.part_out_part_stride)[lane]
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
   T* out = reinterpret_cast<T*>(p.out) + (int64_t)seq * p.out_seq_stride + (int64_t)head * p.out_head_stride;
   if (ctx == 0 || ctx > (uint32_t)p.max_seq_len) {
     for (int d = lane; d < head_size; d += 32) out[d] = from_float<T>(0.f);
@@ -543,32 +561,47 @@ __global__ void __launch_bounds__(kReduceHeadsPerCta * 32) splitk_reduce_few_ker
                                                  ? (int)((ctx - p.prefix_len + p.partition_size - 1) / p.partition_size)
                                                  : 0)
                          : (int)((ctx + p.partition_size - 1) / p.partition_size);
-  const float* pm = p.part_max + (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride;
-  const float* pl = p.part_sum + (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride;
-  float M = -INFINITY;
-  for (int i = lane; i < nparts; i += 32) M = fmaxf(M, pm[i]);
+  const float mi = lane < nparts ? m_raw : -INFINITY;
+  float M = mi;
   for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  float L = 0.f;
-  for (int i = lane; i < nparts; i += 32)
-    L += (M == -INFINITY || pm[i] == -INFINITY) ? 0.f : expf(pm[i] - M) * pl[i];
+  // lane i's weight (0 for a partition without keys, or past the sequence)
+  const float wi = (M == -INFINITY || mi == -INFINITY) ? 0.f : expf(mi - M);
+  float L = lane < nparts ? wi * l_raw : 0.f;
   for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
   const float inv = 1.f / (L + 1e-6f);
-  const float* po = p.part_out + (int64_t)seq * p.part_out_seq_stride + (int64_t)head * p.part_out_head_stride;
   if (VEC) {
-    for (int v4 = lane; v4 < head_size / 4; v4 += 32) {
-      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    // lane's weight of partition i, broadcast (every lane takes part)
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    auto acc = [&](float4& s4, float w, const float4& y) {
+      s4.x += w * y.x;
+      s4.y += w * y.y;
+      s4.z += w * y.z;
+      s4.w += w * y.w;
+    };
+#pragma unroll
+    for (int i = 0; i < PRE; ++i) {
+      const float w = __shfl_sync(0xffffffffu, wi, i);
+      if (i < nparts) acc(a, w, x[i]);
+    }
+    for (int i = PRE; i < nparts; ++i) {
+      const float w = __shfl_sync(0xffffffffu, wi, i);
+      if (col) acc(a, w, reinterpret_cast<const float4*>(po + (int64_t)i * p.part_out_part_stride)[lane]);
+    }
+    auto store4 = [&](int v4, const float4& s4) {
+      out[4 * v4 + 0] = from_float<T>(s4.x * inv);
+      out[4 * v4 + 1] = from_float<T>(s4.y * inv);
+      out[4 * v4 + 2] = from_float<T>(s4.z * inv);
+      out[4 * v4 + 3] = from_float<T>(s4.w * inv);
+    };
+    if (col) store4(lane, a);
+    // head sizes above 128: the further columns, weights read back per partition
+    for (int v4 = lane + 32; v4 < head_size / 4; v4 += 32) {
+      float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int i = 0; i < nparts; ++i) {
         const float w = (M == -INFINITY || pm[i] == -INFINITY) ? 0.f : expf(pm[i] - M);
-        const float4 x = reinterpret_cast<const float4*>(po + (int64_t)i * p.part_out_part_stride)[v4];
-        a.x += w * x.x;
-        a.y += w * x.y;
-        a.z += w * x.z;
-        a.w += w * x.w;
+        acc(b, w, reinterpret_cast<const float4*>(po + (int64_t)i * p.part_out_part_stride)[v4]);
       }
-      out[4 * v4 + 0] = from_float<T>(a.x * inv);
-      out[4 * v4 + 1] = from_float<T>(a.y * inv);
-      out[4 * v4 + 2] = from_float<T>(a.z * inv);
-      out[4 * v4 + 3] = from_float<T>(a.w * inv);
+      store4(v4, b);
     }
   } else {
     for (int d = lane; d < head_size; d += 32) {
