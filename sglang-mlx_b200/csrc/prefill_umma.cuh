@@ -260,9 +260,13 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   const CUtensorMap* vmap = &maps.v;
   const CUtensorMap* kmap = &maps.k;
   static_assert(!GK || PAGES % 4 == 0, "the gathered K layout takes pages in fours");
-  // the shared-prefix form's tail partitions (a programmatic dependent that
-  // waits for this grid before exiting) may start beside it
-  grid_dependents_launch();
+  // The shared-prefix form is itself a programmatic dependent of the kernel
+  // before it (the step's append, which lets its dependents start at once):
+  // its set-up, query staging and block-id reads (nothing an append writes)
+  // overlap that kernel, and its producer waits for it before the first cache
+  // copy, then lets the tail partitions (a programmatic dependent that waits
+  // for this grid before exiting) start beside it.
+  if constexpr (!CASCADE) grid_dependents_launch();
   // (fewer items than CTAs: each CTA has its one item and nothing is claimed)
   const bool dynamic = n_items > (int)gridDim.x;
   // The producer decodes its first item and starts that item's first block-id
@@ -324,6 +328,10 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   };
 
   if (warp == kProducerWarp) {
+    if constexpr (CASCADE) {
+      grid_dependency_wait();
+      if (lane == 0) grid_dependents_launch();
+    }
     // ---- producer: claims items, hands each one with rows to the other warps,
     // then loads its 128-token tiles of whole pages
     int gt = 0;    // tiles issued by this CTA so far
@@ -1136,9 +1144,20 @@ static cudaError_t launch_cascade_umma(const PrefillArgs& a, int prefix_parts, c
   const int slot = umma_sched_slot(stream);
   PrefillArgs aa = a;
   aa.single_issue = umma_single_issue();
-  kern<<<ctas, kUmmaThreads, UG::SMEM, stream>>>(aa, maps, (int)tiles, prefix_parts, slot);
+  // a programmatic dependent of the kernel before it (see the kernel's start)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ctas);
+  cfg.blockDim = dim3(kUmmaThreads);
+  cfg.dynamicSmemBytes = UG::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, aa, maps, (int)tiles, prefix_parts, slot);
   count_launch();
-  return cudaGetLastError();
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 // The prefix of a shared-prefix decode on the tensor cores' own pipeline when
