@@ -498,6 +498,12 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
         psize = 0
     split = psize > 0
     planned = split and (args.decode == "planned" or auto_planned) and not pool
+    # the step's append folded into the planned decode (one launch per layer) where
+    # the step appends one token per sequence to a paged 16-bit cache
+    can_fold = planned and not fp8 and not pool and not cascade and T_new == B
+    if args.append == "folded" and not can_fold:
+        raise SystemExit("--append folded needs the planned paged decode and one new token per sequence")
+    folded = can_fold and args.append != "separate"
     ws = mk.splitk_workspace(B, hq, D, max_seq_len, psize, dev) if split else None
     dplan = mk.DecodePlan(B, hkv, max_seq_len, psize, dev) if planned else None
     torch.cuda.synchronize()
@@ -516,6 +522,9 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
             mk.make_decode_plan(lens_d, hkv, max_seq_len, psize, plan=dplan, stream=stream)
 
     def decode(i, stream=st):
+        if folded:  # the append and the decode in one launch
+            return mk.paged_attention_append(q[i], kn[i], vn[i], kc[i], vc[i], slots_d, tables_d, lens_d, hkv, scale,
+                                             BS, max_seq_len, workspace=ws, out=out[i], stream=stream, plan=dplan)
         if fp8:
             return mk.paged_attention_fp8(q[i], kc[i], vc[i], tables_d, lens_d, hkv, scale, BS, max_seq_len,
                                           k_scale=0.05, v_scale=0.05, fp8_format=fmt, partition_size=psize,
@@ -539,7 +548,8 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
     def step(ev=None):
         make_plan()
         for i in range(L):
-            append(i)
+            if not folded:
+                append(i)
             if ev is not None:
                 ev[i][0].record(st)
             decode(i)
@@ -650,7 +660,8 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
                 st.wait(ev_in[i])
                 if not first:
                     st.wait(ev_out[i])
-                append(i)
+                if not folded:
+                    append(i)
                 decode(i)
                 ev_dec[i].record(st)
                 down.wait(ev_dec[i])
@@ -688,6 +699,9 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
     mean_dec_ms = float(np.mean(dec_ms))
     alg, logical = decode_bytes(page_tables if pool_pages else tables, lens_after, hq, hkv, D,
                                 BS if pool_pages else tab_bs, shared, s_kv=1 if fp8 else 2)
+    if folded:  # the launch also reads the new K/V rows and writes them into the cache
+        alg += 2 * 2 * T_new * hkv * D * 2
+        logical += 2 * 2 * T_new * hkv * D * 2
     sums = np.array([float(alg), float(logical), float(h2d), float(d2h)])
     if dist is not None:
         t = torch.tensor([step_ms, e2e_step_ms, mean_dec_ms, 0.0 if ok else 1.0, err], dtype=torch.float64)
@@ -713,6 +727,8 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
     kernel = f"split-K v2, {psize}-token partitions" if split else "paged_attention_v1"
     if planned:
         kernel = f"planned split-K, {psize}-token partitions longest first, merge fused"
+        if folded:
+            kernel += ", the step's append folded in"
     if pool:
         kernel = "token-pool decode (paged_attention_flash, " + (
             f"{BS}-token page tables, tensor copies" if pool_pages else "slot lists") + (
@@ -1100,6 +1116,9 @@ def main():
                     help="decode form: the shim's choice (default; shared-prefix cascade for config 4), single pass, "
                          "split-K, planned split-K (work list longest first, merge fused), or cascade")
     ap.add_argument("--partition", type=int, default=0, help="split-K partition size (tokens) when split")
+    ap.add_argument("--append", default="auto", choices=["auto", "separate", "folded"],
+                    help="the step's append: folded into the planned decode where it applies (default), or its own "
+                         "launch before each decode")
     ap.add_argument("--partition-prefix", type=int, default=0,
                     help="cascade: shared-prefix chunk size (tokens); default from cascade_partitions")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (profiling cases only)")

@@ -150,6 +150,33 @@ int kvc_paged_attention_planned(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_d
                                 int max_seq_len, const kvc_dltensor* alibi_slopes, int partition_size,
                                 kvc_dltensor* plan, void* stream);
 
+/* A decode step's append and planned decode in one launch: the same results
+ * (cache and `out`) as kvc_reshape_and_cache(key, value, key_cache,
+ * value_cache, slot_mapping) followed by kvc_paged_attention_planned, for a
+ * step that appends one token per sequence.  No reference counterpart (the
+ * reference appends and decodes in two calls, metal_kernels.py:20-74); it
+ * saves the append's launch, which a decode has to wait for.
+ *   key, value    [num_seqs, num_kv_heads, head_size], the cache's dtype
+ *                 (float16 / bfloat16), head_size dimension contiguous,
+ *                 rows 4-byte aligned (even strides, aligned base)
+ *   slot_mapping  int32/int64 [>= num_seqs]: sequence b's new token goes to
+ *                 slot slot_mapping[b], which must be the slot of its last
+ *                 position (context_lens[b] - 1) in block_tables[b]; a
+ *                 negative slot skips the token (padding), a slot past the
+ *                 cache is skipped and sets KVC_STATUS_SLOT_OOB
+ * The CTA that holds a sequence's last token stores it to the cache and uses
+ * the new values for that token in its own attention, without waiting for
+ * the stores.  Paged float16/bfloat16 caches on the tensor-core decode only (query
+ * of the cache's dtype, head size 64/128, block size 8/16/32, up to 16 query
+ * heads per KV head): anything else returns KVC_EUNSUPPORTED and runs nothing. */
+int kvc_paged_attention_planned_append(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltensor* max_logits,
+                                       kvc_dltensor* tmp_out, const kvc_dltensor* query, const kvc_dltensor* key,
+                                       const kvc_dltensor* value, kvc_dltensor* key_cache, kvc_dltensor* value_cache,
+                                       const kvc_dltensor* slot_mapping, const kvc_dltensor* block_tables,
+                                       const kvc_dltensor* context_lens, int num_kv_heads, float scale,
+                                       int block_size, int max_seq_len, const kvc_dltensor* alibi_slopes,
+                                       int partition_size, kvc_dltensor* plan, void* stream);
+
 /* Paged decode over token-major caches: the reshape_and_cache_flash layout
  * [num_blocks, block_size, num_kv_heads, head_size], or the MHATokenPool
  * buffers [slots, num_kv_heads, head_size] (pool_size + 1 slots, slot 0 the

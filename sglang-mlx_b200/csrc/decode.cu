@@ -67,6 +67,14 @@ struct DecodeParams {
   const uint32_t* plan_items;
   uint32_t* plan_counters;
   int fused_merge;
+  // The step's append, folded into the decode (kvc_paged_attention_planned_append):
+  // the CTA holding a sequence's last token writes that token's K row and V
+  // column to slot slots[seq] before its first cache copy.
+  const void* new_k;
+  const void* new_v;
+  const void* slots;
+  int slots_i64;
+  int64_t nk_tok_stride, nk_head_stride, nv_tok_stride, nv_head_stride;
 };
 
 // Programmatic dependent launch: the partition kernels let the split-K reduce be
@@ -694,6 +702,14 @@ static DecodeParams to_params(const DecodeArgs& a) {
   p.part_offset = 0;
   p.wait_prior_at_end = 0;
   p.wait_prior_at_start = 0;
+  p.new_k = a.new_k;
+  p.new_v = a.new_v;
+  p.slots = a.slots;
+  p.slots_i64 = a.slot_type == ElemType::I64 ? 1 : 0;
+  p.nk_tok_stride = a.nk_tok_stride;
+  p.nk_head_stride = a.nk_head_stride;
+  p.nv_tok_stride = a.nv_tok_stride;
+  p.nv_head_stride = a.nv_head_stride;
   p.k_scale = a.cache_type == ElemType::U8 ? a.k_scale : 1.f;
   p.v_scale = a.cache_type == ElemType::U8 ? a.v_scale : 1.f;
   p.table_stride = a.table_stride;
@@ -722,6 +738,14 @@ static bool pages_aligned(const DecodeArgs& a) {
 
 cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   if (a.num_seqs > 65535) return cudaErrorInvalidValue;
+  // the folded append runs in the tensor-core kernel's paged 16-bit forms, planned,
+  // and reads the token's rows as pairs of elements (4-byte aligned rows)
+  const bool pairs = a.new_k && (reinterpret_cast<uintptr_t>(a.new_k) & 3u) == 0 &&
+                     (reinterpret_cast<uintptr_t>(a.new_v) & 3u) == 0 && ((a.nk_tok_stride | a.nk_head_stride) & 1) == 0 &&
+                     ((a.nv_tok_stride | a.nv_head_stride) & 1) == 0;
+  if (a.new_k && (!pairs || !a.plan || a.flash || a.cache_type == ElemType::U8 || !mma_supported(a) ||
+                  plan_max_items(a.num_seqs, a.max_seq_len, a.partition_size) * a.num_kv_heads > 0x7FFFFFFF))
+    return cudaErrorNotSupported;
   DecodeParams p = to_params(a);
   if (a.plan && (!mma_supported(a) ||
                  plan_max_items(a.num_seqs, a.max_seq_len, a.partition_size) * a.num_kv_heads > 0x7FFFFFFF)) {

@@ -759,6 +759,33 @@ __device__ __forceinline__ void mma_group_fp8(GroupState<D>& gs, const uint32_t 
   }
 }
 
+// The step's new token of sequence `seq` and KV head `kvh` (the append folded
+// into the decode): its K row and V column written into the paged cache at slot
+// slots[seq] (K page [D/8][BS][8], V page [D][BS]); a negative slot is a padding
+// token (skipped), a slot past the cache sets SLOT_OOB and is skipped, as the
+// append kernel does.  One warp; lane l takes elements l, l + 32, ...
+template <typename T, int D, int BS>
+__device__ __forceinline__ void append_token(const DecodeParams& p, int seq, int kvh, int lane) {
+  const int64_t slot = p.slots_i64 ? reinterpret_cast<const int64_t*>(p.slots)[seq]
+                                   : (int64_t)reinterpret_cast<const int32_t*>(p.slots)[seq];
+  if (slot < 0) return;
+  const int64_t blk = slot / BS;
+  const int off = (int)(slot - blk * BS);
+  if (blk >= p.num_blocks) {
+    if (lane == 0) set_status(&g_decode_status, KVC_STATUS_SLOT_OOB);
+    return;
+  }
+  const T* k = reinterpret_cast<const T*>(p.new_k) + (int64_t)seq * p.nk_tok_stride + (int64_t)kvh * p.nk_head_stride;
+  const T* v = reinterpret_cast<const T*>(p.new_v) + (int64_t)seq * p.nv_tok_stride + (int64_t)kvh * p.nv_head_stride;
+  T* kc = const_cast<T*>(reinterpret_cast<const T*>(p.k_cache)) + blk * p.k_block_stride + (int64_t)kvh * p.k_head_stride;
+  T* vc = const_cast<T*>(reinterpret_cast<const T*>(p.v_cache)) + blk * p.v_block_stride + (int64_t)kvh * p.v_head_stride;
+#pragma unroll
+  for (int d = lane; d < D; d += 32) {
+    kc[((d >> 3) * BS + off) * 8 + (d & 7)] = k[d];
+    vc[d * BS + off] = v[d];
+  }
+}
+
 template <typename T, int D, int BS, int NW, int STAGES, int GTOK, int MODE>
 __global__ void __launch_bounds__(NW * 32)
     paged_decode_mma_kernel(DecodeParams p, const __grid_constant__ TmaMaps tm) {
@@ -780,10 +807,16 @@ __global__ void __launch_bounds__(NW * 32)
   const uint32_t ctx = p.context_lens[seq];
   int begin = 0, end = 0;
   bool zero_out = false;
+  // the folded append runs in the paged 16-bit forms (the host refuses the others)
+  constexpr bool APPEND = !Geo::FLASH && !Geo::FP8 && !Geo::TROWS;
   if (!partition_range(p, seq, part, ctx, &begin, &end, &zero_out)) {
     // planned: the item of a sequence with zero output (length 0 or past max_seq_len) writes it
-    // (after the kernel before us, which may write the same output buffer, has finished)
+    // (after the kernel before us, which may write the same output buffer, has finished);
+    // with the folded append it also writes the sequence's new token
     if (p.wait_prior_at_start) grid_dependency_wait();
+    if constexpr (APPEND) {
+      if (p.new_k && p.plan_items && warp == 0) append_token<T, D, BS>(p, seq, kvh, lane);
+    }
     if (zero_out || p.plan_items) write_zero_heads<T>(p, seq, h0, G, D);
     if (p.wait_prior_at_end) grid_dependency_wait();
     return;
@@ -1078,6 +1111,41 @@ __global__ void __launch_bounds__(NW * 32)
   // only from here on, after that kernel has finished.
   if (p.wait_prior_at_start) grid_dependency_wait();
 
+  // The folded append: in the CTA holding the sequence's last token
+  // (partitions are whole blocks, so no other CTA reads that page), the warp
+  // whose group holds it loads the token's K and V (pairs of dims, before its
+  // first copies), stores it to the cache once those copies are issued without
+  // waiting for the stores, and patches it into the shared copy of the page
+  // once that copy has landed (the copy may have read the slot before or after
+  // the store).  The patch applies when the caller's slot is the table's slot
+  // of the last position, as the append kernel followed by the decode reads it.
+  constexpr int AP = D / 64;  // dim pairs per lane
+  uint32_t ap_k[AP], ap_v[AP];
+  int append_pos = -1;
+  int64_t ap_slot = -1;
+  bool ap_mine = false;
+  if constexpr (APPEND) {
+    if (p.new_k && end == (int)ctx) {
+      const int pos = (int)ctx - 1;
+      ap_mine = ((pos - begin) / GT) % NW == warp;
+      if (ap_mine) {
+        ap_slot = p.slots_i64 ? reinterpret_cast<const int64_t*>(p.slots)[seq]
+                              : (int64_t)reinterpret_cast<const int32_t*>(p.slots)[seq];
+        const uint32_t* kn = reinterpret_cast<const uint32_t*>(
+            reinterpret_cast<const T*>(p.new_k) + (int64_t)seq * p.nk_tok_stride + (int64_t)kvh * p.nk_head_stride);
+        const uint32_t* vn = reinterpret_cast<const uint32_t*>(
+            reinterpret_cast<const T*>(p.new_v) + (int64_t)seq * p.nv_tok_stride + (int64_t)kvh * p.nv_head_stride);
+#pragma unroll
+        for (int j = 0; j < AP; ++j) {
+          ap_k[j] = __ldg(kn + 32 * j + lane);
+          ap_v[j] = __ldg(vn + 32 * j + lane);
+        }
+        const uint32_t tb = __ldg(table + pos / BS);
+        if (ap_slot >= 0 && (int64_t)tb < p.num_blocks && ap_slot == (int64_t)tb * BS + pos % BS) append_pos = pos;
+      }
+    }
+  }
+
   // ---- prologue: fill the ring
   uint32_t ids_next[IDV];  // token-major caches: the chunk after the current one
   if constexpr (Geo::TOKIDS) {
@@ -1089,6 +1157,28 @@ __global__ void __launch_bounds__(NW * 32)
 #pragma unroll
   for (int s = 0; s < STAGES; ++s) {
     if (s < n_mine) issue(s, s, load_block(s));
+  }
+  if constexpr (APPEND) {
+    // the folded append's stores (dims 64j + 2 lane, + 1 of K and V), not waited for
+    if (ap_mine && ap_slot >= 0) {
+      const int64_t blk = ap_slot / BS;
+      const int off = (int)(ap_slot - blk * BS);
+      if (blk >= p.num_blocks) {
+        if (lane == 0) set_status(&g_decode_status, KVC_STATUS_SLOT_OOB);
+      } else {
+        T* kc = const_cast<T*>(reinterpret_cast<const T*>(p.k_cache)) + blk * p.k_block_stride +
+                (int64_t)kvh * p.k_head_stride;
+        T* vc = const_cast<T*>(reinterpret_cast<const T*>(p.v_cache)) + blk * p.v_block_stride +
+                (int64_t)kvh * p.v_head_stride;
+#pragma unroll
+        for (int j = 0; j < AP; ++j) {
+          const int d = 64 * j + 2 * lane;
+          *reinterpret_cast<uint32_t*>(kc + ((d >> 3) * BS + off) * 8 + (d & 7)) = ap_k[j];
+          reinterpret_cast<uint16_t*>(vc)[d * BS + off] = (uint16_t)(ap_v[j] & 0xFFFFu);
+          reinterpret_cast<uint16_t*>(vc)[(d + 1) * BS + off] = (uint16_t)(ap_v[j] >> 16);
+        }
+      }
+    }
   }
 
   GroupState<D> gs;
@@ -1115,6 +1205,28 @@ __global__ void __launch_bounds__(NW * 32)
     const uint32_t vst = smem_u32(st + NBOX * BOX);
     const int tok0 = begin + (warp + k * NW) * GT;  // first token of the group
     const uint32_t pmask = masks[s];
+    if constexpr (APPEND) {
+      if (append_pos >= tok0 && append_pos < tok0 + GT) {  // this group holds the appended token
+        const int t = append_pos - tok0, bx = t / VBS, off = t % VBS;
+        if ((pmask >> (t / Geo::MBS)) & 1u) {
+          constexpr uint32_t VSW = Geo::VSWZ ? (uint32_t)(Geo::VSWZ / 16 - 1) : 0u;
+          uint8_t* kb = const_cast<uint8_t*>(st) + bx * BOX;
+          uint8_t* vb = const_cast<uint8_t*>(st) + (NBOX + bx) * BOX;
+#pragma unroll
+          for (int j = 0; j < AP; ++j) {
+            const int d = 64 * j + 2 * lane;
+            *reinterpret_cast<uint32_t*>(kb + ((d >> 3) * VBS + off) * 16 + (d & 7) * 2) = ap_k[j];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              uint32_t vo = (uint32_t)((d + e) * VBS + off) * 2;  // (the V box's swizzle, as mma_group reads it)
+              if (VSW) vo ^= ((vo >> 7) & VSW) << 4;
+              *reinterpret_cast<uint16_t*>(vb + vo) = (uint16_t)(e ? ap_v[j] >> 16 : ap_v[j] & 0xFFFFu);
+            }
+          }
+          __syncwarp();
+        }
+      }
+    }
     if constexpr (Geo::FP8) {
       mma_group_fp8<Geo, D, MODE>(gs, qa, kst, vst, tok0, end, pmask, (int)ctx, qk_scale, p.alibi != nullptr,
                                   slope_lo, slope_hi, lane);

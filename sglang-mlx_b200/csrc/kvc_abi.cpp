@@ -1000,6 +1000,52 @@ int kvc_reshape_and_cache_flash(const kvc_dltensor* key, const kvc_dltensor* val
   return KVC_OK;
 }
 
+int kvc_paged_attention_planned_append(kvc_dltensor* out, kvc_dltensor* exp_sums, kvc_dltensor* max_logits,
+                                       kvc_dltensor* tmp_out, const kvc_dltensor* query, const kvc_dltensor* key,
+                                       const kvc_dltensor* value, kvc_dltensor* key_cache, kvc_dltensor* value_cache,
+                                       const kvc_dltensor* slot_mapping, const kvc_dltensor* block_tables,
+                                       const kvc_dltensor* context_lens, int num_kv_heads, float scale,
+                                       int block_size, int max_seq_len, const kvc_dltensor* alibi_slopes,
+                                       int partition_size, kvc_dltensor* plan, void* stream) {
+  DecodeArgs a;
+  int device = -1;
+  if (int rc = prepare_decode(out, query, key_cache, value_cache, block_tables, context_lens, num_kv_heads, scale,
+                              block_size, max_seq_len, alibi_slopes, &a, &device))
+    return rc;
+  if (int rc = attach_splitk_workspace(exp_sums, max_logits, tmp_out, partition_size, block_size, max_seq_len,
+                                       device, &a))
+    return rc;
+  if (int rc = check_plan_args(a.num_seqs, num_kv_heads, max_seq_len, partition_size)) return rc;
+  if (int rc = parse_plan(plan, a.num_seqs, num_kv_heads, max_seq_len, partition_size, &device, &a.plan)) return rc;
+  ReshapeArgs r;
+  int rdev = device;
+  if (int rc = prepare_reshape(key, value, key_cache, value_cache, slot_mapping, false, &r, &rdev)) return rc;
+  if (rdev != device) return fail(KVC_EINVAL, "all tensors must live on the same CUDA device");
+  if (r.num_tokens != a.num_seqs)
+    return fail(KVC_EINVAL, "key/value must hold one new token per sequence: [num_seqs, num_kv_heads, head_size]");
+  if (r.kv_type != a.cache_type || a.cache_type == ElemType::U8)
+    return fail(KVC_EUNSUPPORTED, "paged_attention_planned_append needs key/value of the cache's dtype "
+                                  "(float16/bfloat16)");
+  a.new_k = r.key;
+  a.new_v = r.value;
+  a.slots = r.slots;
+  a.slot_type = r.slot_type;
+  a.nk_tok_stride = r.key_tok_stride;
+  a.nk_head_stride = r.key_head_stride;
+  a.nv_tok_stride = r.value_tok_stride;
+  a.nv_head_stride = r.value_head_stride;
+  if (a.num_seqs == 0) return KVC_OK;
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(KVC_ECUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_paged_decode(a, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorNotSupported)
+    return fail(KVC_EUNSUPPORTED, "paged_attention_planned_append runs on the tensor-core decode only (float16/bfloat16 "
+                                  "query and cache of one dtype, head size 64/128, block size 8/16/32, up to 16 query "
+                                  "heads per KV head)");
+  if (e != cudaSuccess) return cuda_fail(e, "paged_attention_planned_append launch");
+  return KVC_OK;
+}
+
 int kvc_gather_kv(kvc_dltensor* k_out, kvc_dltensor* v_out, const kvc_dltensor* k_buffer,
                   const kvc_dltensor* v_buffer, const kvc_dltensor* indices, void* stream) {
   View ko, vo, kb, vb, ix;

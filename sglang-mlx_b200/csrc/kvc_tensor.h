@@ -103,6 +103,14 @@ struct DecodeArgs {
   // Planned split-K (kvc_paged_attention_planned): the work list of
   // kvc_decode_plan (header, items, arrival counters), or nullptr.
   uint32_t* plan;
+  // kvc_paged_attention_planned_append: one new token per sequence (key/value
+  // [num_seqs, H, D] of the cache's dtype) written to slot_mapping[seq] by the
+  // CTA holding the sequence's last token; new_k == nullptr: no append.
+  const void* new_k;
+  const void* new_v;
+  const void* slots;
+  ElemType slot_type;
+  int64_t nk_tok_stride, nk_head_stride, nv_tok_stride, nv_head_stride;  // elements
 };
 
 // Planned split-K decode: layout of the plan buffer (uint32 elements).

@@ -56,6 +56,10 @@ SIGNATURES: dict[str, tuple] = {
         _i,
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _i, _p, _p],
     ),
+    "kvc_paged_attention_planned_append": (
+        _i,
+        [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _i, _p, _p],
+    ),
     "kvc_paged_attention_cascade": (
         _i,
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _f, _i, _i, _p, _i, _i, _i, _p],

@@ -453,6 +453,44 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens, n
                               workspace=workspace, stream=stream, out=out, plan=plan)
 
 
+def paged_attention_append(query, key, value, key_cache, value_cache, slot_mapping, block_tables, context_lens,
+                           num_kv_heads: int, scale: float, block_size: int, max_seq_len: int, alibi_slopes=None, *,
+                           stream=None, out=None, workspace=None, plan=None):
+    """A decode step's append and planned decode in one launch: the same cache
+    and output as reshape_and_cache(key, value, key_cache, value_cache,
+    slot_mapping) followed by paged_attention(...), for one new token per
+    sequence (key/value [num_seqs, num_kv_heads, head_size] of the cache's
+    dtype) whose slot slot_mapping[b] is the last position (context_lens[b] -
+    1) of sequence b.  The CTA that holds each sequence's last token writes it,
+    so the decode does not wait for a separate append launch.  Paged
+    float16/bfloat16 caches on the tensor-core decode only (NotImplementedError
+    otherwise).  Pass a plan made once per step to skip the plan kernel here."""
+    query, key, value = _dev(query), _dev(key), _dev(value)
+    block_tables, context_lens, alibi_slopes = _dev(block_tables), _dev(context_lens), _dev(alibi_slopes)
+    slot_mapping = _dev(slot_mapping)
+    shape, _, _, _, dev = describe(query)
+    if plan is None:
+        psize = choose_planned_partition(shape[0], num_kv_heads, max_seq_len, block_size)
+        plan = make_decode_plan(context_lens, num_kv_heads, max_seq_len, psize, stream=stream)
+    psize = int(plan.partition_size)
+    if out is None:
+        out = _out_like_query(query)
+    if workspace is None:
+        workspace = splitk_workspace(shape[0], shape[1], shape[2], max_seq_len, psize, dev)
+    es, ml, to = workspace
+    ptrs = [as_dltensor(a, n) for a, n in ((out, "out"), (es, "exp_sums"), (ml, "max_logits"), (to, "tmp_out"),
+                                           (query, "query"), (key, "key"), (value, "value"),
+                                           (key_cache, "key_cache"), (value_cache, "value_cache"),
+                                           (slot_mapping, "slot_mapping"), (block_tables, "block_tables"),
+                                           (context_lens, "context_lens"), (alibi_slopes, "alibi_slopes"))]
+    pl = as_dltensor(plan.array, "plan")
+    _lib.check(_L.kvc_paged_attention_planned_append(
+        ptrs[0][0], ptrs[1][0], ptrs[2][0], ptrs[3][0], ptrs[4][0], ptrs[5][0], ptrs[6][0], ptrs[7][0], ptrs[8][0],
+        ptrs[9][0], ptrs[10][0], ptrs[11][0], int(num_kv_heads), float(scale), int(block_size), int(max_seq_len),
+        ptrs[12][0], psize, pl[0], _stream(stream)))
+    return out
+
+
 def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, *, stream=None):
     """Scatter-write new KV tokens into the paged cache (metal_kernels.py:64-74).
 

@@ -232,3 +232,168 @@ def test_config2_eight_way_share(gpu):
                                    int(t2.shape[1] * 16))
     assert_close(out[rows], ref, ATOL_NS, RTOL_NS, "planned vs oracle")
     assert gpu.get_status(clear=True) == 0
+
+
+# ---- the step's append folded into the decode (kvc_paged_attention_planned_append) ----
+
+def _step_case(seed, dtype, lens, hq, hkv, D, bs):
+    """A paged case whose caches hold every token but each sequence's last one,
+    plus that last token (key/value [B, hkv, D], its slot) as the step's append."""
+    c = cases.paged_batch(seed, dtype, len(lens), hq, hkv, D, bs, lens)
+    ends = np.cumsum(c["context_lens"].astype(np.int64))
+    last = [int(e) - 1 if n > 0 else -1 for e, n in zip(ends, c["context_lens"])]
+    keep = np.ones(len(c["slot_mapping"]), bool)
+    keep[[i for i in last if i >= 0]] = False
+    B, dk = len(lens), c["k"].shape[1:]
+    key = np.zeros((B,) + dk, c["k"].dtype)
+    val = np.zeros((B,) + dk, c["v"].dtype)
+    slot = np.full(B, -1, np.int64)
+    for b, i in enumerate(last):
+        if i >= 0:
+            key[b], val[b], slot[b] = c["k"][i], c["v"][i], c["slot_mapping"][i]
+    return c, keep, key, val, slot
+
+
+def _caches(c, keep):
+    """Fresh device caches holding the tokens of `keep` (every token but the step's)."""
+    dt = c["dtype"]
+    kc = DeviceArray.from_numpy(c["k_cache"], dtype=dt)
+    vc = DeviceArray.from_numpy(c["v_cache"], dtype=dt)
+    mk.reshape_and_cache(DeviceArray.from_numpy(c["k"][keep], dtype=dt), DeviceArray.from_numpy(c["v"][keep], dtype=dt),
+                         kc, vc, DeviceArray.from_numpy(c["slot_mapping"][keep]))
+    return kc, vc
+
+
+def _both(c, keep, key, val, slot, msl, P, slot_dtype=np.int64):
+    """(out, k_cache, v_cache) of append + planned decode, and of the folded call."""
+    dt = c["dtype"]
+    q = DeviceArray.from_numpy(c["q"], dtype=dt)
+    bt, cl = DeviceArray.from_numpy(c["block_tables"]), DeviceArray.from_numpy(c["context_lens"])
+    kd, vd, sd = (DeviceArray.from_numpy(key, dtype=dt), DeviceArray.from_numpy(val, dtype=dt),
+                  DeviceArray.from_numpy(slot.astype(slot_dtype)))
+    plan = mk.make_decode_plan(cl, c["num_kv_heads"], msl, P)
+    kc, vc = _caches(c, keep)
+    mk.reshape_and_cache(kd, vd, kc, vc, sd)
+    two = mk.paged_attention_v2(q, kc, vc, bt, cl, c["num_kv_heads"], c["scale"], c["block_size"], msl,
+                                partition_size=P, plan=plan).to_numpy()
+    sep = (two, kc.to_numpy(), vc.to_numpy())
+    kc2, vc2 = _caches(c, keep)
+    one = mk.paged_attention_append(q, kd, vd, kc2, vc2, sd, bt, cl, c["num_kv_heads"], c["scale"], c["block_size"],
+                                    msl, plan=plan).to_numpy()
+    return sep, (one, kc2.to_numpy(), vc2.to_numpy())
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("bs", [8, 16, 32])
+def test_folded_append_equals_append_then_decode(gpu, dtype, D, bs):
+    """The folded call leaves the caches bit-identical to the append kernel's
+    and gives the same output as the planned decode after it; both agree with
+    the oracle.  Lengths put the new token first in a block, last in a block,
+    and in sequences of one to many partitions."""
+    lens = [1, bs, bs + 1, 300, 1025, 2048, 2049, 5000]
+    c, keep, key, val, slot = _step_case(7600 + D + bs, dtype, lens, 8, 2, D, bs)
+    (two, k2, v2), (one, k1, v1) = _both(c, keep, key, val, slot, c["max_seq_len"], 512)
+    np.testing.assert_array_equal(k1, k2)
+    np.testing.assert_array_equal(v1, v2)
+    np.testing.assert_array_equal(one, two)
+    kc, vc = oracle_fill(c, dtype)
+    ref = kv_oracle.paged_attention_v1(c["q"], kc, vc, c["block_tables"], c["context_lens"], 2, c["scale"], bs,
+                                       c["max_seq_len"])
+    assert_close(one, ref, ATOL_NS, RTOL_NS, f"folded append {dtype} D{D} bs{bs}")
+    assert gpu.get_status(clear=True) == 0
+
+
+def test_folded_append_edge_rules(gpu):
+    """Padding slots (-1) skip their token, sequences of length 0 or past
+    max_seq_len still get their token written (as the append kernel does) and
+    produce zeros, an int32 slot mapping, one partition per sequence and the
+    separate-reduce form (over 32 partitions) all match append + decode; a slot
+    past the cache is skipped and flagged."""
+    lens = [0, 5, 64, 5000, 700, 1, 33, 4096]
+    c, keep, key, val, slot = _step_case(7700, "bfloat16", lens, 32, 8, 128, 16, )
+    slot[2] = -1  # a padding token
+    # sequence 0 (length 0) still appends a token, to the first slot of a block no table uses
+    spare = sorted(set(range(c["k_cache"].shape[0])) - set(c["block_tables"].ravel().tolist()))[0]
+    key[0], val[0], slot[0] = c["k"][0], c["v"][0], spare * 16
+    for msl, P, sdt in ((4096, 512, np.int64), (c["max_seq_len"], 4096, np.int32), (c["max_seq_len"], 32, np.int64)):
+        (two, k2, v2), (one, k1, v1) = _both(c, keep, key, val, slot, msl, P, sdt)
+        np.testing.assert_array_equal(k1, k2)
+        np.testing.assert_array_equal(v1, v2)
+        np.testing.assert_array_equal(one, two)
+        assert not one[0].any()
+        if msl == 4096:
+            assert not one[3].any()
+    assert gpu.get_status(clear=True) == 0
+    slot[4] = 10 ** 9  # past the cache: the folded call alone flags it
+    dt = c["dtype"]
+    kc, vc = _caches(c, keep)
+    mk.paged_attention_append(DeviceArray.from_numpy(c["q"], dtype=dt), DeviceArray.from_numpy(key, dtype=dt),
+                              DeviceArray.from_numpy(val, dtype=dt), kc, vc, DeviceArray.from_numpy(slot),
+                              DeviceArray.from_numpy(c["block_tables"]), DeviceArray.from_numpy(c["context_lens"]), 8,
+                              c["scale"], 16, c["max_seq_len"])
+    assert gpu.get_status(clear=True) & _lib.STATUS_SLOT_OOB
+
+
+def test_folded_append_replays_as_graph(gpu):
+    """Captured once and replayed: every replay rewrites the same token and
+    gives the eager result."""
+    lens = [100, 2000, 3000, 17]
+    c, keep, key, val, slot = _step_case(7800, "bfloat16", lens, 16, 4, 128, 16)
+    dt = c["dtype"]
+    q = DeviceArray.from_numpy(c["q"], dtype=dt)
+    bt, cl = DeviceArray.from_numpy(c["block_tables"]), DeviceArray.from_numpy(c["context_lens"])
+    kd, vd, sd = DeviceArray.from_numpy(key, dtype=dt), DeviceArray.from_numpy(val, dtype=dt), DeviceArray.from_numpy(slot)
+    kc, vc = _caches(c, keep)
+    st = Stream()
+    plan = mk.make_decode_plan(cl, 4, c["max_seq_len"], 512, stream=st)
+    ws = mk.splitk_workspace(len(lens), 16, 128, c["max_seq_len"], 512, 0)
+    o = DeviceArray.empty(q.shape, dt)
+
+    def work():
+        mk.paged_attention_append(q, kd, vd, kc, vc, sd, bt, cl, 4, c["scale"], 16, c["max_seq_len"], plan=plan,
+                                  workspace=ws, out=o, stream=st)
+
+    work()
+    st.synchronize()
+    eager, keager = o.to_numpy(), kc.to_numpy()
+    g = Graph.capture(st, work)
+    for _ in range(2):
+        o.fill_zero(stream=st)
+        g.replay(st)
+        st.synchronize()
+        np.testing.assert_array_equal(o.to_numpy(), eager)
+        np.testing.assert_array_equal(kc.to_numpy(), keager)
+
+
+def test_folded_append_refuses_other_caches(gpu):
+    """FP8 and float32 caches, a key of another dtype, a key without one row
+    per sequence and rows off a 4-byte boundary are refused before anything runs."""
+    lens = [40, 50]
+    c, keep, key, val, slot = _step_case(7900, "float16", lens, 8, 2, 128, 16)
+    q = DeviceArray.from_numpy(c["q"], dtype="float16")
+    bt, cl = DeviceArray.from_numpy(c["block_tables"]), DeviceArray.from_numpy(c["context_lens"])
+    kc, vc = _caches(c, keep)
+    sd = DeviceArray.from_numpy(slot)
+    with pytest.raises(NotImplementedError, match="dtype"):
+        mk.paged_attention_append(q, DeviceArray.from_numpy(key, dtype="float32"),
+                                  DeviceArray.from_numpy(val, dtype="float32"), kc, vc, sd, bt, cl, 2, c["scale"], 16,
+                                  c["max_seq_len"])
+    with pytest.raises(ValueError, match="one new token per sequence"):
+        mk.paged_attention_append(q, DeviceArray.from_numpy(key[:1], dtype="float16"),
+                                  DeviceArray.from_numpy(val[:1], dtype="float16"), kc, vc, sd, bt, cl, 2, c["scale"],
+                                  16, c["max_seq_len"])
+    wide = np.zeros(key.shape[:-1] + (key.shape[-1] + 1,), np.float32)
+    wide[..., 1:] = key
+    kw = DeviceArray.from_numpy(wide, dtype="float16")[:, :, 1:]  # odd offset and strides
+    with pytest.raises(NotImplementedError):
+        mk.paged_attention_append(q, kw, DeviceArray.from_numpy(val, dtype="float16"), kc, vc, sd, bt, cl, 2,
+                                  c["scale"], 16, c["max_seq_len"])
+    c32 = cases.paged_batch(7901, "float32", 2, 8, 2, 128, 16, lens)
+    q32 = DeviceArray.from_numpy(c32["q"], dtype="float32")
+    k32 = DeviceArray.from_numpy(c32["k_cache"], dtype="float32")
+    v32 = DeviceArray.from_numpy(c32["v_cache"], dtype="float32")
+    with pytest.raises(NotImplementedError):
+        mk.paged_attention_append(q32, DeviceArray.from_numpy(key, dtype="float32"),
+                                  DeviceArray.from_numpy(val, dtype="float32"), k32, v32, sd, bt, cl, 2, c["scale"],
+                                  16, c["max_seq_len"])
