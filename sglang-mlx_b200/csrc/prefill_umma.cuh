@@ -12,8 +12,9 @@
 //    persistent (one CTA per SM): CTA c takes item c, then claims further
 //    items from a device counter until none is left.
 //  * TMEM (512 columns): two S buffers of 128 fp32 columns (S = Q K^T of a
-//    128-token tile), O (D fp32 columns) and Q (D/2 columns of bf16/f16
-//    pairs).  P overwrites its own S buffer: hi parts in the first 64
+//    128-token tile), O (D fp32 columns) and two Q buffers (D/2 columns of
+//    bf16/f16 pairs each: the next item's Q is staged while the current item
+//    finishes).  P overwrites its own S buffer: hi parts in the first 64
 //    columns, lo parts (bf16 only) in the next 64.
 //  * Warp 8 (producer) claims the items, hands each to the other warps, and
 //    streams its 128-token tiles into a ring of KST stages: K either as 4-row
@@ -142,8 +143,10 @@ struct UmmaGeom {
   static constexpr int MASK_OFF = BAR_OFF + NBARS * 8;
   static constexpr int XBUF_OFF = (MASK_OFF + KST * 4 + 15) / 16 * 16;
   static constexpr int SMEM = XBUF_OFF + 2 * 2 * 128 * 4;
-  static constexpr uint32_t SCOL = 0, OCOL = 256, QCOL = 256 + D;  // TMEM columns
-  static_assert(QCOL + D / 2 <= 512, "TMEM columns");
+  // TMEM columns: S/P of two tiles, O, and Q of two items (the next item's Q is
+  // staged while the current one finishes)
+  static constexpr uint32_t SCOL = 0, OCOL = 256, QCOL = 256 + D;
+  static_assert(QCOL + D <= 512, "TMEM columns");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
@@ -544,6 +547,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           break;
         }
         umma::fence_after();
+        const uint32_t qcol = tmem + UG::QCOL + (uint32_t)(nit & 1) * (D / 2);  // this item's Q buffer
         ++nit;
         const int kv_beg = it.kv_beg, kv_end = it.kv_end, ntiles = it.ntiles;
         bool o_init = false;
@@ -583,7 +587,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
             // S = Q K^T as one N = 128 product per 16-dim k-step
 #pragma unroll
             for (int ks = 0; ks < D / 16; ++ks)
-              umma::mma_ts(tmem + UG::SCOL + b * 128, tmem + UG::QCOL + 8 * ks,
+              umma::mma_ts(tmem + UG::SCOL + b * 128, qcol + 8 * ks,
                            kd + (uint64_t)((ks * 2 * KT * 16) >> 4), idS, ks > 0 ? 1u : 0u);
             (void)live;
           } else {
@@ -594,7 +598,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
 #pragma unroll
               for (int pg = 0; pg < PAGES; ++pg) {
                 if (pg < live)
-                  umma::mma_ts(tmem + UG::SCOL + b * 128 + pg * BS, tmem + UG::QCOL + 8 * ks,
+                  umma::mma_ts(tmem + UG::SCOL + b * 128 + pg * BS, qcol + 8 * ks,
                                kd + (uint64_t)((pg * PAGE + ks * 2 * BS * 16) >> 4), idS, ks > 0 ? 1u : 0u);
               }
             }
@@ -650,69 +654,95 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       }
       return buf[(half ^ 1) * 128 + r];
     };
-    int gt = 0, nread = 0;  // tiles and ring slots read of this CTA so far
-    while (ok) {
-      const int sl = nread & 1;
-      if (uabort() || !uwait(&item_full[sl], (uint32_t)((nread >> 1) & 1))) {
-        ok = false;
-        break;
-      }
-      const int idx = *(volatile int*)&s_item[sl];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&item_empty[sl]);
-      ++nread;
-      if (idx >= n_items) break;
-      const UmmaItem it = umma_item<CASCADE>(p, idx, tiles_x, ny);
-      if (it.skip) continue;
-      const int kvh = it.kvh, kv_beg = it.kv_beg, kv_end = it.kv_end, ntiles = it.ntiles;
-      const int64_t R = it.R0 + r;
-      const bool in_tile = R < it.rows;  // a row (else padding of the last tile)
-      // t: the new token (prefill) or the sequence (cascade) of the row
-      const int t = in_tile ? (int)(R / G) : 0, g = in_tile ? (int)(R - (int64_t)t * G) : 0;
-      bool on;  // a row that sees keys
-      int end_r, beg_r;
-      if constexpr (CASCADE) {
-        // the row's sequence sees the chunk up to its own length; lengths the
-        // reference zeroes (0 or past max_seq_len) see nothing
-        const uint32_t ctx = in_tile ? __ldg(p.context_lens + t) : 0u;
-        on = in_tile && ctx != 0 && ctx <= (uint32_t)p.max_seq_len;
-        end_r = on ? ((int)ctx < kv_end ? (int)ctx : kv_end) : 0;
-        beg_r = 0;
-      } else {
-        on = in_tile && !it.bad;
-        end_r = on ? it.prefix + t + 1 : 0;
-        beg_r = p.window > 0 ? end_r - p.window : 0;
-      }
-      // Q row -> TMEM columns QCOL .. QCOL + D/2 - 1 (element pairs), QC per
-      // half.  (Every product of the previous item is complete: its last P.V
-      // was waited for before its epilogue.)
-      {
-        const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
-            reinterpret_cast<const T*>(p.q) + (it.q0 + t) * p.q_tok_stride +
-            (int64_t)(kvh * G + g) * p.q_head_stride) + half * QC;
-        uint32_t qv[32];
-        if (on && (reinterpret_cast<uintptr_t>(qrow) & 15u) == 0) {  // 16-byte loads where the row allows
-#pragma unroll
-          for (int i = 0; i < QC; i += 4) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4*>(qrow + i));
-            qv[i] = v.x;
-            qv[i + 1] = v.y;
-            qv[i + 2] = v.z;
-            qv[i + 3] = v.w;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < QC; ++i) qv[i] = on ? __ldg(qrow + i) : 0u;
+    int gt = 0, nread = 0, nq = 0;  // tiles, ring slots read and items with keys of this CTA so far
+    // An item as this thread's row sees it.
+    struct RowItem {
+      int64_t q0;
+      int y, kvh, kv_beg, kv_end, ntiles;
+      int t, g, end_r, beg_r;  // t: the new token (prefill) or the sequence (cascade) of the row
+      bool in_tile;            // a row (else padding of the last tile)
+    };
+    // The next item with work: read from the producer's slots, and its Q rows
+    // staged into TMEM buffer nq & 1 (columns QCOL + (nq & 1) D/2 .., element
+    // pairs, QC per half) and handed over.  It is fetched while the previous
+    // item's last P.V runs: that item used the other buffer, and every product
+    // of the item before it (this buffer's last user) completed before its
+    // epilogue.  False at the end marker or on a failed wait.
+    auto next_item = [&](RowItem& ri) -> bool {
+      for (;;) {
+        const int sl = nread & 1;
+        if (uabort() || !uwait(&item_full[sl], (uint32_t)((nread >> 1) & 1))) {
+          ok = false;
+          return false;
         }
-        if constexpr (QC == 32) umma::st32(lane_base + UG::QCOL + half * QC, qv);
-        else umma::st16(lane_base + UG::QCOL + half * QC, qv);
+        const int idx = *(volatile int*)&s_item[sl];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&item_empty[sl]);
+        ++nread;
+        if (idx >= n_items) return false;
+        const UmmaItem it = umma_item<CASCADE>(p, idx, tiles_x, ny);
+        if (it.skip) continue;
+        ri.q0 = it.q0;
+        ri.y = it.y;
+        ri.kvh = it.kvh;
+        ri.kv_beg = it.kv_beg;
+        ri.kv_end = it.kv_end;
+        ri.ntiles = it.ntiles;
+        bool on;  // a row that sees keys
+        const int64_t R = it.R0 + r;
+        ri.in_tile = R < it.rows;
+        ri.t = ri.in_tile ? (int)(R / G) : 0;
+        ri.g = ri.in_tile ? (int)(R - (int64_t)ri.t * G) : 0;
+        if constexpr (CASCADE) {
+          // the row's sequence sees the chunk up to its own length; lengths the
+          // reference zeroes (0 or past max_seq_len) see nothing
+          const uint32_t ctx = ri.in_tile ? __ldg(p.context_lens + ri.t) : 0u;
+          on = ri.in_tile && ctx != 0 && ctx <= (uint32_t)p.max_seq_len;
+          ri.end_r = on ? ((int)ctx < it.kv_end ? (int)ctx : it.kv_end) : 0;
+          ri.beg_r = 0;
+        } else {
+          on = ri.in_tile && !it.bad;
+          ri.end_r = on ? it.prefix + ri.t + 1 : 0;
+          ri.beg_r = p.window > 0 ? ri.end_r - p.window : 0;
+        }
+        // (an item without keys hands over no Q: the MMA warp could otherwise see
+        // two phases of q_ready complete before it waits for the first)
+        if (it.ntiles > 0) {
+          const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+              reinterpret_cast<const T*>(p.q) + (it.q0 + ri.t) * p.q_tok_stride +
+              (int64_t)(it.kvh * G + ri.g) * p.q_head_stride) + half * QC;
+          uint32_t qv[32];
+          if (on && (reinterpret_cast<uintptr_t>(qrow) & 15u) == 0) {  // 16-byte loads where the row allows
+#pragma unroll
+            for (int i = 0; i < QC; i += 4) {
+              const uint4 v = __ldg(reinterpret_cast<const uint4*>(qrow + i));
+              qv[i] = v.x;
+              qv[i + 1] = v.y;
+              qv[i + 2] = v.z;
+              qv[i + 3] = v.w;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < QC; ++i) qv[i] = on ? __ldg(qrow + i) : 0u;
+          }
+          const uint32_t qcol = lane_base + UG::QCOL + (uint32_t)(nq & 1) * (D / 2) + half * QC;
+          if constexpr (QC == 32) umma::st32(qcol, qv);
+          else umma::st16(qcol, qv);
+          umma::wait_st();
+          umma::fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(q_ready);
+          ++nq;
+        }
+        return true;
       }
-      umma::wait_st();
-      umma::fence_before();
-      __syncwarp();
-      // (an item without keys hands over no Q: the MMA warp could otherwise see
-      // two phases of q_ready complete before it waits for the first)
-      if (lane == 0 && ntiles > 0) mbar_arrive(q_ready);
+    };
+    RowItem cur;
+    bool have_cur = next_item(cur);
+    while (ok && have_cur) {
+      const int kvh = cur.kvh, kv_beg = cur.kv_beg, kv_end = cur.kv_end, ntiles = cur.ntiles;
+      const int t = cur.t, g = cur.g, end_r = cur.end_r, beg_r = cur.beg_r;
+      const bool in_tile = cur.in_tile;
 
       float m_ref = -INFINITY, l = 0.f;
       for (int j = 0; j < ntiles; ++j) {
@@ -867,6 +897,9 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[b]);
       }
+      // the next item's Q goes in while this item's last P.V runs
+      RowItem nxt;
+      const bool have_nxt = ok && next_item(nxt);
       bool have = ok && ntiles > 0;
       if (have) {
         have = uwait(pv_done, (uint32_t)((gt + ntiles - 1) & 1));
@@ -882,7 +915,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         const bool keep = have && l_all > 0.f;
         const int head = kvh * G + g;
         float* po = p.part_out + (int64_t)t * p.part_out_seq_stride + (int64_t)head * p.part_out_head_stride +
-                    (int64_t)it.y * p.part_out_part_stride + half * HD;
+                    (int64_t)cur.y * p.part_out_part_stride + half * HD;
 #pragma unroll
         for (int c = 0; c < HD; c += 32) {
           uint32_t v[32];
@@ -899,7 +932,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           }
         }
         if (in_tile && half == 0) {
-          const int64_t o = (int64_t)t * p.part_seq_stride + (int64_t)head * p.part_head_stride + it.y;
+          const int64_t o = (int64_t)t * p.part_seq_stride + (int64_t)head * p.part_head_stride + cur.y;
           p.part_max[o] = keep ? m_ref * kLn2 : -INFINITY;
           p.part_sum[o] = keep ? l_all : 0.f;
         }
@@ -907,7 +940,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         // ---- epilogue: O / l (a row with no visible key, or after an abort, is 0)
         const bool nonzero = have && l_all > 0.f;  // else explicit zeros (O may hold another item's values)
         const float inv = nonzero ? 1.f / l_all : 0.f;
-        T* orow = reinterpret_cast<T*>(p.out) + (it.q0 + t) * p.out_tok_stride +
+        T* orow = reinterpret_cast<T*>(p.out) + (cur.q0 + t) * p.out_tok_stride +
                   (int64_t)(kvh * G + g) * p.out_head_stride + half * HD;
 #pragma unroll
         for (int c = 0; c < HD; c += 32) {
@@ -927,9 +960,11 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           }
         }
       }
-      // (the next item's Q store and its first P.V come after these O loads)
+      // (the next item's first P.V comes after these O loads)
       umma::fence_before();
       gt += ntiles;
+      cur = nxt;
+      have_cur = have_nxt;
     }
     if (!ok && lane == 0) give_up();
   }
