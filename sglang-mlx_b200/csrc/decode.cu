@@ -405,14 +405,18 @@ __global__ void __launch_bounds__(kGenericWarps * 32) paged_decode_generic_kerne
 // Split-K reduce: out = sum_p e^{m_p - M} o_p / (sum_p e^{m_p - M} l_p + 1e-6)
 // over the partitions that hold tokens of the sequence, for many partitions
 // (long contexts).  CTA = (head, seq, 32-dim slice): lane = dim, warp w
-// accumulates partitions w, w + 8, ... (four rows in flight), then the 8
-// partial rows are summed through shared memory.  Every CTA recomputes M and
-// the weights from the (max, sum) pairs, which are small and L2-resident.
+// accumulates partitions w, w + 8, ..., then the 8 partial rows are summed
+// through shared memory.  Every CTA recomputes M and the weights from the
+// (max, sum) pairs, which are small and L2-resident.  The reduce is a chain of
+// dependent memory latencies after the partition kernel ends, so it issues
+// its loads before using any: the warp's first kReducePre partial rows and the
+// thread's (max, sum) pair go out together, the rest kReduceDepth at a time.
 // Launched as a programmatic dependent of the partition kernel: it may start
 // during that kernel's tail and waits (griddepcontrol.wait) before reading.
 // ---------------------------------------------------------------------------
 constexpr int kReduceWarps = 8;
 constexpr int kReduceSlice = 32;
+constexpr int kReducePre = 16, kReduceDepth = 8;
 
 template <typename T>
 __global__ void __launch_bounds__(kReduceWarps * 32) splitk_reduce_kernel(DecodeParams p, int head_size) {
@@ -436,11 +440,23 @@ __global__ void __launch_bounds__(kReduceWarps * 32) splitk_reduce_kernel(Decode
                          : (int)((ctx + p.partition_size - 1) / p.partition_size);
   const float* pm = p.part_max + (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride;
   const float* pl = p.part_sum + (int64_t)seq * p.part_seq_stride + (int64_t)head * p.part_head_stride;
+  const float* po = p.part_out + (int64_t)seq * p.part_out_seq_stride + (int64_t)head * p.part_out_head_stride;
   float* w = smem_f;
   float* acc_s = smem_f + ((p.num_partitions + 3) & ~3);
+  const bool dim_ok = d < head_size;
 
-  float M = -INFINITY;
-  for (int i = threadIdx.x; i < nparts; i += blockDim.x) M = fmaxf(M, pm[i]);
+  // every load that needs nothing computed first
+  float x[kReducePre];
+#pragma unroll
+  for (int u = 0; u < kReducePre; ++u) {
+    const int i = warp + u * kReduceWarps;
+    x[u] = (dim_ok && i < nparts) ? po[(int64_t)i * p.part_out_part_stride + d] : 0.f;
+  }
+  const int i0 = threadIdx.x;
+  const float m0 = i0 < nparts ? pm[i0] : -INFINITY, l0 = i0 < nparts ? pl[i0] : 0.f;
+
+  float M = m0;
+  for (int i = i0 + blockDim.x; i < nparts; i += blockDim.x) M = fmaxf(M, pm[i]);
   for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
   if (lane == 0) red[warp] = M;
   __syncthreads();
@@ -452,7 +468,12 @@ __global__ void __launch_bounds__(kReduceWarps * 32) splitk_reduce_kernel(Decode
   __syncthreads();
   M = s_M;
   float L = 0.f;
-  for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
+  if (i0 < nparts) {
+    const float wt = (M == -INFINITY || m0 == -INFINITY) ? 0.f : expf(m0 - M);
+    w[i0] = wt;
+    L = wt * l0;
+  }
+  for (int i = i0 + blockDim.x; i < nparts; i += blockDim.x) {
     const float wt = (M == -INFINITY || pm[i] == -INFINITY) ? 0.f : expf(pm[i] - M);
     w[i] = wt;
     L += wt * pl[i];
@@ -466,25 +487,26 @@ __global__ void __launch_bounds__(kReduceWarps * 32) splitk_reduce_kernel(Decode
     for (int i = 0; i < kReduceWarps; ++i) v += red[i];
     s_inv = 1.f / (v + 1e-6f);
   }
-  const float* po = p.part_out + (int64_t)seq * p.part_out_seq_stride + (int64_t)head * p.part_out_head_stride;
   float a = 0.f;
-  if (d < head_size) {
-    int i = warp;
-    for (; i + 3 * kReduceWarps < nparts; i += 4 * kReduceWarps) {
-      float x[4], ww[4];
+  if (dim_ok) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        x[u] = po[(int64_t)(i + u * kReduceWarps) * p.part_out_part_stride + d];
-        ww[u] = w[i + u * kReduceWarps];
-      }
+    for (int u = 0; u < kReducePre; ++u) {
+      const int i = warp + u * kReduceWarps;
+      if (i < nparts) a += w[i] * x[u];
+    }
+    int i = warp + kReducePre * kReduceWarps;
+    for (; i + (kReduceDepth - 1) * kReduceWarps < nparts; i += kReduceDepth * kReduceWarps) {
+      float y[kReduceDepth];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) a += ww[u] * x[u];
+      for (int u = 0; u < kReduceDepth; ++u) y[u] = po[(int64_t)(i + u * kReduceWarps) * p.part_out_part_stride + d];
+#pragma unroll
+      for (int u = 0; u < kReduceDepth; ++u) a += w[i + u * kReduceWarps] * y[u];
     }
     for (; i < nparts; i += kReduceWarps) a += w[i] * po[(int64_t)i * p.part_out_part_stride + d];
   }
   acc_s[warp * kReduceSlice + lane] = a;
   __syncthreads();
-  if (warp == 0 && d < head_size) {
+  if (warp == 0 && dim_ok) {
     float sum = 0.f;
 #pragma unroll
     for (int k = 0; k < kReduceWarps; ++k) sum += acc_s[k * kReduceSlice + lane];
