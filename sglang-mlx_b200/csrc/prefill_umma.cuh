@@ -70,8 +70,10 @@ __device__ __forceinline__ void commit(uint64_t* bar) {
 }
 // Waits for the phase with `parity`, the thread suspended in the barrier
 // (up to 200 us per try, woken when the phase completes) instead of spinning;
-// gives up after ~1 s of wall time (returns false).
+// gives up after ~1 s of wall time (returns false).  A phase already complete
+// returns at the first test, without reading the clock.
 __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity) {
+  if (mma_detail::mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = mma_detail::global_timer_ns();
   for (;;) {
     uint32_t done;
