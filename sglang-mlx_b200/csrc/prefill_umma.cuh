@@ -851,15 +851,17 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           }
         }
         l = l * alpha + (ps.x + ps.y);  // this half's share of the row sum
-        // O and the P buffer are free once P.V of the previous tile is done
-        if (j >= 1) {
+        // O is rescaled once P.V of the previous tile is done.  P needs no wait:
+        // it goes to this tile's S buffer, whose last reader (P.V two tiles
+        // back) completed before this tile's S did.  pv_done cannot run two
+        // phases ahead of this thread (P.V of this tile needs its P), so the
+        // phases not waited for here keep the parity test exact.
+        if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
           if (!uwait(pv_done, (uint32_t)((gg - 1) & 1))) {
             ok = false;
             break;
           }
           umma::fence_after();
-        }
-        if (__any_sync(0xffffffffu, alpha != 1.f) && j >= 1) {
 #pragma unroll
           for (int c = 0; c < HD; c += RC) {
             uint32_t v[RC];
