@@ -474,7 +474,7 @@ def measure_decode(args, config, rank, world, local_rank, top=True):
     # have no planned entry point, the shim's single-pass / split-K heuristic (the
     # token-pool kernel runs 16-token groups, two CTAs per SM)
     heuristic = mk.choose_decode(B, hkv, max_seq_len, 16 if pool else BS)
-    planned_p = mk.choose_planned_partition(B, hkv, max_seq_len, BS, lens_after)
+    planned_p = mk.choose_planned_partition(B, hkv, max_seq_len, BS, lens_after, head_size=D)
     auto_planned = args.decode == "auto" and not (cfg["partition"] or pool)
     if args.decode == "v1":
         psize = 0

@@ -1564,6 +1564,19 @@ static int mma_variant() {
   return (t == 't' ? 100000 : (t == 's' ? 200000 : 0)) + w * 1000 + s * 100 + g;
 }
 
+// SMs of the current device (cached per device; any racing writer stores the same value).
+static int decode_sm_count() {
+  static std::atomic<int> sms[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+  int n = dev >= 0 && dev < 64 ? sms[dev].load() : 0;
+  if (n <= 0) {
+    if (dev < 0 || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    if (dev >= 0 && dev < 64) sms[dev] = n;
+  }
+  return n;
+}
+
 template <typename T, int D, int BS>
 static cudaError_t launch_mma_typed(const DecodeParams& p, cudaStream_t stream) {
   const int v = mma_variant();
@@ -1578,6 +1591,10 @@ static cudaError_t launch_mma_typed(const DecodeParams& p, cudaStream_t stream) 
       case 1316: if constexpr (BS <= 16) e = launch_mma_nw<T, D, BS, 1, 3, 16>(p, stream); break;
       case 1416: if constexpr (BS <= 16) e = launch_mma_nw<T, D, BS, 1, 4, 16>(p, stream); break;
       case 2316: if constexpr (BS <= 16) e = launch_mma_nw<T, D, BS, 2, 3, 16>(p, stream); break;
+      case 6216: if constexpr (BS <= 16) e = launch_mma_nw<T, D, BS, 6, 2, 16>(p, stream); break;
+      case 8216: if constexpr (BS <= 16) e = launch_mma_nw<T, D, BS, 8, 2, 16>(p, stream); break;
+      case 6316: if constexpr (BS <= 16) e = launch_mma_nw<T, D, BS, 6, 3, 16>(p, stream); break;
+      case 8316: if constexpr (BS <= 16) e = launch_mma_nw<T, D, BS, 8, 3, 16>(p, stream); break;
       case 104316: e = launch_mma_nw<T, D, BS, 4, 3, 16, kTiles>(p, stream); break;
       case 102232: e = launch_mma_nw<T, D, BS, 2, 2, 32, kTiles>(p, stream); break;
       case 204316: if constexpr (BS <= 16) e = launch_mma_nw<T, D, BS, 4, 3, 16, kSwizzledV>(p, stream); break;
@@ -1606,6 +1623,17 @@ static cudaError_t launch_mma_typed(const DecodeParams& p, cudaStream_t stream) 
   // hundreds of 16-32 byte rows.  If no tensor map can be encoded for the
   // cache, plain bulk copies are used.
   if constexpr (BS <= 16) {
+    // One rank's share of a head-sharded batch: a planned decode with at most
+    // two (sequence, KV head) pairs per SM whose partitions hold whole
+    // sequences runs on 8 warps x 2 stages (128 KB, one CTA per SM), so the
+    // longest sequences, which end the launch, stream on twice the warps
+    // (256 sequences of U[512, 4096] tokens, one KV head: 1.73 ms per 32-layer
+    // step against 1.89 with 4 warps and 2048-token partitions; with more
+    // pairs per SM the 4-warp CTAs are faster).
+    if (D == 128 && p.plan_items && p.part_offset == 0 && p.partition_size >= 4096 && p.partition_size % 16 == 0 &&
+        p.max_seq_len <= p.partition_size + 2 * BS &&
+        (int64_t)p.num_seqs * p.num_kv_heads <= 2 * (int64_t)decode_sm_count())
+      return launch_mma_nw<T, D, BS, 8, 2, 16>(p, stream);
     if (p.num_partitions == 1 || p.partition_size % 16 == 0) return launch_mma_nw<T, D, BS, 4, 3, 16>(p, stream);
   } else {
     cudaError_t e = launch_mma_nw<T, D, BS, 2, 2, 32, kSwizzledV>(p, stream);

@@ -82,7 +82,8 @@ def test_sharded_decode_matches_unsharded(gpu, full_config, world):
         q = fc["q"].index_select(0, seqs)[:, q0:q1].contiguous()
         tables = np.ascontiguousarray(w["tables"][p.seqs])
         lens = fc["lens"][p.seqs]
-        psize = mk.choose_planned_partition(len(lens), p.num_kv_heads, w["max_seq_len"], BS, lens)
+        psize = mk.choose_planned_partition(len(lens), p.num_kv_heads, w["max_seq_len"], BS, lens,
+                                           head_size=fc["q"].shape[-1])
         out = mk.paged_attention(q, kc, vc, tables, lens, p.num_kv_heads, fc["scale"], BS,
                                  w["max_seq_len"]).to_numpy()
         assert np.isfinite(out).all()
