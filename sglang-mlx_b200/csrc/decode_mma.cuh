@@ -1595,6 +1595,8 @@ static cudaError_t launch_mma_typed(const DecodeParams& p, cudaStream_t stream) 
       case 8216: if constexpr (BS <= 16) e = launch_mma_nw<T, D, BS, 8, 2, 16>(p, stream); break;
       case 6316: if constexpr (BS <= 16) e = launch_mma_nw<T, D, BS, 6, 3, 16>(p, stream); break;
       case 8316: if constexpr (BS <= 16) e = launch_mma_nw<T, D, BS, 8, 3, 16>(p, stream); break;
+      case 10216: if constexpr (BS <= 16) e = launch_mma_nw<T, D, BS, 10, 2, 16>(p, stream); break;
+      case 12216: if constexpr (BS <= 16) e = launch_mma_nw<T, D, BS, 12, 2, 16>(p, stream); break;
       case 104316: e = launch_mma_nw<T, D, BS, 4, 3, 16, kTiles>(p, stream); break;
       case 102232: e = launch_mma_nw<T, D, BS, 2, 2, 32, kTiles>(p, stream); break;
       case 204316: if constexpr (BS <= 16) e = launch_mma_nw<T, D, BS, 4, 3, 16, kSwizzledV>(p, stream); break;
@@ -1625,15 +1627,15 @@ static cudaError_t launch_mma_typed(const DecodeParams& p, cudaStream_t stream) 
   if constexpr (BS <= 16) {
     // One rank's share of a head-sharded batch: a planned decode with at most
     // two (sequence, KV head) pairs per SM whose partitions hold whole
-    // sequences runs on 8 warps x 2 stages (128 KB, one CTA per SM), so the
-    // longest sequences, which end the launch, stream on twice the warps
-    // (256 sequences of U[512, 4096] tokens, one KV head: 1.73 ms per 32-layer
-    // step against 1.89 with 4 warps and 2048-token partitions; with more
-    // pairs per SM the 4-warp CTAs are faster).
+    // sequences runs on 10 warps x 2 stages (160 KB, one CTA per SM), so the
+    // longest sequences, which end the launch, stream on more warps (256
+    // sequences of U[512, 4096] tokens, one KV head: 1.71 ms per 32-layer step
+    // against 1.89 with 4 warps and 2048-token partitions; 8 warps 1.74, 12
+    // warps 1.71; with more pairs per SM the 4-warp CTAs are faster).
     if (D == 128 && p.plan_items && p.part_offset == 0 && p.partition_size >= 4096 && p.partition_size % 16 == 0 &&
         p.max_seq_len <= p.partition_size + 2 * BS &&
         (int64_t)p.num_seqs * p.num_kv_heads <= 2 * (int64_t)decode_sm_count())
-      return launch_mma_nw<T, D, BS, 8, 2, 16>(p, stream);
+      return launch_mma_nw<T, D, BS, 10, 2, 16>(p, stream);
     if (p.num_partitions == 1 || p.partition_size % 16 == 0) return launch_mma_nw<T, D, BS, 4, 3, 16>(p, stream);
   } else {
     cudaError_t e = launch_mma_nw<T, D, BS, 2, 2, 32, kSwizzledV>(p, stream);

@@ -418,7 +418,7 @@ def choose_planned_partition(num_seqs: int, num_kv_heads: int, max_seq_len: int,
     With at most two (sequence, KV head) pairs per SM (one rank's share of a
     head-sharded batch) and sequences of at most 4096 tokens (plus two blocks),
     head size 128 and blocks of up to 16 tokens, every sequence is one 4096-token
-    partition: the library then runs the decode on 8-warp CTAs, one per SM
+    partition: the library then runs the decode on 10-warp CTAs, one per SM
     (1 KV head of config 2: 0.77 of HBM against 0.71 with 2048-token
     partitions on 4-warp CTAs)."""
     if (head_size == 128 and block_size <= 16 and max_seq_len <= 4096 + 2 * block_size

@@ -34,14 +34,14 @@ def test_cascade_partitions_units_and_bounds():
 def test_planned_partition_choice():
     """choose_planned_partition: whole sequences of up to 4096 tokens when there
     are at most two (sequence, KV head) pairs per SM (head size 128, blocks of
-    up to 16 tokens: the 8-warp decode); otherwise the largest of
+    up to 16 tokens: the 10-warp decode); otherwise the largest of
     4096/2048/1024/512 tokens whose items fill 1.25x the resident CTA slots
     (296 for 16-token blocks)."""
     from sglang_mlx_b200 import metal_kernels as mk
 
     lens = cases.baseline_workload(2)["lens"] + 1
-    assert mk.choose_planned_partition(256, 1, 4112, 16, lens) == 4096   # one rank of an 8-GPU run: 8-warp CTAs
-    assert mk.choose_planned_partition(256, 1, 4112, 16, lens, head_size=64) == 2048   # no 8-warp form: 1.25 slots
+    assert mk.choose_planned_partition(256, 1, 4112, 16, lens) == 4096   # one rank of an 8-GPU run: 10-warp CTAs
+    assert mk.choose_planned_partition(256, 1, 4112, 16, lens, head_size=64) == 2048   # no 10-warp form: 1.25 slots
     assert mk.choose_planned_partition(256, 2, 4112, 16, lens) == 4096
     assert mk.choose_planned_partition(256, 8, 4112, 16, lens) == 4096
     assert mk.choose_planned_partition(300, 1, 4112, 16) == 2048   # more than two pairs per SM

@@ -401,9 +401,9 @@ def test_folded_append_refuses_other_caches(gpu):
 
 @pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
 @pytest.mark.parametrize("bs", [8, 16])
-def test_whole_sequence_partitions_on_eight_warps(gpu, dtype, bs, monkeypatch):
+def test_whole_sequence_partitions_on_ten_warps(gpu, dtype, bs, monkeypatch):
     """Few (sequence, KV head) pairs per SM and whole sequences of up to 4096
-    tokens per partition: the decode runs on 8-warp CTAs (one per SM).  Its
+    tokens per partition: the decode runs on 10-warp CTAs (one per SM).  Its
     output matches the oracle and, within the tolerance, the 4-warp CTAs on the
     same plan (forced through KVC_MMA_CONFIG)."""
     lens = [1, bs - 1, bs, bs + 1, 300, 2049, 4000, 4096, 1025, 777]
@@ -416,16 +416,16 @@ def test_whole_sequence_partitions_on_eight_warps(gpu, dtype, bs, monkeypatch):
     ref = kv_oracle.paged_attention_v1(c["q"], kc, vc, c["block_tables"], c["context_lens"], 2, c["scale"], bs,
                                        c["max_seq_len"])
     wide = _run(c, d, 4096)
-    assert_close(wide, ref, ATOL_NS, RTOL_NS, f"8-warp planned {dtype} bs{bs}")
+    assert_close(wide, ref, ATOL_NS, RTOL_NS, f"10-warp planned {dtype} bs{bs}")
     monkeypatch.setenv("KVC_MMA_CONFIG", "4x3x16")
     four = _run(c, d, 4096)
-    assert_close(wide, four, ATOL_NS, RTOL_NS, "8-warp vs 4-warp CTAs")
+    assert_close(wide, four, ATOL_NS, RTOL_NS, "10-warp vs 4-warp CTAs")
     assert gpu.get_status(clear=True) == 0
 
 
 @pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
-def test_folded_append_on_eight_warps(gpu, dtype):
-    """The folded append in the 8-warp form: caches bit-identical to the append
+def test_folded_append_on_ten_warps(gpu, dtype):
+    """The folded append in the 10-warp form: caches bit-identical to the append
     kernel's, output equal to the planned decode after it, and the oracle."""
     lens = [1, 16, 17, 300, 2048, 2049, 4096, 3000]
     c, keep, key, val, slot = _step_case(7800, dtype, lens, 8, 2, 128, 16)
@@ -437,5 +437,5 @@ def test_folded_append_on_eight_warps(gpu, dtype):
     kc, vc = oracle_fill(c, dtype)
     ref = kv_oracle.paged_attention_v1(c["q"], kc, vc, c["block_tables"], c["context_lens"], 2, c["scale"], 16,
                                        c["max_seq_len"])
-    assert_close(one, ref, ATOL_NS, RTOL_NS, f"folded append, 8 warps, {dtype}")
+    assert_close(one, ref, ATOL_NS, RTOL_NS, f"folded append, 10 warps, {dtype}")
     assert gpu.get_status(clear=True) == 0
