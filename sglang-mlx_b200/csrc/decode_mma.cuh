@@ -1636,6 +1636,10 @@ static cudaError_t launch_mma_typed(const DecodeParams& p, cudaStream_t stream) 
         p.max_seq_len <= p.partition_size + 2 * BS &&
         (int64_t)p.num_seqs * p.num_kv_heads <= 2 * (int64_t)decode_sm_count())
       return launch_mma_nw<T, D, BS, 10, 2, 16>(p, stream);
+    // Other planned decodes: 6 warps x 2 stages (96 KB, two CTAs and 12 warps
+    // per SM; config 2 at 2 / 4 / 8 KV heads per GPU: 3.02 / 6.15 / 12.06 ms per
+    // 32-layer step against 3.12 / 6.33 / 12.62 with 4 warps x 3 stages).
+    if (D == 128 && p.plan_items && p.partition_size % 16 == 0) return launch_mma_nw<T, D, BS, 6, 2, 16>(p, stream);
     if (p.num_partitions == 1 || p.partition_size % 16 == 0) return launch_mma_nw<T, D, BS, 4, 3, 16>(p, stream);
   } else {
     cudaError_t e = launch_mma_nw<T, D, BS, 2, 2, 32, kSwizzledV>(p, stream);
