@@ -1669,8 +1669,9 @@ static cudaError_t launch_mma_t(const DecodeParams& p, const DecodeArgs& a, cuda
                 : launch_mma_fp8<T, 64, kFp8E4M3>(p, a.block_size, stream);
   }
   if (a.flash) {
-    // token-major caches: 16-token groups, 4 warps x 3 stages (108 KB for
-    // D = 128, two CTAs per SM); the block size is read at run time.
+    // token-major caches: 16-token groups, 6 warps x 2 stages for D = 128 and
+    // 4 warps x 3 stages for D = 64 (two CTAs per SM); the block size is read
+    // at run time.
     // KVC_FLASH_COPY=bulk selects per-row bulk copies (tuning runs).
     // KVC_FLASH_COPY=cpasync keeps the per-lane row copies where tensor copies apply (tuning runs).
     // KVC_FLASH_COPY=gather reads dense rows in any order by tensor gathers (below).
@@ -1683,8 +1684,13 @@ static cudaError_t launch_mma_t(const DecodeParams& p, const DecodeArgs& a, cuda
     const bool rows_ok = a.block_size % 16 == 0 && a.k_block_stride == (int64_t)a.block_size * a.k_tok_stride &&
                          a.v_block_stride == (int64_t)a.block_size * a.v_tok_stride &&
                          a.num_blocks * (int64_t)a.block_size < (int64_t)1 << 31 && !(fc && fc[0] == 'c');
+    // D = 128: 6 warps x 2 stages (two CTAs and 12 warps per SM; config 2 on
+    // the pool: page tables 12.67 against 13.54 ms per step with 4 x 3, slot
+    // lists 15.67 against 16.66)
+    const bool six = a.head_size == 128;
     if (rows_ok) {
-      cudaError_t e = a.head_size == 128 ? launch_mma_nw<T, 128, 16, 4, 3, 16, kFlashTma>(p, stream)
+      cudaError_t e = six ? launch_mma_nw<T, 128, 16, 6, 2, 16, kFlashTma>(p, stream)
+                    : a.head_size == 128 ? launch_mma_nw<T, 128, 16, 4, 3, 16, kFlashTma>(p, stream)
                                          : launch_mma_nw<T, 64, 16, 4, 3, 16, kFlashTma>(p, stream);
       if (e != cudaErrorNotSupported) return e;
     }
@@ -1704,6 +1710,7 @@ static cudaError_t launch_mma_t(const DecodeParams& p, const DecodeArgs& a, cuda
                                          : launch_mma_nw<T, 64, 16, 4, 3, 16, kFlashGather>(p, stream);
       if (e != cudaErrorNotSupported) return e;
     }
+    if (six) return launch_mma_nw<T, 128, 16, 6, 2, 16, kFlash>(p, stream);
     if (a.head_size == 128) return launch_mma_nw<T, 128, 16, 4, 3, 16, kFlash>(p, stream);
     return launch_mma_nw<T, 64, 16, 4, 3, 16, kFlash>(p, stream);
   }
