@@ -1615,7 +1615,7 @@ static cudaError_t launch_mma_typed(const DecodeParams& p, cudaStream_t stream) 
       return launch_mma_nw<T, D, BS, 2, 3, 16>(p, stream);
   }
   // Defaults from sweeps on B200: 16-token groups, 4 warps x 3 stages (96 KB,
-  // two CTAs and 8 warps per SM) with whole-page 1-D bulk copies where the
+  // two CTAs and 8 warps per SM; 6 x 2 at D = 128, below) with whole-page 1-D bulk copies where the
   // block size allows (98% of copy bandwidth on config 2, against 81% for
   // 32-token groups).  32-token blocks: 32-token groups, 2 warps x 2 stages
   // (64 KB, three CTAs per SM), K by bulk copy and V through the 128-byte
@@ -1636,11 +1636,15 @@ static cudaError_t launch_mma_typed(const DecodeParams& p, cudaStream_t stream) 
         p.max_seq_len <= p.partition_size + 2 * BS &&
         (int64_t)p.num_seqs * p.num_kv_heads <= 2 * (int64_t)decode_sm_count())
       return launch_mma_nw<T, D, BS, 10, 2, 16>(p, stream);
-    // Other planned decodes: 6 warps x 2 stages (96 KB, two CTAs and 12 warps
-    // per SM; config 2 at 2 / 4 / 8 KV heads per GPU: 3.02 / 6.15 / 12.06 ms per
-    // 32-layer step against 3.12 / 6.33 / 12.62 with 4 warps x 3 stages).
-    if (D == 128 && p.plan_items && p.partition_size % 16 == 0) return launch_mma_nw<T, D, BS, 6, 2, 16>(p, stream);
-    if (p.num_partitions == 1 || p.partition_size % 16 == 0) return launch_mma_nw<T, D, BS, 4, 3, 16>(p, stream);
+    // Otherwise, at D = 128, 6 warps x 2 stages (96 KB, two CTAs and 12 warps
+    // per SM).  Config 2 per 32-layer step against 4 warps x 3 stages: planned
+    // at 2 / 4 / 8 KV heads per GPU 3.02 / 6.15 / 12.06 ms against 3.12 / 6.33 /
+    // 12.62; single pass (v1) 12.22 against 13.11; split-K (v2) 15.29 against
+    // 15.61.
+    if (p.num_partitions == 1 || p.partition_size % 16 == 0) {
+      if constexpr (D == 128) return launch_mma_nw<T, D, BS, 6, 2, 16>(p, stream);
+      return launch_mma_nw<T, D, BS, 4, 3, 16>(p, stream);
+    }
   } else {
     cudaError_t e = launch_mma_nw<T, D, BS, 2, 2, 32, kSwizzledV>(p, stream);
     if (e != cudaErrorNotSupported) return e;
